@@ -1,0 +1,429 @@
+#!/usr/bin/env python
+"""Decode throughput of the B200 minq path (one JSON line on rank 0).
+
+Workload (default `qwen3-4b-q4_0`): the Qwen3-4B-shaped model (36 layers,
+hidden 2560, 32/8 heads, head_dim 128, q/k RMSNorm, intermediate 9728,
+vocab 151936, tied f32 lm_head) with seeded N(0, 0.02) random-init weights
+quantized to Q4_0, batch 1: a 2048-token random prompt is prefilled, then
+every step is ONE greedy decode token (the full forward: 36 layers of fused
+Q4_0 matvecs, RoPE / q-k norm / KV append, split-KV decode attention over
+the f32 cache, f32 lm_head + argmax), each step's token fed from the
+previous step's argmax on the device. Weights (3.8 GB) are far larger than
+L2 (126 MB), so every step streams them from HBM.
+
+  metric   decode tok/s (whole job: sum over ranks)
+  value    device-resident loop, CUDA events on the model stream
+  e2e      same metric through the public C-ABI call minq_forward with host
+           buffers: the token id from pinned host memory in, logits
+           (vocab floats) and the argmax out to host memory, every step
+  roofline dominant kernel (largest device-time share), per-launch CUDA
+           events over a second pass of the same timed loop
+  cpu_baseline  the C++ oracle (reference algorithm, AVX2, OpenMP on all
+           host cores) decoding the same model from the same cache state
+
+`--impl reference` times the reference's CPU algorithm (oracle) alone.
+With torchrun (N>1) every rank decodes its own replica (the batch-1 decode
+does not shard; replicas only) and value = N * steps / max-over-ranks time.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    # name: (arch, prompt tokens)
+    "qwen3-4b-q4_0": ("qwen3-4b", 2048),
+    "qwen2-0.5b-q8_0": ("qwen2-0.5b", 128),
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["minq", "reference"], default="minq")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="qwen3-4b-q4_0")
+    ap.add_argument("--prompt", type=int, default=None, help="prefill length override")
+    ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.idx)], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ helpers
+
+def dist_init():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(world, v: float) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def physical_gpu_index(local: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v for v in vis.split(",") if v.strip()]
+        if local < len(ids) and ids[local].strip().isdigit():
+            return int(ids[local])
+    return local
+
+
+def build_model(mq, synth, cfg, qk_norm, tied, seed):
+    import torch
+    recs = synth.synth_records(cfg, seed, qk_norm, tied, device="cuda")
+    model = mq.Model.from_tensors(cfg, recs)
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return model
+
+
+def cpu_model(orc, synth, cfg, qk_norm, tied, seed):
+    """The same seeded model for the oracle: drawn on the GPU (plumbing), then
+    quantized on the host by the oracle's own quantizer (reference algorithm)."""
+    from minq_b200.minq_format import quantize_tensor_rule, DTYPE_TAGS
+    qtag = DTYPE_TAGS[cfg.dtype]
+    tensors = {}
+    for name, tag, shape, data in synth.synth_records(cfg, seed, qk_norm, tied, device="cuda",
+                                                      quantize=lambda t, x: x):
+        host = data.detach().cpu().numpy()
+        if qtag and quantize_tensor_rule(name, shape):
+            tensors[name] = (qtag, shape, orc.quantize(qtag, host))
+        else:
+            tensors[name] = (0, shape, host)
+        del data
+    cfgd = {k: getattr(cfg, k) for k in cfg.__dataclass_fields__}
+    return orc.Model.from_tensors(cfgd, tensors)
+
+
+def time_cpu_decode(orc, om, oc, first_tok, min_tokens, seconds):
+    """Greedy decode on the oracle for about `seconds` (at least `min_tokens`)."""
+    tok = first_tok
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        logits = om.forward([tok], oc)
+        tok = orc.argmax(logits)
+        n += 1
+        el = time.perf_counter() - t0
+        if n >= min_tokens and el >= seconds:
+            return n, el
+
+
+# ------------------------------------------------------------------ arms
+
+def run_reference(args, world, rank):
+    """The reference's CPU algorithm (oracle, AVX2 + OpenMP on all host cores)."""
+    if rank != 0:
+        return
+    from oracle import oracle as orc
+    from minq_b200 import synth
+    from dataclasses import replace
+    arch, prompt_len = WORKLOADS[args.workload]
+    prompt_len = args.prompt or prompt_len
+    cfg0, qk_norm, tied = synth.ARCH[arch]
+    max_seq = prompt_len + args.warmup + args.steps + 8
+    cfg = replace(cfg0, max_seq_len=max_seq)
+    om = cpu_model(orc, synth, cfg, qk_norm, tied, args.seed)
+    oc = om.new_cache()
+    # KV history of `prompt_len` positions (seeded N(0,1)); decode cost per
+    # token depends only on the history length.
+    kvd = cfg.n_kv_heads * cfg.head_dim
+    rng = np.random.default_rng(args.seed)
+    k = rng.standard_normal((cfg.n_layers, prompt_len, kvd), dtype=np.float32)
+    v = rng.standard_normal((cfg.n_layers, prompt_len, kvd), dtype=np.float32)
+    oc.fill(k, v)
+    del k, v
+    tok = 1
+    for _ in range(args.warmup):
+        tok = orc.argmax(om.forward([tok], oc))
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tok = orc.argmax(om.forward([tok], oc))
+    el = time.perf_counter() - t0
+    value = args.steps / el
+    cores = orc.max_threads()
+    line = {
+        "impl": "reference", "metric": "decode tok/s", "value": value, "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000 * el / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.workload} decode bs=1 at KV length {prompt_len}",
+                   "cache_flush": "weights 3.8 GB > L2"},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} decode tokens after {args.warmup} warm-up, "
+                                   f"KV history {prompt_len}"},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_minq(args, world, rank, local):
+    import torch
+    import minq_b200 as mq
+    from minq_b200 import _lib, synth
+    from dataclasses import replace
+    torch.cuda.set_device(local)
+    L = _lib.lib()
+    arch, prompt_len = WORKLOADS[args.workload]
+    prompt_len = args.prompt or prompt_len
+    cfg0, qk_norm, tied = synth.ARCH[arch]
+    K, W = args.steps, args.warmup
+    max_seq = prompt_len + W + 2 * K + 3 * min(K, 16) + 16
+    cfg = replace(cfg0, max_seq_len=max_seq)
+    model = build_model(mq, synth, cfg, qk_norm, tied, args.seed + rank)
+    cache = model.new_cache()
+    stream = torch.cuda.ExternalStream(model.stream)
+    V = cfg.vocab_size
+
+    # ---- prefill (token-by-token on the device) ----
+    prompt = np.random.default_rng(args.seed).integers(0, V, prompt_len).astype(np.uint32)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    first = model.forward_argmax(prompt, cache)
+    prefill_s = time.perf_counter() - t0
+
+    d_tok = torch.tensor([first], dtype=torch.int32, device="cuda")
+    d_logits = torch.empty(V, dtype=torch.float32, device="cuda")
+
+    def step():
+        model.forward_device(d_tok.data_ptr(), 1, cache, d_logits.data_ptr(), d_tok.data_ptr())
+
+    for _ in range(W):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- timed device-resident loop ----
+    clocks = ClockSampler(physical_gpu_index(local))
+    clocks.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = L.minq_kernel_launches()
+    ev0.record(stream)
+    for _ in range(K):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    launches = L.minq_kernel_launches() - n0
+    barrier(world)
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    ms_max = max_over_ranks(world, ms)
+    value = world * K / (ms_max / 1000.0)
+
+    # ---- e2e through the public C-ABI call with host buffers ----
+    h_tok = torch.empty(1, dtype=torch.int32, pin_memory=True)
+    h_logits = torch.empty(V, dtype=torch.float32, pin_memory=True)
+    h_arg = torch.empty(1, dtype=torch.int32, pin_memory=True)
+    h_tok[0] = int(d_tok.item())
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(K):
+        _lib.check(L.minq_forward(model._h, cache._h, C.c_void_p(h_tok.data_ptr()), 1,
+                                  C.c_void_p(h_logits.data_ptr()), C.c_void_p(h_arg.data_ptr())))
+        h_tok[0] = h_arg[0]
+    e1.record(stream)
+    torch.cuda.synchronize()
+    wall_e2e = time.perf_counter() - t0
+    ms_e2e = max(e0.elapsed_time(e1), 1000.0 * wall_e2e)
+    ms_e2e_max = max_over_ranks(world, ms_e2e)
+    e2e_value = world * K / (ms_e2e_max / 1000.0)
+
+    # ---- per-kernel timing pass (same loop, events around each launch) ----
+    fams = {}
+    for fam in ("qmatvec", "f32_matvec", "attention"):
+        _lib.check(L.minq_kernel_timer_start(fam.encode()))
+        for _ in range(min(K, 16)):
+            step()
+        n = C.c_uint64()
+        tms = C.c_double()
+        byt = C.c_double()
+        _lib.check(L.minq_kernel_timer_stop(C.byref(n), C.byref(tms), C.byref(byt)))
+        if n.value:
+            fams[fam] = {"launches": n.value, "ms": tms.value, "bytes": byt.value,
+                         "avg_us": 1000 * tms.value / n.value,
+                         "gbs": byt.value / (tms.value / 1000.0) / 1e9}
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    peak = peaks.get("hbm_gbs") or 6650.0
+    peak_src = "measured" if peaks.get("hbm_gbs") else "fallback"
+    dom = max(fams, key=lambda k: fams[k]["ms"]) if fams else None
+    roof = None
+    if dom:
+        d = fams[dom]
+        roof = {"bound": "hbm", "kernel": dom, "achieved": d["gbs"], "peak": peak,
+                "unit": "GB/s", "frac": d["gbs"] / peak, "peak_source": peak_src,
+                "traffic": None,
+                "per_launch_bytes": d["bytes"] / d["launches"], "avg_launch_us": d["avg_us"]}
+
+    # ---- CPU baseline (rank 0, N=1): oracle continues the same sequence ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            from oracle import oracle as orc
+            om = cpu_model(orc, synth, replace(cfg, max_seq_len=max_seq), qk_norm, tied,
+                           args.seed + rank)
+            oc = om.new_cache()
+            n_pos = cache.len
+            kvd = cfg.n_kv_heads * cfg.head_dim
+            kall = np.empty((cfg.n_layers, n_pos, kvd), np.float32)
+            vall = np.empty((cfg.n_layers, n_pos, kvd), np.float32)
+            for li in range(cfg.n_layers):
+                kall[li], vall[li] = cache.read(li, 0, n_pos)
+            oc.fill(kall, vall)
+            del kall, vall
+            n, el = time_cpu_decode(orc, om, oc, int(h_tok[0]), 3, args.cpu_seconds)
+            cpu = {"value": n / el, "unit": "tok/s", "cores": orc.max_threads(), "kind": "port",
+                   "sample": f"{n} greedy decode tokens of the same model from the same "
+                             f"{n_pos}-position cache state, {el:.1f} s"}
+            del om, oc
+        except Exception as e:  # the baseline must not sink the GPU number
+            cpu = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                   "sample": f"failed: {type(e).__name__}: {e}"}
+
+    if rank == 0:
+        line = {
+            "metric": "decode tok/s", "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": ms_max / K, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{args.workload} decode bs=1 after a {prompt_len}-token "
+                                   f"prefill (KV length {prompt_len}..{prompt_len + W + K})",
+                       "model": arch, "quant": cfg.dtype, "global_batch": world,
+                       "parallelism": f"replicas x{world}",
+                       "cache_flush": "inputs > L2: 3.8 GB of weights streamed per step"
+                       if arch == "qwen3-4b" else "inputs > L2",
+                       "weight_bytes": model.weight_bytes},
+            "prefill": {"tokens": prompt_len, "tok_s": prompt_len / prefill_s,
+                        "mode": "token-by-token"},
+            "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4,
+                    "d2h_bytes_per_step": 4 * V + 4},
+            "gpu_launches": int(launches),
+            "roofline": roof,
+            "kernels": fams,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    del cache, model
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_init()
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_minq(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

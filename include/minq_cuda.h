@@ -1,0 +1,235 @@
+/*
+ * minq_cuda.h — C ABI of the B200 (sm_100a) implementation of minq's
+ * KV-cached forward path.
+ *
+ * The reference (kn1g78/minq) is a Rust crate with no FFI; every entry point
+ * below replaces one Rust function on the hot path and is what a thin Rust
+ * FFI crate (`minq-cuda-sys`) would bind. The Rust-side `extern "C"` block
+ * and the hook points in `Linear::matvec` / `Model::forward` are written out
+ * in INTEGRATION.md.
+ *
+ * Conventions
+ *  - Every function returns a minq_status; on error, minq_last_error()
+ *    returns a thread-local message (the text of the MinqError variant the
+ *    reference would have produced, error.rs:5-28).
+ *  - "device" pointers are CUDA global memory on the current device; "host"
+ *    pointers are ordinary (pageable or pinned) host memory.
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *    stream). Op-level calls are asynchronous on that stream; model-level
+ *    calls (minq_forward, minq_generate) are synchronous for the caller, like
+ *    the Rust functions they replace.
+ *  - Handles are not thread-safe; use one model/cache per host thread.
+ *  - No entry point falls back to a CPU path: without a usable CUDA device
+ *    every compute call returns MINQ_ERR_CUDA.
+ */
+#ifndef MINQ_CUDA_H_
+#define MINQ_CUDA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MINQ_ABI_VERSION 1
+
+/* error.rs:5-28 MinqError variants, plus the device-side failures. */
+typedef enum minq_status {
+  MINQ_OK = 0,
+  MINQ_ERR_IO = 1,      /* MinqError::Io */
+  MINQ_ERR_SHAPE = 2,   /* MinqError::Shape */
+  MINQ_ERR_FORMAT = 3,  /* MinqError::Format */
+  MINQ_ERR_MODEL = 4,   /* MinqError::Model */
+  MINQ_ERR_CUDA = 5,    /* CUDA runtime / launch failure */
+  MINQ_ERR_NCCL = 6,    /* NCCL failure (tensor-parallel decode) */
+  MINQ_ERR_TIMEOUT = 7, /* a bounded device or collective wait gave up */
+  MINQ_ERR_ARG = 8      /* null pointer / invalid enum */
+} minq_status;
+
+/* Storage tags of the .minq format (format.rs:37-39). */
+typedef enum minq_dtype { MINQ_F32 = 0, MINQ_Q8_0 = 1, MINQ_Q4_0 = 2 } minq_dtype;
+
+/* ModelConfig (model.rs:29-45). `dtype` is the storage tag of the file. */
+typedef struct minq_config {
+  uint64_t hidden_size;
+  uint64_t intermediate_size;
+  uint64_t n_layers;
+  uint64_t n_heads;
+  uint64_t n_kv_heads;
+  uint64_t head_dim;
+  uint64_t vocab_size;
+  uint64_t max_seq_len;
+  float rope_theta;
+  float rms_norm_eps;
+  int32_t has_qkv_bias;
+  int32_t dtype;
+} minq_config;
+
+/* GenStats (engine.rs:11-27). */
+typedef struct minq_gen_stats {
+  uint64_t prompt_tokens;
+  uint64_t gen_tokens;
+  double prefill_secs;
+  double decode_secs;
+} minq_gen_stats;
+
+typedef struct minq_model minq_model;
+typedef struct minq_cache minq_cache;
+
+/* Engine::generate's `on_token` callback (engine.rs:56); a non-zero return
+ * aborts generation and is reported as MINQ_ERR_MODEL (engine.rs:73). */
+typedef int (*minq_token_cb)(uint32_t token, void* user);
+
+const char* minq_last_error(void);
+int minq_abi_version(void);
+/* Number of CUDA kernels this library has launched in this process (all
+ * devices, all threads); a diagnostic for benchmarks. No reference
+ * counterpart. */
+uint64_t minq_kernel_launches(void);
+
+/* Kernel timer (diagnostic; no reference counterpart). Between start and
+ * stop, every launch of the named kernel family ("qmatvec", "f32_matvec",
+ * "attention") is bracketed by CUDA events on its own stream. stop()
+ * synchronises and returns the number of timed launches, their summed
+ * device time in milliseconds and their summed algorithmic bytes (weights
+ * or K/V read plus vectors read and written). */
+minq_status minq_kernel_timer_start(const char* family);
+minq_status minq_kernel_timer_stop(uint64_t* launches, double* total_ms, double* bytes);
+
+/* ---------------------------------------------------------------------- */
+/* Quantized blocks (quantize.rs)                                          */
+
+/* quantize_q8_0 / quantize_q4_0 (quantize.rs:78,120) on the GPU; device x
+ * [n] -> device out [n/32 * {36,20}] bytes, bit-identical to the reference.
+ * n % 32 != 0 -> MINQ_ERR_SHAPE (quantize.rs:67-75). */
+minq_status minq_quantize(minq_dtype dtype, const float* x, size_t n, void* out, void* stream);
+
+/* dequantize_q8_0 / dequantize_q4_0 (quantize.rs:99,146); device in/out. */
+minq_status minq_dequantize(minq_dtype dtype, const void* blocks, size_t nbytes, float* out,
+                            size_t n_out, void* stream);
+
+/* QuantizedTensor::matvec (quantize.rs:215-249): y[rows] = W[rows, cols] x.
+ * `blocks` is the reference's row-major block layout, device memory.
+ * x_len != cols -> MINQ_ERR_SHAPE (quantize.rs:216-222). */
+minq_status minq_qmatvec(minq_dtype dtype, const void* blocks, size_t rows, size_t cols,
+                         const float* x, size_t x_len, float* y, void* stream);
+
+/* tensor::matvec (tensor.rs:181-192) for a dense f32 [rows, cols] weight. */
+minq_status minq_matvec_f32(const float* w, size_t rows, size_t cols, const float* x,
+                            size_t x_len, float* y, void* stream);
+
+/* sampler::argmax (sampler.rs:10-17): total_cmp order, ties to the lowest
+ * index. Device logits [n] -> device *out. */
+minq_status minq_argmax(const float* logits, size_t n, uint32_t* out, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Decode attention (model.rs:223-248 `attend`, plus the RoPE / q-k norm /  */
+/* cache append that precede it in forward_token, model.rs:291-303)         */
+
+/* Bytes of device workspace minq_attn_decode / minq_attend need for up to
+ * `max_len` attended positions (any head_dim <= 256). */
+size_t minq_attn_workspace_bytes(size_t batch, size_t n_heads, size_t max_len);
+
+/* One decode-attention step for `batch` independent sequences at the same
+ * position `pos`:
+ *   q      [batch, n_heads, head_dim]     pre-RoPE query (left unchanged;
+ *                                         the rotated copy lives in the
+ *                                         workspace)
+ *   k_new  [batch, n_kv, head_dim]        pre-RoPE key of this position
+ *   v_new  [batch, n_kv, head_dim]
+ *   q_norm, k_norm  [head_dim] or NULL    Qwen3 per-head RMSNorm gains
+ *   rope_cos, rope_sin [>pos, head_dim/2] tables built like RopeTables::new
+ *   k_cache, v_cache  cache of sequence b, kv-head h, position t at
+ *                     element b*seq_stride + h*head_stride + t*pos_stride
+ *                     (the reference's LayerCache layout is head_stride =
+ *                     head_dim, pos_stride = n_kv*head_dim)
+ *   out    [batch, n_heads, head_dim]
+ * The rotated key and the value are appended at position `pos`, then every
+ * query head attends over positions 0..=pos. `workspace` (device) must hold
+ * minq_attn_workspace_bytes(batch, n_heads, pos+1) bytes. */
+minq_status minq_attn_decode(const float* q, const float* k_new, const float* v_new,
+                             const float* q_norm, const float* k_norm, float eps,
+                             const float* rope_cos, const float* rope_sin, size_t batch,
+                             size_t n_heads, size_t n_kv, size_t head_dim, size_t pos,
+                             float* k_cache, float* v_cache, size_t seq_stride,
+                             size_t head_stride, size_t pos_stride, float* out, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
+/* attend() alone (no RoPE / append) over a position-major history
+ * k, v [len, n_kv*head_dim] for one query q [n_heads*head_dim]; device
+ * pointers. Unit-parity entry for model.rs:223-248. */
+minq_status minq_attend(const float* q, const float* k, const float* v, size_t len,
+                        size_t n_heads, size_t n_kv, size_t head_dim, float* out,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Model (model.rs:88-98, assemble :522-574, load_minq :711-715)           */
+
+/* load_minq: parse a .minq file (format.rs:149-277) and upload it to the
+ * current device. */
+minq_status minq_model_load(const char* path, minq_model** out);
+
+/* Builder mirroring assemble(config, get): create, add named tensors (host
+ * or device data in the .minq record encoding), then finish, which validates
+ * the geometry exactly like assemble and builds the RoPE tables. */
+minq_status minq_model_new(const minq_config* cfg, minq_model** out);
+minq_status minq_model_add_tensor(minq_model* m, const char* name, minq_dtype tag,
+                                  size_t ndim, const uint64_t* shape, const void* data,
+                                  size_t nbytes, int data_on_device);
+minq_status minq_model_finish(minq_model* m);
+minq_status minq_model_config(const minq_model* m, minq_config* out);
+/* Device bytes held by the model's weights (the per-token weight traffic). */
+minq_status minq_model_weight_bytes(const minq_model* m, uint64_t* out);
+void minq_model_free(minq_model* m);
+
+/* KVCache::new / reset (model.rs:117-130). The cache is preallocated in HBM
+ * for `max_seq` positions (0 = config.max_seq_len) and `batch` independent
+ * sequences (1 for the reference's single-sequence API). */
+minq_status minq_cache_new(minq_model* m, size_t batch, size_t max_seq, minq_cache** out);
+minq_status minq_cache_reset(minq_cache* c);
+minq_status minq_cache_len(const minq_cache* c, size_t* out);
+/* Write / read positions [start, start+n) of one layer, sequence 0, in the
+ * reference's LayerCache layout ([n, n_kv*head_dim] f32, K post-RoPE), host
+ * memory. Writing past the current length extends it (the reference's
+ * public `LayerCache` fields allow the same pre-fill, model.rs:103-114).
+ * minq_cache_set_len sets the length after a pre-fill of every layer. */
+minq_status minq_cache_write(minq_cache* c, size_t layer, size_t start, size_t n,
+                             const float* k, const float* v);
+minq_status minq_cache_read(const minq_cache* c, size_t layer, size_t start, size_t n, float* k,
+                            float* v);
+minq_status minq_cache_set_len(minq_cache* c, size_t len);
+void minq_cache_free(minq_cache* c);
+
+/* Model::forward (model.rs:254-270): run `tokens` (host) through the model,
+ * appending to the cache; writes the last token's logits to `logits_out`
+ * (host, vocab_size floats, or NULL) and its argmax to `argmax_out` (host,
+ * or NULL). Empty input -> MINQ_ERR_MODEL "empty token sequence"; a position
+ * at max_seq_len -> MINQ_ERR_MODEL "sequence exceeds max_seq_len (N)";
+ * token >= vocab -> MINQ_ERR_SHAPE. n > 1 runs the batched prefill path;
+ * the cache and last logits match n single-token calls. */
+minq_status minq_forward(minq_model* m, minq_cache* c, const uint32_t* tokens, size_t n,
+                         float* logits_out, uint32_t* argmax_out);
+
+/* Same as minq_forward with device-resident token ids and outputs on the
+ * model's stream (no host synchronisation): used to measure the kernels
+ * without host copies and to chain decode steps. */
+minq_status minq_forward_device(minq_model* m, minq_cache* c, const uint32_t* d_tokens,
+                                size_t n, float* d_logits, uint32_t* d_argmax);
+
+/* Engine::generate with Sampler::greedy (engine.rs:52-88): prefill the
+ * prompt, then up to max_tokens greedy steps; `on_token` may be NULL;
+ * `stop_tokens` (host, n_stop) end generation after reporting the token. */
+minq_status minq_generate(minq_model* m, const uint32_t* prompt, size_t n_prompt,
+                          size_t max_tokens, const uint32_t* stop_tokens, size_t n_stop,
+                          minq_token_cb on_token, void* user, uint32_t* tokens_out,
+                          minq_gen_stats* stats);
+
+/* The model's CUDA stream (cudaStream_t as void*). */
+void* minq_model_stream(minq_model* m);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MINQ_CUDA_H_ */

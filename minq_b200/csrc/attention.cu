@@ -1,0 +1,435 @@
+// Decode attention over the HBM-resident f32 KV cache (model.rs:223-248
+// `attend`, with the RoPE / Qwen3 q-k RMSNorm / cache append of
+// forward_token, model.rs:291-303, in a small pre-kernel).
+//
+// Split-KV flash-decode:
+//   * grid = (splits, n_kv * ceil(G/8), batch): one CTA owns one KV head, up
+//     to 8 of the G query heads that share it (GQA, model.rs:226,232), and a
+//     chunk of positions. K and V are each read from HBM exactly once per
+//     query-head group.
+//   * QK^T: 8-element lane slices (HD/8 lanes per position), float4 loads of
+//     K that are contiguous across the lanes of a position, a shuffle
+//     reduction inside the position's lane group; the query slice for every
+//     head of the group lives in registers.
+//   * Online softmax per warp over tiles of 32 positions (lane t owns
+//     position t of the tile), exp via expf, running max / sum rescaling.
+//   * PV: lanes split head_dim (float4 for HD=128), V rows are read fully
+//     coalesced, the probability of position t is broadcast by a shuffle.
+//   * Warps of a CTA merge their (max, sum, out) in shared memory; CTAs of a
+//     split write unnormalised partials to the workspace and a combine kernel
+//     merges the splits. With one split the CTA writes the output directly.
+#include <math.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "ktimer.h"
+
+namespace minq {
+
+struct AttnParams {
+  const float* q;        // [B, nh, HD] rotated queries
+  const float* k;        // cache base
+  const float* v;
+  size_t seq_stride, head_stride, pos_stride;  // element strides of the cache
+  int nh, nkv, len, chunk, nsplit;
+  float scale;           // 1/sqrt(HD)
+  float* out;            // [B, nh, HD]
+  float* ws_o;           // [B, nh, nsplit, HD]
+  float* ws_ml;          // [B, nh, nsplit, 2]
+};
+
+template <int HD, int GMAX>
+__global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
+  constexpr int EPL = 8;                       // elements per lane in QK
+  constexpr int LPP = HD / EPL;                // lanes per position (1..32)
+  constexpr int PPS = 32 / LPP;                // positions per sub-step
+  constexpr int DPL = HD >= 32 ? HD / 32 : 1;  // PV dims per lane
+  constexpr int PV_LANES = HD / DPL;           // lanes active in PV
+  static_assert(HD % 8 == 0 && HD <= 256, "head_dim");
+
+  __shared__ float s_sc[4][GMAX][32];
+  __shared__ float s_m[4][GMAX], s_l[4][GMAX];
+  __shared__ float s_o[4][GMAX][HD];
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int b = blockIdx.z;
+  const int G = p.nh / p.nkv;
+  const int qgroups = (G + 7) / 8;
+  const int kvh = blockIdx.y / qgroups;
+  const int g0 = (blockIdx.y % qgroups) * 8;
+  const int ng = min(GMAX, G - g0);
+  const int split = blockIdx.x;
+  const int t_begin = split * p.chunk;
+  const int t_end = min(p.len, t_begin + p.chunk);
+
+  const float* kb = p.k + b * p.seq_stride + kvh * p.head_stride;
+  const float* vb = p.v + b * p.seq_stride + kvh * p.head_stride;
+
+  // Query slices: lane part j owns elements [4j, 4j+4) and [HD/2 + 4j, ...)
+  // for HD >= 16 (two float4 per lane), or all 8 elements for HD == 8.
+  const int j = lane % LPP;
+  const int pslot = lane / LPP;
+  float qr[GMAX][EPL];
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g) {
+    const float* qh = p.q + ((size_t)b * p.nh + kvh * G + g0 + (g < ng ? g : 0)) * HD;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      int idx = HD >= 16 ? ((e < 4) ? 4 * j + e : HD / 2 + 4 * j + e - 4) : e;
+      qr[g][e] = g < ng ? qh[idx] * p.scale : 0.0f;
+    }
+  }
+
+  float m_w[GMAX], l_w[GMAX], o[GMAX][DPL];
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g) {
+    m_w[g] = -INFINITY;
+    l_w[g] = 0.0f;
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) o[g][d] = 0.0f;
+  }
+
+  for (int tile = t_begin + warp * 32; tile < t_end; tile += nwarps * 32) {
+    // --- scores for the 32 positions of this tile ---
+#pragma unroll 2
+    for (int ss = 0; ss < 32 / PPS; ++ss) {
+      const int tl = ss * PPS + pslot;  // tile-local position
+      const int t = tile + tl;
+      float kv[EPL];
+      if (t < t_end) {
+        const float* kt = kb + (size_t)t * p.pos_stride;
+        if constexpr (HD >= 16) {
+          float4 a = *reinterpret_cast<const float4*>(kt + 4 * j);
+          float4 c = *reinterpret_cast<const float4*>(kt + HD / 2 + 4 * j);
+          kv[0] = a.x; kv[1] = a.y; kv[2] = a.z; kv[3] = a.w;
+          kv[4] = c.x; kv[5] = c.y; kv[6] = c.z; kv[7] = c.w;
+        } else {
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) kv[e] = kt[e];
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) kv[e] = 0.0f;
+      }
+#pragma unroll
+      for (int g = 0; g < GMAX; ++g) {
+        float s = 0.0f;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) s = fmaf(qr[g][e], kv[e], s);
+#pragma unroll
+        for (int off = LPP / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+        if (j == 0) s_sc[warp][g][tl] = t < t_end ? s : -INFINITY;
+      }
+    }
+    __syncwarp();
+    // --- online softmax over the tile; lane owns position `lane` ---
+    float pr[GMAX];
+#pragma unroll
+    for (int g = 0; g < GMAX; ++g) {
+      const float s = s_sc[warp][g][lane];
+      const float mt = warp_max(s);
+      const float mn = fmaxf(m_w[g], mt);
+      const float corr = m_w[g] == -INFINITY ? 0.0f : expf(m_w[g] - mn);
+      pr[g] = s == -INFINITY ? 0.0f : expf(s - mn);
+      l_w[g] = l_w[g] * corr + pr[g];
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) o[g][d] *= corr;
+      m_w[g] = mn;
+    }
+    __syncwarp();
+    // --- PV ---
+    const int nt = min(32, t_end - tile);
+    for (int tl = 0; tl < nt; ++tl) {
+      const float* vt = vb + (size_t)(tile + tl) * p.pos_stride;
+      float vv[DPL];
+      if (lane < PV_LANES) {
+        if constexpr (DPL == 4) {
+          float4 a = *reinterpret_cast<const float4*>(vt + 4 * lane);
+          vv[0] = a.x; vv[1] = a.y; vv[2] = a.z; vv[3] = a.w;
+        } else if constexpr (DPL == 2) {
+          float2 a = *reinterpret_cast<const float2*>(vt + 2 * lane);
+          vv[0] = a.x; vv[1] = a.y;
+        } else {
+#pragma unroll
+          for (int d = 0; d < DPL; ++d) vv[d] = vt[DPL * lane + d];
+        }
+      } else {
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) vv[d] = 0.0f;
+      }
+#pragma unroll
+      for (int g = 0; g < GMAX; ++g) {
+        const float pt = __shfl_sync(0xffffffffu, pr[g], tl);
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) o[g][d] = fmaf(pt, vv[d], o[g][d]);
+      }
+    }
+  }
+
+  // --- merge warps ---
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g) {
+    const float lsum = warp_sum(l_w[g]);
+    if (lane == 0) {
+      s_m[warp][g] = m_w[g];
+      s_l[warp][g] = lsum;
+    }
+    if (lane < PV_LANES) {
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) s_o[warp][g][DPL * lane + d] = o[g][d];
+    }
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < ng * HD; idx += blockDim.x) {
+    const int g = idx / HD, d = idx % HD;
+    float M = -INFINITY;
+    for (int w = 0; w < nwarps; ++w) M = fmaxf(M, s_m[w][g]);
+    float L = 0.0f, O = 0.0f;
+    for (int w = 0; w < nwarps; ++w) {
+      if (s_m[w][g] == -INFINITY) continue;
+      const float f = expf(s_m[w][g] - M);
+      L = fmaf(s_l[w][g], f, L);
+      O = fmaf(s_o[w][g][d], f, O);
+    }
+    const int qh = kvh * G + g0 + g;
+    const size_t row = (size_t)b * p.nh + qh;
+    if (p.nsplit == 1) {
+      p.out[row * HD + d] = O / L;
+    } else {
+      p.ws_o[(row * p.nsplit + split) * HD + d] = O;
+      if (d == 0) {
+        p.ws_ml[(row * p.nsplit + split) * 2 + 0] = M;
+        p.ws_ml[(row * p.nsplit + split) * 2 + 1] = L;
+      }
+    }
+  }
+}
+
+// Merge the splits of every (sequence, query head).
+__global__ void attn_combine_kernel(const float* ws_o, const float* ws_ml, int nsplit, int hd,
+                                    float* out) {
+  const size_t row = blockIdx.x;  // b * nh + h
+  const float* ml = ws_ml + row * nsplit * 2;
+  float M = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, ml[2 * s]);
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float L = 0.0f, O = 0.0f;
+    for (int s = 0; s < nsplit; ++s) {
+      const float m = ml[2 * s];
+      if (m == -INFINITY) continue;
+      const float f = expf(m - M);
+      L = fmaf(ml[2 * s + 1], f, L);
+      O = fmaf(ws_o[(row * nsplit + s) * hd + d], f, O);
+    }
+    out[row * hd + d] = O / L;
+  }
+}
+
+// Per-head RMSNorm (model.rs:206-216), RoPE from tables (model.rs:189-201),
+// and the cache append (model.rs:300-301). grid = (nh + 2*nkv heads, B);
+// one warp per head.
+struct RopeParams {
+  const float* q_in;   // [B, nh, HD]
+  const float* k_in;   // [B, nkv, HD]
+  const float* v_in;   // [B, nkv, HD]
+  size_t q_in_bstride, kv_in_bstride;  // element stride between sequences
+  const float* q_norm;
+  const float* k_norm;
+  float eps;
+  const float* cos_t;  // [max_seq, HD/2]
+  const float* sin_t;
+  int nh, nkv, hd, pos;
+  float* q_out;        // [B, nh, HD]
+  float* k_cache;
+  float* v_cache;
+  size_t seq_stride, head_stride, pos_stride;
+};
+
+__global__ void rope_append_kernel(RopeParams p) {
+  const int lane = threadIdx.x & 31;
+  const int head = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int b = blockIdx.y;
+  const int nheads = p.nh + 2 * p.nkv;
+  if (head >= nheads) return;
+  const int hd = p.hd, half = hd / 2;
+  float vals[8];  // hd <= 256
+  const float* src;
+  const float* gain = nullptr;
+  float* dst;
+  bool rope = true;
+  if (head < p.nh) {
+    src = p.q_in + b * p.q_in_bstride + (size_t)head * hd;
+    gain = p.q_norm;
+    dst = p.q_out + ((size_t)b * p.nh + head) * hd;
+  } else if (head < p.nh + p.nkv) {
+    const int h = head - p.nh;
+    src = p.k_in + b * p.kv_in_bstride + (size_t)h * hd;
+    gain = p.k_norm;
+    dst = p.k_cache + b * p.seq_stride + h * p.head_stride + (size_t)p.pos * p.pos_stride;
+  } else {
+    const int h = head - p.nh - p.nkv;
+    src = p.v_in + b * p.kv_in_bstride + (size_t)h * hd;
+    dst = p.v_cache + b * p.seq_stride + h * p.head_stride + (size_t)p.pos * p.pos_stride;
+    rope = false;
+  }
+  // Lane owns element pairs (i, i + half) for i = lane, lane + 32, ...
+  const int npairs = (half + 31) / 32;
+  for (int k = 0; k < npairs; ++k) {
+    const int i = lane + 32 * k;
+    vals[2 * k] = i < half ? src[i] : 0.0f;
+    vals[2 * k + 1] = i < half ? src[i + half] : 0.0f;
+  }
+  if (gain) {
+    float ss = 0.0f;
+    for (int k = 0; k < npairs; ++k) ss = fmaf(vals[2 * k], vals[2 * k], fmaf(vals[2 * k + 1], vals[2 * k + 1], ss));
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)hd + p.eps);
+    for (int k = 0; k < npairs; ++k) {
+      const int i = lane + 32 * k;
+      if (i < half) {
+        vals[2 * k] = vals[2 * k] * inv * gain[i];
+        vals[2 * k + 1] = vals[2 * k + 1] * inv * gain[i + half];
+      }
+    }
+  }
+  for (int k = 0; k < npairs; ++k) {
+    const int i = lane + 32 * k;
+    if (i >= half) continue;
+    float x1 = vals[2 * k], x2 = vals[2 * k + 1];
+    if (rope) {
+      const float c = p.cos_t[(size_t)p.pos * half + i];
+      const float s = p.sin_t[(size_t)p.pos * half + i];
+      // head[i] = x1*cos - x2*sin; head[i+half] = x2*cos + x1*sin (un-fused)
+      const float y1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+      const float y2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+      x1 = y1;
+      x2 = y2;
+    }
+    dst[i] = x1;
+    dst[i + half] = x2;
+  }
+}
+
+// ---------------------------------------------------------------------------
+
+static int pick_chunk(int len, size_t units) {
+  const size_t target = (size_t)sm_count() * 8;
+  size_t c = ((size_t)len * units + target - 1) / target;
+  c = (c + 31) / 32 * 32;
+  if (c < 32) c = 32;
+  if (c > 4096) c = 4096;
+  return (int)c;
+}
+
+size_t attn_workspace_bytes(size_t batch, size_t nh, size_t len, size_t hd_max) {
+  // Upper bound over every chunk choice: splits <= ceil(len / 32).
+  const size_t splits = (len + 31) / 32;
+  return batch * nh * splits * (hd_max + 2) * sizeof(float) + 256;
+}
+
+template <int HD>
+static minq_status launch_split_hd(const AttnParams& p, int gmax, dim3 grid, int threads,
+                                   cudaStream_t s) {
+  switch (gmax) {
+    case 1: attn_split_kernel<HD, 1><<<grid, threads, 0, s>>>(p); break;
+    case 2: attn_split_kernel<HD, 2><<<grid, threads, 0, s>>>(p); break;
+    case 4: attn_split_kernel<HD, 4><<<grid, threads, 0, s>>>(p); break;
+    default: attn_split_kernel<HD, 8><<<grid, threads, 0, s>>>(p); break;
+  }
+  return MINQ_OK;
+}
+
+minq_status launch_attention(const float* q, const float* k, const float* v, size_t batch,
+                             int nh, int nkv, int hd, int len, size_t seq_stride,
+                             size_t head_stride, size_t pos_stride, float* out, void* ws,
+                             size_t ws_bytes, cudaStream_t s) {
+  if (len <= 0) return fail(MINQ_ERR_SHAPE, "attention over an empty history");
+  if (nkv <= 0 || nh % nkv != 0)
+    return fail(MINQ_ERR_MODEL, "n_heads must be a multiple of n_kv_heads");
+  const int G = nh / nkv;
+  const int qgroups = (G + 7) / 8;
+  const int gmax = G >= 8 ? 8 : (G > 4 ? 8 : (G > 2 ? 4 : (G > 1 ? 2 : 1)));
+  AttnParams p{};
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.seq_stride = seq_stride;
+  p.head_stride = head_stride;
+  p.pos_stride = pos_stride;
+  p.nh = nh;
+  p.nkv = nkv;
+  p.len = len;
+  p.chunk = pick_chunk(len, batch * nkv * qgroups);
+  p.nsplit = (len + p.chunk - 1) / p.chunk;
+  p.scale = 1.0f / sqrtf((float)hd);
+  p.out = out;
+  if (p.nsplit > 1) {
+    const size_t need = batch * nh * p.nsplit * (hd + 2) * sizeof(float);
+    if (!ws || ws_bytes < need)
+      return fail(MINQ_ERR_ARG, "attention workspace too small (need " + std::to_string(need) +
+                                    " bytes)");
+    p.ws_o = static_cast<float*>(ws);
+    p.ws_ml = p.ws_o + batch * nh * p.nsplit * hd;
+  }
+  const int threads = 32 * std::min(4, (p.chunk + 31) / 32);
+  dim3 grid(p.nsplit, nkv * qgroups, (unsigned)batch);
+  ScopedKTimer timer(KF_ATTENTION, s,
+                     8.0 * batch * nkv * hd * (double)len + 8.0 * batch * nh * hd);
+  switch (hd) {
+    case 8: MINQ_TRY(launch_split_hd<8>(p, gmax, grid, threads, s)); break;
+    case 16: MINQ_TRY(launch_split_hd<16>(p, gmax, grid, threads, s)); break;
+    case 32: MINQ_TRY(launch_split_hd<32>(p, gmax, grid, threads, s)); break;
+    case 64: MINQ_TRY(launch_split_hd<64>(p, gmax, grid, threads, s)); break;
+    case 128: MINQ_TRY(launch_split_hd<128>(p, gmax, grid, threads, s)); break;
+    case 256: MINQ_TRY(launch_split_hd<256>(p, gmax, grid, threads, s)); break;
+    default:
+      return fail(MINQ_ERR_SHAPE, "unsupported head_dim " + std::to_string(hd) +
+                                      " (supported: 8, 16, 32, 64, 128, 256)");
+  }
+  MINQ_LAUNCH_CHECK("attn_split_kernel");
+  if (p.nsplit > 1) {
+    attn_combine_kernel<<<(unsigned)(batch * nh), std::min(hd, 128), 0, s>>>(p.ws_o, p.ws_ml,
+                                                                            p.nsplit, hd, out);
+    MINQ_LAUNCH_CHECK("attn_combine_kernel");
+  }
+  return MINQ_OK;
+}
+
+minq_status launch_rope_append(const float* q_in, const float* k_in, const float* v_in,
+                               size_t q_in_bstride, size_t kv_in_bstride, const float* q_norm,
+                               const float* k_norm, float eps, const float* cos_t,
+                               const float* sin_t, size_t batch, int nh, int nkv, int hd,
+                               int pos, float* q_out, float* k_cache, float* v_cache,
+                               size_t seq_stride, size_t head_stride, size_t pos_stride,
+                               cudaStream_t s) {
+  if (hd % 2 != 0 || hd > 256) return fail(MINQ_ERR_SHAPE, "head_dim must be even and <= 256");
+  RopeParams p{};
+  p.q_in = q_in;
+  p.k_in = k_in;
+  p.v_in = v_in;
+  p.q_in_bstride = q_in_bstride;
+  p.kv_in_bstride = kv_in_bstride;
+  p.q_norm = q_norm;
+  p.k_norm = k_norm;
+  p.eps = eps;
+  p.cos_t = cos_t;
+  p.sin_t = sin_t;
+  p.nh = nh;
+  p.nkv = nkv;
+  p.hd = hd;
+  p.pos = pos;
+  p.q_out = q_out;
+  p.k_cache = k_cache;
+  p.v_cache = v_cache;
+  p.seq_stride = seq_stride;
+  p.head_stride = head_stride;
+  p.pos_stride = pos_stride;
+  const int heads = nh + 2 * nkv;
+  dim3 grid((heads + 3) / 4, (unsigned)batch);
+  rope_append_kernel<<<grid, 128, 0, s>>>(p);
+  MINQ_LAUNCH_CHECK("rope_append_kernel");
+  return MINQ_OK;
+}
+
+}  // namespace minq

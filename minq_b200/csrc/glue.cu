@@ -1,0 +1,88 @@
+// Small elementwise kernels of the forward step that are not fused into a
+// matvec: embedding row gather (model.rs:275), standalone RMSNorm
+// (tensor.rs:219-227, for dense-f32 layers), bias/residual epilogue
+// (tensor.rs:195 add_) and SwiGLU (tensor.rs:203-215) after f32 matvecs.
+#include "common.cuh"
+
+namespace minq {
+
+__global__ void embed_kernel(const float* __restrict__ embed, const uint32_t* tok, size_t vocab,
+                             int hidden, float* __restrict__ x) {
+  uint32_t t = *tok;
+  if (t >= vocab) t = 0;  // host validates tokens; never read out of bounds
+  const float* row = embed + (size_t)t * hidden;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < hidden; i += gridDim.x * blockDim.x)
+    x[i] = row[i];
+}
+
+__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                               float eps, int n, float* __restrict__ out) {
+  __shared__ float red[33];
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[32] = 1.0f / sqrtf(v / (float)n + eps);
+  }
+  __syncthreads();
+  const float inv = red[32];
+  for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = x[i] * inv * w[i];
+}
+
+__global__ void epilogue_kernel(const float* acc, const float* bias, const float* residual,
+                                float* y, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    float v = acc[i];
+    if (bias) v += bias[i];
+    if (residual) v = residual[i] + v;
+    y[i] = v;
+  }
+}
+
+__global__ void swiglu_kernel(const float* g, const float* u, float* h, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const float v = g[i];
+    h[i] = (v / (1.0f + expf(-v))) * u[i];
+  }
+}
+
+static unsigned ew_grid(size_t n) {
+  size_t g = (n + 255) / 256;
+  size_t cap = (size_t)sm_count() * 8;
+  return (unsigned)(g < 1 ? 1 : (g > cap ? cap : g));
+}
+
+minq_status launch_embed(const float* embed, const uint32_t* d_tok, size_t vocab, int hidden,
+                         float* x, cudaStream_t s) {
+  embed_kernel<<<(hidden + 255) / 256, 256, 0, s>>>(embed, d_tok, vocab, hidden, x);
+  MINQ_LAUNCH_CHECK("embed_kernel");
+  return MINQ_OK;
+}
+
+minq_status launch_rmsnorm(const float* x, const float* w, float eps, int n, float* out,
+                           cudaStream_t s) {
+  rmsnorm_kernel<<<1, 1024, 0, s>>>(x, w, eps, n, out);
+  MINQ_LAUNCH_CHECK("rmsnorm_kernel");
+  return MINQ_OK;
+}
+
+minq_status launch_epilogue(const float* acc, const float* bias, const float* residual, float* y,
+                            size_t n, cudaStream_t s) {
+  epilogue_kernel<<<ew_grid(n), 256, 0, s>>>(acc, bias, residual, y, n);
+  MINQ_LAUNCH_CHECK("epilogue_kernel");
+  return MINQ_OK;
+}
+
+minq_status launch_swiglu(const float* g, const float* u, float* h, size_t n, cudaStream_t s) {
+  swiglu_kernel<<<ew_grid(n), 256, 0, s>>>(g, u, h, n);
+  MINQ_LAUNCH_CHECK("swiglu_kernel");
+  return MINQ_OK;
+}
+
+}  // namespace minq

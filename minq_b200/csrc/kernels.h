@@ -1,0 +1,53 @@
+// Host launchers of the CUDA kernels (one declaration per .cu entry).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/minq_cuda.h"
+
+namespace minq {
+
+// quant.cu
+minq_status launch_quantize(int dtype, const float* x, size_t n, void* out, cudaStream_t s);
+minq_status launch_dequantize(int dtype, const void* in, size_t nblocks, float* out,
+                              cudaStream_t s);
+
+// matvec.cu
+minq_status launch_qmatvec(int dtype, const void* w0, const void* w1, size_t rows, int cols,
+                           const float* x, const float* norm_w, float eps, const float* bias,
+                           const float* residual, float* y, cudaStream_t s);
+minq_status launch_f32_matvec(const float* w, size_t rows, int cols, const float* x,
+                              const float* norm_w, float eps, float* y,
+                              unsigned long long* argmax_part, int* n_part, cudaStream_t s);
+minq_status launch_argmax_final(const unsigned long long* part, int n, uint32_t* out,
+                                cudaStream_t s);
+minq_status launch_argmax(const float* x, size_t n, unsigned long long* part, int n_part,
+                          uint32_t* out, cudaStream_t s);
+int argmax_parts_capacity();
+
+// attention.cu
+size_t attn_workspace_bytes(size_t batch, size_t nh, size_t len, size_t hd_max);
+minq_status launch_attention(const float* q, const float* k, const float* v, size_t batch,
+                             int nh, int nkv, int hd, int len, size_t seq_stride,
+                             size_t head_stride, size_t pos_stride, float* out, void* ws,
+                             size_t ws_bytes, cudaStream_t s);
+minq_status launch_rope_append(const float* q_in, const float* k_in, const float* v_in,
+                               size_t q_in_bstride, size_t kv_in_bstride, const float* q_norm,
+                               const float* k_norm, float eps, const float* cos_t,
+                               const float* sin_t, size_t batch, int nh, int nkv, int hd,
+                               int pos, float* q_out, float* k_cache, float* v_cache,
+                               size_t seq_stride, size_t head_stride, size_t pos_stride,
+                               cudaStream_t s);
+
+// glue.cu
+minq_status launch_embed(const float* embed, const uint32_t* d_tok, size_t vocab, int hidden,
+                         float* x, cudaStream_t s);
+minq_status launch_rmsnorm(const float* x, const float* w, float eps, int n, float* out,
+                           cudaStream_t s);
+minq_status launch_epilogue(const float* acc, const float* bias, const float* residual, float* y,
+                            size_t n, cudaStream_t s);
+minq_status launch_swiglu(const float* g, const float* u, float* h, size_t n, cudaStream_t s);
+
+}  // namespace minq

@@ -1,0 +1,764 @@
+// Device-resident model, KV cache and the KV-cached forward step
+// (model.rs:88-318, engine.rs:52-88) behind the C ABI of include/minq_cuda.h.
+//
+// Layout in HBM:
+//   * weights keep the .minq encoding: quantized matrices in the reference's
+//     row-major AoS block layout; q/k/v of a layer are concatenated into one
+//     [qd + 2*kvd, H] matrix when they share a quantized dtype, so one matvec
+//     launch covers all three projections (plus the concatenated bias);
+//   * the tied lm_head aliases the f32 embedding table (no clone, unlike
+//     model.rs:564);
+//   * the KV cache is preallocated per layer as [batch][n_kv][max_seq][hd]
+//     f32 (head-major: one contiguous stream per KV head for decode
+//     attention), K stored post-RoPE like LayerCache (model.rs:100-106);
+//   * RoPE cos/sin tables [max_seq_len, hd/2] are built on the host with the
+//     reference's f32 expression and glibc (model.rs:170-186) and uploaded.
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "minq_format.h"
+
+namespace minq {
+
+struct DevTensor {
+  int tag = -1;
+  std::vector<uint64_t> shape;
+  void* ptr = nullptr;
+  size_t nbytes = 0;
+};
+
+struct DevLinear {
+  int tag = -1;  // MINQ_F32 / MINQ_Q8_0 / MINQ_Q4_0; -1 absent
+  uint64_t rows = 0, cols = 0;
+  const void* ptr = nullptr;
+  size_t nbytes = 0;
+};
+
+struct DevLayer {
+  const float* attn_norm = nullptr;
+  const float* ffn_norm = nullptr;
+  DevLinear q, k, v, o, gate, up, down;
+  DevLinear qkv;                 // fused q|k|v (tag -1 when not fused)
+  float* bias_qkv = nullptr;     // [qd + 2*kvd] when any bias exists
+  const float* q_bias = nullptr;
+  const float* k_bias = nullptr;
+  const float* v_bias = nullptr;
+  const float* q_norm = nullptr;
+  const float* k_norm = nullptr;
+};
+
+}  // namespace minq
+
+using minq::DevLayer;
+using minq::DevLinear;
+using minq::DevTensor;
+
+struct minq_model {
+  minq_config cfg{};
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  bool finished = false;
+  std::map<std::string, DevTensor> pending;
+  std::vector<void*> allocs;
+  // assembled
+  const float* embed = nullptr;
+  std::vector<DevLayer> layers;
+  const float* final_norm = nullptr;
+  DevLinear lm_head;
+  float* rope_cos = nullptr;
+  float* rope_sin = nullptr;
+  std::string shape_error;  // reported by forward as MinqError::Shape
+  uint64_t weight_bytes = 0;
+  // activation scratch (single sequence)
+  float *x = nullptr, *xn = nullptr, *qkv = nullptr, *q_rot = nullptr, *att = nullptr;
+  float *hbuf = nullptr, *gbuf = nullptr, *ubuf = nullptr, *tmp = nullptr, *logits = nullptr;
+  unsigned long long* argmax_part = nullptr;
+  int argmax_cap = 0;
+  uint32_t* d_argmax = nullptr;
+  uint32_t* d_tokens = nullptr;
+  size_t d_tokens_cap = 0;
+};
+
+struct minq_cache {
+  minq_model* m = nullptr;
+  size_t batch = 1, max_seq = 0, len = 0;
+  float* k = nullptr;  // [n_layers][batch][n_kv][max_seq][hd]
+  float* v = nullptr;
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+};
+
+namespace minq {
+
+namespace {
+
+minq_status dmalloc(minq_model* m, void** p, size_t bytes) {
+  if (bytes == 0) bytes = 16;
+  cudaError_t e = cudaMalloc(p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+  m->allocs.push_back(*p);
+  return MINQ_OK;
+}
+
+// RopeTables::new (model.rs:171-186): freq = 1 / theta^(2i/hd), angle =
+// pos * freq, (sin, cos) = angle.sin_cos(), all in f32 through glibc. The
+// calls go through volatile pointers so the host compiler neither folds nor
+// fuses them into a different routine.
+void build_rope_tables(uint64_t hd, uint64_t max_seq, float theta, std::vector<float>* cs,
+                       std::vector<float>* sn) {
+  float (*volatile powf_p)(float, float) = ::powf;
+  float (*volatile sinf_p)(float) = ::sinf;
+  float (*volatile cosf_p)(float) = ::cosf;
+  const uint64_t half = hd / 2;
+  cs->assign(max_seq * half, 0.0f);
+  sn->assign(max_seq * half, 0.0f);
+  std::vector<float> freq(half);
+  for (uint64_t i = 0; i < half; ++i) {
+    volatile float e = 2.0f * (float)i / (float)hd;
+    freq[i] = 1.0f / powf_p(theta, e);
+  }
+  for (uint64_t pos = 0; pos < max_seq; ++pos) {
+    for (uint64_t i = 0; i < half; ++i) {
+      volatile float angle = (float)pos * freq[i];
+      (*sn)[pos * half + i] = sinf_p(angle);
+      (*cs)[pos * half + i] = cosf_p(angle);
+    }
+  }
+}
+
+std::string shape_str(const std::vector<uint64_t>& s) {
+  std::string o = "[";
+  for (size_t i = 0; i < s.size(); ++i) o += (i ? ", " : "") + std::to_string(s[i]);
+  return o + "]";
+}
+
+minq_status need(minq_model* m, const std::string& name, DevTensor** out) {
+  auto it = m->pending.find(name);
+  if (it == m->pending.end()) return fail(MINQ_ERR_MODEL, "missing tensor `" + name + "`");
+  *out = &it->second;
+  return MINQ_OK;
+}
+
+minq_status get_linear(minq_model* m, const std::string& name, DevLinear* out) {
+  DevTensor* t;
+  MINQ_TRY(need(m, name, &t));
+  if (t->tag == MINQ_F32 && t->shape.size() != 2)
+    return fail(MINQ_ERR_MODEL, "tensor `" + name + "` must be 2-D, got " + shape_str(t->shape));
+  out->tag = t->tag;
+  out->rows = t->shape[0];
+  out->cols = t->shape[1];
+  out->ptr = t->ptr;
+  out->nbytes = t->nbytes;
+  return MINQ_OK;
+}
+
+minq_status get_vec(minq_model* m, const std::string& name, bool required, const float** out,
+                    uint64_t* len) {
+  auto it = m->pending.find(name);
+  if (it == m->pending.end()) {
+    if (required) return fail(MINQ_ERR_MODEL, "missing tensor `" + name + "`");
+    *out = nullptr;
+    return MINQ_OK;
+  }
+  const DevTensor& t = it->second;
+  if (t.tag != MINQ_F32 || t.shape.size() != 1)
+    return fail(MINQ_ERR_MODEL, "tensor `" + name + "` must be a 1-D f32 vector");
+  *out = static_cast<const float*>(t.ptr);
+  if (len) *len = t.shape[0];
+  return MINQ_OK;
+}
+
+// Record the first geometry mismatch; the reference reports it as
+// MinqError::Shape from the first matvec that sees it (quantize.rs:216-222,
+// tensor.rs:182-188), so forward returns it rather than load.
+void check_linear(minq_model* m, const DevLinear& l, uint64_t rows, uint64_t cols,
+                  const char* what) {
+  if (!m->shape_error.empty()) return;
+  if (l.cols != cols)
+    m->shape_error = std::string(l.tag == MINQ_F32 ? "matvec" : "quantized matvec") + ": " +
+                     what + " has " + std::to_string(l.cols) + " cols vs input len " +
+                     std::to_string(cols);
+  else if (l.rows != rows)
+    m->shape_error = std::string(what) + ": " + std::to_string(l.rows) + " rows, expected " +
+                     std::to_string(rows);
+}
+
+void check_vec(minq_model* m, const float* p, uint64_t len, uint64_t want, const char* what) {
+  if (!m->shape_error.empty() || !p) return;
+  if (len != want)
+    m->shape_error = std::string(what) + ": length " + std::to_string(len) + ", expected " +
+                     std::to_string(want);
+}
+
+}  // namespace
+
+// assemble (model.rs:522-574) on device tensors.
+minq_status model_finish(minq_model* m) {
+  const minq_config& c = m->cfg;
+  if (c.head_dim % 2 != 0) return fail(MINQ_ERR_MODEL, "head_dim must be even (RoPE)");
+  if (c.n_kv_heads == 0 || c.n_heads % c.n_kv_heads != 0)
+    return fail(MINQ_ERR_MODEL, "n_heads must be a multiple of n_kv_heads");
+  DevTensor* emb;
+  MINQ_TRY(need(m, "model.embed_tokens.weight", &emb));
+  if (emb->tag != MINQ_F32 || emb->shape.size() != 2)
+    return fail(MINQ_ERR_MODEL, "model.embed_tokens.weight must be 2-D f32");
+  m->embed = static_cast<const float*>(emb->ptr);
+  const uint64_t H = c.hidden_size, hd = c.head_dim, qd = c.n_heads * hd,
+                 kvd = c.n_kv_heads * hd, I = c.intermediate_size;
+  if (!m->shape_error.empty()) {}
+  if (emb->shape[1] != H && m->shape_error.empty())
+    m->shape_error = "embedding width " + std::to_string(emb->shape[1]) + " != hidden_size";
+  if (emb->shape[0] < c.vocab_size && m->shape_error.empty())
+    m->shape_error = "embedding has " + std::to_string(emb->shape[0]) + " rows < vocab_size";
+  m->layers.assign(c.n_layers, DevLayer());
+  m->weight_bytes = 0;
+  for (uint64_t i = 0; i < c.n_layers; ++i) {
+    const std::string p = "model.layers." + std::to_string(i);
+    DevLayer& L = m->layers[i];
+    uint64_t n1 = 0, n2 = 0, nqb = 0, nkb = 0, nvb = 0, nqn = 0, nkn = 0;
+    MINQ_TRY(get_vec(m, p + ".input_layernorm.weight", true, &L.attn_norm, &n1));
+    MINQ_TRY(get_linear(m, p + ".self_attn.q_proj.weight", &L.q));
+    MINQ_TRY(get_linear(m, p + ".self_attn.k_proj.weight", &L.k));
+    MINQ_TRY(get_linear(m, p + ".self_attn.v_proj.weight", &L.v));
+    MINQ_TRY(get_linear(m, p + ".self_attn.o_proj.weight", &L.o));
+    MINQ_TRY(get_vec(m, p + ".self_attn.q_proj.bias", false, &L.q_bias, &nqb));
+    MINQ_TRY(get_vec(m, p + ".self_attn.k_proj.bias", false, &L.k_bias, &nkb));
+    MINQ_TRY(get_vec(m, p + ".self_attn.v_proj.bias", false, &L.v_bias, &nvb));
+    MINQ_TRY(get_vec(m, p + ".self_attn.q_norm.weight", false, &L.q_norm, &nqn));
+    MINQ_TRY(get_vec(m, p + ".self_attn.k_norm.weight", false, &L.k_norm, &nkn));
+    MINQ_TRY(get_vec(m, p + ".post_attention_layernorm.weight", true, &L.ffn_norm, &n2));
+    MINQ_TRY(get_linear(m, p + ".mlp.gate_proj.weight", &L.gate));
+    MINQ_TRY(get_linear(m, p + ".mlp.up_proj.weight", &L.up));
+    MINQ_TRY(get_linear(m, p + ".mlp.down_proj.weight", &L.down));
+    check_vec(m, L.attn_norm, n1, H, "input_layernorm");
+    check_linear(m, L.q, qd, H, "q_proj");
+    check_linear(m, L.k, kvd, H, "k_proj");
+    check_linear(m, L.v, kvd, H, "v_proj");
+    check_vec(m, L.q_bias, nqb, qd, "q_proj.bias");
+    check_vec(m, L.k_bias, nkb, kvd, "k_proj.bias");
+    check_vec(m, L.v_bias, nvb, kvd, "v_proj.bias");
+    check_vec(m, L.q_norm, nqn, hd, "q_norm");
+    check_vec(m, L.k_norm, nkn, hd, "k_norm");
+    check_linear(m, L.o, H, qd, "o_proj");
+    check_vec(m, L.ffn_norm, n2, H, "post_attention_layernorm");
+    check_linear(m, L.gate, I, H, "gate_proj");
+    check_linear(m, L.up, I, H, "up_proj");
+    check_linear(m, L.down, H, I, "down_proj");
+    for (const DevLinear* l : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down})
+      m->weight_bytes += l->nbytes;
+    // Fuse q|k|v (same quantized dtype, consistent shapes) into one matrix.
+    if (m->shape_error.empty() && L.q.tag != MINQ_F32 && L.q.tag == L.k.tag &&
+        L.q.tag == L.v.tag) {
+      void* buf;
+      const size_t nb = L.q.nbytes + L.k.nbytes + L.v.nbytes;
+      MINQ_TRY(dmalloc(m, &buf, nb));
+      char* d = static_cast<char*>(buf);
+      MINQ_CUDA_TRY(cudaMemcpyAsync(d, L.q.ptr, L.q.nbytes, cudaMemcpyDeviceToDevice, m->stream));
+      MINQ_CUDA_TRY(cudaMemcpyAsync(d + L.q.nbytes, L.k.ptr, L.k.nbytes,
+                                    cudaMemcpyDeviceToDevice, m->stream));
+      MINQ_CUDA_TRY(cudaMemcpyAsync(d + L.q.nbytes + L.k.nbytes, L.v.ptr, L.v.nbytes,
+                                    cudaMemcpyDeviceToDevice, m->stream));
+      L.qkv.tag = L.q.tag;
+      L.qkv.rows = qd + 2 * kvd;
+      L.qkv.cols = H;
+      L.qkv.ptr = buf;
+      L.qkv.nbytes = nb;
+      if (L.q_bias || L.k_bias || L.v_bias) {
+        void* bb;
+        MINQ_TRY(dmalloc(m, &bb, (qd + 2 * kvd) * 4));
+        L.bias_qkv = static_cast<float*>(bb);
+        MINQ_CUDA_TRY(cudaMemsetAsync(bb, 0, (qd + 2 * kvd) * 4, m->stream));
+        if (L.q_bias)
+          MINQ_CUDA_TRY(cudaMemcpyAsync(L.bias_qkv, L.q_bias, qd * 4, cudaMemcpyDeviceToDevice,
+                                        m->stream));
+        if (L.k_bias)
+          MINQ_CUDA_TRY(cudaMemcpyAsync(L.bias_qkv + qd, L.k_bias, kvd * 4,
+                                        cudaMemcpyDeviceToDevice, m->stream));
+        if (L.v_bias)
+          MINQ_CUDA_TRY(cudaMemcpyAsync(L.bias_qkv + qd + kvd, L.v_bias, kvd * 4,
+                                        cudaMemcpyDeviceToDevice, m->stream));
+      }
+    }
+  }
+  uint64_t nf = 0;
+  MINQ_TRY(get_vec(m, "model.norm.weight", true, &m->final_norm, &nf));
+  check_vec(m, m->final_norm, nf, H, "model.norm");
+  if (m->pending.count("lm_head.weight")) {
+    MINQ_TRY(get_linear(m, "lm_head.weight", &m->lm_head));
+  } else {  // tied embeddings (model.rs:561-565), aliased instead of cloned
+    m->lm_head.tag = MINQ_F32;
+    m->lm_head.rows = emb->shape[0];
+    m->lm_head.cols = emb->shape[1];
+    m->lm_head.ptr = emb->ptr;
+    m->lm_head.nbytes = emb->nbytes;
+  }
+  check_linear(m, m->lm_head, m->lm_head.rows, H, "lm_head");
+  if (m->shape_error.empty() && m->lm_head.rows < c.vocab_size)
+    m->shape_error = "lm_head has fewer rows than vocab_size";
+  m->weight_bytes += m->lm_head.nbytes;
+  if (m->lm_head.tag == MINQ_F32 && (H % 4 != 0) && m->shape_error.empty())
+    m->shape_error = "hidden_size must be a multiple of 4 for the f32 lm_head kernel";
+
+  // RoPE tables.
+  std::vector<float> cs, sn;
+  build_rope_tables(hd, c.max_seq_len, c.rope_theta, &cs, &sn);
+  void *pc, *ps;
+  MINQ_TRY(dmalloc(m, &pc, cs.size() * 4));
+  MINQ_TRY(dmalloc(m, &ps, sn.size() * 4));
+  m->rope_cos = static_cast<float*>(pc);
+  m->rope_sin = static_cast<float*>(ps);
+  MINQ_CUDA_TRY(cudaMemcpy(pc, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+  MINQ_CUDA_TRY(cudaMemcpy(ps, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+
+  // Activation scratch.
+  const uint64_t V = m->lm_head.rows;
+  const uint64_t big = std::max<uint64_t>({qd + 2 * kvd, I, H, V, 1});
+  void* p;
+  auto alloc_f = [&](float** dst, uint64_t n) -> minq_status {
+    MINQ_TRY(dmalloc(m, &p, n * 4));
+    *dst = static_cast<float*>(p);
+    return MINQ_OK;
+  };
+  MINQ_TRY(alloc_f(&m->x, H));
+  MINQ_TRY(alloc_f(&m->xn, H));
+  MINQ_TRY(alloc_f(&m->qkv, qd + 2 * kvd));
+  MINQ_TRY(alloc_f(&m->q_rot, qd));
+  MINQ_TRY(alloc_f(&m->att, qd));
+  MINQ_TRY(alloc_f(&m->hbuf, I));
+  MINQ_TRY(alloc_f(&m->gbuf, I));
+  MINQ_TRY(alloc_f(&m->ubuf, I));
+  MINQ_TRY(alloc_f(&m->tmp, big));
+  MINQ_TRY(alloc_f(&m->logits, V));
+  m->argmax_cap = argmax_parts_capacity();
+  MINQ_TRY(dmalloc(m, &p, m->argmax_cap * sizeof(unsigned long long)));
+  m->argmax_part = static_cast<unsigned long long*>(p);
+  MINQ_TRY(dmalloc(m, &p, 16));
+  m->d_argmax = static_cast<uint32_t*>(p);
+  m->d_tokens_cap = 4096;
+  MINQ_TRY(dmalloc(m, &p, m->d_tokens_cap * 4));
+  m->d_tokens = static_cast<uint32_t*>(p);
+  MINQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  m->finished = true;
+  return MINQ_OK;
+}
+
+namespace {
+
+// y = L x (+ bias) (+ residual), optionally with RMSNorm(x; norm_w) applied
+// first. Quantized weights use the fused matvec; dense f32 weights use the
+// f32 matvec then an elementwise epilogue.
+minq_status linear(minq_model* m, const DevLinear& l, const float* x, const float* norm_w,
+                   const float* bias, const float* residual, float* y) {
+  const float eps = m->cfg.rms_norm_eps;
+  if (l.tag != MINQ_F32)
+    return launch_qmatvec(l.tag, l.ptr, nullptr, l.rows, (int)l.cols, x, norm_w, eps, bias,
+                          residual, y, m->stream);
+  const bool epi = bias || residual;
+  float* dst = epi ? m->tmp : y;
+  if (l.cols % 4 != 0) return fail(MINQ_ERR_SHAPE, "f32 matvec needs cols % 4 == 0");
+  MINQ_TRY(launch_f32_matvec(static_cast<const float*>(l.ptr), l.rows, (int)l.cols, x, norm_w,
+                             eps, dst, nullptr, nullptr, m->stream));
+  if (epi) MINQ_TRY(launch_epilogue(m->tmp, bias, residual, y, l.rows, m->stream));
+  return MINQ_OK;
+}
+
+}  // namespace
+
+// model.rs:273-318 for one token at `pos`; the token id is read from device
+// memory. Logits (and their argmax) only when `want_logits`.
+minq_status forward_token(minq_model* m, minq_cache* c, const uint32_t* d_tok, size_t pos,
+                          bool want_logits, float* d_logits, uint32_t* d_argmax) {
+  const minq_config& cfg = m->cfg;
+  const int H = (int)cfg.hidden_size, hd = (int)cfg.head_dim, nh = (int)cfg.n_heads,
+            nkv = (int)cfg.n_kv_heads;
+  const uint64_t qd = (uint64_t)nh * hd, kvd = (uint64_t)nkv * hd, I = cfg.intermediate_size;
+  const float eps = cfg.rms_norm_eps;
+  cudaStream_t s = m->stream;
+  const size_t seq_stride = (size_t)nkv * c->max_seq * hd, head_stride = c->max_seq * hd,
+               pos_stride = hd;
+  const size_t layer_elems = c->batch * seq_stride;
+  MINQ_TRY(launch_embed(m->embed, d_tok, cfg.vocab_size, H, m->x, s));
+  for (uint64_t li = 0; li < cfg.n_layers; ++li) {
+    const DevLayer& L = m->layers[li];
+    // attention sub-layer: q|k|v = W (rmsnorm(x)) + bias
+    if (L.qkv.tag >= 0) {
+      MINQ_TRY(launch_qmatvec(L.qkv.tag, L.qkv.ptr, nullptr, L.qkv.rows, H, m->x, L.attn_norm,
+                              eps, L.bias_qkv, nullptr, m->qkv, s));
+    } else {
+      MINQ_TRY(launch_rmsnorm(m->x, L.attn_norm, eps, H, m->xn, s));
+      MINQ_TRY(linear(m, L.q, m->xn, nullptr, L.q_bias, nullptr, m->qkv));
+      MINQ_TRY(linear(m, L.k, m->xn, nullptr, L.k_bias, nullptr, m->qkv + qd));
+      MINQ_TRY(linear(m, L.v, m->xn, nullptr, L.v_bias, nullptr, m->qkv + qd + kvd));
+    }
+    float* kc = c->k + li * layer_elems;
+    float* vc = c->v + li * layer_elems;
+    MINQ_TRY(launch_rope_append(m->qkv, m->qkv + qd, m->qkv + qd + kvd, 0, 0, L.q_norm,
+                                L.k_norm, eps, m->rope_cos, m->rope_sin, 1, nh, nkv, hd,
+                                (int)pos, m->q_rot, kc, vc, seq_stride, head_stride, pos_stride,
+                                s));
+    MINQ_TRY(launch_attention(m->q_rot, kc, vc, 1, nh, nkv, hd, (int)pos + 1, seq_stride,
+                              head_stride, pos_stride, m->att, c->ws, c->ws_bytes, s));
+    MINQ_TRY(linear(m, L.o, m->att, nullptr, nullptr, m->x, m->x));  // x += o
+    // MLP sub-layer: h = silu(gate(rmsnorm(x))) * up(rmsnorm(x)); x += down(h)
+    if (L.gate.tag != MINQ_F32 && L.gate.tag == L.up.tag) {
+      MINQ_TRY(launch_qmatvec(L.gate.tag, L.gate.ptr, L.up.ptr, I, H, m->x, L.ffn_norm, eps,
+                              nullptr, nullptr, m->hbuf, s));
+    } else {
+      MINQ_TRY(launch_rmsnorm(m->x, L.ffn_norm, eps, H, m->xn, s));
+      MINQ_TRY(linear(m, L.gate, m->xn, nullptr, nullptr, nullptr, m->gbuf));
+      MINQ_TRY(linear(m, L.up, m->xn, nullptr, nullptr, nullptr, m->ubuf));
+      MINQ_TRY(launch_swiglu(m->gbuf, m->ubuf, m->hbuf, I, s));
+    }
+    MINQ_TRY(linear(m, L.down, m->hbuf, nullptr, nullptr, m->x, m->x));  // x += down
+  }
+  if (!want_logits) return MINQ_OK;
+  const uint64_t V = cfg.vocab_size;
+  if (m->lm_head.tag == MINQ_F32) {
+    int nparts = m->argmax_cap;
+    MINQ_TRY(launch_f32_matvec(static_cast<const float*>(m->lm_head.ptr), V, H, m->x,
+                               m->final_norm, eps, d_logits, m->argmax_part, &nparts, s));
+    MINQ_TRY(launch_argmax_final(m->argmax_part, nparts, d_argmax, s));
+  } else {
+    MINQ_TRY(launch_qmatvec(m->lm_head.tag, m->lm_head.ptr, nullptr, V, H, m->x, m->final_norm,
+                            eps, nullptr, nullptr, d_logits, s));
+    MINQ_TRY(launch_argmax(d_logits, V, m->argmax_part, m->argmax_cap, d_argmax, s));
+  }
+  return MINQ_OK;
+}
+
+}  // namespace minq
+
+using namespace minq;
+
+// ---------------------------------------------------------------------------
+// C ABI: model
+
+extern "C" {
+
+minq_status minq_model_new(const minq_config* cfg, minq_model** out) {
+  if (!cfg || !out) return fail(MINQ_ERR_ARG, "null argument");
+  int dev_count = 0;
+  cudaError_t e = cudaGetDeviceCount(&dev_count);
+  if (e != cudaSuccess || dev_count == 0)
+    return fail(MINQ_ERR_CUDA, "no CUDA device available (the CUDA path has no CPU fallback)");
+  minq_model* m = new minq_model();
+  m->cfg = *cfg;
+  cudaGetDevice(&m->device);
+  e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
+  if (e != cudaSuccess) {
+    delete m;
+    return cuda_fail(e, "cudaStreamCreate");
+  }
+  *out = m;
+  return MINQ_OK;
+}
+
+minq_status minq_model_add_tensor(minq_model* m, const char* name, minq_dtype tag, size_t ndim,
+                                  const uint64_t* shape, const void* data, size_t nbytes,
+                                  int data_on_device) {
+  if (!m || !name || (ndim && !shape) || (nbytes && !data))
+    return fail(MINQ_ERR_ARG, "null argument");
+  if (m->finished) return fail(MINQ_ERR_MODEL, "model already finished");
+  if (tag != MINQ_F32 && tag != MINQ_Q8_0 && tag != MINQ_Q4_0)
+    return fail(MINQ_ERR_FORMAT, std::string("tensor `") + name + "`: unknown storage tag " +
+                                     std::to_string((int)tag));
+  uint64_t numel = 1;
+  for (size_t i = 0; i < ndim; ++i) numel *= shape[i];
+  uint64_t expected;
+  if (tag == MINQ_F32) {
+    expected = numel * 4;
+  } else {
+    if (ndim != 2)
+      return fail(MINQ_ERR_FORMAT, std::string("quantized tensor `") + name + "` must be 2-D");
+    if (shape[1] % 32 != 0)
+      return fail(MINQ_ERR_FORMAT,
+                  std::string("quantized tensor `") + name + "`: cols not block-aligned");
+    expected = shape[0] * (shape[1] / 32) * (uint64_t)block_bytes(tag);
+  }
+  if (expected != nbytes)
+    return fail(MINQ_ERR_FORMAT, std::string("tensor `") + name + "`: data length " +
+                                     std::to_string(nbytes) + " != shape-derived " +
+                                     std::to_string(expected));
+  DevTensor t;
+  t.tag = tag;
+  t.shape.assign(shape, shape + ndim);
+  t.nbytes = nbytes;
+  MINQ_CUDA_TRY(cudaSetDevice(m->device));
+  void* p;
+  MINQ_TRY(dmalloc(m, &p, nbytes));
+  t.ptr = p;
+  MINQ_CUDA_TRY(cudaMemcpy(p, data, nbytes,
+                           data_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
+  auto it = m->pending.find(name);
+  if (it != m->pending.end()) it->second = t;  // last record wins, like the HashMap
+  else m->pending.emplace(name, t);
+  return MINQ_OK;
+}
+
+minq_status minq_model_finish(minq_model* m) {
+  if (!m) return fail(MINQ_ERR_ARG, "null model");
+  if (m->finished) return MINQ_OK;
+  MINQ_CUDA_TRY(cudaSetDevice(m->device));
+  return model_finish(m);
+}
+
+minq_status minq_model_load(const char* path, minq_model** out) {
+  if (!path || !out) return fail(MINQ_ERR_ARG, "null argument");
+  minq_config cfg{};
+  std::vector<MinqRecord> recs;
+  std::string err;
+  minq_status st = read_minq_file(path, &cfg, &recs, &err);
+  if (st != MINQ_OK) return fail(st, err);
+  minq_model* m = nullptr;
+  MINQ_TRY(minq_model_new(&cfg, &m));
+  for (MinqRecord& r : recs) {
+    st = minq_model_add_tensor(m, r.name.c_str(), (minq_dtype)r.tag, r.shape.size(),
+                               r.shape.data(), r.data.data(), r.data.size(), 0);
+    std::vector<uint8_t>().swap(r.data);
+    if (st != MINQ_OK) {
+      minq_model_free(m);
+      return st;
+    }
+  }
+  st = minq_model_finish(m);
+  if (st != MINQ_OK) {
+    std::string msg = minq_last_error();
+    minq_model_free(m);
+    return fail(st, msg);
+  }
+  *out = m;
+  return MINQ_OK;
+}
+
+minq_status minq_model_config(const minq_model* m, minq_config* out) {
+  if (!m || !out) return fail(MINQ_ERR_ARG, "null argument");
+  *out = m->cfg;
+  return MINQ_OK;
+}
+
+minq_status minq_model_weight_bytes(const minq_model* m, uint64_t* out) {
+  if (!m || !out) return fail(MINQ_ERR_ARG, "null argument");
+  *out = m->weight_bytes;
+  return MINQ_OK;
+}
+
+void* minq_model_stream(minq_model* m) { return m ? (void*)m->stream : nullptr; }
+
+void minq_model_free(minq_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  if (m->stream) cudaStreamSynchronize(m->stream);
+  for (void* p : m->allocs) cudaFree(p);
+  if (m->stream) cudaStreamDestroy(m->stream);
+  delete m;
+}
+
+// ---------------------------------------------------------------------------
+// C ABI: cache
+
+minq_status minq_cache_new(minq_model* m, size_t batch, size_t max_seq, minq_cache** out) {
+  if (!m || !out) return fail(MINQ_ERR_ARG, "null argument");
+  if (!m->finished) return fail(MINQ_ERR_MODEL, "model not finished");
+  if (batch == 0) return fail(MINQ_ERR_ARG, "batch must be >= 1");
+  if (max_seq == 0 || max_seq > m->cfg.max_seq_len) max_seq = m->cfg.max_seq_len;
+  MINQ_CUDA_TRY(cudaSetDevice(m->device));
+  minq_cache* c = new minq_cache();
+  c->m = m;
+  c->batch = batch;
+  c->max_seq = max_seq;
+  const size_t per_layer = batch * m->cfg.n_kv_heads * max_seq * m->cfg.head_dim;
+  const size_t bytes = m->cfg.n_layers * per_layer * sizeof(float);
+  cudaError_t e = cudaMalloc(&c->k, bytes ? bytes : 16);
+  if (e == cudaSuccess) e = cudaMalloc(&c->v, bytes ? bytes : 16);
+  c->ws_bytes = attn_workspace_bytes(batch, m->cfg.n_heads, max_seq, m->cfg.head_dim);
+  if (e == cudaSuccess) e = cudaMalloc(&c->ws, c->ws_bytes);
+  if (e != cudaSuccess) {
+    cudaFree(c->k);
+    cudaFree(c->v);
+    cudaFree(c->ws);
+    delete c;
+    return cuda_fail(e, "cudaMalloc(kv cache)");
+  }
+  *out = c;
+  return MINQ_OK;
+}
+
+minq_status minq_cache_reset(minq_cache* c) {
+  if (!c) return fail(MINQ_ERR_ARG, "null cache");
+  c->len = 0;
+  return MINQ_OK;
+}
+
+minq_status minq_cache_len(const minq_cache* c, size_t* out) {
+  if (!c || !out) return fail(MINQ_ERR_ARG, "null argument");
+  *out = c->len;
+  return MINQ_OK;
+}
+
+minq_status minq_cache_set_len(minq_cache* c, size_t len) {
+  if (!c) return fail(MINQ_ERR_ARG, "null cache");
+  if (len > c->max_seq) return fail(MINQ_ERR_MODEL, "length exceeds cache capacity");
+  c->len = len;
+  return MINQ_OK;
+}
+
+static minq_status cache_copy(const minq_cache* c, size_t layer, size_t start, size_t n,
+                              float* host_k, float* host_v, bool to_device) {
+  const minq_config& cfg = c->m->cfg;
+  if (layer >= cfg.n_layers) return fail(MINQ_ERR_SHAPE, "layer out of range");
+  if (start + n > c->max_seq) return fail(MINQ_ERR_SHAPE, "positions exceed cache capacity");
+  if (n == 0) return MINQ_OK;
+  const size_t hd = cfg.head_dim, nkv = cfg.n_kv_heads;
+  const size_t per_layer = c->batch * nkv * c->max_seq * hd;
+  MINQ_CUDA_TRY(cudaSetDevice(c->m->device));
+  for (int which = 0; which < 2; ++which) {
+    float* dev = (which ? c->v : c->k) + layer * per_layer;
+    float* host = which ? host_v : host_k;
+    if (!host) continue;
+    for (size_t h = 0; h < nkv; ++h) {
+      float* d = dev + h * c->max_seq * hd + start * hd;
+      float* hp = host + h * hd;
+      if (to_device)
+        MINQ_CUDA_TRY(cudaMemcpy2D(d, hd * 4, hp, nkv * hd * 4, hd * 4, n,
+                                   cudaMemcpyHostToDevice));
+      else
+        MINQ_CUDA_TRY(cudaMemcpy2D(hp, nkv * hd * 4, d, hd * 4, hd * 4, n,
+                                   cudaMemcpyDeviceToHost));
+    }
+  }
+  return MINQ_OK;
+}
+
+minq_status minq_cache_write(minq_cache* c, size_t layer, size_t start, size_t n, const float* k,
+                             const float* v) {
+  if (!c) return fail(MINQ_ERR_ARG, "null cache");
+  return cache_copy(c, layer, start, n, const_cast<float*>(k), const_cast<float*>(v), true);
+}
+
+minq_status minq_cache_read(const minq_cache* c, size_t layer, size_t start, size_t n, float* k,
+                            float* v) {
+  if (!c) return fail(MINQ_ERR_ARG, "null cache");
+  MINQ_CUDA_TRY(cudaStreamSynchronize(c->m->stream));
+  return cache_copy(c, layer, start, n, k, v, false);
+}
+
+void minq_cache_free(minq_cache* c) {
+  if (!c) return;
+  cudaSetDevice(c->m->device);
+  cudaStreamSynchronize(c->m->stream);
+  cudaFree(c->k);
+  cudaFree(c->v);
+  cudaFree(c->ws);
+  delete c;
+}
+
+// ---------------------------------------------------------------------------
+// C ABI: forward / generate
+
+static minq_status forward_impl(minq_model* m, minq_cache* c, const uint32_t* h_tokens,
+                                const uint32_t* d_tokens, size_t n, float* d_logits,
+                                uint32_t* d_argmax) {
+  if (!m || !c) return fail(MINQ_ERR_ARG, "null argument");
+  if (c->m != m) return fail(MINQ_ERR_ARG, "cache belongs to another model");
+  if (n == 0) return fail(MINQ_ERR_MODEL, "empty token sequence");  // model.rs:255-257
+  if (!m->shape_error.empty()) return fail(MINQ_ERR_SHAPE, m->shape_error);
+  if (c->batch != 1) return fail(MINQ_ERR_ARG, "minq_forward drives a batch-1 cache");
+  MINQ_CUDA_TRY(cudaSetDevice(m->device));
+  const uint32_t* toks = d_tokens;
+  if (h_tokens) {
+    if (n > m->d_tokens_cap) {
+      void* p;
+      MINQ_TRY(dmalloc(m, &p, n * 4));
+      m->d_tokens = static_cast<uint32_t*>(p);
+      m->d_tokens_cap = n;
+    }
+    MINQ_CUDA_TRY(cudaMemcpyAsync(m->d_tokens, h_tokens, n * 4, cudaMemcpyHostToDevice,
+                                  m->stream));
+    toks = m->d_tokens;
+  }
+  for (size_t i = 0; i < n; ++i) {
+    if (c->len >= m->cfg.max_seq_len)  // model.rs:260-265
+      return fail(MINQ_ERR_MODEL,
+                  "sequence exceeds max_seq_len (" + std::to_string(m->cfg.max_seq_len) + ")");
+    if (c->len >= c->max_seq)
+      return fail(MINQ_ERR_MODEL,
+                  "sequence exceeds the cache capacity (" + std::to_string(c->max_seq) + ")");
+    if (h_tokens && h_tokens[i] >= m->cfg.vocab_size)  // Tensor::row (tensor.rs:73-78)
+      return fail(MINQ_ERR_SHAPE, "row index " + std::to_string(h_tokens[i]) +
+                                      " out of bounds for " + std::to_string(m->cfg.vocab_size) +
+                                      " rows");
+    MINQ_TRY(forward_token(m, c, toks + i, c->len, i + 1 == n, d_logits, d_argmax));
+    c->len += 1;
+  }
+  return MINQ_OK;
+}
+
+minq_status minq_forward_device(minq_model* m, minq_cache* c, const uint32_t* d_tokens,
+                                size_t n, float* d_logits, uint32_t* d_argmax) {
+  if (!d_tokens) return fail(MINQ_ERR_ARG, "null tokens");
+  return forward_impl(m, c, nullptr, d_tokens, n, d_logits ? d_logits : m->logits,
+                      d_argmax ? d_argmax : m->d_argmax);
+}
+
+minq_status minq_forward(minq_model* m, minq_cache* c, const uint32_t* tokens, size_t n,
+                         float* logits_out, uint32_t* argmax_out) {
+  if (!m) return fail(MINQ_ERR_ARG, "null model");
+  if (n && !tokens) return fail(MINQ_ERR_ARG, "null tokens");
+  minq_status st = forward_impl(m, c, tokens, nullptr, n, m->logits, m->d_argmax);
+  if (st != MINQ_OK) {
+    cudaStreamSynchronize(m->stream);
+    return st;
+  }
+  if (logits_out)
+    MINQ_CUDA_TRY(cudaMemcpyAsync(logits_out, m->logits, m->cfg.vocab_size * 4,
+                                  cudaMemcpyDeviceToHost, m->stream));
+  if (argmax_out)
+    MINQ_CUDA_TRY(cudaMemcpyAsync(argmax_out, m->d_argmax, 4, cudaMemcpyDeviceToHost, m->stream));
+  MINQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  return MINQ_OK;
+}
+
+minq_status minq_generate(minq_model* m, const uint32_t* prompt, size_t n_prompt,
+                          size_t max_tokens, const uint32_t* stop_tokens, size_t n_stop,
+                          minq_token_cb on_token, void* user, uint32_t* tokens_out,
+                          minq_gen_stats* stats) {
+  if (!m) return fail(MINQ_ERR_ARG, "null model");
+  if (n_prompt == 0) return fail(MINQ_ERR_MODEL, "empty prompt");  // engine.rs:58-60
+  minq_cache* c = nullptr;
+  MINQ_TRY(minq_cache_new(m, 1, 0, &c));
+  using clk = std::chrono::steady_clock;
+  minq_gen_stats st{};
+  st.prompt_tokens = n_prompt;
+  uint32_t tok = 0;
+  auto t0 = clk::now();
+  minq_status rc = minq_forward(m, c, prompt, n_prompt, nullptr, &tok);
+  st.prefill_secs = std::chrono::duration<double>(clk::now() - t0).count();
+  auto t1 = clk::now();
+  for (size_t i = 0; rc == MINQ_OK && i < max_tokens; ++i) {
+    if (tokens_out) tokens_out[i] = tok;
+    st.gen_tokens += 1;
+    if (on_token && on_token(tok, user) != 0) {
+      rc = fail(MINQ_ERR_MODEL, "on_token callback aborted generation");
+      break;
+    }
+    bool stop = false;
+    for (size_t k = 0; k < n_stop; ++k) stop |= stop_tokens[k] == tok;
+    if (stop) break;
+    uint32_t next;
+    rc = minq_forward(m, c, &tok, 1, nullptr, &next);
+    tok = next;
+  }
+  st.decode_secs = std::chrono::duration<double>(clk::now() - t1).count();
+  minq_cache_free(c);
+  if (stats) *stats = st;
+  return rc;
+}
+
+}  // extern "C"

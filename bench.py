@@ -264,7 +264,7 @@ def run_minq(args, world, rank, local):
     prompt_len = args.prompt or prompt_len
     cfg0, qk_norm, tied = synth.ARCH[arch]
     K, W = args.steps, args.warmup
-    max_seq = prompt_len + W + 2 * K + 3 * min(K, 16) + 16
+    max_seq = prompt_len + W + 2 * K + 3 * min(K, 16) + 32
     cfg = replace(cfg0, max_seq_len=max_seq)
     model = build_model(mq, synth, cfg, qk_norm, tied, args.seed + rank)
     cache = model.new_cache()
@@ -278,11 +278,11 @@ def run_minq(args, world, rank, local):
     first = model.forward_argmax(prompt, cache)
     prefill_s = time.perf_counter() - t0
 
-    d_tok = torch.tensor([first], dtype=torch.int32, device="cuda")
-    d_logits = torch.empty(V, dtype=torch.float32, device="cuda")
+    d_out = torch.zeros(1, dtype=torch.int32, device="cuda")
 
     def step():
-        model.forward_device(d_tok.data_ptr(), 1, cache, d_logits.data_ptr(), d_tok.data_ptr())
+        # one greedy decode token, fed on the device by the previous argmax
+        model.decode_steps(cache, 1)
 
     for _ in range(W):
         step()
@@ -295,13 +295,13 @@ def run_minq(args, world, rank, local):
     barrier(world)
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    n0 = L.minq_kernel_launches()
     ev0.record(stream)
+    th0 = time.perf_counter()
     for _ in range(K):
         step()
+    host_enqueue_ms = 1000.0 * (time.perf_counter() - th0)
     ev1.record(stream)
     torch.cuda.synchronize()
-    launches = L.minq_kernel_launches() - n0
     barrier(world)
     clk = clocks.stop()
     ms = ev0.elapsed_time(ev1)
@@ -312,7 +312,8 @@ def run_minq(args, world, rank, local):
     h_tok = torch.empty(1, dtype=torch.int32, pin_memory=True)
     h_logits = torch.empty(V, dtype=torch.float32, pin_memory=True)
     h_arg = torch.empty(1, dtype=torch.int32, pin_memory=True)
-    h_tok[0] = int(d_tok.item())
+    model.decode_steps(cache, 1, d_out.data_ptr())
+    h_tok[0] = int(d_out.item())
     barrier(world)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -329,7 +330,14 @@ def run_minq(args, world, rank, local):
     ms_e2e_max = max_over_ranks(world, ms_e2e)
     e2e_value = world * K / (ms_e2e_max / 1000.0)
 
-    # ---- per-kernel timing pass (same loop, events around each launch) ----
+    # ---- per-kernel timing pass (same loop launched eagerly, events around
+    # each launch of one kernel family) ----
+    model.set_graphs(False)
+    n0 = L.minq_kernel_launches()
+    step()
+    torch.cuda.synchronize()
+    launches_per_step = L.minq_kernel_launches() - n0
+    launches = launches_per_step * K
     fams = {}
     for fam in ("qmatvec", "f32_matvec", "attention"):
         _lib.check(L.minq_kernel_timer_start(fam.encode()))
@@ -365,10 +373,10 @@ def run_minq(args, world, rank, local):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             from oracle import oracle as orc
-            om = cpu_model(orc, synth, replace(cfg, max_seq_len=max_seq), qk_norm, tied,
+            n_pos = cache.len
+            om = cpu_model(orc, synth, replace(cfg, max_seq_len=n_pos + 256), qk_norm, tied,
                            args.seed + rank)
             oc = om.new_cache()
-            n_pos = cache.len
             kvd = cfg.n_kv_heads * cfg.head_dim
             kall = np.empty((cfg.n_layers, n_pos, kvd), np.float32)
             vall = np.empty((cfg.n_layers, n_pos, kvd), np.float32)
@@ -402,6 +410,7 @@ def run_minq(args, world, rank, local):
             "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4,
                     "d2h_bytes_per_step": 4 * V + 4},
             "gpu_launches": int(launches),
+            "host_enqueue_ms_per_step": host_enqueue_ms / K,
             "roofline": roof,
             "kernels": fams,
             "cpu_baseline": cpu,

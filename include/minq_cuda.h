@@ -88,6 +88,12 @@ int minq_abi_version(void);
  * counterpart. */
 uint64_t minq_kernel_launches(void);
 
+/* Synchronise the current device and report whether any bounded
+ * device-side wait (TMA pipeline barriers) gave up since the last check:
+ * MINQ_ERR_TIMEOUT if so (and clear it), else MINQ_OK. minq_forward and
+ * minq_generate check this themselves. */
+minq_status minq_device_status(void);
+
 /* Kernel timer (diagnostic; no reference counterpart). Between start and
  * stop, every launch of the named kernel family ("qmatvec", "f32_matvec",
  * "attention") is bracketed by CUDA events on its own stream. stop()
@@ -216,6 +222,20 @@ minq_status minq_forward(minq_model* m, minq_cache* c, const uint32_t* tokens, s
  * without host copies and to chain decode steps. */
 minq_status minq_forward_device(minq_model* m, minq_cache* c, const uint32_t* d_tokens,
                                 size_t n, float* d_logits, uint32_t* d_argmax);
+
+/* Greedy decode continuation on the device (the decode loop of
+ * engine.rs:71-79 with Sampler::greedy, without the host in the loop):
+ * n_steps forward passes on the model's stream, each consuming the argmax
+ * left by the previous minq_forward / minq_decode_steps step and appending
+ * to the cache. No host synchronisation; `d_tokens_out` (device, n_steps
+ * ids, or NULL) receives the generated ids. The cache must be non-empty. */
+minq_status minq_decode_steps(minq_model* m, minq_cache* c, size_t n_steps,
+                              uint32_t* d_tokens_out);
+
+/* Replay each single-token step as a CUDA graph captured once per cache
+ * (default on; MINQ_GRAPHS=0 in the environment turns the default off), or
+ * launch its kernels one by one (needed by minq_kernel_timer_*). */
+minq_status minq_model_set_graphs(minq_model* m, int enabled);
 
 /* Engine::generate with Sampler::greedy (engine.rs:52-88): prefill the
  * prompt, then up to max_tokens greedy steps; `on_token` may be NULL;

@@ -66,6 +66,7 @@ SIGNATURES = {
     "minq_last_error": (C.c_char_p, []),
     "minq_abi_version": (I, []),
     "minq_kernel_launches": (C.c_uint64, []),
+    "minq_device_status": (I, []),
     "minq_kernel_timer_start": (I, [C.c_char_p]),
     "minq_kernel_timer_stop": (I, [U64P, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "minq_quantize": (I, [I, P, S, P, P]),
@@ -94,6 +95,8 @@ SIGNATURES = {
     "minq_cache_free": (None, [P]),
     "minq_forward": (I, [P, P, P, S, P, P]),
     "minq_forward_device": (I, [P, P, P, S, P, P]),
+    "minq_decode_steps": (I, [P, P, S, P]),
+    "minq_model_set_graphs": (I, [P, I]),
     "minq_generate": (I, [P, P, S, S, P, S, TOKEN_CB, P, P, C.POINTER(GenStats)]),
 }
 

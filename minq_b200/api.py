@@ -288,6 +288,16 @@ class Model:
                                  am.ctypes.data_as(C.c_void_p)))
         return (int(am[0]), out) if logits else int(am[0])
 
+    def set_graphs(self, enabled: bool) -> None:
+        """Replay decode steps as captured CUDA graphs (default) or launch eagerly."""
+        check(lib().minq_model_set_graphs(self._h, 1 if enabled else 0))
+
+    def decode_steps(self, cache: "KVCache", n: int, d_tokens_out: int | None = None) -> None:
+        """Greedy continuation on the device: n steps, each fed by the previous
+        step's argmax; no host synchronisation."""
+        check(lib().minq_decode_steps(self._h, cache._h, n,
+                                      C.c_void_p(d_tokens_out) if d_tokens_out else None))
+
     def forward_device(self, d_tokens, n: int, cache: "KVCache", d_logits=None, d_argmax=None):
         """Device-resident variant (no host synchronisation) on the model's stream."""
         check(lib().minq_forward_device(self._h, cache._h, C.c_void_p(d_tokens), n,

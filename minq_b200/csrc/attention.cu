@@ -24,6 +24,7 @@
 
 #include "common.cuh"
 #include "ktimer.h"
+#include "pipeline.cuh"
 
 namespace minq {
 
@@ -36,8 +37,20 @@ struct AttnParams {
   float scale;           // 1/sqrt(HD)
   float* out;            // [B, nh, HD]
   float* ws_o;           // [B, nh, nsplit, HD]
-  float* ws_ml;          // [B, nh, nsplit, 2]
+  float* ws_ml;          // [B, nh, ws_stride, 2]
+  int* status;           // device status word (bounded-wait timeouts)
+  const int* d_pos;      // if set: len = *d_pos + 1 and the split is derived on the device
+  int ws_stride;         // split slots per (sequence, head) in the workspace
+  int q_round;           // chunk granularity (positions)
 };
+
+// Split of `len` positions into at most `cap` chunks of a multiple of `q`.
+__device__ __forceinline__ void derive_split(int len, int cap, int q, int* chunk, int* nsplit) {
+  int c = (len + cap - 1) / cap;
+  c = (c + q - 1) / q * q;
+  *chunk = c;
+  *nsplit = (len + c - 1) / c;
+}
 
 template <int HD, int GMAX>
 __global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
@@ -52,6 +65,15 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
   __shared__ float s_m[4][GMAX], s_l[4][GMAX];
   __shared__ float s_o[4][GMAX][HD];
 
+  pdl_wait();
+  pdl_launch_dependents();
+  int len = p.len, chunk = p.chunk, nsplit = p.nsplit;
+  if (p.d_pos) {
+    len = *p.d_pos + 1;
+    derive_split(len, gridDim.x, p.q_round, &chunk, &nsplit);
+  }
+  const int split = blockIdx.x;
+  if (split >= nsplit) return;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int b = blockIdx.z;
   const int G = p.nh / p.nkv;
@@ -59,9 +81,8 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
   const int kvh = blockIdx.y / qgroups;
   const int g0 = (blockIdx.y % qgroups) * 8;
   const int ng = min(GMAX, G - g0);
-  const int split = blockIdx.x;
-  const int t_begin = split * p.chunk;
-  const int t_end = min(p.len, t_begin + p.chunk);
+  const int t_begin = split * chunk;
+  const int t_end = min(len, t_begin + chunk);
 
   const float* kb = p.k + b * p.seq_stride + kvh * p.head_stride;
   const float* vb = p.v + b * p.seq_stride + kvh * p.head_stride;
@@ -194,23 +215,248 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
     }
     const int qh = kvh * G + g0 + g;
     const size_t row = (size_t)b * p.nh + qh;
-    if (p.nsplit == 1) {
+    if (nsplit == 1) {
       p.out[row * HD + d] = O / L;
     } else {
-      p.ws_o[(row * p.nsplit + split) * HD + d] = O;
+      p.ws_o[(row * p.ws_stride + split) * HD + d] = O;
       if (d == 0) {
-        p.ws_ml[(row * p.nsplit + split) * 2 + 0] = M;
-        p.ws_ml[(row * p.nsplit + split) * 2 + 1] = L;
+        p.ws_ml[(row * p.ws_stride + split) * 2 + 0] = M;
+        p.ws_ml[(row * p.ws_stride + split) * 2 + 1] = L;
       }
     }
   }
 }
 
+// ---------------------------------------------------------------------------
+// TMA-fed variant for caches whose positions are contiguous per KV head
+// (pos_stride == HD, the model's head-major layout). CTA = 4 consumer warps
+// + 1 producer warp. The producer streams K and V tiles of TP positions
+// (TP*HD*4 = 8 KB each) into an 8-deep shared-memory ring with one bulk copy
+// per tile; consumer warp w takes tiles w, w+4, ... and runs the same QK^T /
+// online-softmax / PV math as attn_split_kernel from shared memory.
+template <int HD>
+struct TmaAttnCfg {
+  static constexpr int TP = (2048 / HD) < 32 ? (2048 / HD) : 32;  // positions per tile
+  static constexpr int S = 8;                                       // ring depth
+  static constexpr int TILE_FLOATS = TP * HD;
+};
+
+template <int HD, int GMAX>
+__global__ void __launch_bounds__(160) attn_tma_kernel(AttnParams p) {
+  using CFG = TmaAttnCfg<HD>;
+  constexpr int TP = CFG::TP, S = CFG::S, TF = CFG::TILE_FLOATS;
+  constexpr int NWC = 4;                       // consumer warps
+  constexpr int EPL = 8;
+  constexpr int LPP = HD / EPL;
+  constexpr int PPS = 32 / LPP;
+  constexpr int NSUB = TP / PPS;
+  constexpr int DPL = HD >= 32 ? HD / 32 : 1;
+  constexpr int PV_LANES = HD / DPL;
+  static_assert(HD >= 16 && HD <= 256 && TP % PPS == 0, "head_dim");
+
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);
+  uint64_t* empty = full + S;
+  float* tiles = reinterpret_cast<float*>(smem_raw + 128);            // [S][2][TF]
+  float* s_sc = tiles + (size_t)S * 2 * TF;                            // [NWC][GMAX][32]
+  float* s_m = s_sc + NWC * GMAX * 32;                                 // [NWC][GMAX]
+  float* s_l = s_m + NWC * GMAX;                                       // [NWC][GMAX]
+  float* s_o = s_l + NWC * GMAX;                                       // [NWC][GMAX][HD]
+
+  pdl_wait();  // K/V (this position) and q come from the previous kernel
+  pdl_launch_dependents();
+  int len = p.len, chunk = p.chunk, nsplit = p.nsplit;
+  if (p.d_pos) {
+    len = *p.d_pos + 1;
+    derive_split(len, gridDim.x, p.q_round, &chunk, &nsplit);
+  }
+  const int split = blockIdx.x;
+  if (split >= nsplit) return;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int b = blockIdx.z;
+  const int G = p.nh / p.nkv;
+  const int qgroups = (G + 7) / 8;
+  const int kvh = blockIdx.y / qgroups;
+  const int g0 = (blockIdx.y % qgroups) * 8;
+  const int ng = min(GMAX, G - g0);
+  const int t_begin = split * chunk;
+  const int t_end = min(len, t_begin + chunk);
+  const int ntiles = (t_end - t_begin + TP - 1) / TP;
+  const float* kb = p.k + b * p.seq_stride + kvh * p.head_stride;
+  const float* vb = p.v + b * p.seq_stride + kvh * p.head_stride;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (warp == NWC) {  // producer
+    bool ok = true;
+    for (int i = 0; i < ntiles && ok; ++i) {
+      const int s = i % S;
+      ok = mbar_wait(&empty[s], ((uint32_t)(i / S) & 1u) ^ 1u, p.status);
+      if (!ok) break;
+      const int t0 = t_begin + i * TP;
+      const uint32_t bytes = (uint32_t)(min(TP, t_end - t0) * HD * 4);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&full[s], 2 * bytes);
+        bulk_g2s(tiles + (size_t)s * 2 * TF, kb + (size_t)t0 * HD, bytes, &full[s]);
+        bulk_g2s(tiles + (size_t)s * 2 * TF + TF, vb + (size_t)t0 * HD, bytes, &full[s]);
+      }
+      __syncwarp();
+    }
+    for (int i = max(0, ntiles - S); ok && i < ntiles; ++i)
+      ok = mbar_wait(&empty[i % S], (uint32_t)(i / S) & 1u, p.status);
+  } else {
+    const int j = lane % LPP;
+    const int pslot = lane / LPP;
+    float qr[GMAX][EPL];
+#pragma unroll
+    for (int g = 0; g < GMAX; ++g) {
+      const float* qh = p.q + ((size_t)b * p.nh + kvh * G + g0 + (g < ng ? g : 0)) * HD;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        const int idx = (e < 4) ? 4 * j + e : HD / 2 + 4 * j + e - 4;
+        qr[g][e] = g < ng ? qh[idx] * p.scale : 0.0f;
+      }
+    }
+    float m_w[GMAX], l_w[GMAX], o[GMAX][DPL];
+#pragma unroll
+    for (int g = 0; g < GMAX; ++g) {
+      m_w[g] = -INFINITY;
+      l_w[g] = 0.0f;
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) o[g][d] = 0.0f;
+    }
+    float* sc = s_sc + warp * GMAX * 32;
+    for (int i = warp; i < ntiles; i += NWC) {
+      const int s = i % S;
+      if (!mbar_wait(&full[s], (uint32_t)(i / S) & 1u, p.status)) break;
+      const float* kt_s = tiles + (size_t)s * 2 * TF;
+      const float* vt_s = kt_s + TF;
+      const int npos = min(TP, t_end - (t_begin + i * TP));
+#pragma unroll 2
+      for (int ss = 0; ss < NSUB; ++ss) {
+        const int tl = ss * PPS + pslot;
+        const float* kt = kt_s + tl * HD;
+        const float4 a = *reinterpret_cast<const float4*>(kt + 4 * j);
+        const float4 c = *reinterpret_cast<const float4*>(kt + HD / 2 + 4 * j);
+        const float kv[EPL] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+#pragma unroll
+        for (int g = 0; g < GMAX; ++g) {
+          float sv = 0.0f;
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) sv = fmaf(qr[g][e], kv[e], sv);
+#pragma unroll
+          for (int off = LPP / 2; off > 0; off >>= 1) sv += __shfl_xor_sync(0xffffffffu, sv, off);
+          if (j == 0) sc[g * 32 + tl] = tl < npos ? sv : -INFINITY;
+        }
+      }
+      __syncwarp();
+      float pr[GMAX];
+#pragma unroll
+      for (int g = 0; g < GMAX; ++g) {
+        const float sv = lane < TP ? sc[g * 32 + lane] : -INFINITY;
+        const float mt = warp_max(sv);
+        const float mn = fmaxf(m_w[g], mt);
+        const float corr = m_w[g] == -INFINITY ? 0.0f : expf(m_w[g] - mn);
+        pr[g] = sv == -INFINITY ? 0.0f : expf(sv - mn);
+        l_w[g] = l_w[g] * corr + pr[g];
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) o[g][d] *= corr;
+        m_w[g] = mn;
+      }
+#pragma unroll 4
+      for (int tl = 0; tl < npos; ++tl) {
+        const float* vt = vt_s + tl * HD;
+        float vv[DPL];
+        if (lane < PV_LANES) {
+          if constexpr (DPL == 4) {
+            const float4 a = *reinterpret_cast<const float4*>(vt + 4 * lane);
+            vv[0] = a.x; vv[1] = a.y; vv[2] = a.z; vv[3] = a.w;
+          } else if constexpr (DPL == 2) {
+            const float2 a = *reinterpret_cast<const float2*>(vt + 2 * lane);
+            vv[0] = a.x; vv[1] = a.y;
+          } else {
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) vv[d] = vt[DPL * lane + d];
+          }
+        } else {
+#pragma unroll
+          for (int d = 0; d < DPL; ++d) vv[d] = 0.0f;
+        }
+#pragma unroll
+        for (int g = 0; g < GMAX; ++g) {
+          const float pt = __shfl_sync(0xffffffffu, pr[g], tl);
+#pragma unroll
+          for (int d = 0; d < DPL; ++d) o[g][d] = fmaf(pt, vv[d], o[g][d]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+#pragma unroll
+    for (int g = 0; g < GMAX; ++g) {
+      const float lsum = warp_sum(l_w[g]);
+      if (lane == 0) {
+        s_m[warp * GMAX + g] = m_w[g];
+        s_l[warp * GMAX + g] = lsum;
+      }
+      if (lane < PV_LANES) {
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) s_o[(warp * GMAX + g) * HD + DPL * lane + d] = o[g][d];
+      }
+    }
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < ng * HD; idx += blockDim.x) {
+    const int g = idx / HD, d = idx % HD;
+    float M = -INFINITY;
+    for (int w = 0; w < NWC; ++w) M = fmaxf(M, s_m[w * GMAX + g]);
+    float L = 0.0f, O = 0.0f;
+    for (int w = 0; w < NWC; ++w) {
+      const float mw = s_m[w * GMAX + g];
+      if (mw == -INFINITY) continue;
+      const float f = expf(mw - M);
+      L = fmaf(s_l[w * GMAX + g], f, L);
+      O = fmaf(s_o[(w * GMAX + g) * HD + d], f, O);
+    }
+    const size_t row = (size_t)b * p.nh + kvh * G + g0 + g;
+    if (nsplit == 1) {
+      p.out[row * HD + d] = O / L;
+    } else {
+      p.ws_o[(row * p.ws_stride + split) * HD + d] = O;
+      if (d == 0) {
+        p.ws_ml[(row * p.ws_stride + split) * 2 + 0] = M;
+        p.ws_ml[(row * p.ws_stride + split) * 2 + 1] = L;
+      }
+    }
+  }
+}
+
+template <int HD, int GMAX>
+static size_t tma_attn_smem() {
+  using CFG = TmaAttnCfg<HD>;
+  return 128 + sizeof(float) * ((size_t)CFG::S * 2 * CFG::TILE_FLOATS + 4 * GMAX * 32 +
+                                2 * 4 * GMAX + 4 * GMAX * HD);
+}
+
 // Merge the splits of every (sequence, query head).
-__global__ void attn_combine_kernel(const float* ws_o, const float* ws_ml, int nsplit, int hd,
-                                    float* out) {
+__global__ void attn_combine_kernel(const float* ws_o, const float* ws_ml, int nsplit, int stride,
+                                    int hd, float* out, const int* d_pos, int cap, int q) {
+  pdl_wait();
+  pdl_launch_dependents();
+  if (d_pos) {
+    int chunk;
+    derive_split(*d_pos + 1, cap, q, &chunk, &nsplit);
+    if (nsplit == 1) return;  // the split kernel wrote the output directly
+  }
   const size_t row = blockIdx.x;  // b * nh + h
-  const float* ml = ws_ml + row * nsplit * 2;
+  const float* ml = ws_ml + row * stride * 2;
   float M = -INFINITY;
   for (int s = 0; s < nsplit; ++s) M = fmaxf(M, ml[2 * s]);
   for (int d = threadIdx.x; d < hd; d += blockDim.x) {
@@ -220,7 +466,7 @@ __global__ void attn_combine_kernel(const float* ws_o, const float* ws_ml, int n
       if (m == -INFINITY) continue;
       const float f = expf(m - M);
       L = fmaf(ml[2 * s + 1], f, L);
-      O = fmaf(ws_o[(row * nsplit + s) * hd + d], f, O);
+      O = fmaf(ws_o[(row * stride + s) * hd + d], f, O);
     }
     out[row * hd + d] = O / L;
   }
@@ -240,6 +486,7 @@ struct RopeParams {
   const float* cos_t;  // [max_seq, HD/2]
   const float* sin_t;
   int nh, nkv, hd, pos;
+  const int* d_pos;    // if set, the position is read from the device
   float* q_out;        // [B, nh, HD]
   float* k_cache;
   float* v_cache;
@@ -247,6 +494,9 @@ struct RopeParams {
 };
 
 __global__ void rope_append_kernel(RopeParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int pos = p.d_pos ? *p.d_pos : p.pos;
   const int lane = threadIdx.x & 31;
   const int head = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int b = blockIdx.y;
@@ -266,11 +516,11 @@ __global__ void rope_append_kernel(RopeParams p) {
     const int h = head - p.nh;
     src = p.k_in + b * p.kv_in_bstride + (size_t)h * hd;
     gain = p.k_norm;
-    dst = p.k_cache + b * p.seq_stride + h * p.head_stride + (size_t)p.pos * p.pos_stride;
+    dst = p.k_cache + b * p.seq_stride + h * p.head_stride + (size_t)pos * p.pos_stride;
   } else {
     const int h = head - p.nh - p.nkv;
     src = p.v_in + b * p.kv_in_bstride + (size_t)h * hd;
-    dst = p.v_cache + b * p.seq_stride + h * p.head_stride + (size_t)p.pos * p.pos_stride;
+    dst = p.v_cache + b * p.seq_stride + h * p.head_stride + (size_t)pos * p.pos_stride;
     rope = false;
   }
   // Lane owns element pairs (i, i + half) for i = lane, lane + 32, ...
@@ -298,8 +548,8 @@ __global__ void rope_append_kernel(RopeParams p) {
     if (i >= half) continue;
     float x1 = vals[2 * k], x2 = vals[2 * k + 1];
     if (rope) {
-      const float c = p.cos_t[(size_t)p.pos * half + i];
-      const float s = p.sin_t[(size_t)p.pos * half + i];
+      const float c = p.cos_t[(size_t)pos * half + i];
+      const float s = p.sin_t[(size_t)pos * half + i];
       // head[i] = x1*cos - x2*sin; head[i+half] = x2*cos + x1*sin (un-fused)
       const float y1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
       const float y2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
@@ -323,7 +573,7 @@ static int pick_chunk(int len, size_t units) {
 }
 
 size_t attn_workspace_bytes(size_t batch, size_t nh, size_t len, size_t hd_max) {
-  // Upper bound over every chunk choice: splits <= ceil(len / 32).
+  // Upper bound over every split choice: at most ceil(len / 32) splits.
   const size_t splits = (len + 31) / 32;
   return batch * nh * splits * (hd_max + 2) * sizeof(float) + 256;
 }
@@ -332,24 +582,48 @@ template <int HD>
 static minq_status launch_split_hd(const AttnParams& p, int gmax, dim3 grid, int threads,
                                    cudaStream_t s) {
   switch (gmax) {
-    case 1: attn_split_kernel<HD, 1><<<grid, threads, 0, s>>>(p); break;
-    case 2: attn_split_kernel<HD, 2><<<grid, threads, 0, s>>>(p); break;
-    case 4: attn_split_kernel<HD, 4><<<grid, threads, 0, s>>>(p); break;
-    default: attn_split_kernel<HD, 8><<<grid, threads, 0, s>>>(p); break;
+    case 1: MINQ_CUDA_TRY(launch_k(attn_split_kernel<HD, 1>, grid, dim3(threads), 0, s, p)); break;
+    case 2: MINQ_CUDA_TRY(launch_k(attn_split_kernel<HD, 2>, grid, dim3(threads), 0, s, p)); break;
+    case 4: MINQ_CUDA_TRY(launch_k(attn_split_kernel<HD, 4>, grid, dim3(threads), 0, s, p)); break;
+    default: MINQ_CUDA_TRY(launch_k(attn_split_kernel<HD, 8>, grid, dim3(threads), 0, s, p)); break;
   }
   return MINQ_OK;
 }
 
+template <int HD, int GMAX>
+static minq_status launch_tma_inst(const AttnParams& p, dim3 grid, cudaStream_t s) {
+  const size_t smem = tma_attn_smem<HD, GMAX>();
+  auto k = attn_tma_kernel<HD, GMAX>;
+  MINQ_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(k), smem));
+  MINQ_CUDA_TRY(launch_k(k, grid, dim3(160), smem, s, p));
+  return MINQ_OK;
+}
+
+template <int HD>
+static minq_status launch_tma_hd(const AttnParams& p, int gmax, dim3 grid, cudaStream_t s) {
+  switch (gmax) {
+    case 1: return launch_tma_inst<HD, 1>(p, grid, s);
+    case 2: return launch_tma_inst<HD, 2>(p, grid, s);
+    case 4: return launch_tma_inst<HD, 4>(p, grid, s);
+    default: return launch_tma_inst<HD, 8>(p, grid, s);
+  }
+}
+
+// Decode attention over `len` positions (host-known), or, when `d_pos` is
+// set, over *d_pos + 1 positions read on the device, with the grid sized
+// for `cap_len` positions (a graph-captured step replays for any length up
+// to the cache capacity).
 minq_status launch_attention(const float* q, const float* k, const float* v, size_t batch,
                              int nh, int nkv, int hd, int len, size_t seq_stride,
                              size_t head_stride, size_t pos_stride, float* out, void* ws,
-                             size_t ws_bytes, cudaStream_t s) {
-  if (len <= 0) return fail(MINQ_ERR_SHAPE, "attention over an empty history");
+                             size_t ws_bytes, cudaStream_t s, const int* d_pos, int cap_len) {
+  if (!d_pos && len <= 0) return fail(MINQ_ERR_SHAPE, "attention over an empty history");
   if (nkv <= 0 || nh % nkv != 0)
     return fail(MINQ_ERR_MODEL, "n_heads must be a multiple of n_kv_heads");
   const int G = nh / nkv;
   const int qgroups = (G + 7) / 8;
-  const int gmax = G >= 8 ? 8 : (G > 4 ? 8 : (G > 2 ? 4 : (G > 1 ? 2 : 1)));
+  const int gmax = G > 4 ? 8 : (G > 2 ? 4 : (G > 1 ? 2 : 1));
+  const int size_len = d_pos ? cap_len : len;  // sizes the grid
   AttnParams p{};
   p.q = q;
   p.k = k;
@@ -360,11 +634,31 @@ minq_status launch_attention(const float* q, const float* k, const float* v, siz
   p.nh = nh;
   p.nkv = nkv;
   p.len = len;
-  p.chunk = pick_chunk(len, batch * nkv * qgroups);
-  p.nsplit = (len + p.chunk - 1) / p.chunk;
+  p.status = device_status_word();
+  p.d_pos = d_pos;
+  // The TMA path needs each KV head's positions contiguous (head-major
+  // cache) and 16-byte aligned tiles.
+  const bool tma = hd >= 16 && hd <= 256 && (hd & (hd - 1)) == 0 && pos_stride == (size_t)hd &&
+                   (uintptr_t)k % 16 == 0 && (uintptr_t)v % 16 == 0 &&
+                   seq_stride % 4 == 0 && head_stride % 4 == 0;
+  const size_t units = batch * nkv * qgroups;
+  if (tma) {
+    const int tp = std::min(32, 2048 / hd);
+    p.q_round = 4 * tp;
+    const size_t target = (size_t)sm_count() * 2;
+    size_t c = ((size_t)size_len * units + target - 1) / target;
+    c = (c + p.q_round - 1) / p.q_round * p.q_round;
+    p.chunk = (int)std::min<size_t>(c, (size_t)((size_len + p.q_round - 1) / p.q_round * p.q_round));
+  } else {
+    p.q_round = 32;
+    p.chunk = pick_chunk(size_len, units);
+  }
+  p.nsplit = (size_len + p.chunk - 1) / p.chunk;  // grid (split slots)
+  p.ws_stride = p.nsplit;
   p.scale = 1.0f / sqrtf((float)hd);
   p.out = out;
-  if (p.nsplit > 1) {
+  const bool may_split = p.nsplit > 1;
+  if (may_split) {
     const size_t need = batch * nh * p.nsplit * (hd + 2) * sizeof(float);
     if (!ws || ws_bytes < need)
       return fail(MINQ_ERR_ARG, "attention workspace too small (need " + std::to_string(need) +
@@ -375,22 +669,35 @@ minq_status launch_attention(const float* q, const float* k, const float* v, siz
   const int threads = 32 * std::min(4, (p.chunk + 31) / 32);
   dim3 grid(p.nsplit, nkv * qgroups, (unsigned)batch);
   ScopedKTimer timer(KF_ATTENTION, s,
-                     8.0 * batch * nkv * hd * (double)len + 8.0 * batch * nh * hd);
-  switch (hd) {
-    case 8: MINQ_TRY(launch_split_hd<8>(p, gmax, grid, threads, s)); break;
-    case 16: MINQ_TRY(launch_split_hd<16>(p, gmax, grid, threads, s)); break;
-    case 32: MINQ_TRY(launch_split_hd<32>(p, gmax, grid, threads, s)); break;
-    case 64: MINQ_TRY(launch_split_hd<64>(p, gmax, grid, threads, s)); break;
-    case 128: MINQ_TRY(launch_split_hd<128>(p, gmax, grid, threads, s)); break;
-    case 256: MINQ_TRY(launch_split_hd<256>(p, gmax, grid, threads, s)); break;
-    default:
-      return fail(MINQ_ERR_SHAPE, "unsupported head_dim " + std::to_string(hd) +
-                                      " (supported: 8, 16, 32, 64, 128, 256)");
+                     8.0 * batch * nkv * hd * (double)(d_pos ? cap_len : len) +
+                         8.0 * batch * nh * hd);
+  if (tma) {
+    switch (hd) {
+      case 16: MINQ_TRY(launch_tma_hd<16>(p, gmax, grid, s)); break;
+      case 32: MINQ_TRY(launch_tma_hd<32>(p, gmax, grid, s)); break;
+      case 64: MINQ_TRY(launch_tma_hd<64>(p, gmax, grid, s)); break;
+      case 128: MINQ_TRY(launch_tma_hd<128>(p, gmax, grid, s)); break;
+      default: MINQ_TRY(launch_tma_hd<256>(p, gmax, grid, s)); break;
+    }
+  } else {
+    switch (hd) {
+      case 8: MINQ_TRY(launch_split_hd<8>(p, gmax, grid, threads, s)); break;
+      case 16: MINQ_TRY(launch_split_hd<16>(p, gmax, grid, threads, s)); break;
+      case 32: MINQ_TRY(launch_split_hd<32>(p, gmax, grid, threads, s)); break;
+      case 64: MINQ_TRY(launch_split_hd<64>(p, gmax, grid, threads, s)); break;
+      case 128: MINQ_TRY(launch_split_hd<128>(p, gmax, grid, threads, s)); break;
+      case 256: MINQ_TRY(launch_split_hd<256>(p, gmax, grid, threads, s)); break;
+      default:
+        return fail(MINQ_ERR_SHAPE, "unsupported head_dim " + std::to_string(hd) +
+                                        " (supported: 8, 16, 32, 64, 128, 256)");
+    }
   }
   MINQ_LAUNCH_CHECK("attn_split_kernel");
-  if (p.nsplit > 1) {
-    attn_combine_kernel<<<(unsigned)(batch * nh), std::min(hd, 128), 0, s>>>(p.ws_o, p.ws_ml,
-                                                                            p.nsplit, hd, out);
+  if (may_split) {
+    MINQ_CUDA_TRY(launch_k(attn_combine_kernel, dim3((unsigned)(batch * nh)),
+                           dim3(std::min(hd, 128)), 0, s, (const float*)p.ws_o,
+                           (const float*)p.ws_ml, p.nsplit, p.ws_stride, hd, out, d_pos,
+                           (int)p.nsplit, p.q_round));
     MINQ_LAUNCH_CHECK("attn_combine_kernel");
   }
   return MINQ_OK;
@@ -402,7 +709,7 @@ minq_status launch_rope_append(const float* q_in, const float* k_in, const float
                                const float* sin_t, size_t batch, int nh, int nkv, int hd,
                                int pos, float* q_out, float* k_cache, float* v_cache,
                                size_t seq_stride, size_t head_stride, size_t pos_stride,
-                               cudaStream_t s) {
+                               cudaStream_t s, const int* d_pos) {
   if (hd % 2 != 0 || hd > 256) return fail(MINQ_ERR_SHAPE, "head_dim must be even and <= 256");
   RopeParams p{};
   p.q_in = q_in;
@@ -419,6 +726,7 @@ minq_status launch_rope_append(const float* q_in, const float* k_in, const float
   p.nkv = nkv;
   p.hd = hd;
   p.pos = pos;
+  p.d_pos = d_pos;
   p.q_out = q_out;
   p.k_cache = k_cache;
   p.v_cache = v_cache;
@@ -427,7 +735,7 @@ minq_status launch_rope_append(const float* q_in, const float* k_in, const float
   p.pos_stride = pos_stride;
   const int heads = nh + 2 * nkv;
   dim3 grid((heads + 3) / 4, (unsigned)batch);
-  rope_append_kernel<<<grid, 128, 0, s>>>(p);
+  MINQ_CUDA_TRY(launch_k(rope_append_kernel, grid, dim3(128), 0, s, p));
   MINQ_LAUNCH_CHECK("rope_append_kernel");
   return MINQ_OK;
 }

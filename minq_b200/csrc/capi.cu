@@ -1,5 +1,7 @@
 // Op-level C ABI entry points (include/minq_cuda.h) and error plumbing.
 #include <atomic>
+#include <cstdlib>
+#include <map>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -39,6 +41,56 @@ int sm_count() {
     cached[dev] = n;
   }
   return cached[dev];
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("MINQ_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+minq_status ensure_dynamic_smem(const void* kernel, size_t bytes) {
+  if (bytes <= 48 * 1024) return MINQ_OK;
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, size_t> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> g(mu);
+  size_t& cur = done[{dev, kernel}];
+  if (cur >= bytes) return MINQ_OK;
+  MINQ_CUDA_TRY(
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+  cur = bytes;
+  return MINQ_OK;
+}
+
+int* device_status_word() {
+  static int* words[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> g(mu);
+  if (!words[dev]) {
+    int* p = nullptr;
+    if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
+    cudaMemset(p, 0, sizeof(int));
+    words[dev] = p;
+  }
+  return words[dev];
+}
+
+minq_status take_device_status() {
+  int* w = device_status_word();
+  if (!w) return MINQ_OK;
+  int v = 0;
+  MINQ_CUDA_TRY(cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost));
+  if (v == 0) return MINQ_OK;
+  MINQ_CUDA_TRY(cudaMemset(w, 0, sizeof(int)));
+  return fail(MINQ_ERR_TIMEOUT,
+              "a bounded device-side wait timed out (status " + std::to_string(v) + ")");
 }
 
 static minq_status require_device() {
@@ -100,6 +152,12 @@ const char* minq_last_error(void) { return g_error.c_str(); }
 int minq_abi_version(void) { return MINQ_ABI_VERSION; }
 
 uint64_t minq_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+
+minq_status minq_device_status(void) {
+  MINQ_TRY(require_device());
+  MINQ_CUDA_TRY(cudaDeviceSynchronize());
+  return take_device_status();
+}
 
 minq_status minq_kernel_timer_start(const char* family) {
   if (!family) return fail(MINQ_ERR_ARG, "null family");

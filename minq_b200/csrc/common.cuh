@@ -5,6 +5,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "../../include/minq_cuda.h"
 
@@ -23,6 +24,15 @@ minq_status cuda_fail(cudaError_t e, const char* what);
 
 // Number of SMs of the current device (cached per device).
 int sm_count();
+
+// Raise a kernel's dynamic shared-memory limit to at least `bytes` (cached
+// per device and kernel, so the attribute call happens once).
+minq_status ensure_dynamic_smem(const void* kernel, size_t bytes);
+
+// Per-device status word that bounded device-side waits set on timeout
+// (allocated once per device), and its synchronous read-and-clear.
+int* device_status_word();
+minq_status take_device_status();
 
 #define MINQ_CUDA_TRY(expr)                                    \
   do {                                                         \
@@ -46,6 +56,34 @@ void count_launch();
     cudaError_t _e = cudaGetLastError();                            \
     if (_e != cudaSuccess) return ::minq::cuda_fail(_e, what);      \
   } while (0)
+
+// Programmatic dependent launch (PDL): every kernel of this library calls
+// pdl_wait() before it reads or writes anything a preceding kernel on the
+// stream touches, so any launch may carry the programmatic-serialization
+// attribute; work that depends on nothing (weight prefetch) goes before it.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Whether launches carry the PDL attribute (MINQ_PDL=0 disables it).
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                     cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

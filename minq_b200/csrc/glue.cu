@@ -1,13 +1,16 @@
-// Small elementwise kernels of the forward step that are not fused into a
-// matvec: embedding row gather (model.rs:275), standalone RMSNorm
-// (tensor.rs:219-227, for dense-f32 layers), bias/residual epilogue
-// (tensor.rs:195 add_) and SwiGLU (tensor.rs:203-215) after f32 matvecs.
+// Small kernels of the forward step that are not fused into a matvec:
+// embedding row gather (model.rs:275), standalone RMSNorm (tensor.rs:219-227,
+// dense-f32 layers), bias/residual epilogue (tensor.rs:195 add_) and SwiGLU
+// (tensor.rs:203-215) after f32 matvecs, and the device-side position
+// counter of a graph-captured decode step.
 #include "common.cuh"
 
 namespace minq {
 
 __global__ void embed_kernel(const float* __restrict__ embed, const uint32_t* tok, size_t vocab,
                              int hidden, float* __restrict__ x) {
+  pdl_wait();
+  pdl_launch_dependents();
   uint32_t t = *tok;
   if (t >= vocab) t = 0;  // host validates tokens; never read out of bounds
   const float* row = embed + (size_t)t * hidden;
@@ -17,6 +20,8 @@ __global__ void embed_kernel(const float* __restrict__ embed, const uint32_t* to
 
 __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                float eps, int n, float* __restrict__ out) {
+  pdl_wait();
+  pdl_launch_dependents();
   __shared__ float red[33];
   float ss = 0.0f;
   for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
@@ -35,6 +40,8 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
 
 __global__ void epilogue_kernel(const float* acc, const float* bias, const float* residual,
                                 float* y, size_t n) {
+  pdl_wait();
+  pdl_launch_dependents();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x) {
     float v = acc[i];
@@ -45,11 +52,19 @@ __global__ void epilogue_kernel(const float* acc, const float* bias, const float
 }
 
 __global__ void swiglu_kernel(const float* g, const float* u, float* h, size_t n) {
+  pdl_wait();
+  pdl_launch_dependents();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x) {
     const float v = g[i];
     h[i] = (v / (1.0f + expf(-v))) * u[i];
   }
+}
+
+__global__ void advance_pos_kernel(int* pos, int by) {
+  pdl_wait();
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) *pos += by;
 }
 
 static unsigned ew_grid(size_t n) {
@@ -60,28 +75,36 @@ static unsigned ew_grid(size_t n) {
 
 minq_status launch_embed(const float* embed, const uint32_t* d_tok, size_t vocab, int hidden,
                          float* x, cudaStream_t s) {
-  embed_kernel<<<(hidden + 255) / 256, 256, 0, s>>>(embed, d_tok, vocab, hidden, x);
+  MINQ_CUDA_TRY(launch_k(embed_kernel, dim3((hidden + 255) / 256), dim3(256), 0, s, embed, d_tok,
+                         vocab, hidden, x));
   MINQ_LAUNCH_CHECK("embed_kernel");
   return MINQ_OK;
 }
 
 minq_status launch_rmsnorm(const float* x, const float* w, float eps, int n, float* out,
                            cudaStream_t s) {
-  rmsnorm_kernel<<<1, 1024, 0, s>>>(x, w, eps, n, out);
+  MINQ_CUDA_TRY(launch_k(rmsnorm_kernel, dim3(1), dim3(1024), 0, s, x, w, eps, n, out));
   MINQ_LAUNCH_CHECK("rmsnorm_kernel");
   return MINQ_OK;
 }
 
 minq_status launch_epilogue(const float* acc, const float* bias, const float* residual, float* y,
                             size_t n, cudaStream_t s) {
-  epilogue_kernel<<<ew_grid(n), 256, 0, s>>>(acc, bias, residual, y, n);
+  MINQ_CUDA_TRY(
+      launch_k(epilogue_kernel, dim3(ew_grid(n)), dim3(256), 0, s, acc, bias, residual, y, n));
   MINQ_LAUNCH_CHECK("epilogue_kernel");
   return MINQ_OK;
 }
 
 minq_status launch_swiglu(const float* g, const float* u, float* h, size_t n, cudaStream_t s) {
-  swiglu_kernel<<<ew_grid(n), 256, 0, s>>>(g, u, h, n);
+  MINQ_CUDA_TRY(launch_k(swiglu_kernel, dim3(ew_grid(n)), dim3(256), 0, s, g, u, h, n));
   MINQ_LAUNCH_CHECK("swiglu_kernel");
+  return MINQ_OK;
+}
+
+minq_status launch_advance_pos(int* pos, int by, cudaStream_t s) {
+  MINQ_CUDA_TRY(launch_k(advance_pos_kernel, dim3(1), dim3(32), 0, s, pos, by));
+  MINQ_LAUNCH_CHECK("advance_pos_kernel");
   return MINQ_OK;
 }
 

@@ -1,6 +1,7 @@
 // Host launchers of the CUDA kernels (one declaration per .cu entry).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -15,9 +16,24 @@ minq_status launch_dequantize(int dtype, const void* in, size_t nblocks, float* 
                               cudaStream_t s);
 
 // matvec.cu
+// Launch plan of the TMA-fed quantized matvec (qmatvec_tma.cu).
+struct QmvPlan {
+  int nr;        // rows (row pairs in the dual mode) per CTA
+  int stages;    // ring depth
+  int nchunks;   // column chunks of 128
+  size_t nctas;  // grid size
+  size_t smem;   // dynamic shared memory bytes
+};
+QmvPlan plan_qmatvec_tma(int dtype, bool dual, size_t rows, int cols, bool norm);
+bool qmatvec_uses_tma(int cols, const void* w0, const void* w1, const float* x,
+                      const float* norm_w);
+minq_status encode_qmatvec_map(const void* w, size_t rows, int cols, int dtype, int nr,
+                               CUtensorMap* out);
+// m0 / m1: optional tensor maps pre-encoded with plan_qmatvec_tma's nr.
 minq_status launch_qmatvec(int dtype, const void* w0, const void* w1, size_t rows, int cols,
                            const float* x, const float* norm_w, float eps, const float* bias,
-                           const float* residual, float* y, cudaStream_t s);
+                           const float* residual, float* y, cudaStream_t s,
+                           const CUtensorMap* m0 = nullptr, const CUtensorMap* m1 = nullptr);
 minq_status launch_f32_matvec(const float* w, size_t rows, int cols, const float* x,
                               const float* norm_w, float eps, float* y,
                               unsigned long long* argmax_part, int* n_part, cudaStream_t s);
@@ -32,14 +48,15 @@ size_t attn_workspace_bytes(size_t batch, size_t nh, size_t len, size_t hd_max);
 minq_status launch_attention(const float* q, const float* k, const float* v, size_t batch,
                              int nh, int nkv, int hd, int len, size_t seq_stride,
                              size_t head_stride, size_t pos_stride, float* out, void* ws,
-                             size_t ws_bytes, cudaStream_t s);
+                             size_t ws_bytes, cudaStream_t s, const int* d_pos = nullptr,
+                             int cap_len = 0);
 minq_status launch_rope_append(const float* q_in, const float* k_in, const float* v_in,
                                size_t q_in_bstride, size_t kv_in_bstride, const float* q_norm,
                                const float* k_norm, float eps, const float* cos_t,
                                const float* sin_t, size_t batch, int nh, int nkv, int hd,
                                int pos, float* q_out, float* k_cache, float* v_cache,
                                size_t seq_stride, size_t head_stride, size_t pos_stride,
-                               cudaStream_t s);
+                               cudaStream_t s, const int* d_pos = nullptr);
 
 // glue.cu
 minq_status launch_embed(const float* embed, const uint32_t* d_tok, size_t vocab, int hidden,
@@ -49,5 +66,6 @@ minq_status launch_rmsnorm(const float* x, const float* w, float eps, int n, flo
 minq_status launch_epilogue(const float* acc, const float* bias, const float* residual, float* y,
                             size_t n, cudaStream_t s);
 minq_status launch_swiglu(const float* g, const float* u, float* h, size_t n, cudaStream_t s);
+minq_status launch_advance_pos(int* pos, int by, cudaStream_t s);
 
 }  // namespace minq

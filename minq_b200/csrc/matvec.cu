@@ -1,127 +1,47 @@
 // Batch-1 matvec kernels (HBM-bound, CUDA cores) for the block-quantized
-// weights of quantize.rs and the dense f32 lm_head of tensor.rs.
+// weights of quantize.rs and the dense f32 lm_head of tensor.rs, and the
+// launch dispatch.
 //
-// QuantizedTensor::matvec (quantize.rs:215-280) — design:
-//   * The weight stays in the reference's row-major AoS block layout
-//     (Q8_0: f32 d + 32 x i8 = 36 B; Q4_0: f32 d + 16 B of nibbles = 20 B).
-//   * A warp sweeps the full row of R rows in chunks of 8 blocks (256
-//     columns). Lane = 4*block + sub: each lane owns 8 consecutive columns of
-//     one block, so its codes are one 32-bit word (Q4_0) or two (Q8_0) at a
-//     4-byte-aligned offset, the block scale is a broadcast 32-bit load, and
-//     its 8 x-values are two float4s of a shared-memory copy of x.
-//     Per warp-instruction the 32 lanes read a contiguous 128-256 B span of
-//     the row, so every HBM sector fetched is used.
-//   * Codes become exact floats with a byte permute into the mantissa of
-//     2^23 and one subtract (Q8_0: code+128 after an xor with 0x80; Q4_0:
-//     nibbles split into low/high byte planes first), then one FMA each.
-//   * Per block the lane applies the scale once (acc += d * partial), as the
-//     reference does; the partial sums are reduced with warp shuffles.
-//   * x is staged once per CTA in shared memory; an optional RMSNorm
-//     (tensor.rs:219-227) is applied while staging, so the normalised input
-//     never round-trips through HBM. Epilogues: bias add (Qwen2 QKV bias,
-//     model.rs:282-290), residual add (model.rs:305,314) and the SwiGLU
-//     product silu(gate)*up (model.rs:309-312) over a gate/up row pair.
-//   * CTAs are persistent over row groups (grid = a few waves of SMs); when
-//     there are too few row groups, KS warps split each row's columns and
-//     reduce through shared memory.
-#include "common.cuh"
+// QuantizedTensor::matvec (quantize.rs:215-280):
+//   * rows whose byte length is a multiple of 16 (cols % 128 == 0, every
+//     benchmark shape) go to the TMA-fed kernel of qmatvec_tma.cu;
+//   * other shapes use the generic kernel below: a warp sweeps R rows in
+//     chunks of 8 blocks (256 columns); lane = 4*block + sub owns 8
+//     consecutive columns of one block, so its codes are one 32-bit word
+//     (Q4_0) or two (Q8_0) at a 4-byte-aligned offset and its 8 x-values are
+//     two float4s of a shared-memory copy of x; when there are too few row
+//     groups, KS warps split the columns and reduce through shared memory.
+// Both paths: the weight stays in the reference's AoS block layout, codes
+// become exact floats (byte permute into the mantissa of 2^23, subtract),
+// the block scale is applied once per block (acc += d * partial, as the
+// reference does), x is staged once per CTA with the optional RMSNorm
+// (tensor.rs:219-227) applied on the way, and the epilogue adds the bias
+// (model.rs:282-290), the residual (model.rs:305,314) or forms the SwiGLU
+// product silu(gate)*up (model.rs:309-312) over a gate/up row pair.
+#include <cuda.h>
+
+#include <algorithm>
+
+#include "kernels.h"
 #include "ktimer.h"
+#include "matvec_common.cuh"
+#include "pipeline.cuh"
 
 namespace minq {
 
-struct MatvecParams {
-  const uint8_t* w0;     // quantized [rows, nb blocks] (or f32 rows for the dense kernel)
-  const uint8_t* w1;     // second matrix for the SwiGLU dual mode (up_proj), else null
-  size_t rows;           // output rows
-  int cols;              // input length
-  const float* x;        // [cols]
-  const float* norm_w;   // RMSNorm gain applied to x while staging, or null
-  float eps;
-  const float* bias;     // [rows] or null
-  const float* residual; // [rows] or null: y = residual + W x (may alias y)
-  float* y;              // [rows]
-  int ks;                // warps per row group (column split)
-  unsigned long long* argmax_part;  // per-CTA packed argmax (dense kernel), or null
-};
-
-// Stage x (optionally RMS-normalised) into shared memory. Returns after a
-// __syncthreads(). rmsnorm: out = x * (1/sqrt(mean(x^2)+eps)) * w.
-__device__ __forceinline__ void stage_x(const MatvecParams& p, float* xs, float* red) {
-  const int tid = threadIdx.x, nt = blockDim.x;
-  float inv = 1.0f;
-  if (p.norm_w) {
-    float ss = 0.0f;
-    for (int i = tid; i < p.cols; i += nt) {
-      float v = p.x[i];
-      ss = fmaf(v, v, ss);
-    }
-    ss = warp_sum(ss);
-    if ((tid & 31) == 0) red[tid >> 5] = ss;
-    __syncthreads();
-    if (tid < 32) {
-      float v = tid < (nt >> 5) ? red[tid] : 0.0f;
-      v = warp_sum(v);
-      if (tid == 0) red[32] = 1.0f / sqrtf(v / (float)p.cols + p.eps);
-    }
-    __syncthreads();
-    inv = red[32];
-    for (int i = tid; i < p.cols; i += nt) xs[i] = p.x[i] * inv * p.norm_w[i];
-  } else {
-    for (int i = tid; i < p.cols; i += nt) xs[i] = p.x[i];
-  }
-  __syncthreads();
-}
-
-__device__ __forceinline__ float byte_to_float(uint32_t w, int k) {
-  // byte k of w placed in the low mantissa byte of 2^23: value 2^23 + byte.
-  return __int_as_float((int)__byte_perm(w, 0x4B000000u, 0x7440u | (unsigned)k));
-}
-
-// Partial dot of one lane's 8 columns of one block (no scale applied).
-template <int DT>
-__device__ __forceinline__ float lane_dot(const uint8_t* blk, int sub, const float4& xa,
-                                          const float4& xb) {
-  float s;
-  if (DT == MINQ_Q8_0) {
-    const uint32_t* wp = reinterpret_cast<const uint32_t*>(blk + 4 + 8 * sub);
-    uint32_t w0 = __ldg(wp) ^ 0x80808080u;
-    uint32_t w1 = __ldg(wp + 1) ^ 0x80808080u;
-    const float k = 8388736.0f;  // 2^23 + 128
-    s = (byte_to_float(w0, 0) - k) * xa.x;
-    s = fmaf(byte_to_float(w0, 1) - k, xa.y, s);
-    s = fmaf(byte_to_float(w0, 2) - k, xa.z, s);
-    s = fmaf(byte_to_float(w0, 3) - k, xa.w, s);
-    s = fmaf(byte_to_float(w1, 0) - k, xb.x, s);
-    s = fmaf(byte_to_float(w1, 1) - k, xb.y, s);
-    s = fmaf(byte_to_float(w1, 2) - k, xb.z, s);
-    s = fmaf(byte_to_float(w1, 3) - k, xb.w, s);
-  } else {
-    uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(blk + 4 + 4 * sub));
-    uint32_t lo = w & 0x0F0F0F0Fu;         // elements 0,2,4,6 of this lane
-    uint32_t hi = (w >> 4) & 0x0F0F0F0Fu;  // elements 1,3,5,7
-    const float k = 8388616.0f;            // 2^23 + 8
-    s = (byte_to_float(lo, 0) - k) * xa.x;
-    s = fmaf(byte_to_float(hi, 0) - k, xa.y, s);
-    s = fmaf(byte_to_float(lo, 1) - k, xa.z, s);
-    s = fmaf(byte_to_float(hi, 1) - k, xa.w, s);
-    s = fmaf(byte_to_float(lo, 2) - k, xb.x, s);
-    s = fmaf(byte_to_float(hi, 2) - k, xb.y, s);
-    s = fmaf(byte_to_float(lo, 3) - k, xb.z, s);
-    s = fmaf(byte_to_float(hi, 3) - k, xb.w, s);
-  }
-  return s;
-}
-
-__device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
+minq_status launch_qmatvec_tma(const MatvecParams& p, int dtype, const QmvPlan& t,
+                               const CUtensorMap* m0, const CUtensorMap* m1, cudaStream_t s);
 
 // R = rows per row group; DUAL = rows come in (gate, up) pairs.
 template <int DT, int R, bool DUAL>
 __global__ void __launch_bounds__(256) qmatvec_kernel(MatvecParams p) {
   extern __shared__ float smem[];
-  float* red = smem;            // [8 warps * NR + 33]
+  float* red = smem;              // [8 warps * NR] + 33
   float* xs = smem + 8 * 8 + 40;  // [cols]
   constexpr int NR = DUAL ? 2 * R : R;
   constexpr int BB = DT == MINQ_Q8_0 ? kQ8Bytes : kQ4Bytes;
+  pdl_wait();
+  pdl_launch_dependents();
   stage_x(p, xs, red + 8 * NR);
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -184,7 +104,6 @@ __global__ void __launch_bounds__(256) qmatvec_kernel(MatvecParams p) {
       }
     }
     if (g < ngroups && kslot == 0 && lane < R) {
-      // lane r writes row r0 + r (values are warp-uniform after the reduce).
       float v0 = 0.0f, v1 = 0.0f;
 #pragma unroll
       for (int r = 0; r < R; ++r) {
@@ -210,15 +129,19 @@ __global__ void __launch_bounds__(256) qmatvec_kernel(MatvecParams p) {
   }
 }
 
-// Dense f32 matvec (tensor.rs:181-192), lm_head: R rows per warp, float4
-// loads of W with the lanes covering 128 consecutive columns per step; x
-// (optionally RMS-normalised) in shared memory. Optional fused argmax: each
-// CTA writes its best (value, index) packed for a final reduction.
+// Dense f32 matvec (tensor.rs:181-192), the tied lm_head: R rows per warp,
+// float4 streaming loads of W (evict-first) with the 32 lanes covering 128
+// consecutive columns per step; x (optionally RMS-normalised) in shared
+// memory. Fused argmax: each CTA writes its best (value, index), packed so
+// that an integer max reproduces f32::total_cmp with ties to the lowest
+// index (sampler.rs:10-17).
 template <int R>
 __global__ void __launch_bounds__(256) f32_matvec_kernel(MatvecParams p) {
   extern __shared__ float smem[];
   float* red = smem;
   float* xs = smem + 8 * 8 + 40;
+  pdl_wait();
+  pdl_launch_dependents();
   stage_x(p, xs, red + 8 * R);
   __shared__ unsigned long long best_s[8];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -243,7 +166,7 @@ __global__ void __launch_bounds__(256) f32_matvec_kernel(MatvecParams p) {
       const float4 xv = reinterpret_cast<const float4*>(xs)[v];
 #pragma unroll
       for (int i = 0; i < R; ++i) {
-        const float4 wv = __ldcs(rowp[i] + v);  // streamed once: evict-first
+        const float4 wv = __ldcs(rowp[i] + v);
         acc[i] = fmaf(wv.x, xv.x, acc[i]);
         acc[i] = fmaf(wv.y, xv.y, acc[i]);
         acc[i] = fmaf(wv.z, xv.z, acc[i]);
@@ -276,6 +199,8 @@ __global__ void __launch_bounds__(256) f32_matvec_kernel(MatvecParams p) {
 
 // Reduce per-CTA packed argmax partials to one index.
 __global__ void argmax_final_kernel(const unsigned long long* part, int n, uint32_t* out) {
+  pdl_wait();
+  pdl_launch_dependents();
   unsigned long long b = 0;
   for (int i = threadIdx.x; i < n; i += blockDim.x) b = part[i] > b ? part[i] : b;
   b = warp_max_u64(b);
@@ -291,6 +216,8 @@ __global__ void argmax_final_kernel(const unsigned long long* part, int n, uint3
 
 // Standalone argmax over a logits vector (sampler.rs:10-17).
 __global__ void argmax_partial_kernel(const float* x, size_t n, unsigned long long* part) {
+  pdl_wait();
+  pdl_launch_dependents();
   unsigned long long b = 0;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x) {
@@ -315,11 +242,7 @@ static size_t xs_smem_bytes(int cols) { return (size_t)(8 * 8 + 40 + cols) * siz
 
 template <typename K>
 static minq_status set_smem(K kernel, size_t bytes) {
-  if (bytes > 48 * 1024) {
-    MINQ_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)bytes));
-  }
-  return MINQ_OK;
+  return ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), bytes);
 }
 
 // Pick the column split so that enough warps are resident to keep HBM busy.
@@ -331,7 +254,6 @@ static int choose_ks(size_t ngroups, int nchunks) {
 }
 
 static unsigned persistent_grid(size_t ctas_needed, size_t smem_bytes) {
-  // A few waves of CTAs; the rest of the row groups are looped over.
   size_t per_sm = smem_bytes > 0 ? (200 * 1024) / smem_bytes : 8;
   if (per_sm > 8) per_sm = 8;
   if (per_sm < 1) per_sm = 1;
@@ -340,9 +262,18 @@ static unsigned persistent_grid(size_t ctas_needed, size_t smem_bytes) {
   return (unsigned)(g ? g : 1);
 }
 
+bool qmatvec_uses_tma(int cols, const void* w0, const void* w1, const float* x,
+                      const float* norm_w) {
+  return cols % 128 == 0 && (uintptr_t)w0 % 16 == 0 && (!w1 || (uintptr_t)w1 % 16 == 0) &&
+         (uintptr_t)x % 16 == 0 && (!norm_w || (uintptr_t)norm_w % 16 == 0);
+}
+
+// `m0` / `m1`: optional pre-encoded tensor maps for the TMA path (encoded
+// with plan_qmatvec_tma's nr for this shape).
 minq_status launch_qmatvec(int dtype, const void* w0, const void* w1, size_t rows, int cols,
                            const float* x, const float* norm_w, float eps, const float* bias,
-                           const float* residual, float* y, cudaStream_t s) {
+                           const float* residual, float* y, cudaStream_t s,
+                           const CUtensorMap* m0, const CUtensorMap* m1) {
   if (rows == 0) return MINQ_OK;
   MatvecParams p{};
   p.w0 = (const uint8_t*)w0;
@@ -355,7 +286,16 @@ minq_status launch_qmatvec(int dtype, const void* w0, const void* w1, size_t row
   p.bias = bias;
   p.residual = residual;
   p.y = y;
+  p.status = device_status_word();
   const bool dual = w1 != nullptr;
+  const double wbytes = (double)rows * (cols / kBlock) * block_bytes(dtype) * (dual ? 2 : 1);
+  ScopedKTimer timer(KF_QMATVEC, s,
+                     wbytes + 4.0 * cols * (norm_w ? 2 : 1) +
+                         4.0 * rows * (1 + (bias ? 1 : 0) + (residual ? 1 : 0)));
+  if (qmatvec_uses_tma(cols, w0, w1, x, norm_w)) {
+    const QmvPlan t = plan_qmatvec_tma(dtype, dual, rows, cols, norm_w != nullptr);
+    return launch_qmatvec_tma(p, dtype, t, m0, m1, s);
+  }
   constexpr int R_SINGLE = 4, R_DUAL = 2;
   const int R = dual ? R_DUAL : R_SINGLE;
   const size_t ngroups = (rows + R - 1) / R;
@@ -364,15 +304,11 @@ minq_status launch_qmatvec(int dtype, const void* w0, const void* w1, size_t row
   const size_t smem = xs_smem_bytes(cols);
   const size_t ctas = (ngroups + (8 / p.ks) - 1) / (8 / p.ks);
   const unsigned grid = persistent_grid(ctas, smem);
-  const double wbytes = (double)rows * (cols / kBlock) * block_bytes(dtype) * (dual ? 2 : 1);
-  ScopedKTimer timer(KF_QMATVEC, s,
-                     wbytes + 4.0 * cols * (norm_w ? 2 : 1) +
-                         4.0 * rows * (1 + (bias ? 1 : 0) + (residual ? 1 : 0)));
-#define MINQ_QMV(DT, RR, DU)                                  \
-  do {                                                        \
-    auto k = qmatvec_kernel<DT, RR, DU>;                      \
-    MINQ_TRY(set_smem(k, smem));                              \
-    k<<<grid, 256, smem, s>>>(p);                             \
+#define MINQ_QMV(DT, RR, DU)             \
+  do {                                   \
+    auto k = qmatvec_kernel<DT, RR, DU>; \
+    MINQ_TRY(set_smem(k, smem));         \
+    MINQ_CUDA_TRY(launch_k(k, dim3(grid), dim3(256), smem, s, p)); \
   } while (0)
   if (dtype == MINQ_Q8_0) {
     if (dual) MINQ_QMV(MINQ_Q8_0, R_DUAL, true);
@@ -412,14 +348,14 @@ minq_status launch_f32_matvec(const float* w, size_t rows, int cols, const float
   MINQ_TRY(set_smem(k, smem));
   ScopedKTimer timer(KF_F32_MATVEC, s,
                      4.0 * rows * cols + 4.0 * cols * (norm_w ? 2 : 1) + 4.0 * rows);
-  k<<<grid, 256, smem, s>>>(p);
+  MINQ_CUDA_TRY(launch_k(k, dim3(grid), dim3(256), smem, s, p));
   MINQ_LAUNCH_CHECK("f32_matvec_kernel");
   return MINQ_OK;
 }
 
 minq_status launch_argmax_final(const unsigned long long* part, int n, uint32_t* out,
                                 cudaStream_t s) {
-  argmax_final_kernel<<<1, 256, 0, s>>>(part, n, out);
+  MINQ_CUDA_TRY(launch_k(argmax_final_kernel, dim3(1), dim3(256), 0, s, part, n, out));
   MINQ_LAUNCH_CHECK("argmax_final_kernel");
   return MINQ_OK;
 }
@@ -429,7 +365,7 @@ minq_status launch_argmax(const float* x, size_t n, unsigned long long* part, in
   size_t g = (n + 255) / 256;
   if (g > (size_t)n_part) g = n_part;
   if (g == 0) g = 1;
-  argmax_partial_kernel<<<(unsigned)g, 256, 0, s>>>(x, n, part);
+  MINQ_CUDA_TRY(launch_k(argmax_partial_kernel, dim3((unsigned)g), dim3(256), 0, s, x, n, part));
   MINQ_LAUNCH_CHECK("argmax_partial_kernel");
   return launch_argmax_final(part, (int)g, out, s);
 }

@@ -13,9 +13,16 @@
 //     attention), K stored post-RoPE like LayerCache (model.rs:100-106);
 //   * RoPE cos/sin tables [max_seq_len, hd/2] are built on the host with the
 //     reference's f32 expression and glibc (model.rs:170-186) and uploaded.
+//
+// Execution: one decode step is ~5 kernels per layer, each launched with
+// programmatic dependent launch. The step reads its position from a device
+// counter (advanced by the step itself), so it is captured once per cache as
+// a CUDA graph and replayed for every token; prefill replays the no-logits
+// graph token by token.
 #include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <string>
@@ -39,6 +46,8 @@ struct DevLinear {
   uint64_t rows = 0, cols = 0;
   const void* ptr = nullptr;
   size_t nbytes = 0;
+  CUtensorMap tm;     // 2-D TMA map for the TMA-fed matvec (when tm_ok)
+  bool tm_ok = false;
 };
 
 struct DevLayer {
@@ -65,6 +74,7 @@ struct minq_model {
   int device = 0;
   cudaStream_t stream = nullptr;
   bool finished = false;
+  bool use_graphs = true;
   std::map<std::string, DevTensor> pending;
   std::vector<void*> allocs;
   // assembled
@@ -81,8 +91,8 @@ struct minq_model {
   float *hbuf = nullptr, *gbuf = nullptr, *ubuf = nullptr, *tmp = nullptr, *logits = nullptr;
   unsigned long long* argmax_part = nullptr;
   int argmax_cap = 0;
-  uint32_t* d_argmax = nullptr;
-  uint32_t* d_tokens = nullptr;
+  uint32_t* d_tok = nullptr;     // the step's input token and, after it, its argmax
+  uint32_t* d_tokens = nullptr;  // staged prompt
   size_t d_tokens_cap = 0;
 };
 
@@ -93,6 +103,9 @@ struct minq_cache {
   float* v = nullptr;
   void* ws = nullptr;
   size_t ws_bytes = 0;
+  int* d_pos = nullptr;        // device copy of `len` read by graph-captured steps
+  bool d_pos_valid = false;
+  cudaGraphExec_t step[2] = {nullptr, nullptr};  // [0]: no logits, [1]: logits + argmax
 };
 
 namespace minq {
@@ -197,6 +210,18 @@ void check_vec(minq_model* m, const float* p, uint64_t len, uint64_t want, const
                      std::to_string(want);
 }
 
+// Pre-encode the TMA tensor map of a quantized linear for its launch plan.
+minq_status prepare_map(DevLinear* l, bool dual, bool norm) {
+  if (l->tag != MINQ_Q8_0 && l->tag != MINQ_Q4_0) return MINQ_OK;
+  if (l->cols % 128 != 0 || (uintptr_t)l->ptr % 16 != 0) return MINQ_OK;
+  const QmvPlan t = plan_qmatvec_tma(l->tag, dual, l->rows, (int)l->cols, norm);
+  MINQ_TRY(encode_qmatvec_map(l->ptr, l->rows, (int)l->cols, l->tag, t.nr, &l->tm));
+  l->tm_ok = true;
+  return MINQ_OK;
+}
+
+const CUtensorMap* map_of(const DevLinear& l) { return l.tm_ok ? &l.tm : nullptr; }
+
 }  // namespace
 
 // assemble (model.rs:522-574) on device tensors.
@@ -212,7 +237,6 @@ minq_status model_finish(minq_model* m) {
   m->embed = static_cast<const float*>(emb->ptr);
   const uint64_t H = c.hidden_size, hd = c.head_dim, qd = c.n_heads * hd,
                  kvd = c.n_kv_heads * hd, I = c.intermediate_size;
-  if (!m->shape_error.empty()) {}
   if (emb->shape[1] != H && m->shape_error.empty())
     m->shape_error = "embedding width " + std::to_string(emb->shape[1]) + " != hidden_size";
   if (emb->shape[0] < c.vocab_size && m->shape_error.empty())
@@ -286,6 +310,15 @@ minq_status model_finish(minq_model* m) {
                                         cudaMemcpyDeviceToDevice, m->stream));
       }
     }
+    if (m->shape_error.empty()) {
+      if (L.qkv.tag >= 0) MINQ_TRY(prepare_map(&L.qkv, false, true));
+      MINQ_TRY(prepare_map(&L.o, false, false));
+      MINQ_TRY(prepare_map(&L.down, false, false));
+      if (L.gate.tag != MINQ_F32 && L.gate.tag == L.up.tag) {
+        MINQ_TRY(prepare_map(&L.gate, true, true));
+        MINQ_TRY(prepare_map(&L.up, true, true));
+      }
+    }
   }
   uint64_t nf = 0;
   MINQ_TRY(get_vec(m, "model.norm.weight", true, &m->final_norm, &nf));
@@ -305,6 +338,14 @@ minq_status model_finish(minq_model* m) {
   m->weight_bytes += m->lm_head.nbytes;
   if (m->lm_head.tag == MINQ_F32 && (H % 4 != 0) && m->shape_error.empty())
     m->shape_error = "hidden_size must be a multiple of 4 for the f32 lm_head kernel";
+  if (m->shape_error.empty() && m->lm_head.tag != MINQ_F32) {
+    DevLinear& lm = m->lm_head;
+    if (lm.cols % 128 == 0 && (uintptr_t)lm.ptr % 16 == 0) {
+      const QmvPlan t = plan_qmatvec_tma(lm.tag, false, c.vocab_size, (int)lm.cols, true);
+      MINQ_TRY(encode_qmatvec_map(lm.ptr, c.vocab_size, (int)lm.cols, lm.tag, t.nr, &lm.tm));
+      lm.tm_ok = true;
+    }
+  }
 
   // RoPE tables.
   std::vector<float> cs, sn;
@@ -340,10 +381,12 @@ minq_status model_finish(minq_model* m) {
   MINQ_TRY(dmalloc(m, &p, m->argmax_cap * sizeof(unsigned long long)));
   m->argmax_part = static_cast<unsigned long long*>(p);
   MINQ_TRY(dmalloc(m, &p, 16));
-  m->d_argmax = static_cast<uint32_t*>(p);
+  m->d_tok = static_cast<uint32_t*>(p);
+  MINQ_CUDA_TRY(cudaMemsetAsync(m->d_tok, 0, 16, m->stream));
   m->d_tokens_cap = 4096;
   MINQ_TRY(dmalloc(m, &p, m->d_tokens_cap * 4));
   m->d_tokens = static_cast<uint32_t*>(p);
+  if (!device_status_word()) return fail(MINQ_ERR_CUDA, "cannot allocate the device status word");
   MINQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
   m->finished = true;
   return MINQ_OK;
@@ -359,7 +402,7 @@ minq_status linear(minq_model* m, const DevLinear& l, const float* x, const floa
   const float eps = m->cfg.rms_norm_eps;
   if (l.tag != MINQ_F32)
     return launch_qmatvec(l.tag, l.ptr, nullptr, l.rows, (int)l.cols, x, norm_w, eps, bias,
-                          residual, y, m->stream);
+                          residual, y, m->stream, norm_w ? nullptr : map_of(l));
   const bool epi = bias || residual;
   float* dst = epi ? m->tmp : y;
   if (l.cols % 4 != 0) return fail(MINQ_ERR_SHAPE, "f32 matvec needs cols % 4 == 0");
@@ -371,10 +414,12 @@ minq_status linear(minq_model* m, const DevLinear& l, const float* x, const floa
 
 }  // namespace
 
-// model.rs:273-318 for one token at `pos`; the token id is read from device
-// memory. Logits (and their argmax) only when `want_logits`.
+// model.rs:273-318 for one token. The token id is read from `d_tok`. In
+// graph mode the position comes from c->d_pos (device) and the attention
+// grid is sized for the cache capacity; otherwise `pos` is used. Logits (and
+// their argmax into d_argmax) only when `want_logits`.
 minq_status forward_token(minq_model* m, minq_cache* c, const uint32_t* d_tok, size_t pos,
-                          bool want_logits, float* d_logits, uint32_t* d_argmax) {
+                          bool want_logits, float* d_logits, uint32_t* d_argmax, bool graph) {
   const minq_config& cfg = m->cfg;
   const int H = (int)cfg.hidden_size, hd = (int)cfg.head_dim, nh = (int)cfg.n_heads,
             nkv = (int)cfg.n_kv_heads;
@@ -384,13 +429,14 @@ minq_status forward_token(minq_model* m, minq_cache* c, const uint32_t* d_tok, s
   const size_t seq_stride = (size_t)nkv * c->max_seq * hd, head_stride = c->max_seq * hd,
                pos_stride = hd;
   const size_t layer_elems = c->batch * seq_stride;
+  const int* dpos = graph ? c->d_pos : nullptr;
   MINQ_TRY(launch_embed(m->embed, d_tok, cfg.vocab_size, H, m->x, s));
   for (uint64_t li = 0; li < cfg.n_layers; ++li) {
     const DevLayer& L = m->layers[li];
     // attention sub-layer: q|k|v = W (rmsnorm(x)) + bias
     if (L.qkv.tag >= 0) {
       MINQ_TRY(launch_qmatvec(L.qkv.tag, L.qkv.ptr, nullptr, L.qkv.rows, H, m->x, L.attn_norm,
-                              eps, L.bias_qkv, nullptr, m->qkv, s));
+                              eps, L.bias_qkv, nullptr, m->qkv, s, map_of(L.qkv)));
     } else {
       MINQ_TRY(launch_rmsnorm(m->x, L.attn_norm, eps, H, m->xn, s));
       MINQ_TRY(linear(m, L.q, m->xn, nullptr, L.q_bias, nullptr, m->qkv));
@@ -402,14 +448,15 @@ minq_status forward_token(minq_model* m, minq_cache* c, const uint32_t* d_tok, s
     MINQ_TRY(launch_rope_append(m->qkv, m->qkv + qd, m->qkv + qd + kvd, 0, 0, L.q_norm,
                                 L.k_norm, eps, m->rope_cos, m->rope_sin, 1, nh, nkv, hd,
                                 (int)pos, m->q_rot, kc, vc, seq_stride, head_stride, pos_stride,
-                                s));
+                                s, dpos));
     MINQ_TRY(launch_attention(m->q_rot, kc, vc, 1, nh, nkv, hd, (int)pos + 1, seq_stride,
-                              head_stride, pos_stride, m->att, c->ws, c->ws_bytes, s));
+                              head_stride, pos_stride, m->att, c->ws, c->ws_bytes, s, dpos,
+                              (int)c->max_seq));
     MINQ_TRY(linear(m, L.o, m->att, nullptr, nullptr, m->x, m->x));  // x += o
     // MLP sub-layer: h = silu(gate(rmsnorm(x))) * up(rmsnorm(x)); x += down(h)
     if (L.gate.tag != MINQ_F32 && L.gate.tag == L.up.tag) {
       MINQ_TRY(launch_qmatvec(L.gate.tag, L.gate.ptr, L.up.ptr, I, H, m->x, L.ffn_norm, eps,
-                              nullptr, nullptr, m->hbuf, s));
+                              nullptr, nullptr, m->hbuf, s, map_of(L.gate), map_of(L.up)));
     } else {
       MINQ_TRY(launch_rmsnorm(m->x, L.ffn_norm, eps, H, m->xn, s));
       MINQ_TRY(linear(m, L.gate, m->xn, nullptr, nullptr, nullptr, m->gbuf));
@@ -418,18 +465,62 @@ minq_status forward_token(minq_model* m, minq_cache* c, const uint32_t* d_tok, s
     }
     MINQ_TRY(linear(m, L.down, m->hbuf, nullptr, nullptr, m->x, m->x));  // x += down
   }
-  if (!want_logits) return MINQ_OK;
-  const uint64_t V = cfg.vocab_size;
-  if (m->lm_head.tag == MINQ_F32) {
-    int nparts = m->argmax_cap;
-    MINQ_TRY(launch_f32_matvec(static_cast<const float*>(m->lm_head.ptr), V, H, m->x,
-                               m->final_norm, eps, d_logits, m->argmax_part, &nparts, s));
-    MINQ_TRY(launch_argmax_final(m->argmax_part, nparts, d_argmax, s));
-  } else {
-    MINQ_TRY(launch_qmatvec(m->lm_head.tag, m->lm_head.ptr, nullptr, V, H, m->x, m->final_norm,
-                            eps, nullptr, nullptr, d_logits, s));
-    MINQ_TRY(launch_argmax(d_logits, V, m->argmax_part, m->argmax_cap, d_argmax, s));
+  if (want_logits) {
+    const uint64_t V = cfg.vocab_size;
+    if (m->lm_head.tag == MINQ_F32) {
+      int nparts = m->argmax_cap;
+      MINQ_TRY(launch_f32_matvec(static_cast<const float*>(m->lm_head.ptr), V, H, m->x,
+                                 m->final_norm, eps, d_logits, m->argmax_part, &nparts, s));
+      MINQ_TRY(launch_argmax_final(m->argmax_part, nparts, d_argmax, s));
+    } else {
+      MINQ_TRY(launch_qmatvec(m->lm_head.tag, m->lm_head.ptr, nullptr, V, H, m->x,
+                              m->final_norm, eps, nullptr, nullptr, d_logits, s,
+                              map_of(m->lm_head)));
+      MINQ_TRY(launch_argmax(d_logits, V, m->argmax_part, m->argmax_cap, d_argmax, s));
+    }
   }
+  if (graph) MINQ_TRY(launch_advance_pos(c->d_pos, 1, s));
+  return MINQ_OK;
+}
+
+// Capture one decode step (with or without logits) of cache `c` as a graph.
+static minq_status capture_step(minq_model* m, minq_cache* c, bool logits, cudaGraphExec_t* out) {
+  cudaGraph_t g = nullptr;
+  MINQ_CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+  minq_status st = forward_token(m, c, m->d_tok, 0, logits, m->logits, m->d_tok, true);
+  cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+  if (st != MINQ_OK) {
+    if (g) cudaGraphDestroy(g);
+    return st;
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+  e = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+  return MINQ_OK;
+}
+
+static minq_status sync_dpos(minq_cache* c) {
+  if (c->d_pos_valid) return MINQ_OK;
+  const int v = (int)c->len;
+  MINQ_CUDA_TRY(cudaMemcpyAsync(c->d_pos, &v, sizeof(int), cudaMemcpyHostToDevice, c->m->stream));
+  MINQ_CUDA_TRY(cudaStreamSynchronize(c->m->stream));
+  c->d_pos_valid = true;
+  return MINQ_OK;
+}
+
+// Run one step for the token already in m->d_tok (graph replay or eager).
+static minq_status run_step(minq_model* m, minq_cache* c, bool logits) {
+  if (m->use_graphs) {
+    MINQ_TRY(sync_dpos(c));
+    cudaGraphExec_t& g = c->step[logits ? 1 : 0];
+    if (!g) MINQ_TRY(capture_step(m, c, logits, &g));
+    MINQ_CUDA_TRY(cudaGraphLaunch(g, m->stream));
+  } else {
+    c->d_pos_valid = false;
+    MINQ_TRY(forward_token(m, c, m->d_tok, c->len, logits, m->logits, m->d_tok, false));
+  }
+  c->len += 1;
   return MINQ_OK;
 }
 
@@ -451,6 +542,8 @@ minq_status minq_model_new(const minq_config* cfg, minq_model** out) {
   minq_model* m = new minq_model();
   m->cfg = *cfg;
   cudaGetDevice(&m->device);
+  const char* g = std::getenv("MINQ_GRAPHS");
+  m->use_graphs = !(g && g[0] == '0');
   e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
   if (e != cudaSuccess) {
     delete m;
@@ -549,6 +642,12 @@ minq_status minq_model_weight_bytes(const minq_model* m, uint64_t* out) {
   return MINQ_OK;
 }
 
+minq_status minq_model_set_graphs(minq_model* m, int enabled) {
+  if (!m) return fail(MINQ_ERR_ARG, "null model");
+  m->use_graphs = enabled != 0;
+  return MINQ_OK;
+}
+
 void* minq_model_stream(minq_model* m) { return m ? (void*)m->stream : nullptr; }
 
 void minq_model_free(minq_model* m) {
@@ -579,10 +678,12 @@ minq_status minq_cache_new(minq_model* m, size_t batch, size_t max_seq, minq_cac
   if (e == cudaSuccess) e = cudaMalloc(&c->v, bytes ? bytes : 16);
   c->ws_bytes = attn_workspace_bytes(batch, m->cfg.n_heads, max_seq, m->cfg.head_dim);
   if (e == cudaSuccess) e = cudaMalloc(&c->ws, c->ws_bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&c->d_pos, 16);
   if (e != cudaSuccess) {
     cudaFree(c->k);
     cudaFree(c->v);
     cudaFree(c->ws);
+    cudaFree(c->d_pos);
     delete c;
     return cuda_fail(e, "cudaMalloc(kv cache)");
   }
@@ -593,6 +694,7 @@ minq_status minq_cache_new(minq_model* m, size_t batch, size_t max_seq, minq_cac
 minq_status minq_cache_reset(minq_cache* c) {
   if (!c) return fail(MINQ_ERR_ARG, "null cache");
   c->len = 0;
+  c->d_pos_valid = false;
   return MINQ_OK;
 }
 
@@ -606,6 +708,7 @@ minq_status minq_cache_set_len(minq_cache* c, size_t len) {
   if (!c) return fail(MINQ_ERR_ARG, "null cache");
   if (len > c->max_seq) return fail(MINQ_ERR_MODEL, "length exceeds cache capacity");
   c->len = len;
+  c->d_pos_valid = false;
   return MINQ_OK;
 }
 
@@ -639,6 +742,7 @@ static minq_status cache_copy(const minq_cache* c, size_t layer, size_t start, s
 minq_status minq_cache_write(minq_cache* c, size_t layer, size_t start, size_t n, const float* k,
                              const float* v) {
   if (!c) return fail(MINQ_ERR_ARG, "null cache");
+  MINQ_CUDA_TRY(cudaStreamSynchronize(c->m->stream));
   return cache_copy(c, layer, start, n, const_cast<float*>(k), const_cast<float*>(v), true);
 }
 
@@ -653,18 +757,22 @@ void minq_cache_free(minq_cache* c) {
   if (!c) return;
   cudaSetDevice(c->m->device);
   cudaStreamSynchronize(c->m->stream);
+  for (cudaGraphExec_t g : c->step)
+    if (g) cudaGraphExecDestroy(g);
   cudaFree(c->k);
   cudaFree(c->v);
   cudaFree(c->ws);
+  cudaFree(c->d_pos);
   delete c;
 }
 
 // ---------------------------------------------------------------------------
 // C ABI: forward / generate
 
+// Common checks, then one step per token; token i comes from host h_tokens
+// or device d_tokens. Results land in m->logits / m->d_tok.
 static minq_status forward_impl(minq_model* m, minq_cache* c, const uint32_t* h_tokens,
-                                const uint32_t* d_tokens, size_t n, float* d_logits,
-                                uint32_t* d_argmax) {
+                                const uint32_t* d_tokens, size_t n) {
   if (!m || !c) return fail(MINQ_ERR_ARG, "null argument");
   if (c->m != m) return fail(MINQ_ERR_ARG, "cache belongs to another model");
   if (n == 0) return fail(MINQ_ERR_MODEL, "empty token sequence");  // model.rs:255-257
@@ -694,8 +802,8 @@ static minq_status forward_impl(minq_model* m, minq_cache* c, const uint32_t* h_
       return fail(MINQ_ERR_SHAPE, "row index " + std::to_string(h_tokens[i]) +
                                       " out of bounds for " + std::to_string(m->cfg.vocab_size) +
                                       " rows");
-    MINQ_TRY(forward_token(m, c, toks + i, c->len, i + 1 == n, d_logits, d_argmax));
-    c->len += 1;
+    MINQ_CUDA_TRY(cudaMemcpyAsync(m->d_tok, toks + i, 4, cudaMemcpyDeviceToDevice, m->stream));
+    MINQ_TRY(run_step(m, c, i + 1 == n));
   }
   return MINQ_OK;
 }
@@ -703,15 +811,43 @@ static minq_status forward_impl(minq_model* m, minq_cache* c, const uint32_t* h_
 minq_status minq_forward_device(minq_model* m, minq_cache* c, const uint32_t* d_tokens,
                                 size_t n, float* d_logits, uint32_t* d_argmax) {
   if (!d_tokens) return fail(MINQ_ERR_ARG, "null tokens");
-  return forward_impl(m, c, nullptr, d_tokens, n, d_logits ? d_logits : m->logits,
-                      d_argmax ? d_argmax : m->d_argmax);
+  MINQ_TRY(forward_impl(m, c, nullptr, d_tokens, n));
+  if (d_logits && d_logits != m->logits)
+    MINQ_CUDA_TRY(cudaMemcpyAsync(d_logits, m->logits, m->cfg.vocab_size * 4,
+                                  cudaMemcpyDeviceToDevice, m->stream));
+  if (d_argmax && d_argmax != m->d_tok)
+    MINQ_CUDA_TRY(cudaMemcpyAsync(d_argmax, m->d_tok, 4, cudaMemcpyDeviceToDevice, m->stream));
+  return MINQ_OK;
+}
+
+minq_status minq_decode_steps(minq_model* m, minq_cache* c, size_t n_steps,
+                              uint32_t* d_tokens_out) {
+  if (!m || !c) return fail(MINQ_ERR_ARG, "null argument");
+  if (c->m != m) return fail(MINQ_ERR_ARG, "cache belongs to another model");
+  if (!m->shape_error.empty()) return fail(MINQ_ERR_SHAPE, m->shape_error);
+  if (c->batch != 1) return fail(MINQ_ERR_ARG, "minq_decode_steps drives a batch-1 cache");
+  if (c->len == 0) return fail(MINQ_ERR_MODEL, "decode continuation needs a prefilled cache");
+  MINQ_CUDA_TRY(cudaSetDevice(m->device));
+  for (size_t i = 0; i < n_steps; ++i) {
+    if (c->len >= m->cfg.max_seq_len)
+      return fail(MINQ_ERR_MODEL,
+                  "sequence exceeds max_seq_len (" + std::to_string(m->cfg.max_seq_len) + ")");
+    if (c->len >= c->max_seq)
+      return fail(MINQ_ERR_MODEL,
+                  "sequence exceeds the cache capacity (" + std::to_string(c->max_seq) + ")");
+    MINQ_TRY(run_step(m, c, true));
+    if (d_tokens_out)
+      MINQ_CUDA_TRY(cudaMemcpyAsync(d_tokens_out + i, m->d_tok, 4, cudaMemcpyDeviceToDevice,
+                                    m->stream));
+  }
+  return MINQ_OK;
 }
 
 minq_status minq_forward(minq_model* m, minq_cache* c, const uint32_t* tokens, size_t n,
                          float* logits_out, uint32_t* argmax_out) {
   if (!m) return fail(MINQ_ERR_ARG, "null model");
   if (n && !tokens) return fail(MINQ_ERR_ARG, "null tokens");
-  minq_status st = forward_impl(m, c, tokens, nullptr, n, m->logits, m->d_argmax);
+  minq_status st = forward_impl(m, c, tokens, nullptr, n);
   if (st != MINQ_OK) {
     cudaStreamSynchronize(m->stream);
     return st;
@@ -720,9 +856,9 @@ minq_status minq_forward(minq_model* m, minq_cache* c, const uint32_t* tokens, s
     MINQ_CUDA_TRY(cudaMemcpyAsync(logits_out, m->logits, m->cfg.vocab_size * 4,
                                   cudaMemcpyDeviceToHost, m->stream));
   if (argmax_out)
-    MINQ_CUDA_TRY(cudaMemcpyAsync(argmax_out, m->d_argmax, 4, cudaMemcpyDeviceToHost, m->stream));
+    MINQ_CUDA_TRY(cudaMemcpyAsync(argmax_out, m->d_tok, 4, cudaMemcpyDeviceToHost, m->stream));
   MINQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
-  return MINQ_OK;
+  return take_device_status();
 }
 
 minq_status minq_generate(minq_model* m, const uint32_t* prompt, size_t n_prompt,
@@ -743,11 +879,11 @@ minq_status minq_generate(minq_model* m, const uint32_t* prompt, size_t n_prompt
   auto t1 = clk::now();
   for (size_t i = 0; rc == MINQ_OK && i < max_tokens; ++i) {
     if (tokens_out) tokens_out[i] = tok;
-    st.gen_tokens += 1;
     if (on_token && on_token(tok, user) != 0) {
       rc = fail(MINQ_ERR_MODEL, "on_token callback aborted generation");
       break;
     }
+    st.gen_tokens += 1;
     bool stop = false;
     for (size_t k = 0; k < n_stop; ++k) stop |= stop_tokens[k] == tok;
     if (stop) break;

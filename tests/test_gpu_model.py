@@ -207,6 +207,49 @@ def test_engine_stop_tokens(mq):
     assert seen == first and st.gen_tokens == 1
 
 
+def test_graph_replay_and_eager_launch_agree(mq, orc):
+    """The captured-graph step (device-side position, capacity-sized attention
+    grid) and the eager step give the same logits and cache."""
+    cfg = tiny_config(2, dtype="q4_0", hidden=128, inter=256)
+    recs = quantize_records(synth.random_model_records(cfg, 13), 2, orc)
+    gm, om = both(mq, orc, cfg, recs)
+    toks = [3, 1, 4, 1, 5, 9, 2, 6, 5, 3]
+    ca = gm.new_cache()
+    a = gm.forward(toks, ca)
+    gm.set_graphs(False)
+    cb = gm.new_cache()
+    b = gm.forward(toks, cb)
+    gm.set_graphs(True)
+    close(a, b, 1e-4)
+    close(om.forward(toks, om.new_cache()), a)
+    for layer in range(cfg.n_layers):
+        assert np.abs(ca.read(layer)[0] - cb.read(layer)[0]).max() < 1e-5
+    # mixing: eager steps then graph steps on one cache
+    cc = gm.new_cache()
+    gm.set_graphs(False)
+    gm.forward(toks[:4], cc)
+    gm.set_graphs(True)
+    close(a, gm.forward(toks[4:], cc), 1e-4)
+
+
+def test_decode_steps_matches_oracle_greedy(mq, orc):
+    """minq_decode_steps (greedy continuation without the host in the loop)."""
+    import torch
+    cfg = tiny_config(4, dtype="q8_0", hidden=128, inter=256)
+    recs = quantize_records(synth.random_model_records(cfg, 21), 1, orc)
+    gm, om = both(mq, orc, cfg, recs)
+    prompt = [7, 7, 3, 100, 42]
+    ref, _ = orc.greedy_generate(om, prompt, 12)
+    c = gm.new_cache()
+    first = gm.forward_argmax(prompt, c)
+    out = torch.zeros(11, dtype=torch.int32, device="cuda")
+    gm.decode_steps(c, 11, out.data_ptr())
+    torch.cuda.synchronize()
+    got = [first] + [int(v) for v in out.cpu().numpy()]
+    assert got == ref
+    assert c.len == len(prompt) + 11
+
+
 # ------------------------------------------------ benchmark architectures
 
 def _greedy_parity(mq, orc, arch, prompt_len, n_tokens, max_seq, seed=1234):

@@ -296,10 +296,14 @@ def run_minq(args, world, rank, local):
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
+    # NVTX range: lets `ncu --nvtx --nvtx-include timed_decode/` list exactly
+    # the launches of the timed region
+    torch.cuda.nvtx.range_push("timed_decode")
     th0 = time.perf_counter()
     for _ in range(K):
         step()
     host_enqueue_ms = 1000.0 * (time.perf_counter() - th0)
+    torch.cuda.nvtx.range_pop()
     ev1.record(stream)
     torch.cuda.synchronize()
     barrier(world)

@@ -40,6 +40,12 @@ import time
 import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
+
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per algorithmic
+# byte, from one ncu --set full capture of three decode-shaped Q4_0 qmatvec
+# launches (q/k/v, o_proj, gate/up): 47.72 MB / 47.62 MB. Summary and command
+# under profiles/.
+NCU_TRAFFIC_RATIO = {"qmatvec": 1.002}
 sys.path.insert(0, ROOT)
 
 WORKLOADS = {
@@ -369,7 +375,8 @@ def run_minq(args, world, rank, local):
         d = fams[dom]
         roof = {"bound": "hbm", "kernel": dom, "achieved": d["gbs"], "peak": peak,
                 "unit": "GB/s", "frac": d["gbs"] / peak, "peak_source": peak_src,
-                "traffic": None,
+                "traffic": (d["bytes"] / d["launches"] * NCU_TRAFFIC_RATIO[dom]
+                            if dom in NCU_TRAFFIC_RATIO else None),
                 "per_launch_bytes": d["bytes"] / d["launches"], "avg_launch_us": d["avg_us"]}
 
     # ---- CPU baseline (rank 0, N=1): oracle continues the same sequence ----

@@ -169,6 +169,23 @@ minq_status minq_attend(const float* q, const float* k, const float* v, size_t l
                         size_t n_heads, size_t n_kv, size_t head_dim, float* out,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* minq_attend without a workspace argument: the split-KV scratch is a
+ * 32 MiB array inside the library, so the call allocates no device memory.
+ * No reference counterpart: added for callers that cannot allocate or own
+ * device memory (a host language binding without a device allocator, a
+ * real-time thread that must not take cudaMalloc's implicit
+ * synchronisation). Limit: n_heads * ceil(len/32) * (head_dim+2) * 4 + 256
+ * bytes <= 32 MiB, else MINQ_ERR_ARG and nothing is launched. The first
+ * call on each device takes the scratch's address (cudaGetSymbolAddress)
+ * with that device current; make that first call before any stream capture.
+ * Calls that may overlap on the GPU (other streams, other host threads)
+ * share the one scratch and race: order them on one stream or with events.
+ * Nothing in the scratch needs to start at zero. Bounded-wait timeouts
+ * inside this call are not recorded for minq_device_status. */
+minq_status minq_attend_static(const float* q, const float* k, const float* v, size_t len,
+                               size_t n_heads, size_t n_kv, size_t head_dim, float* out,
+                               void* stream);
+
 /* ---------------------------------------------------------------------- */
 /* Model (model.rs:88-98, assemble :522-574, load_minq :711-715)           */
 

@@ -616,7 +616,8 @@ static minq_status launch_tma_hd(const AttnParams& p, int gmax, dim3 grid, cudaS
 minq_status launch_attention(const float* q, const float* k, const float* v, size_t batch,
                              int nh, int nkv, int hd, int len, size_t seq_stride,
                              size_t head_stride, size_t pos_stride, float* out, void* ws,
-                             size_t ws_bytes, cudaStream_t s, const int* d_pos, int cap_len) {
+                             size_t ws_bytes, cudaStream_t s, const int* d_pos, int cap_len,
+                             bool record_status) {
   if (!d_pos && len <= 0) return fail(MINQ_ERR_SHAPE, "attention over an empty history");
   if (nkv <= 0 || nh % nkv != 0)
     return fail(MINQ_ERR_MODEL, "n_heads must be a multiple of n_kv_heads");
@@ -634,7 +635,7 @@ minq_status launch_attention(const float* q, const float* k, const float* v, siz
   p.nh = nh;
   p.nkv = nkv;
   p.len = len;
-  p.status = device_status_word();
+  p.status = record_status ? device_status_word() : nullptr;
   p.d_pos = d_pos;
   // The TMA path needs each KV head's positions contiguous (head-major
   // cache) and 16-byte aligned tiles.

@@ -49,7 +49,9 @@ minq_status launch_attention(const float* q, const float* k, const float* v, siz
                              int nh, int nkv, int hd, int len, size_t seq_stride,
                              size_t head_stride, size_t pos_stride, float* out, void* ws,
                              size_t ws_bytes, cudaStream_t s, const int* d_pos = nullptr,
-                             int cap_len = 0);
+                             int cap_len = 0, bool record_status = true);
+// record_status = false: bounded-wait timeouts are not recorded (and the
+// lazily allocated device status word is never touched).
 minq_status launch_rope_append(const float* q_in, const float* k_in, const float* v_in,
                                size_t q_in_bstride, size_t kv_in_bstride, const float* q_norm,
                                const float* k_norm, float eps, const float* cos_t,

@@ -2,6 +2,7 @@
 #include <atomic>
 #include <cstdlib>
 #include <map>
+#include <set>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -64,6 +65,17 @@ minq_status ensure_dynamic_smem(const void* kernel, size_t bytes) {
       cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
   cur = bytes;
   return MINQ_OK;
+}
+
+void prefer_max_shared(const void* kernel) {
+  static std::mutex mu;
+  static std::set<std::pair<int, const void*>> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> g(mu);
+  if (done.insert({dev, kernel}).second)
+    cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                         (int)cudaSharedmemCarveoutMaxShared);
 }
 
 int* device_status_word() {

@@ -69,9 +69,16 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 // Whether launches carry the PDL attribute (MINQ_PDL=0 disables it).
 bool pdl_enabled();
 
+// Every kernel of the library asks for the largest shared-memory carveout
+// (cached per device and kernel), so an SM never has to drain to change its
+// L1/shared split between two kernels of a stream: the next kernel's CTAs can
+// become resident beside the running ones (Programmatic Dependent Launch).
+void prefer_max_shared(const void* kernel);
+
 template <typename... KArgs, typename... Args>
 cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                      cudaStream_t s, Args&&... args) {
+  prefer_max_shared(reinterpret_cast<const void*>(kernel));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;

@@ -65,6 +65,49 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   return false;
 }
 
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// try_wait that may suspend the thread for up to `ns` nanoseconds (woken
+// early when the phase completes), so waiting warps do not take issue slots
+// from working ones.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s of wall time per wait
+
+// Time-bounded wait for the phase with the given parity: suspends between
+// polls, gives up after kWaitLimitNs (status word set, returns false).
+__device__ __forceinline__ bool mbar_wait_timed(uint64_t* bar, uint32_t parity, int* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      if (status) atomicOr(status, kDeviceTimeout);
+      return false;
+    }
+  }
+}
+
+// Named barrier over the first `threads` threads of the CTA (barrier 1;
+// barrier 0 is __syncthreads).
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // 1-D bulk copy global -> this CTA's shared memory; `bytes` % 16 == 0 and
 // both addresses 16-byte aligned. Completion is reported to `bar`.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,

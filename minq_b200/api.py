@@ -15,6 +15,7 @@ only: the kernels never see torch types).
 from __future__ import annotations
 
 import ctypes as C
+import sys
 from typing import Callable, Iterable
 
 import numpy as np
@@ -251,7 +252,7 @@ class Model:
 
     def __del__(self):
         h = getattr(self, "_h", None)
-        if h:
+        if h and not sys.is_finalizing():  # at interpreter exit the process frees it
             lib().minq_model_free(h)
             self._h = None
 
@@ -315,7 +316,7 @@ class KVCache:
 
     def __del__(self):
         h = getattr(self, "_h", None)
-        if h:
+        if h and not sys.is_finalizing():
             lib().minq_cache_free(h)
             self._h = None
 

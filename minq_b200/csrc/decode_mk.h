@@ -1,0 +1,76 @@
+// Decode megakernel (decode_mk.cu): launch parameters and host helpers.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/minq_cuda.h"
+
+namespace minq {
+
+// Plan of one projection phase, the same for every layer.
+struct MkMat {
+  int rows;     // output rows (gate/up row pairs for the dual phase)
+  int cols;
+  int nr;       // rows per pass, first tensor-map box
+  int nr_b;     // second box (passes of nr - 1 rows)
+  int nchunks;  // 32-block column chunks per row
+  int up_off;   // dual: offset of the up rows' box in a ring slot
+};
+
+// Per-layer vectors (device array).
+struct MkLayerPtrs {
+  const float* attn_norm;
+  const float* ffn_norm;
+  const float* bias_qkv;  // may be null
+  const float* q_norm;    // may be null
+  const float* k_norm;    // may be null
+};
+
+struct MkParams {
+  const CUtensorMap* maps;     // [n_layers][qkv, o, gate, up, down][box nr, box nr-1]
+  const MkLayerPtrs* layers;   // [n_layers]
+  int n_layers;
+  MkMat qkv, o, gu, down;
+  int H, I, nh, nkv, hd, G, qd, kvd, nsplit, vocab;
+  float eps, scale;
+  const float* embed;          // [vocab][H] f32
+  const float* lm_head;        // tied: == embed
+  const float* final_norm;
+  const float* rope_cos;       // [max_seq][hd/2]
+  const float* rope_sin;
+  float* kc;                   // [n_layers][nkv][max_seq][hd]
+  float* vc;
+  size_t cache_layer_stride;   // nkv * max_seq * hd
+  int max_seq;
+  float* x;                    // residual stream [H]
+  float* qkv_out;              // [qd + 2 kvd]
+  float* att;                  // [qd]
+  float* h;                    // [I]
+  float* logits;               // [vocab]
+  float* part;                 // [nkv * nsplit][G][hd + 2]
+  int* head_ctr;               // [nkv]
+  unsigned long long* argmax_part;  // [grid]
+  uint32_t* d_tok;             // in: this token; out: its argmax
+  int* d_pos;                  // in: history length; out: + 1
+  unsigned long long* bar_ctr;   // monotonic grid-barrier counter
+  unsigned long long* bar_base;  // counter value at the start of the next launch
+  int* status;                 // device status word (bounded-wait timeouts)
+  int* abort_flag;             // set when any CTA gives up; every CTA stops
+  int want_logits;
+  int S;                       // ring slots
+  int scratch_bytes;           // x / attention scratch in shared memory
+};
+
+MkMat mk_plan_mat(int dtype, bool dual, uint64_t rows, uint64_t cols, int grid);
+minq_status mk_encode_pair(const void* w, uint64_t rows, uint64_t cols, int dtype,
+                           const MkMat& m, CUtensorMap* out2);
+size_t mk_scratch_bytes(int H, int I, int qd, int G, int hd);
+int mk_ring_slots(size_t scratch_bytes);
+size_t mk_smem_bytes(size_t scratch_bytes, int S);
+minq_status launch_decode_mk(const MkParams& p, int dtype, int grid, size_t smem,
+                             cudaStream_t s);
+
+}  // namespace minq

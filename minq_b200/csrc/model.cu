@@ -29,6 +29,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "decode_mk.h"
 #include "kernels.h"
 #include "minq_format.h"
 
@@ -94,6 +95,20 @@ struct minq_model {
   uint32_t* d_tok = nullptr;     // the step's input token and, after it, its argmax
   uint32_t* d_tokens = nullptr;  // staged prompt
   size_t d_tokens_cap = 0;
+  // decode megakernel (decode_mk.cu): set up at finish when the model fits it
+  struct {
+    bool ok = false;
+    int dtype = 0, grid = 0, S = 0, scratch = 0, nsplit = 0;
+    size_t smem = 0;
+    minq::MkMat qkv{}, o{}, gu{}, down{};
+    CUtensorMap* maps = nullptr;  // device [n_layers][10]
+    minq::MkLayerPtrs* layers = nullptr;
+    float* part = nullptr;
+    int* head_ctr = nullptr;
+    unsigned long long* argmax_part = nullptr;
+    unsigned long long* bar = nullptr;  // [0] counter, [1] base
+    int* abort_flag = nullptr;
+  } mk;
 };
 
 struct minq_cache {
@@ -225,6 +240,74 @@ const CUtensorMap* map_of(const DevLinear& l) { return l.tm_ok ? &l.tm : nullptr
 }  // namespace
 
 // assemble (model.rs:522-574) on device tensors.
+// Decide whether the batch-1 decode step runs as the megakernel and set it up
+// (tensor maps for its tile plans, per-layer pointers, barrier state).
+minq_status setup_megakernel(minq_model* m) {
+  const char* env = std::getenv("MINQ_MEGAKERNEL");
+  if (env && env[0] == '0') return MINQ_OK;
+  const minq_config& c = m->cfg;
+  const uint64_t H = c.hidden_size, I = c.intermediate_size, hd = c.head_dim;
+  const uint64_t nh = c.n_heads, nkv = c.n_kv_heads, qd = nh * hd, kvd = nkv * hd;
+  if (c.n_layers == 0 || nkv == 0 || nh % nkv != 0) return MINQ_OK;
+  const uint64_t G = nh / nkv;
+  if ((hd != 64 && hd != 128) || G > 8) return MINQ_OK;
+  if (H % 128 || I % 128 || qd % 128) return MINQ_OK;
+  if (m->lm_head.tag != MINQ_F32 || m->lm_head.cols != H) return MINQ_OK;
+  const int dt = m->layers[0].o.tag;
+  if (dt != MINQ_Q8_0 && dt != MINQ_Q4_0) return MINQ_OK;
+  auto ok_lin = [&](const DevLinear& l) {
+    return l.tag == dt && (uintptr_t)l.ptr % 16 == 0;
+  };
+  for (const DevLayer& L : m->layers)
+    if (!ok_lin(L.qkv) || !ok_lin(L.o) || !ok_lin(L.gate) || !ok_lin(L.up) || !ok_lin(L.down))
+      return MINQ_OK;
+  const int grid = sm_count();
+  auto& k = m->mk;
+  k.dtype = dt;
+  k.grid = grid;
+  k.qkv = mk_plan_mat(dt, false, qd + 2 * kvd, H, grid);
+  k.o = mk_plan_mat(dt, false, H, qd, grid);
+  k.gu = mk_plan_mat(dt, true, I, H, grid);
+  k.down = mk_plan_mat(dt, false, H, I, grid);
+  k.scratch = (int)mk_scratch_bytes((int)H, (int)I, (int)qd, (int)G, (int)hd);
+  k.S = mk_ring_slots(k.scratch);
+  if (k.S < 4) return MINQ_OK;
+  k.smem = mk_smem_bytes(k.scratch, k.S);
+  k.nsplit = std::max(1, grid / (int)nkv);
+  const size_t nl = c.n_layers;
+  std::vector<CUtensorMap> maps(nl * 10);
+  std::vector<MkLayerPtrs> lps(nl);
+  for (size_t li = 0; li < nl; ++li) {
+    const DevLayer& L = m->layers[li];
+    CUtensorMap* mp = maps.data() + li * 10;
+    MINQ_TRY(mk_encode_pair(L.qkv.ptr, qd + 2 * kvd, H, dt, k.qkv, mp + 0));
+    MINQ_TRY(mk_encode_pair(L.o.ptr, H, qd, dt, k.o, mp + 2));
+    MINQ_TRY(mk_encode_pair(L.gate.ptr, I, H, dt, k.gu, mp + 4));
+    MINQ_TRY(mk_encode_pair(L.up.ptr, I, H, dt, k.gu, mp + 6));
+    MINQ_TRY(mk_encode_pair(L.down.ptr, H, I, dt, k.down, mp + 8));
+    lps[li] = MkLayerPtrs{L.attn_norm, L.ffn_norm, L.bias_qkv, L.q_norm, L.k_norm};
+  }
+  void* p;
+  MINQ_TRY(dmalloc(m, &p, maps.size() * sizeof(CUtensorMap)));
+  k.maps = static_cast<CUtensorMap*>(p);
+  MINQ_CUDA_TRY(cudaMemcpy(p, maps.data(), maps.size() * sizeof(CUtensorMap),
+                           cudaMemcpyHostToDevice));
+  MINQ_TRY(dmalloc(m, &p, lps.size() * sizeof(MkLayerPtrs)));
+  k.layers = static_cast<MkLayerPtrs*>(p);
+  MINQ_CUDA_TRY(cudaMemcpy(p, lps.data(), lps.size() * sizeof(MkLayerPtrs),
+                           cudaMemcpyHostToDevice));
+  MINQ_TRY(dmalloc(m, &p, nkv * k.nsplit * G * (hd + 2) * 4));
+  k.part = static_cast<float*>(p);
+  MINQ_TRY(dmalloc(m, &p, nkv * 4 + 4 + 2 * 8 + (size_t)grid * 8 + 64));
+  k.bar = static_cast<unsigned long long*>(p);                         // 2 u64
+  k.argmax_part = k.bar + 2;                                           // grid u64
+  k.head_ctr = reinterpret_cast<int*>(k.argmax_part + grid);           // nkv
+  k.abort_flag = k.head_ctr + nkv;                                     // 1
+  MINQ_CUDA_TRY(cudaMemset(p, 0, nkv * 4 + 4 + 2 * 8 + (size_t)grid * 8 + 64));
+  k.ok = true;
+  return MINQ_OK;
+}
+
 minq_status model_finish(minq_model* m) {
   const minq_config& c = m->cfg;
   if (c.head_dim % 2 != 0) return fail(MINQ_ERR_MODEL, "head_dim must be even (RoPE)");
@@ -387,6 +470,7 @@ minq_status model_finish(minq_model* m) {
   MINQ_TRY(dmalloc(m, &p, m->d_tokens_cap * 4));
   m->d_tokens = static_cast<uint32_t*>(p);
   if (!device_status_word()) return fail(MINQ_ERR_CUDA, "cannot allocate the device status word");
+  if (m->shape_error.empty()) MINQ_TRY(setup_megakernel(m));
   MINQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
   m->finished = true;
   return MINQ_OK;
@@ -509,8 +593,78 @@ static minq_status sync_dpos(minq_cache* c) {
   return MINQ_OK;
 }
 
-// Run one step for the token already in m->d_tok (graph replay or eager).
+// One decode step of a batch-1 cache as the megakernel.
+static minq_status run_megakernel(minq_model* m, minq_cache* c, bool logits) {
+  const minq_config& cfg = m->cfg;
+  auto& k = m->mk;
+  MkParams p{};
+  p.maps = k.maps;
+  p.layers = k.layers;
+  p.n_layers = (int)cfg.n_layers;
+  p.qkv = k.qkv;
+  p.o = k.o;
+  p.gu = k.gu;
+  p.down = k.down;
+  p.H = (int)cfg.hidden_size;
+  p.I = (int)cfg.intermediate_size;
+  p.nh = (int)cfg.n_heads;
+  p.nkv = (int)cfg.n_kv_heads;
+  p.hd = (int)cfg.head_dim;
+  p.G = p.nh / p.nkv;
+  p.qd = p.nh * p.hd;
+  p.kvd = p.nkv * p.hd;
+  p.nsplit = k.nsplit;
+  p.vocab = (int)cfg.vocab_size;
+  p.eps = cfg.rms_norm_eps;
+  p.scale = 1.0f / sqrtf((float)cfg.head_dim);
+  p.embed = m->embed;
+  p.lm_head = static_cast<const float*>(m->lm_head.ptr);
+  p.final_norm = m->final_norm;
+  p.rope_cos = m->rope_cos;
+  p.rope_sin = m->rope_sin;
+  p.kc = c->k;
+  p.vc = c->v;
+  p.cache_layer_stride = (size_t)p.nkv * c->max_seq * p.hd;
+  p.max_seq = (int)c->max_seq;
+  p.x = m->x;
+  p.qkv_out = m->qkv;
+  p.att = m->att;
+  p.h = m->hbuf;
+  p.logits = m->logits;
+  p.part = k.part;
+  p.head_ctr = k.head_ctr;
+  p.argmax_part = k.argmax_part;
+  p.d_tok = m->d_tok;
+  p.d_pos = c->d_pos;
+  p.bar_ctr = k.bar;
+  p.bar_base = k.bar + 1;
+  p.status = device_status_word();
+  p.abort_flag = k.abort_flag;
+  p.want_logits = logits ? 1 : 0;
+  p.S = k.S;
+  p.scratch_bytes = k.scratch;
+  return launch_decode_mk(p, k.dtype, k.grid, k.smem, m->stream);
+}
+
+// Clear the megakernel's barrier / merge state after a device-side timeout.
+static minq_status reset_megakernel(minq_model* m) {
+  auto& k = m->mk;
+  if (!k.ok) return MINQ_OK;
+  const size_t nkv = m->cfg.n_kv_heads;
+  MINQ_CUDA_TRY(cudaMemsetAsync(k.bar, 0, nkv * 4 + 4 + 2 * 8 + (size_t)k.grid * 8 + 64,
+                                m->stream));
+  return MINQ_OK;
+}
+
+// Run one step for the token already in m->d_tok (megakernel, graph replay or
+// eager).
 static minq_status run_step(minq_model* m, minq_cache* c, bool logits) {
+  if (m->mk.ok && c->batch == 1) {
+    MINQ_TRY(sync_dpos(c));
+    MINQ_TRY(run_megakernel(m, c, logits));
+    c->len += 1;
+    return MINQ_OK;
+  }
   if (m->use_graphs) {
     MINQ_TRY(sync_dpos(c));
     cudaGraphExec_t& g = c->step[logits ? 1 : 0];
@@ -858,7 +1012,9 @@ minq_status minq_forward(minq_model* m, minq_cache* c, const uint32_t* tokens, s
   if (argmax_out)
     MINQ_CUDA_TRY(cudaMemcpyAsync(argmax_out, m->d_tok, 4, cudaMemcpyDeviceToHost, m->stream));
   MINQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
-  return take_device_status();
+  const minq_status ds = take_device_status();
+  if (ds != MINQ_OK) reset_megakernel(m);
+  return ds;
 }
 
 minq_status minq_generate(minq_model* m, const uint32_t* prompt, size_t n_prompt,

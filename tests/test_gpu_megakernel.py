@@ -1,0 +1,125 @@
+"""The batch-1 decode megakernel (one cooperative launch per token) against the
+CPU oracle and against the kernel-per-op path of the same library, on models
+small enough to run the oracle fast but shaped like the benchmark models
+(all projections Q8_0 or Q4_0, cols % 128 == 0, head_dim 64/128, GQA 1..8).
+
+Tolerances as in test_gpu_model.py: logits max-abs < 1e-3 (model.rs:932-940),
+K/V cache within 1e-4, greedy tokens identical."""
+import os
+
+import numpy as np
+import pytest
+
+from minq_b200 import synth
+from minq_b200.minq_format import ModelConfig
+
+pytestmark = pytest.mark.gpu
+
+
+def _cfg_dict(c):
+    return {k: getattr(c, k) for k in c.__dataclass_fields__}
+
+
+def _records(cfg, dtype, orc, seed, qk_norm, bias):
+    from minq_b200.minq_format import quantize_tensor_rule
+    dt = 1 if dtype == "q8_0" else 2
+    out = []
+    for n, t, s, d in synth.random_model_records(cfg, seed, qk_norm=qk_norm, with_bias=bias):
+        if n == "lm_head.weight":
+            continue  # tied embeddings: the f32 lm_head of the Qwen configurations
+        if quantize_tensor_rule(n, s):
+            out.append((n, dt, s, orc.quantize(dt, d)))
+        else:
+            out.append((n, t, s, d))
+    return out
+
+
+def _models(mq, orc, cfg, recs):
+    mk = mq.Model.from_tensors(cfg, recs)
+    os.environ["MINQ_MEGAKERNEL"] = "0"
+    try:
+        ops = mq.Model.from_tensors(cfg, recs)
+    finally:
+        del os.environ["MINQ_MEGAKERNEL"]
+    om = orc.Model.from_tensors(_cfg_dict(cfg), {n: (t, s, d) for n, t, s, d in recs})
+    return mk, ops, om
+
+
+def _launches_per_step(mq, model, cache):
+    from minq_b200 import _lib
+    import torch
+    lib = _lib.lib()
+    n0 = lib.minq_kernel_launches()
+    model.decode_steps(cache, 1)
+    torch.cuda.synchronize()
+    return lib.minq_kernel_launches() - n0
+
+
+CASES = [
+    # name, dtype, hidden, inter, heads, kv heads, head_dim, vocab, qk_norm, bias, prompt
+    ("q8_gqa7_hd64_bias", "q8_0", 896, 512, 14, 2, 64, 300, False, True, 12),
+    ("q4_gqa4_hd128_qknorm", "q4_0", 512, 768, 8, 2, 128, 257, True, False, 12),
+    ("q4_mha_hd64", "q4_0", 128, 256, 2, 2, 64, 129, False, False, 7),
+    ("q8_gqa8_hd128", "q8_0", 256, 384, 8, 1, 128, 200, True, True, 9),
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
+def test_megakernel_matches_oracle_and_per_op_path(mq, orc, case):
+    import torch
+    name, dtype, H, I, nh, nkv, hd, V, qkn, bias, plen = case
+    cfg = ModelConfig(H, I, 2, nh, nkv, hd, V, 64, 1e6, 1e-6, bias, dtype)
+    recs = _records(cfg, dtype, orc, 11, qkn, bias)
+    mk, ops, om = _models(mq, orc, cfg, recs)
+    prompt = list(np.random.default_rng(3).integers(0, V, plen))
+    # prefill: every prompt token through the megakernel, logits of the last
+    c_mk, c_ops, oc = mk.new_cache(), ops.new_cache(), om.new_cache()
+    l_mk = mk.forward(prompt, c_mk)
+    l_ops = ops.forward(prompt, c_ops)
+    l_ref = om.forward(prompt, oc)
+    assert np.abs(l_mk - l_ref).max() < 1e-3
+    assert np.abs(l_mk - l_ops).max() < 1e-3
+    for layer in range(cfg.n_layers):
+        gk, gv = c_mk.read(layer)
+        rk, rv = oc.read(layer)
+        assert np.abs(gk - rk).max() < 1e-4 and np.abs(gv - rv).max() < 1e-4
+    # one launch per decode token on the megakernel path, many on the other
+    assert _launches_per_step(mq, mk, c_mk) == 1
+    ops.set_graphs(False)  # graph replays launch nothing the counter sees
+    assert _launches_per_step(mq, ops, c_ops) > 1
+    # greedy continuation on the device
+    c = mk.new_cache()
+    first = mk.forward_argmax(prompt, c)
+    out = torch.zeros(10, dtype=torch.int32, device="cuda")
+    mk.decode_steps(c, 10, out.data_ptr())
+    torch.cuda.synchronize()
+    got = [first] + [int(v) for v in out.cpu().numpy()]
+    ref, _ = orc.greedy_generate(om, prompt, 11)
+    assert got == ref
+
+
+def test_megakernel_long_history_splits(mq, orc):
+    """8 KV heads -> 18 history splits per head on 148 SMs; 400 positions of
+    hd 128 (16-position tiles) give every split several K/V tiles."""
+    cfg = ModelConfig(512, 512, 2, 16, 8, 128, 160, 512, 1e6, 1e-6, False, "q4_0")
+    recs = _records(cfg, "q4_0", orc, 5, True, False)
+    mk, _ops, om = _models(mq, orc, cfg, recs)
+    prompt = list(np.random.default_rng(9).integers(0, cfg.vocab_size, 400))
+    c = mk.new_cache()
+    got = mk.forward(prompt, c)
+    ref = om.forward(prompt, om.new_cache())
+    assert np.abs(got - ref).max() < 1e-3
+    assert _launches_per_step(mq, mk, c) == 1
+
+
+def test_megakernel_steps_are_repeatable(mq, orc):
+    """Two caches fed the same tokens give bit-identical logits: the grid
+    barrier counter and the split-merge counters carry over correctly from
+    one launch to the next."""
+    cfg = ModelConfig(256, 512, 2, 4, 2, 64, 300, 64, 1e6, 1e-6, False, "q4_0")
+    recs = _records(cfg, "q4_0", orc, 2, False, False)
+    mk = mq.Model.from_tensors(cfg, recs)
+    toks = [1, 5, 9, 200, 17, 33]
+    a = mk.forward(toks, mk.new_cache())
+    b = mk.forward(toks, mk.new_cache())
+    assert np.array_equal(a, b)

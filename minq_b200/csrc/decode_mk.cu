@@ -73,8 +73,8 @@ __host__ __device__ constexpr int mk_acc(int dt, bool dual) {
   return dual ? (dt == MINQ_Q4_0 ? 3 : 2) : (dt == MINQ_Q4_0 ? 7 : 4);
 }
 constexpr int kMkMiscOff = 256;                // after the full/empty barriers
-constexpr int kMkRedOff = 1024;                // projection pass reduction [8][32][2]
-constexpr int kMkScrOff = 3072;                // x / attention scratch, then the ring
+constexpr int kMkRedOff = 1024;                // projection pass reduction 2 x [8][32][2]
+constexpr int kMkScrOff = 5120;                // x / attention scratch, then the ring
 
 __device__ __forceinline__ float ldcg(const float* p) { return __ldcg(p); }
 __device__ __forceinline__ float4 ldcg4(const float* p) {
@@ -130,19 +130,28 @@ __device__ __forceinline__ void mk_share(int units, int* begin, int* cnt) {
   *cnt = q + (b < rem ? 1 : 0);
 }
 
+// Splits of each kv head's history for a history of L positions: about two
+// K/V tiles per split at least, at most p.nsplit (CTAs / kv heads).
+__device__ __forceinline__ int mk_nsplit(const MkParams& p, int L) {
+  const int tp = 2048 / p.hd;
+  const int ntiles = (L + tp - 1) / tp;
+  return max(1, min(p.nsplit, (ntiles + 1) / 2));
+}
+
 // Attention work item of this CTA: kv head, history tiles [t0, t1), whether
 // it also takes the new position. Returns false when the CTA has none.
 __device__ __forceinline__ bool mk_attn_item(const MkParams& p, int L, int* kh, int* t0, int* t1,
                                              bool* last) {
+  const int ns = mk_nsplit(p, L);
   const int item = blockIdx.x;
-  if (item >= p.nkv * p.nsplit) return false;
-  *kh = item / p.nsplit;
-  const int sp = item % p.nsplit;
+  if (item >= p.nkv * ns) return false;
+  *kh = item / ns;
+  const int sp = item % ns;
   const int tp = 2048 / p.hd;
   const int ntiles = (L + tp - 1) / tp;
-  *t0 = (int)(((long long)ntiles * sp) / p.nsplit);
-  *t1 = (int)(((long long)ntiles * (sp + 1)) / p.nsplit);
-  *last = sp == p.nsplit - 1;
+  *t0 = (int)(((long long)ntiles * sp) / ns);
+  *t1 = (int)(((long long)ntiles * (sp + 1)) / ns);
+  *last = sp == ns - 1;
   return true;
 }
 
@@ -291,7 +300,6 @@ __device__ bool mk_grid_sync(const MkParams& p, unsigned long long target, int* 
         ok = 0;
         break;
       }
-      __nanosleep(64);
     }
     __threadfence();
     *reinterpret_cast<volatile int*>(flag) = ok;
@@ -301,35 +309,40 @@ __device__ bool mk_grid_sync(const MkParams& p, unsigned long long target, int* 
 }
 
 // Stage the phase input in shared memory: xs = src (n floats, n % 8 == 0),
-// times rmsnorm(src) * gain when gain is set (tensor.rs:219-227), then in the
-// Q4_0 pair layout when q4.
+// times rmsnorm(src) * gain when gain is set (tensor.rs:219-227), in the
+// Q4_0 pair layout when q4. Each thread transforms the groups of 8 it loaded
+// itself, so only the sum of squares needs a block-wide step.
 __device__ void mk_stage_x(const MkParams& p, float* xs, const float* src, int n,
                            const float* gain, bool q4, float* misc) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ng = n >> 3;
   float4* xs4 = reinterpret_cast<float4*>(xs);
+  float inv = 1.0f;
   if (gain) {
     float ss = 0.0f;
-    for (int i = tid; i < (n >> 2); i += kMkConsumers) {
-      const float4 v = ldcg4(src + 4 * i);
-      xs4[i] = v;
-      ss = fmaf(v.x, v.x, ss);
-      ss = fmaf(v.y, v.y, ss);
-      ss = fmaf(v.z, v.z, ss);
-      ss = fmaf(v.w, v.w, ss);
+    for (int gi = tid; gi < ng; gi += kMkConsumers) {
+      const float4 a = ldcg4(src + 8 * gi), b = ldcg4(src + 8 * gi + 4);
+      xs4[2 * gi] = a;
+      xs4[2 * gi + 1] = b;
+      ss = fmaf(a.x, a.x, ss);
+      ss = fmaf(a.y, a.y, ss);
+      ss = fmaf(a.z, a.z, ss);
+      ss = fmaf(a.w, a.w, ss);
+      ss = fmaf(b.x, b.x, ss);
+      ss = fmaf(b.y, b.y, ss);
+      ss = fmaf(b.z, b.z, ss);
+      ss = fmaf(b.w, b.w, ss);
     }
     ss = warp_sum(ss);
     if (lane == 0) misc[warp] = ss;
     mk_sync();
-    if (warp == 0) {
-      float v = lane < kMkCW ? misc[lane] : 0.0f;
-      v = warp_sum(v);
-      if (lane == 0) misc[32] = 1.0f / sqrtf(v / (float)n + p.eps);
-    }
-    mk_sync();
+    float v = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kMkCW; ++w) v += misc[w];
+    inv = 1.0f / sqrtf(v / (float)n + p.eps);
   }
-  const float inv = gain ? misc[32] : 1.0f;
   const float4* g4 = reinterpret_cast<const float4*>(gain);
-  for (int gi = tid; gi < (n >> 3); gi += kMkConsumers) {
+  for (int gi = tid; gi < ng; gi += kMkConsumers) {
     float4 a, b;
     if (gain) {
       a = xs4[2 * gi];
@@ -412,7 +425,9 @@ __device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const float* x
       if (lane == 0) mbar_arrive(&r.empty[s]);
     }
     // sum over the 16 lanes of each half (4 blocks x 4 column slices), then
-    // over the 8 groups in a fixed order
+    // over the 8 groups in a fixed order; passes alternate between two
+    // buffers so one barrier per pass suffices
+    float* rb_ = red + (j & 1) * 512;
 #pragma unroll
     for (int k = 0; k < kMkAcc; ++k) {
       float v = acc[k], v1 = DUAL ? acc1[k] : 0.0f;
@@ -423,8 +438,8 @@ __device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const float* x
       }
       const int row = 4 * k + 2 * rs + h;
       if ((lane & 15) == 0) {
-        red[(grp * 32 + row) * 2] = v;
-        if (DUAL) red[(grp * 32 + row) * 2 + 1] = v1;
+        rb_[(grp * 32 + row) * 2] = v;
+        if (DUAL) rb_[(grp * 32 + row) * 2 + 1] = v1;
       }
     }
     mk_sync();
@@ -432,12 +447,11 @@ __device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const float* x
       float v0 = 0.0f, v1 = 0.0f;
 #pragma unroll
       for (int g = 0; g < 8; ++g) {
-        v0 += red[(g * 32 + tid) * 2];
-        if (DUAL) v1 += red[(g * 32 + tid) * 2 + 1];
+        v0 += rb_[(g * 32 + tid) * 2];
+        if (DUAL) v1 += rb_[(g * 32 + tid) * 2 + 1];
       }
       epi(rb + pr0 + tid, v0, v1);
     }
-    mk_sync();
   }
 }
 
@@ -611,31 +625,53 @@ __device__ void mk_consume_attn(const MkParams& p, int li, int L, float* scr, co
     }
   }
   // the last split of this kv head to finish merges all of them
+  const int ns = mk_nsplit(p, L);
   __threadfence();
   mk_sync();
   if (tid == 0) {
     const int old = atomicAdd(p.head_ctr + kh, 1);
-    misc_i[0] = old == p.nsplit - 1;
+    misc_i[0] = old == ns - 1;
   }
   mk_sync();
   if (misc_i[0]) {
     __threadfence();
-    const float* hp = p.part + (size_t)kh * p.nsplit * G * (hd + 2);
+    const float* hp = p.part + (size_t)kh * ns * G * (hd + 2);  // items of head kh
+    float* mm = scr;             // [ns][G] split maxima, then weights
+    float* ll = mm + ns * G;     // [ns][G]
+    for (int i = tid; i < ns * G; i += kMkConsumers) {
+      const float* e = hp + (size_t)i * (hd + 2);  // i = sp * G + g
+      mm[i] = ldcg(e + hd);
+      ll[i] = ldcg(e + hd + 1);
+    }
+    mk_sync();
+    if (tid < G) {
+      float M = -INFINITY;
+      for (int sp = 0; sp < ns; ++sp) M = fmaxf(M, mm[sp * G + tid]);
+      float Ls = 0.0f;
+      for (int sp = 0; sp < ns; ++sp) {
+        const float ms = mm[sp * G + tid];
+        const float f = ms == -INFINITY ? 0.0f : expf(ms - M);
+        Ls = fmaf(ll[sp * G + tid], f, Ls);
+        mm[sp * G + tid] = f;  // weight of the split before the division
+      }
+      ll[tid] = 1.0f / Ls;    // ll[0..G) reused: 1 / sum (ll no longer read)
+    }
+    mk_sync();
     for (int idx = tid; idx < G * hd; idx += kMkConsumers) {
       const int g = idx / hd, d = idx % hd;
-      float M = -INFINITY;
-      for (int sp = 0; sp < p.nsplit; ++sp)
-        M = fmaxf(M, ldcg(hp + ((size_t)sp * G + g) * (hd + 2) + hd));
-      float Ls = 0.0f, O = 0.0f;
-      for (int sp = 0; sp < p.nsplit; ++sp) {
-        const float* e = hp + ((size_t)sp * G + g) * (hd + 2);
-        const float ms = ldcg(e + hd);
-        if (ms == -INFINITY) continue;
-        const float f = expf(ms - M);
-        Ls = fmaf(ldcg(e + hd + 1), f, Ls);
-        O = fmaf(ldcg(e + d), f, O);
+      float O = 0.0f;
+      for (int sp0 = 0; sp0 < ns; sp0 += 8) {  // 8 independent loads in flight
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int sp = sp0 + u;
+          v[u] = sp < ns ? ldcg(hp + ((size_t)sp * G + g) * (hd + 2) + d) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (sp0 + u < ns) O = fmaf(v[u], mm[(sp0 + u) * G + g], O);
       }
-      p.att[(size_t)(kh * G + g) * hd + d] = O / Ls;
+      p.att[(size_t)(kh * G + g) * hd + d] = O * ll[g];
     }
     if (tid == 0) p.head_ctr[kh] = 0;
   }

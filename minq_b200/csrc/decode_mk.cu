@@ -8,19 +8,24 @@
 // kernel per step spends most of its time launching, ramping up and draining.
 // Here every CTA (one per SM) runs the whole token:
 //
-//   * a producer warp streams this CTA's share of every layer's weights and of
-//     every layer's K/V history into a ring of 16 KB shared-memory slots, in
-//     the order the consumers use them, without ever waiting on other CTAs:
-//     TMA tensor boxes (rows x 32 blocks) for the projections, 1-D bulk copies
-//     of TP positions of K and V for attention. It runs ahead across phase and
-//     layer boundaries, so HBM keeps streaming while the consumers wait at a
-//     grid barrier;
+//   * four producer warps stream this CTA's share of every layer's weights and
+//     of every layer's K/V history into an 8-slot ring of 16 KB shared-memory
+//     tiles with cp.async (16-byte pieces; the slot's full mbarrier tracks them
+//     through cp.async.mbarrier.arrive), in the order the consumers use them
+//     and without waiting on other CTAs: projection tiles are rows x 32 blocks
+//     of the reference's row-major blocks, attention tiles TP positions of K
+//     and V. Producer k owns the tiles k, k + 4, ... and so its own slots. The
+//     producers run ahead across phase and layer boundaries, so HBM keeps
+//     streaming while the consumers wait at a grid barrier. (One CTA per SM
+//     issuing TMA copies was measured at half of the HBM bandwidth; cp.async
+//     from several warps sustains it.)
 //   * 16 consumer warps execute the phases of each layer:
 //       P1 q|k|v = W_qkv rmsnorm(x) + bias                 (rows split over CTAs)
 //       P2 attention: CTA = (kv head, split of the history); q/k RMSNorm +
 //          RoPE for the new position, the split's online softmax, the new
-//          position's k/v appended to the cache by the last split; the last
-//          CTA of a kv head to finish merges the splits
+//          position's k/v appended to the cache by the last split; the
+//          splits of a head then meet at a per-head counter and each merges
+//          a slice of the head's outputs
 //       P3 x = x + W_o att                                  (rows split)
 //       P4 h = silu(W_gate rmsnorm(x)) * (W_up rmsnorm(x))  (row pairs split)
 //       P5 x = x + W_down h                                 (rows split)
@@ -33,14 +38,9 @@
 // Every consumer warp waits for and releases every slot in order (a warp
 // that skipped slots could reach a slot two phases early, where a parity wait
 // cannot tell the phases apart): in projections each warp owns one 4-block
-// group of every chunk and a quarter of the rows; in attention each warp owns
-// one position of every K/V tile.
+// group of every chunk and a quarter of the rows; in attention the 16 warps
+// cooperate on each step of up to 32 positions (scores, softmax, p v).
 //
-// The quantized dot products are those of the streaming matvec: exact code ->
-// float conversion (byte permute into 2^23 + code), packed f32x2 FMAs, the
-// block scale applied once per block (quantize.rs:252-280). Cross-CTA data
-// (x, q|k|v, attention output, h, split partials) is read with ld.global.cg
-// so no stale L1 line is used after a barrier.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -56,11 +56,13 @@
 
 namespace minq {
 
-constexpr int kMkCW = 16;                      // consumer warps
-constexpr int kMkConsumers = 32 * kMkCW;       // consumer threads
-constexpr int kMkThreads = kMkConsumers + 32;  // + the producer warp
+constexpr int kMkCW = 16;                      // warps
+constexpr int kMkConsumers = 32 * kMkCW;       // threads (all of them load and compute)
+constexpr int kMkProducers = 4;                // copy warps; warp k issues tiles k, k + 4, ...
+constexpr int kMkThreads = kMkConsumers + 32 * kMkProducers;
 constexpr int kMkSlot = 16384;                 // bytes per ring slot
-constexpr int kMkMaxS = 12;                    // max ring slots
+constexpr int kMkS = 8;                        // ring slots (a multiple of kMkProducers)
+static_assert(kMkS % kMkProducers == 0, "each producer warp owns its own slots");
 constexpr int kMkCK = 32;                      // blocks per projection chunk (8 groups of 4)
 // Row slots per lane (rows 4k + 2*half + h of a pass): enough for the most
 // rows of each format whose box fits a 16 KB slot (Q4_0: 25 single / 12
@@ -72,9 +74,11 @@ struct MkAccN {
 __host__ __device__ constexpr int mk_acc(int dt, bool dual) {
   return dual ? (dt == MINQ_Q4_0 ? 3 : 2) : (dt == MINQ_Q4_0 ? 7 : 4);
 }
-constexpr int kMkMiscOff = 256;                // after the full/empty barriers
+constexpr int kMkMiscOff = 256;                // small reductions and flags
+constexpr int kMkCtaOff = 768;                 // the CTA's plan (MkCta)
 constexpr int kMkRedOff = 1024;                // projection pass reduction 2 x [8][32][2]
-constexpr int kMkScrOff = 5120;                // x / attention scratch, then the ring
+constexpr int kMkRopeOff = 5120;               // cos | sin of this position's RoPE row
+constexpr int kMkScrOff = 5632;                // x / attention scratch, then the ring
 
 __device__ __forceinline__ float ldcg(const float* p) { return __ldcg(p); }
 __device__ __forceinline__ float4 ldcg4(const float* p) {
@@ -115,13 +119,6 @@ __device__ __forceinline__ float2 mk_dot8(uint32_t c0, uint32_t c1, const float4
   return s;
 }
 
-struct MkRing {
-  uint64_t* full;
-  uint64_t* empty;
-  unsigned char* base;
-  int S;
-};
-
 // Balanced contiguous share [begin, begin + cnt) of `units` for this CTA.
 __device__ __forceinline__ void mk_share(int units, int* begin, int* cnt) {
   const int q = units / (int)gridDim.x, rem = units % (int)gridDim.x;
@@ -155,19 +152,94 @@ __device__ __forceinline__ bool mk_attn_item(const MkParams& p, int L, int* kh, 
   return true;
 }
 
-// ---------------------------------------------------------------- producer
+// ---------------------------------------------------------------- feed
+//
+// Every thread of the CTA copies its share of each tile with cp.async
+// (16-byte pieces, one commit group per tile), kMkS - 1 tiles ahead of the
+// tile being computed on, in the order the phases use them. The tile
+// sequence runs across phase and layer boundaries, so the next phase's
+// weights are already streaming while the CTA waits at a grid barrier.
+// (With one CTA per SM, copies issued by all 512 threads sustain the full
+// HBM bandwidth; a single TMA-issuing warp was measured at half of it.)
 
-// Wait until slot it % S may be refilled; false on abort or timeout. Lane 0
-// decides and the warp follows it, so the producer warp never diverges.
-__device__ bool mk_wait_empty(const MkParams& p, const MkRing& r, int it) {
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// Rows of this CTA in a projection and its passes of at most m.nr rows.
+struct MkShare {
+  int rb, cnt, passes;
+};
+__device__ __forceinline__ MkShare mk_mat_share(const MkMat& m) {
+  MkShare s;
+  mk_share(m.rows, &s.rb, &s.cnt);
+  s.passes = (s.cnt + m.nr - 1) / m.nr;
+  return s;
+}
+__device__ __forceinline__ int mk_pass_row(const MkShare& s, int j) {
+  return (int)(((long long)s.cnt * j) / s.passes);
+}
+
+// This CTA's plan for the launch (the same for every layer), computed once
+// into shared memory: row shares of the four projections and the attention
+// work item. Phases: 0 q|k|v, 1 attention, 2 o, 3 gate/up, 4 down.
+struct MkCta {
+  MkShare sh[5];   // projections (index 1 unused)
+  int tiles[5];    // tiles of each phase
+  int kh, t0, t1, last;
+};
+
+__device__ __forceinline__ const MkMat& mk_mat(const MkParams& p, int ph) {
+  return ph == 0 ? p.qkv : ph == 2 ? p.o : ph == 3 ? p.gu : p.down;
+}
+
+__device__ void mk_cta_plan(const MkParams& p, int L, MkCta* c) {
+  for (int ph = 0; ph < 5; ++ph) {
+    if (ph == 1) continue;
+    const MkMat& m = mk_mat(p, ph);
+    c->sh[ph] = mk_mat_share(m);
+    c->tiles[ph] = c->sh[ph].passes * m.nchunks;
+  }
+  int kh = 0, t0 = 0, t1 = 0;
+  bool last = false;
+  const bool has = mk_attn_item(p, L, &kh, &t0, &t1, &last);
+  c->kh = kh;
+  c->t0 = t0;
+  c->t1 = has ? t1 : t0;
+  c->last = has && last;
+  c->tiles[1] = c->t1 - c->t0;
+}
+
+struct MkFeed {
+  unsigned char* ring;
+  uint64_t* full;   // [kMkS]: the producer lanes' copies of the slot's tile landed
+  uint64_t* empty;  // [kMkS]: every consumer warp released the slot
+  int li, ph, idx;  // next tile to issue: layer, phase, index in the phase
+  int issued;       // tiles issued so far (slot = issued % kMkS)
+  int j, c;         // projection pass and chunk of the next tile
+  int pr0, n;       // rows of that pass
+};
+
+__device__ __forceinline__ void mk_feed_pass(MkFeed& f, const MkShare& sh) {
+  f.pr0 = mk_pass_row(sh, f.j);
+  f.n = mk_pass_row(sh, f.j + 1) - f.pr0;
+}
+
+// Producer wait until slot `it % kMkS` may be refilled; false on abort or
+// timeout. Lane 0 decides and the warp follows it.
+__device__ bool mk_wait_empty(const MkParams& p, const MkFeed& f, int it) {
   int ok = 1;
   if ((threadIdx.x & 31) == 0) {
-    const int s = it % r.S;
-    const uint32_t parity = ((uint32_t)(it / r.S) & 1u) ^ 1u;
-    if (!mbar_try_wait(&r.empty[s], parity)) {
+    const int s = it % kMkS;
+    const uint32_t parity = ((uint32_t)(it / kMkS) & 1u) ^ 1u;
+    if (!mbar_try_wait(&f.empty[s], parity)) {
       const uint64_t t0 = global_timer_ns();
       for (;;) {
-        if (mbar_try_wait_sleep(&r.empty[s], parity, 20000u)) break;
+        if (mbar_try_wait_sleep(&f.empty[s], parity, 2000u)) break;
         if (*reinterpret_cast<volatile int*>(p.abort_flag)) {
           ok = 0;
           break;
@@ -184,99 +256,135 @@ __device__ bool mk_wait_empty(const MkParams& p, const MkRing& r, int it) {
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-template <int DT, bool DUAL>
-__device__ bool mk_produce_mat(const MkParams& p, const MkMat& m, const CUtensorMap* g,
-                               const CUtensorMap* u, const MkRing& r, int& it) {
+// Producer: copy the next tile into its slot with the warp's 32 lanes, then
+// have the slot's full barrier track the copies (cp.async.mbarrier.arrive).
+// Projection tiles: lane l copies 16-byte pieces l, l + 32, ... of each row
+// chunk (40 pieces for Q4_0, 72 for Q8_0), the up rows of the gate/up phase
+// after the gate rows. Attention tiles: pieces l, l + 32, ... of K and of V.
+// Returns false when every tile is issued (or on abort).
+// Advance the iterator past phases without tiles; false past the last layer.
+__device__ __forceinline__ bool mk_feed_settle(const MkParams& p, MkFeed& f, const MkCta* cta) {
+  while (f.li < p.n_layers && f.idx >= cta->tiles[f.ph]) {
+    f.idx = 0;
+    if (++f.ph == 5) {
+      f.ph = 0;
+      ++f.li;
+    }
+    f.j = 0;
+    f.c = 0;
+    if (f.ph != 1) mk_feed_pass(f, cta->sh[f.ph]);
+  }
+  return f.li < p.n_layers;
+}
+
+// Step the iterator over one tile without copying it.
+__device__ __forceinline__ void mk_feed_skip(const MkParams& p, MkFeed& f, const MkCta* cta) {
+  if (f.ph != 1 && ++f.c == mk_mat(p, f.ph).nchunks) {
+    f.c = 0;
+    if (++f.j < cta->sh[f.ph].passes) mk_feed_pass(f, cta->sh[f.ph]);
+  }
+  ++f.idx;
+  ++f.issued;
+}
+
+// Producer warp: copy the current tile into its slot with the warp's 32
+// lanes, then have the slot's full barrier track the copies
+// (cp.async.mbarrier.arrive). Projection tiles: the rows x 16-byte pieces of
+// the row chunk (40 pieces for Q4_0, 72 for Q8_0) flattened over the lanes,
+// the up rows of the gate/up phase after the gate rows. Attention tiles: the
+// pieces of K and of V. False on abort.
+template <int DT>
+__device__ bool mk_issue(const MkParams& p, MkFeed& f, const MkCta* cta, int L) {
   constexpr int BB = DT == MINQ_Q8_0 ? kQ8Bytes : kQ4Bytes;
   constexpr int PITCH = kMkCK * BB;
+  constexpr int PPR = PITCH / 16;  // pieces of a full row chunk
   const int lane = threadIdx.x & 31;
-  int rb, cnt;
-  mk_share(m.rows, &rb, &cnt);
-  const int passes = (cnt + m.nr - 1) / m.nr;
-  for (int j = 0; j < passes; ++j) {
-    const int pr0 = (int)(((long long)cnt * j) / passes);
-    const int n = (int)(((long long)cnt * (j + 1)) / passes) - pr0;
-    const bool big = n == m.nr;
-    const uint32_t box = (uint32_t)((big ? m.nr : m.nr_b) * PITCH);
-    for (int c = 0; c < m.nchunks; ++c, ++it) {
-      if (!mk_wait_empty(p, r, it)) return false;
-      if (lane == 0) {
-        const int s = it % r.S;
-        unsigned char* dst = r.base + (size_t)s * kMkSlot;
-        mbar_arrive_expect_tx(&r.full[s], (DUAL ? 2u : 1u) * box);
-        const int x = c * (PITCH / 8), y = rb + pr0;  // 8-byte elements
-        tma_load_2d_nohint(dst, big ? g : g + 1, x, y, &r.full[s]);
-        if (DUAL) tma_load_2d_nohint(dst + m.up_off, big ? u : u + 1, x, y, &r.full[s]);
-      }
-      __syncwarp();
+  if (!mk_wait_empty(p, f, f.issued)) return false;
+  const int slot = f.issued % kMkS;
+  unsigned char* dst = f.ring + (size_t)slot * kMkSlot;
+  const MkLayerPtrs& lp = p.layers[f.li];
+  if (f.ph == 1) {
+    const int hd = p.hd, tp = 2048 / hd;
+    const int p0 = (cta->t0 + f.idx) * tp, np = min(tp, L - p0);
+    const size_t off = (size_t)f.li * p.cache_layer_stride + (size_t)cta->kh * p.max_seq * hd +
+                       (size_t)p0 * hd;
+    const int pieces = np * hd / 4;  // 16-byte pieces of K (and of V)
+    for (int i = lane; i < pieces; i += 32) {
+      cp_async16(dst + i * 16, p.kc + off + i * 4);
+      cp_async16(dst + tp * hd * 4 + i * 16, p.vc + off + i * 4);
+    }
+  } else {
+    const bool dual = f.ph == 3;
+    const MkMat& m = mk_mat(p, f.ph);
+    const uint8_t* w0 = f.ph == 0 ? lp.w_qkv : f.ph == 2 ? lp.w_o : dual ? lp.w_gate : lp.w_down;
+    const int nb = m.cols / kBlock;
+    const int ppr = min(kMkCK, nb - f.c * kMkCK) * BB / 16;  // pieces per row (nb % 4 == 0)
+    const size_t row_bytes = (size_t)nb * BB;
+    const size_t first = (size_t)(cta->sh[f.ph].rb + f.pr0) * row_bytes + (size_t)f.c * PITCH;
+    const int n = f.n, total = (dual ? 2 : 1) * n * ppr;
+    for (int i = lane; i < total; i += 32) {
+      const int r = ppr == PPR ? i / PPR : i / ppr;  // constant divisor for full chunks
+      const int pc = i - r * ppr;
+      const bool up = dual && r >= n;
+      const int row = up ? r - n : r;
+      cp_async16(dst + (up ? m.up_off : 0) + row * PITCH + pc * 16,
+                 (up ? lp.w_up : w0) + first + (size_t)row * row_bytes + pc * 16);
     }
   }
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&f.full[slot]))
+               : "memory");
+  mk_feed_skip(p, f, cta);
   return true;
 }
 
-__device__ bool mk_produce_attn(const MkParams& p, int li, int L, const MkRing& r, int& it) {
-  int kh, t0, t1;
-  bool last;
-  if (!mk_attn_item(p, L, &kh, &t0, &t1, &last)) return true;
-  const int lane = threadIdx.x & 31;
-  const int hd = p.hd, tp = 2048 / hd;
-  const size_t head_off = (size_t)li * p.cache_layer_stride + (size_t)kh * p.max_seq * hd;
-  for (int t = t0; t < t1; ++t, ++it) {
-    if (!mk_wait_empty(p, r, it)) return false;
-    if (lane == 0) {
-      const int s = it % r.S;
-      const int p0 = t * tp, np = min(tp, L - p0);
-      const uint32_t bytes = (uint32_t)(np * hd * 4);  // hd*4 % 16 == 0
-      unsigned char* dst = r.base + (size_t)s * kMkSlot;
-      mbar_arrive_expect_tx(&r.full[s], 2u * bytes);
-      bulk_g2s(dst, p.kc + head_off + (size_t)p0 * hd, bytes, &r.full[s]);
-      bulk_g2s(dst + tp * hd * 4, p.vc + head_off + (size_t)p0 * hd, bytes, &r.full[s]);
-    }
-    __syncwarp();
-  }
-  return true;
-}
-
+// Producer warp k (of kMkProducers) issues the tiles k, k + kMkProducers, ...
+// Because kMkS is a multiple of kMkProducers it alone refills those slots.
 template <int DT>
-__device__ void mk_producer(const MkParams& p, const MkRing& r, int L) {
-  int it = 0;
-  bool ok = !*reinterpret_cast<volatile int*>(p.abort_flag);
-  for (int li = 0; li < p.n_layers && ok; ++li) {
-    const CUtensorMap* mp = p.maps + (size_t)li * 10;
-    ok = mk_produce_mat<DT, false>(p, p.qkv, mp + 0, nullptr, r, it) &&
-         mk_produce_attn(p, li, L, r, it) &&
-         mk_produce_mat<DT, false>(p, p.o, mp + 2, nullptr, r, it) &&
-         mk_produce_mat<DT, true>(p, p.gu, mp + 4, mp + 6, r, it) &&
-         mk_produce_mat<DT, false>(p, p.down, mp + 8, nullptr, r, it);
+__device__ void mk_producer(const MkParams& p, MkFeed& f, const MkCta* cta, int L) {
+  const int k = ((int)threadIdx.x - kMkConsumers) >> 5;
+  if (!*reinterpret_cast<volatile int*>(p.abort_flag)) {
+    while (mk_feed_settle(p, f, cta)) {
+      if (f.issued % kMkProducers == k) {
+        if (!mk_issue<DT>(p, f, cta, L)) break;
+      } else {
+        mk_feed_skip(p, f, cta);
+      }
+    }
   }
-  // Every issued copy lands before the CTA may exit.
-  for (int t = max(0, it - r.S); t < it; ++t)
-    mbar_wait_timed(&r.full[t % r.S], (uint32_t)(t / r.S) & 1u, p.status);
+  asm volatile("cp.async.wait_all;" ::: "memory");  // nothing in flight at exit
+}
+
+// Consumer wait for the tile `it`; never leaves the caller's barrier
+// sequence: after an abort (or its own timeout, which raises the abort) it
+// returns at once with stale data, and every CTA stops at the next grid
+// barrier.
+__device__ const unsigned char* mk_next_tile(const MkParams& p, const MkFeed& f, int it) {
+  const int s = it % kMkS;
+  const uint32_t parity = (uint32_t)(it / kMkS) & 1u;
+  if (!mbar_try_wait(&f.full[s], parity)) {
+    const uint64_t t0 = global_timer_ns();
+    for (;;) {
+      if (mbar_try_wait_sleep(&f.full[s], parity, 2000u)) break;
+      if (*reinterpret_cast<volatile int*>(p.abort_flag)) break;
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        atomicOr(p.status, kDeviceTimeout);
+        atomicExch(p.abort_flag, 1);
+        break;
+      }
+    }
+  }
+  return f.ring + (size_t)s * kMkSlot;
+}
+
+// The warp is done with tile `it`.
+__device__ __forceinline__ void mk_release(const MkFeed& f, int it) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(&f.empty[it % kMkS]);
 }
 
 // ---------------------------------------------------------------- consumers
 
 __device__ __forceinline__ void mk_sync() { named_barrier_sync(1, kMkConsumers); }
-
-// Consumer wait for slot it % S. Never leaves the caller's barrier sequence:
-// after an abort (or its own timeout, which raises the abort) it returns at
-// once and the caller goes on with stale data; every CTA then stops at the
-// next grid barrier.
-__device__ __forceinline__ void mk_wait_full(const MkParams& p, const MkRing& r, int it) {
-  const int s = it % r.S;
-  const uint32_t parity = (uint32_t)(it / r.S) & 1u;
-  if (mbar_try_wait(&r.full[s], parity)) return;
-  const uint64_t t0 = global_timer_ns();
-  for (;;) {
-    if (mbar_try_wait_sleep(&r.full[s], parity, 20000u)) return;
-    if (*reinterpret_cast<volatile int*>(p.abort_flag)) return;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
-      atomicOr(p.status, kDeviceTimeout);
-      atomicExch(p.abort_flag, 1);
-      return;
-    }
-  }
-}
 
 // Grid barrier over the consumers of all CTAs (monotonic 64-bit counter).
 __device__ bool mk_grid_sync(const MkParams& p, unsigned long long target, int* flag) {
@@ -370,8 +478,8 @@ __device__ void mk_stage_x(const MkParams& p, float* xs, const float* src, int n
 // One projection phase. epi(row, v0, v1) gets the finished row (v1 = up for
 // the dual gate/up form).
 template <int DT, bool DUAL, class Epi>
-__device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const float* xs,
-                               const MkRing& r, float* red, int& it, Epi epi) {
+__device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const float* xs, MkFeed& f,
+                               const MkCta* cta, int L, float* red, int& it, Epi epi) {
   constexpr int BB = DT == MINQ_Q8_0 ? kQ8Bytes : kQ4Bytes;
   constexpr int PITCH = kMkCK * BB;
   constexpr int kMkAcc = MkAccN<DT, DUAL>::value;
@@ -392,37 +500,44 @@ __device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const float* x
       if (DUAL) acc1[k] = 0.0f;
     }
     for (int c = 0; c < m.nchunks; ++c, ++it) {
-      const int s = it % r.S;
-      mk_wait_full(p, r, it);
+      const unsigned char* tile = mk_next_tile(p, f, it);
       if (c * kMkCK + 4 * grp < nb) {  // nb % 4 == 0: the group is whole or absent
         const int bl = 4 * grp + bi;
         const int bg = c * kMkCK + bl;
         const float4 xa = *reinterpret_cast<const float4*>(xs + 32 * bg + 8 * sub);
         const float4 xb = *reinterpret_cast<const float4*>(xs + 32 * bg + 8 * sub + 4);
-        const unsigned char* bp =
-            r.base + (size_t)s * kMkSlot + (size_t)(2 * rs + h) * PITCH + bl * BB;
+        const unsigned char* bp = tile + (size_t)(2 * rs + h) * PITCH + bl * BB;
+        // all of the lane's code words and scales first (rows past the pass
+        // read nothing and count as zero), then the arithmetic: the loads of
+        // every row slot are in flight together
+        constexpr int NW = DT == MINQ_Q8_0 ? 2 : 1;
+        constexpr int NM = DUAL ? 2 : 1;
+        uint32_t cw[kMkAcc][NM][NW];
+        float dd[kMkAcc][NM];
 #pragma unroll
         for (int k = 0; k < kMkAcc; ++k) {
-          if (4 * k + 2 * rs + h < n) {
-            const unsigned char* blk = bp + (size_t)(4 * k) * PITCH;
-            const uint32_t* wp =
-                reinterpret_cast<const uint32_t*>(blk + 4 + (DT == MINQ_Q8_0 ? 8 : 4) * sub);
-            const float d = *reinterpret_cast<const float*>(blk);
-            const float2 part = mk_dot8<DT>(wp[0], DT == MINQ_Q8_0 ? wp[1] : 0u, xa, xb);
-            acc[k] = fmaf(d, part.x + part.y, acc[k]);
-            if (DUAL) {
-              const unsigned char* blk1 = blk + m.up_off;
-              const uint32_t* wp1 = reinterpret_cast<const uint32_t*>(
-                  blk1 + 4 + (DT == MINQ_Q8_0 ? 8 : 4) * sub);
-              const float d1 = *reinterpret_cast<const float*>(blk1);
-              const float2 part1 = mk_dot8<DT>(wp1[0], DT == MINQ_Q8_0 ? wp1[1] : 0u, xa, xb);
-              acc1[k] = fmaf(d1, part1.x + part1.y, acc1[k]);
-            }
+          const bool ok = 4 * k + 2 * rs + h < n;
+#pragma unroll
+          for (int mm = 0; mm < NM; ++mm) {
+            const unsigned char* blk = bp + (size_t)(4 * k) * PITCH + (mm ? m.up_off : 0);
+            const uint32_t* wp = reinterpret_cast<const uint32_t*>(blk + 4 + 4 * NW * sub);
+            dd[k][mm] = ok ? *reinterpret_cast<const float*>(blk) : 0.0f;
+#pragma unroll
+            for (int w = 0; w < NW; ++w) cw[k][mm][w] = ok ? wp[w] : 0u;
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < kMkAcc; ++k) {
+          const float2 part = mk_dot8<DT>(cw[k][0][0], NW == 2 ? cw[k][0][NW - 1] : 0u, xa, xb);
+          acc[k] = fmaf(dd[k][0], part.x + part.y, acc[k]);
+          if (DUAL) {
+            const float2 part1 =
+                mk_dot8<DT>(cw[k][NM - 1][0], NW == 2 ? cw[k][NM - 1][NW - 1] : 0u, xa, xb);
+            acc1[k] = fmaf(dd[k][NM - 1], part1.x + part1.y, acc1[k]);
           }
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&r.empty[s]);
+      mk_release(f, it);
     }
     // sum over the 16 lanes of each half (4 blocks x 4 column slices), then
     // over the 8 groups in a fixed order; passes alternate between two
@@ -458,7 +573,7 @@ __device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const float* x
 // RMSNorm (optional) + NeoX RoPE of one head held by a warp (model.rs:140-216):
 // lane owns pairs (i, i + hd/2), i = lane + 32k. Writes the head to dst.
 __device__ void mk_head_prep(const MkParams& p, const float* src, const float* gain, bool rope,
-                             int pos, float* dst) {
+                             const float* rope_cs, float* dst) {
   const int lane = threadIdx.x & 31, hd = p.hd, half = hd / 2;
   float a[2], b[2];  // hd <= 128: at most 2 pairs per lane
 #pragma unroll
@@ -488,8 +603,8 @@ __device__ void mk_head_prep(const MkParams& p, const float* src, const float* g
     if (i >= half) continue;
     float x1 = a[k], x2 = b[k];
     if (rope) {
-      const float c = p.rope_cos[(size_t)pos * half + i];
-      const float s = p.rope_sin[(size_t)pos * half + i];
+      const float c = rope_cs[i];         // cos / sin of this position (shared memory)
+      const float s = rope_cs[half + i];
       const float y1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
       const float y2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
       x1 = y1;
@@ -500,180 +615,250 @@ __device__ void mk_head_prep(const MkParams& p, const float* src, const float* g
   }
 }
 
-// Online-softmax update of one warp's state with one position (attend,
-// model.rs:223-248: s = q.k / sqrt(hd), softmax over positions, sum p v).
-// Lane holds dims [DPL*lane, DPL*lane + DPL) of q, k, v and o.
+// Shared-memory layout of the attention phase (in the scratch region).
+struct MkAttnSmem {
+  float* qs;    // [G][hd]   RoPE'd (and normed) query heads
+  float* knew;  // [hd]      the new position's key (last split)
+  float* vnew;  // [hd]
+  float* sc;    // [G][32]   scores of the tile
+  float* pp;    // [G][32]   softmax numerators of the tile
+  float* corr;  // [G]       rescale of the running output
+};
+
+// One step of attend (model.rs:223-248: s = q.k / sqrt(hd), softmax over
+// positions, o = sum p v) over up to 32 positions held in shared memory:
+// positions j < base1 are rows j of (k0, v0) (j < n0), positions j >= base1
+// rows j - base1 of (k1, v1) (j - base1 < n1). As an online softmax: (A)
+// warp w scores positions w and w + 16 for every head, (B) warp g < G
+// updates head g's running max m and sum l and forms the numerators, (C)
+// every thread rescales and accumulates its outputs (head, dim) =
+// (idx / hd, idx % hd) for idx = tid, tid + 512. m, l live in warp g's lanes
+// (replicated); o in the owning thread.
 template <int DPL, int GM>
-__device__ __forceinline__ void mk_attn_update(const float (&q)[GM][DPL], const float* k,
-                                               const float* v, int G, float scale,
-                                               float (&m)[GM], float (&l)[GM],
-                                               float (&o)[GM][DPL]) {
-  const int lane = threadIdx.x & 31;
-  float kv[DPL], vv[DPL];
+__device__ void mk_attn_step(const MkParams& p, const MkAttnSmem& a, const float (&q)[GM][DPL],
+                             const float* k0, const float* v0, int n0, const float* k1,
+                             const float* v1, int n1, int base1, float& m, float& l,
+                             float (&o)[2]) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = p.G, hd = p.hd;
+  // (A) scores
+  float sv[2][GM];
 #pragma unroll
-  for (int e = 0; e < DPL; ++e) {
-    kv[e] = k[DPL * lane + e];
-    vv[e] = v[DPL * lane + e];
+  for (int rep = 0; rep < 2; ++rep) {
+    const int j = warp + 16 * rep;
+    const bool t1 = j >= base1;
+    const int r = t1 ? j - base1 : j;
+    const bool ok = r < (t1 ? n1 : n0);
+    const float* kr = (t1 ? k1 : k0) + (ok ? r : 0) * hd;
+    float kv[DPL];
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) kv[e] = ok ? kr[DPL * lane + e] : 0.0f;
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+      sv[rep][g] = 0.0f;
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) sv[rep][g] = fmaf(q[g][e], kv[e], sv[rep][g]);
+    }
   }
 #pragma unroll
-  for (int g = 0; g < GM; ++g) {
-    if (g < G) {
-      float sv = 0.0f;
+  for (int off = 16; off > 0; off >>= 1)
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) sv = fmaf(q[g][e], kv[e], sv);
-      sv = warp_sum(sv) * scale;
-      const float mn = fmaxf(m[g], sv);
-      const float corr = m[g] == -INFINITY ? 0.0f : expf(m[g] - mn);
-      const float pr = expf(sv - mn);
-      l[g] = fmaf(l[g], corr, pr);
+    for (int rep = 0; rep < 2; ++rep)
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) o[g][e] = fmaf(pr, vv[e], o[g][e] * corr);
-      m[g] = mn;
+      for (int g = 0; g < GM; ++g) sv[rep][g] += __shfl_xor_sync(0xffffffffu, sv[rep][g], off);
+  if (lane < GM && lane < G) {
+#pragma unroll
+    for (int rep = 0; rep < 2; ++rep) {
+      float v = sv[rep][0];
+#pragma unroll
+      for (int g = 1; g < GM; ++g) v = lane == g ? sv[rep][g] : v;
+      a.sc[lane * 32 + warp + 16 * rep] = v * p.scale;
+    }
+  }
+  mk_sync();
+  // (B) online softmax per head
+  if (warp < G) {
+    const bool t1 = lane >= base1;
+    const bool ok = (t1 ? lane - base1 : lane) < (t1 ? n1 : n0);
+    const float s_ = ok ? a.sc[warp * 32 + lane] : -INFINITY;
+    const float mt = warp_max(s_);
+    const float mn = fmaxf(m, mt);
+    const float c = m == -INFINITY ? 0.0f : expf(m - mn);
+    const float pr = s_ == -INFINITY ? 0.0f : expf(s_ - mn);
+    l = fmaf(l, c, warp_sum(pr));
+    m = mn;
+    a.pp[warp * 32 + lane] = pr;
+    if (lane == 0) a.corr[warp] = c;
+  }
+  mk_sync();
+  // (C) o = o * corr + sum_j p_j v_j
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int idx = tid + kMkConsumers * u;
+    if (idx < G * hd) {
+      const int g = idx / hd, d = idx - g * hd;
+      const float* pg = a.pp + g * 32;
+      const float* va = v0 + d;
+      const float* vb = v1 + d;
+      float acc = o[u] * a.corr[g], acc2 = 0.0f;
+      int j = 0;
+#pragma unroll 4
+      for (; j + 1 < n0; j += 2) {
+        acc = fmaf(pg[j], va[j * hd], acc);
+        acc2 = fmaf(pg[j + 1], va[(j + 1) * hd], acc2);
+      }
+      if (j < n0) acc = fmaf(pg[j], va[j * hd], acc);
+      pg += base1;
+#pragma unroll 4
+      for (j = 0; j + 1 < n1; j += 2) {
+        acc = fmaf(pg[j], vb[j * hd], acc);
+        acc2 = fmaf(pg[j + 1], vb[(j + 1) * hd], acc2);
+      }
+      if (j < n1) acc = fmaf(pg[j], vb[j * hd], acc);
+      o[u] = acc + acc2;
     }
   }
 }
 
-template <int DPL, int GM>
-__device__ void mk_consume_attn(const MkParams& p, int li, int L, float* scr, const MkRing& r,
-                                int* misc_i, int& it) {
+template <int DT, int DPL, int GM>
+__device__ void mk_consume_attn(const MkParams& p, int li, int L, float* scr, MkFeed& f,
+                                const MkCta* cta, const float* rope_cs, int* misc_i, int& it) {
   int kh, t0, t1;
   bool last;
   if (!mk_attn_item(p, L, &kh, &t0, &t1, &last)) return;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = p.G, hd = p.hd, tp = 2048 / hd;
-  float* qs = scr;                // [G][hd]
-  float* knew = qs + G * hd;      // [hd]
-  float* vnew = knew + hd;        // [hd]
-  float* mg = vnew + hd;          // [16][G]
-  float* lg = mg + kMkCW * G;     // [16][G]
-  float* og = lg + kMkCW * G;     // [16][G][hd]
+  MkAttnSmem a;
+  a.qs = scr;
+  a.knew = a.qs + G * hd;
+  a.vnew = a.knew + hd;
+  a.sc = a.vnew + hd;
+  a.pp = a.sc + 32 * G;
+  a.corr = a.pp + 32 * G;
   const MkLayerPtrs& lp = p.layers[li];
   const size_t head_off = (size_t)li * p.cache_layer_stride + (size_t)kh * p.max_seq * hd;
   // q heads (q_norm, RoPE at position L); the last split also builds the new
   // k (k_norm, RoPE) and v and appends them to the cache
   if (warp < G) {
-    mk_head_prep(p, p.qkv_out + (size_t)(kh * G + warp) * hd, lp.q_norm, true, L,
-                 qs + warp * hd);
+    mk_head_prep(p, p.qkv_out + (size_t)(kh * G + warp) * hd, lp.q_norm, true, rope_cs,
+                 a.qs + warp * hd);
   } else if (last && warp == G) {
-    mk_head_prep(p, p.qkv_out + p.qd + (size_t)kh * hd, lp.k_norm, true, L, knew);
+    mk_head_prep(p, p.qkv_out + p.qd + (size_t)kh * hd, lp.k_norm, true, rope_cs, a.knew);
     __syncwarp();
-    for (int i = lane; i < hd; i += 32) p.kc[head_off + (size_t)L * hd + i] = knew[i];
+    for (int i = lane; i < hd; i += 32) p.kc[head_off + (size_t)L * hd + i] = a.knew[i];
   } else if (last && warp == G + 1) {
     for (int i = lane; i < hd; i += 32) {
       const float v = ldcg(p.qkv_out + p.qd + p.kvd + (size_t)kh * hd + i);
-      vnew[i] = v;
+      a.vnew[i] = v;
       p.vc[head_off + (size_t)L * hd + i] = v;
     }
   }
   mk_sync();
-  float q[GM][DPL], m[GM], l[GM], o[GM][DPL];
+  float q[GM][DPL];
 #pragma unroll
-  for (int g = 0; g < GM; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.0f;
+  for (int g = 0; g < GM; ++g)
 #pragma unroll
-    for (int e = 0; e < DPL; ++e) {
-      q[g][e] = g < G ? qs[g * hd + DPL * lane + e] : 0.0f;
-      o[g][e] = 0.0f;
+    for (int e = 0; e < DPL; ++e) q[g][e] = g < G ? a.qs[g * hd + DPL * lane + e] : 0.0f;
+  float m = -INFINITY, l = 0.0f, o[2] = {0.0f, 0.0f};
+  // two 16-position tiles per step for head_dim 128, one 32-position tile for 64
+  const int per_step = 32 / tp;
+  for (int t = t0; t < t1; t += per_step) {
+    const float* ka = reinterpret_cast<const float*>(mk_next_tile(p, f, it));
+    const int na = min(tp, L - t * tp);
+    const float* kb = ka;
+    int nb_ = 0;
+    if (per_step == 2 && t + 1 < t1) {
+      kb = reinterpret_cast<const float*>(mk_next_tile(p, f, it + 1));
+      nb_ = min(tp, L - (t + 1) * tp);
+    }
+    mk_attn_step<DPL, GM>(p, a, q, ka, ka + tp * hd, na, kb, kb + tp * hd, nb_, tp, m, l, o);
+    mk_release(f, it);
+    ++it;
+    if (nb_ > 0) {
+      mk_release(f, it);
+      ++it;
     }
   }
-  for (int t = t0; t < t1; ++t, ++it) {
-    const int s = it % r.S;
-    mk_wait_full(p, r, it);
-    const float* kt = reinterpret_cast<const float*>(r.base + (size_t)s * kMkSlot);
-    const float* vt = kt + tp * hd;
-    const int np = min(tp, L - t * tp);
-    for (int pi = warp; pi < np; pi += kMkCW)
-      mk_attn_update<DPL, GM>(q, kt + pi * hd, vt + pi * hd, G, p.scale, m, l, o);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&r.empty[s]);
-  }
-  if (last && warp == 0) mk_attn_update<DPL, GM>(q, knew, vnew, G, p.scale, m, l, o);
-  // merge the 16 warps' states
-#pragma unroll
-  for (int g = 0; g < GM; ++g) {
-    if (g < G) {
-      if (lane == 0) {
-        mg[warp * G + g] = m[g];
-        lg[warp * G + g] = l[g];
-      }
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) og[(warp * G + g) * hd + DPL * lane + e] = o[g][e];
-    }
-  }
-  mk_sync();
+  if (last) mk_attn_step<DPL, GM>(p, a, q, a.knew, a.vnew, 1, a.knew, a.vnew, 0, 32, m, l, o);
+  // this split's partial: unnormalised o, running max m and sum l per head
   const int item = blockIdx.x;
   float* part = p.part + (size_t)item * G * (hd + 2);  // [G][hd + 2]: o, m, l
-  for (int idx = tid; idx < G * hd; idx += kMkConsumers) {
-    const int g = idx / hd, d = idx % hd;
-    float M = -INFINITY;
-    for (int w = 0; w < kMkCW; ++w) M = fmaxf(M, mg[w * G + g]);
-    float Ls = 0.0f, O = 0.0f;
-    if (M != -INFINITY) {
-      for (int w = 0; w < kMkCW; ++w) {
-        const float mw = mg[w * G + g];
-        if (mw == -INFINITY) continue;
-        const float f = expf(mw - M);
-        Ls = fmaf(lg[w * G + g], f, Ls);
-        O = fmaf(og[(w * G + g) * hd + d], f, O);
-      }
-    }
-    part[g * (hd + 2) + d] = O;
-    if (d == 0) {
-      part[g * (hd + 2) + hd] = M;
-      part[g * (hd + 2) + hd + 1] = Ls;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int idx = tid + kMkConsumers * u;
+    if (idx < G * hd) {
+      const int g = idx / hd, d = idx - g * hd;
+      part[g * (hd + 2) + d] = o[u];
     }
   }
-  // the last split of this kv head to finish merges all of them
+  if (warp < G && lane == 0) {
+    part[warp * (hd + 2) + hd] = m;
+    part[warp * (hd + 2) + hd + 1] = l;
+  }
+  // every split of this kv head waits for the others (an arrival counter per
+  // head, reset after the next grid barrier), then merges its own slice of
+  // the head's G * hd outputs from all splits' partials
   const int ns = mk_nsplit(p, L);
+  const int sp = item - kh * ns;
   __threadfence();
   mk_sync();
   if (tid == 0) {
-    const int old = atomicAdd(p.head_ctr + kh, 1);
-    misc_i[0] = old == ns - 1;
+    atomicAdd(p.head_ctr + kh, 1);
+    const uint64_t tw = global_timer_ns();
+    for (;;) {
+      int v;
+      asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p.head_ctr + kh) : "memory");
+      if (v >= ns) break;
+      if (*reinterpret_cast<volatile int*>(p.abort_flag)) break;
+      if (global_timer_ns() - tw > kWaitLimitNs) {
+        atomicOr(p.status, kDeviceTimeout);
+        atomicExch(p.abort_flag, 1);
+        break;
+      }
+    }
+    __threadfence();
   }
   mk_sync();
-  if (misc_i[0]) {
-    __threadfence();
-    const float* hp = p.part + (size_t)kh * ns * G * (hd + 2);  // items of head kh
-    float* mm = scr;             // [ns][G] split maxima, then weights
-    float* ll = mm + ns * G;     // [ns][G]
-    for (int i = tid; i < ns * G; i += kMkConsumers) {
-      const float* e = hp + (size_t)i * (hd + 2);  // i = sp * G + g
-      mm[i] = ldcg(e + hd);
-      ll[i] = ldcg(e + hd + 1);
+  const int GH = G * hd;
+  const int o0 = (int)((long long)GH * sp / ns), o1 = (int)((long long)GH * (sp + 1) / ns);
+  const int nout = o1 - o0;
+  const int g0 = o0 / hd, ng = (o1 - 1) / hd - g0 + 1;  // heads the slice touches
+  const float* hp = p.part + (size_t)kh * ns * G * (hd + 2);
+  float* mm = scr;             // [ns][ng] split maxima, then weights
+  float* ll = mm + ns * ng;    // [ns][ng]
+  float* inv = ll + ns * ng;   // [ng]
+  float* vals = inv + ng;      // [ns][nout] weighted partial outputs
+  for (int i = tid; i < ns * ng; i += kMkConsumers) {
+    const int s_ = i / ng, gg = i - s_ * ng;
+    const float* e = hp + ((size_t)s_ * G + g0 + gg) * (hd + 2);
+    mm[i] = ldcg(e + hd);
+    ll[i] = ldcg(e + hd + 1);
+  }
+  mk_sync();
+  if (tid < ng) {
+    float M = -INFINITY;
+    for (int s_ = 0; s_ < ns; ++s_) M = fmaxf(M, mm[s_ * ng + tid]);
+    float Ls = 0.0f;
+    for (int s_ = 0; s_ < ns; ++s_) {
+      const float ms = mm[s_ * ng + tid];
+      const float f = ms == -INFINITY ? 0.0f : expf(ms - M);
+      Ls = fmaf(ll[s_ * ng + tid], f, Ls);
+      mm[s_ * ng + tid] = f;
     }
-    mk_sync();
-    if (tid < G) {
-      float M = -INFINITY;
-      for (int sp = 0; sp < ns; ++sp) M = fmaxf(M, mm[sp * G + tid]);
-      float Ls = 0.0f;
-      for (int sp = 0; sp < ns; ++sp) {
-        const float ms = mm[sp * G + tid];
-        const float f = ms == -INFINITY ? 0.0f : expf(ms - M);
-        Ls = fmaf(ll[sp * G + tid], f, Ls);
-        mm[sp * G + tid] = f;  // weight of the split before the division
-      }
-      ll[tid] = 1.0f / Ls;    // ll[0..G) reused: 1 / sum (ll no longer read)
-    }
-    mk_sync();
-    for (int idx = tid; idx < G * hd; idx += kMkConsumers) {
-      const int g = idx / hd, d = idx % hd;
-      float O = 0.0f;
-      for (int sp0 = 0; sp0 < ns; sp0 += 8) {  // 8 independent loads in flight
-        float v[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int sp = sp0 + u;
-          v[u] = sp < ns ? ldcg(hp + ((size_t)sp * G + g) * (hd + 2) + d) : 0.0f;
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-          if (sp0 + u < ns) O = fmaf(v[u], mm[(sp0 + u) * G + g], O);
-      }
-      p.att[(size_t)(kh * G + g) * hd + d] = O * ll[g];
-    }
-    if (tid == 0) p.head_ctr[kh] = 0;
+    inv[tid] = 1.0f / Ls;
+  }
+  mk_sync();
+  for (int i = tid; i < ns * nout; i += kMkConsumers) {
+    const int s_ = i / nout, oi = i - s_ * nout;
+    const int g = (o0 + oi) / hd, d = (o0 + oi) - g * hd;
+    vals[i] = ldcg(hp + ((size_t)s_ * G + g) * (hd + 2) + d) * mm[s_ * ng + g - g0];
+  }
+  mk_sync();
+  for (int oi = tid; oi < nout; oi += kMkConsumers) {
+    const int g = (o0 + oi) / hd, d = (o0 + oi) - g * hd;
+    float O = 0.0f;
+    for (int s_ = 0; s_ < ns; ++s_) O += vals[s_ * nout + oi];
+    p.att[(size_t)(kh * G + g) * hd + d] = O * inv[g - g0];
   }
 }
 
@@ -727,7 +912,8 @@ __device__ void mk_lm_head(const MkParams& p, const float* xs, unsigned long lon
 }
 
 template <int DT>
-__device__ void mk_consumers(const MkParams& p, unsigned char* sm, const MkRing& r, int L,
+__device__ void mk_consumers(const MkParams& p, unsigned char* sm, MkFeed& f, const MkCta* cta,
+                             int L,
                              uint32_t tok, unsigned long long bbase) {
   float* misc = reinterpret_cast<float*>(sm + kMkMiscOff);         // [0..32]: reductions
   int* misc_i = reinterpret_cast<int*>(sm + kMkMiscOff + 160);     // flags
@@ -739,42 +925,50 @@ __device__ void mk_consumers(const MkParams& p, unsigned char* sm, const MkRing&
   bool ok = !*reinterpret_cast<volatile int*>(p.abort_flag);
   auto barrier = [&]() { return mk_grid_sync(p, bbase + (unsigned long long)(++nbar) * G, misc_i + 1); };
   const float* xsrc = p.embed + (size_t)tok * p.H;  // residual source before layer 0's o_proj
+  // this position's RoPE row (model.rs:170-186 tables), used by every layer
+  float* rope_cs = reinterpret_cast<float*>(sm + kMkRopeOff);
+  {
+    const int half = p.hd / 2;
+    for (int i = threadIdx.x; i < 2 * half; i += kMkConsumers)
+      rope_cs[i] = i < half ? p.rope_cos[(size_t)L * half + i] : p.rope_sin[(size_t)L * half + i - half];
+  }
   constexpr bool Q4 = DT == MINQ_Q4_0;
   for (int li = 0; li < p.n_layers && ok; ++li) {
     const MkLayerPtrs& lp = p.layers[li];
     // P1: q|k|v
     mk_stage_x(p, xs, xsrc, p.H, lp.attn_norm, Q4, misc);
     const float* bias = lp.bias_qkv;
-    mk_consume_mat<DT, false>(p, p.qkv, xs, r, red, it, [&](int row, float v, float) {
+    mk_consume_mat<DT, false>(p, p.qkv, xs, f, cta, L, red, it, [&](int row, float v, float) {
       p.qkv_out[row] = bias ? v + bias[row] : v;
     });
     if (!(ok = barrier())) break;
     // P2: attention
     if (p.hd == 128) {
-      if (p.G <= 4) mk_consume_attn<4, 4>(p, li, L, xs, r, misc_i, it);
-      else mk_consume_attn<4, 8>(p, li, L, xs, r, misc_i, it);
+      if (p.G <= 4) mk_consume_attn<DT, 4, 4>(p, li, L, xs, f, cta, rope_cs, misc_i, it);
+      else mk_consume_attn<DT, 4, 8>(p, li, L, xs, f, cta, rope_cs, misc_i, it);
     } else {
-      if (p.G <= 4) mk_consume_attn<2, 4>(p, li, L, xs, r, misc_i, it);
-      else mk_consume_attn<2, 8>(p, li, L, xs, r, misc_i, it);
+      if (p.G <= 4) mk_consume_attn<DT, 2, 4>(p, li, L, xs, f, cta, rope_cs, misc_i, it);
+      else mk_consume_attn<DT, 2, 8>(p, li, L, xs, f, cta, rope_cs, misc_i, it);
     }
     if (!(ok = barrier())) break;
-    // P3: x = x + W_o att
+    // P3: x = x + W_o att (every split is past its head's counter now)
+    if (blockIdx.x < (unsigned)p.nkv && threadIdx.x == 0) p.head_ctr[blockIdx.x] = 0;
     mk_stage_x(p, xs, p.att, p.qd, nullptr, Q4, misc);
     const float* res = xsrc;
-    mk_consume_mat<DT, false>(p, p.o, xs, r, red, it, [&](int row, float v, float) {
+    mk_consume_mat<DT, false>(p, p.o, xs, f, cta, L, red, it, [&](int row, float v, float) {
       p.x[row] = ldcg(res + row) + v;
     });
     xsrc = p.x;
     if (!(ok = barrier())) break;
     // P4: h = silu(gate) * up
     mk_stage_x(p, xs, p.x, p.H, lp.ffn_norm, Q4, misc);
-    mk_consume_mat<DT, true>(p, p.gu, xs, r, red, it, [&](int row, float g, float u) {
+    mk_consume_mat<DT, true>(p, p.gu, xs, f, cta, L, red, it, [&](int row, float g, float u) {
       p.h[row] = silu(g) * u;
     });
     if (!(ok = barrier())) break;
     // P5: x = x + W_down h
     mk_stage_x(p, xs, p.h, p.I, nullptr, Q4, misc);
-    mk_consume_mat<DT, false>(p, p.down, xs, r, red, it, [&](int row, float v, float) {
+    mk_consume_mat<DT, false>(p, p.down, xs, f, cta, L, red, it, [&](int row, float v, float) {
       p.x[row] = ldcg(p.x + row) + v;
     });
     if (!(ok = barrier())) break;
@@ -807,63 +1001,39 @@ __device__ void mk_consumers(const MkParams& p, unsigned char* sm, const MkRing&
 template <int DT>
 __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_constant__ MkParams p) {
   extern __shared__ __align__(128) unsigned char sm[];
-  MkRing r;
-  r.full = reinterpret_cast<uint64_t*>(sm);
-  r.empty = r.full + kMkMaxS;
-  r.S = p.S;
-  r.base = sm + kMkScrOff + (size_t)p.scratch_bytes;
   const int L = *reinterpret_cast<volatile const int*>(p.d_pos);
   const uint32_t tok = *reinterpret_cast<volatile const uint32_t*>(p.d_tok);
   const unsigned long long bbase = *reinterpret_cast<volatile const unsigned long long*>(p.bar_base);
+  MkCta* cta = reinterpret_cast<MkCta*>(sm + kMkCtaOff);
+  if (threadIdx.x == 0) mk_cta_plan(p, L, cta);
+  __syncthreads();
+  MkFeed f;
+  f.ring = sm + kMkScrOff + (size_t)p.scratch_bytes;
+  f.full = reinterpret_cast<uint64_t*>(sm);
+  f.empty = f.full + kMkS;
+  f.li = 0;
+  f.ph = 0;
+  f.idx = 0;
+  f.issued = 0;
+  f.j = 0;
+  f.c = 0;
+  mk_feed_pass(f, cta->sh[0]);
   if (threadIdx.x == 0) {
-    for (int s = 0; s < r.S; ++s) {
-      mbar_init(&r.full[s], 1);
-      mbar_init(&r.empty[s], kMkCW);
+    for (int s = 0; s < kMkS; ++s) {
+      mbar_init(&f.full[s], 32);     // the issuing producer warp's lanes (cp.async.mbarrier.arrive)
+      mbar_init(&f.empty[s], kMkCW);  // every consumer warp
     }
     mbar_fence_init();
   }
   __syncthreads();
   if ((int)threadIdx.x >= kMkConsumers) {
-    mk_producer<DT>(p, r, L);
+    mk_producer<DT>(p, f, cta, L);
     return;
   }
-  mk_consumers<DT>(p, sm, r, L, tok, bbase);
+  mk_consumers<DT>(p, sm, f, cta, L, tok, bbase);
 }
 
 // ---------------------------------------------------------------- host
-
-static PFN_cuTensorMapEncodeTiled_v12000 mk_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaDriverEntryPointQueryResult q;
-    void* f = nullptr;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-  });
-  return fn;
-}
-
-// Tensor map of a quantized [rows x cols] weight for boxes of box_rows rows x
-// 32 blocks, in 8-byte elements (80 of them per Q4_0 chunk, 144 per Q8_0).
-static minq_status mk_encode(const void* w, uint64_t rows, uint64_t cols, int dtype,
-                             int box_rows, CUtensorMap* out) {
-  auto fn = mk_encode_fn();
-  if (!fn) return fail(MINQ_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  const uint64_t row_bytes = cols / kBlock * block_bytes(dtype);
-  cuuint64_t dims[2] = {row_bytes / 8, rows};
-  cuuint64_t strides[1] = {row_bytes};
-  cuuint32_t box[2] = {(cuuint32_t)(kMkCK * block_bytes(dtype) / 8), (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(w), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return fail(MINQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
-  return MINQ_OK;
-}
 
 MkMat mk_plan_mat(int dtype, bool dual, uint64_t rows, uint64_t cols, int grid) {
   MkMat m{};
@@ -878,32 +1048,28 @@ MkMat mk_plan_mat(int dtype, bool dual, uint64_t rows, uint64_t cols, int grid) 
   m.rows = (int)rows;
   m.cols = (int)cols;
   m.nr = (int)((rmax + passes - 1) / passes);
-  m.nr_b = m.nr > 1 ? m.nr - 1 : 1;
   m.nchunks = (int)((cols / kBlock + kMkCK - 1) / kMkCK);
   m.up_off = dual ? (int)(((size_t)m.nr * pitch + 127) & ~(size_t)127) : 0;
   return m;
 }
 
-minq_status mk_encode_pair(const void* w, uint64_t rows, uint64_t cols, int dtype, const MkMat& m,
-                           CUtensorMap* out2) {
-  MINQ_TRY(mk_encode(w, rows, cols, dtype, m.nr, &out2[0]));
-  MINQ_TRY(mk_encode(w, rows, cols, dtype, m.nr_b, &out2[1]));
-  return MINQ_OK;
-}
-
-size_t mk_scratch_bytes(int H, int I, int qd, int G, int hd) {
+size_t mk_scratch_bytes(int H, int I, int qd, int G, int hd, int nsplit) {
   const size_t xs = (size_t)std::max({H, I, qd}) * 4;
-  const size_t att = ((size_t)G * hd + 2 * hd + 2 * kMkCW * G + (size_t)kMkCW * G * hd) * 4;
+  // attention: q heads, new k and v, scores / numerators / rescales of a
+  // tile; then, in the CTA merging a kv head, every split's partial
+  // (o, max, sum) plus a weight per split and head
+  // merge of a slice of one kv head's outputs: (max, sum) per split and
+  // head, 1 / sum per head, weighted partials per split and output
+  const size_t splits = (size_t)nsplit;
+  const size_t slice = ((size_t)G * hd + splits - 1) / splits + 1;
+  const size_t att = std::max((size_t)G * hd + 2 * hd + 2 * 32 * G + G,
+                              2 * splits * G + G + splits * slice) * 4;
   return (std::max(xs, att) + 127) & ~(size_t)127;
 }
 
-int mk_ring_slots(size_t scratch_bytes) {
-  const size_t avail = 227 * 1024 - kMkScrOff - scratch_bytes;
-  return (int)std::min<size_t>(kMkMaxS, avail / kMkSlot);
-}
-
-size_t mk_smem_bytes(size_t scratch_bytes, int S) {
-  return kMkScrOff + scratch_bytes + (size_t)S * kMkSlot;
+size_t mk_smem_bytes(size_t scratch_bytes) {
+  const size_t total = kMkScrOff + scratch_bytes + (size_t)kMkS * kMkSlot;
+  return total <= 227 * 1024 ? total : 0;
 }
 
 template <int DT>

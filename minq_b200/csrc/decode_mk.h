@@ -14,14 +14,18 @@ namespace minq {
 struct MkMat {
   int rows;     // output rows (gate/up row pairs for the dual phase)
   int cols;
-  int nr;       // rows per pass, first tensor-map box
-  int nr_b;     // second box (passes of nr - 1 rows)
+  int nr;       // max rows per pass
   int nchunks;  // 32-block column chunks per row
-  int up_off;   // dual: offset of the up rows' box in a ring slot
+  int up_off;   // dual: offset of the up rows in a ring slot
 };
 
-// Per-layer vectors (device array).
+// Per-layer weights and vectors (device array).
 struct MkLayerPtrs {
+  const uint8_t* w_qkv;   // fused q|k|v blocks [qd + 2 kvd][H]
+  const uint8_t* w_o;     // [H][qd]
+  const uint8_t* w_gate;  // [I][H]
+  const uint8_t* w_up;    // [I][H]
+  const uint8_t* w_down;  // [H][I]
   const float* attn_norm;
   const float* ffn_norm;
   const float* bias_qkv;  // may be null
@@ -30,7 +34,6 @@ struct MkLayerPtrs {
 };
 
 struct MkParams {
-  const CUtensorMap* maps;     // [n_layers][qkv, o, gate, up, down][box nr, box nr-1]
   const MkLayerPtrs* layers;   // [n_layers]
   int n_layers;
   MkMat qkv, o, gu, down;
@@ -60,16 +63,15 @@ struct MkParams {
   int* status;                 // device status word (bounded-wait timeouts)
   int* abort_flag;             // set when any CTA gives up; every CTA stops
   int want_logits;
-  int S;                       // ring slots
   int scratch_bytes;           // x / attention scratch in shared memory
 };
 
 MkMat mk_plan_mat(int dtype, bool dual, uint64_t rows, uint64_t cols, int grid);
-minq_status mk_encode_pair(const void* w, uint64_t rows, uint64_t cols, int dtype,
-                           const MkMat& m, CUtensorMap* out2);
-size_t mk_scratch_bytes(int H, int I, int qd, int G, int hd);
-int mk_ring_slots(size_t scratch_bytes);
-size_t mk_smem_bytes(size_t scratch_bytes, int S);
+// Shared-memory scratch: the staged input vector, or the attention state
+// and the partials of up to nsplit history splits.
+size_t mk_scratch_bytes(int H, int I, int qd, int G, int hd, int nsplit);
+// Shared memory of the launch, or 0 when it does not fit one SM.
+size_t mk_smem_bytes(size_t scratch_bytes);
 minq_status launch_decode_mk(const MkParams& p, int dtype, int grid, size_t smem,
                              cudaStream_t s);
 

@@ -98,10 +98,9 @@ struct minq_model {
   // decode megakernel (decode_mk.cu): set up at finish when the model fits it
   struct {
     bool ok = false;
-    int dtype = 0, grid = 0, S = 0, scratch = 0, nsplit = 0;
+    int dtype = 0, grid = 0, scratch = 0, nsplit = 0;
     size_t smem = 0;
     minq::MkMat qkv{}, o{}, gu{}, down{};
-    CUtensorMap* maps = nullptr;  // device [n_layers][10]
     minq::MkLayerPtrs* layers = nullptr;
     float* part = nullptr;
     int* head_ctr = nullptr;
@@ -269,29 +268,25 @@ minq_status setup_megakernel(minq_model* m) {
   k.o = mk_plan_mat(dt, false, H, qd, grid);
   k.gu = mk_plan_mat(dt, true, I, H, grid);
   k.down = mk_plan_mat(dt, false, H, I, grid);
-  k.scratch = (int)mk_scratch_bytes((int)H, (int)I, (int)qd, (int)G, (int)hd);
-  k.S = mk_ring_slots(k.scratch);
-  if (k.S < 4) return MINQ_OK;
-  k.smem = mk_smem_bytes(k.scratch, k.S);
+  // history splits per kv head: up to one CTA each, as many as the merge
+  // buffer in shared memory allows
   k.nsplit = std::max(1, grid / (int)nkv);
+  for (;;) {
+    k.scratch = (int)mk_scratch_bytes((int)H, (int)I, (int)qd, (int)G, (int)hd, k.nsplit);
+    k.smem = mk_smem_bytes(k.scratch);
+    if (k.smem != 0 || k.nsplit == 1) break;
+    --k.nsplit;
+  }
+  if (k.smem == 0) return MINQ_OK;
   const size_t nl = c.n_layers;
-  std::vector<CUtensorMap> maps(nl * 10);
   std::vector<MkLayerPtrs> lps(nl);
   for (size_t li = 0; li < nl; ++li) {
     const DevLayer& L = m->layers[li];
-    CUtensorMap* mp = maps.data() + li * 10;
-    MINQ_TRY(mk_encode_pair(L.qkv.ptr, qd + 2 * kvd, H, dt, k.qkv, mp + 0));
-    MINQ_TRY(mk_encode_pair(L.o.ptr, H, qd, dt, k.o, mp + 2));
-    MINQ_TRY(mk_encode_pair(L.gate.ptr, I, H, dt, k.gu, mp + 4));
-    MINQ_TRY(mk_encode_pair(L.up.ptr, I, H, dt, k.gu, mp + 6));
-    MINQ_TRY(mk_encode_pair(L.down.ptr, H, I, dt, k.down, mp + 8));
-    lps[li] = MkLayerPtrs{L.attn_norm, L.ffn_norm, L.bias_qkv, L.q_norm, L.k_norm};
+    auto u8 = [](const DevLinear& l) { return static_cast<const uint8_t*>(l.ptr); };
+    lps[li] = MkLayerPtrs{u8(L.qkv), u8(L.o), u8(L.gate), u8(L.up), u8(L.down),
+                          L.attn_norm, L.ffn_norm, L.bias_qkv, L.q_norm, L.k_norm};
   }
   void* p;
-  MINQ_TRY(dmalloc(m, &p, maps.size() * sizeof(CUtensorMap)));
-  k.maps = static_cast<CUtensorMap*>(p);
-  MINQ_CUDA_TRY(cudaMemcpy(p, maps.data(), maps.size() * sizeof(CUtensorMap),
-                           cudaMemcpyHostToDevice));
   MINQ_TRY(dmalloc(m, &p, lps.size() * sizeof(MkLayerPtrs)));
   k.layers = static_cast<MkLayerPtrs*>(p);
   MINQ_CUDA_TRY(cudaMemcpy(p, lps.data(), lps.size() * sizeof(MkLayerPtrs),
@@ -598,7 +593,6 @@ static minq_status run_megakernel(minq_model* m, minq_cache* c, bool logits) {
   const minq_config& cfg = m->cfg;
   auto& k = m->mk;
   MkParams p{};
-  p.maps = k.maps;
   p.layers = k.layers;
   p.n_layers = (int)cfg.n_layers;
   p.qkv = k.qkv;
@@ -641,7 +635,6 @@ static minq_status run_megakernel(minq_model* m, minq_cache* c, bool logits) {
   p.status = device_status_word();
   p.abort_flag = k.abort_flag;
   p.want_logits = logits ? 1 : 0;
-  p.S = k.S;
   p.scratch_bytes = k.scratch;
   return launch_decode_mk(p, k.dtype, k.grid, k.smem, m->stream);
 }

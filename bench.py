@@ -301,6 +301,7 @@ def run_minq(args, world, rank, local):
     barrier(world)
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    len_timed0 = cache.len  # history length at the first timed step
     ev0.record(stream)
     # NVTX range: lets `ncu --nvtx --nvtx-include timed_decode/` list exactly
     # the launches of the timed region
@@ -371,7 +372,26 @@ def run_minq(args, world, rank, local):
     peak_src = "measured" if peaks.get("hbm_gbs") else "fallback"
     dom = max(fams, key=lambda k: fams[k]["ms"]) if fams else None
     roof = None
-    if dom:
+    if launches_per_step == 1:
+        # The whole token is one launch of the decode megakernel, so the
+        # dominant kernel is that launch and its duration is the timed step
+        # (CUDA events on the model's stream around K back-to-back launches).
+        # Algorithmic bytes per launch: every weight byte (quantized
+        # projections + the f32 lm_head) plus the K/V history read at the
+        # average position of the timed steps.
+        kv_pos = len_timed0 + (K - 1) / 2.0
+        kv_bytes = 2 * 4 * cfg.n_kv_heads * cfg.head_dim * kv_pos * cfg.n_layers
+        per_launch = float(model.weight_bytes) + kv_bytes
+        avg_us = 1000.0 * ms_max / K
+        gbs = per_launch / (avg_us * 1e-6) / 1e9
+        fams = {"decode_mk": {"launches": K, "ms": ms_max, "bytes": per_launch * K,
+                              "avg_us": avg_us, "gbs": gbs}}
+        roof = {"bound": "hbm", "kernel": "decode_mk", "achieved": gbs, "peak": peak,
+                "unit": "GB/s", "frac": gbs / peak, "peak_source": peak_src,
+                "traffic": (per_launch * NCU_TRAFFIC_RATIO["decode_mk"]
+                            if "decode_mk" in NCU_TRAFFIC_RATIO else None),
+                "per_launch_bytes": per_launch, "avg_launch_us": avg_us}
+    elif dom:
         d = fams[dom]
         roof = {"bound": "hbm", "kernel": dom, "achieved": d["gbs"], "peak": peak,
                 "unit": "GB/s", "frac": d["gbs"] / peak, "peak_source": peak_src,

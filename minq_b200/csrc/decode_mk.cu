@@ -41,6 +41,11 @@
 // group of every chunk and a quarter of the rows; in attention the 16 warps
 // cooperate on each step of up to 32 positions (scores, softmax, p v).
 //
+// The quantized dot products are those of the streaming matvec: exact code ->
+// float conversion (byte permute into 2^23 + code), packed f32x2 FMAs, the
+// block scale applied once per block (quantize.rs:252-280). Cross-CTA data
+// (x, q|k|v, attention output, h, split partials) is read with ld.global.cg
+// so no stale L1 line is used after a barrier.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 

@@ -42,10 +42,11 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per algorithmic
-# byte, from one ncu --set full capture of three decode-shaped Q4_0 qmatvec
-# launches (q/k/v, o_proj, gate/up): 47.72 MB / 47.62 MB. Summary and command
-# under profiles/.
-NCU_TRAFFIC_RATIO = {"qmatvec": 1.002}
+# byte, from ncu --set full captures (summaries and commands under profiles/):
+# three decode-shaped Q4_0 qmatvec launches (q/k/v, o_proj, gate/up), 47.72 MB
+# / 47.62 MB; one decode megakernel launch of a 12-layer cut of the Q4_0
+# model, 2.36884 GB / 2.36344 GB.
+NCU_TRAFFIC_RATIO = {"qmatvec": 1.002, "decode_mk": 1.002}
 sys.path.insert(0, ROOT)
 
 WORKLOADS = {
@@ -66,6 +67,9 @@ def parse():
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--layers", type=int, default=None,
+                    help="keep only the first N layers: a smaller case of the same kernels "
+                         "for profiler captures (its number is not the workload's)")
     return ap.parse_args()
 
 
@@ -269,6 +273,8 @@ def run_minq(args, world, rank, local):
     arch, prompt_len = WORKLOADS[args.workload]
     prompt_len = args.prompt or prompt_len
     cfg0, qk_norm, tied = synth.ARCH[arch]
+    if args.layers:
+        cfg0 = replace(cfg0, n_layers=args.layers)
     K, W = args.steps, args.warmup
     max_seq = prompt_len + W + 2 * K + 3 * min(K, 16) + 32
     cfg = replace(cfg0, max_seq_len=max_seq)
@@ -431,7 +437,7 @@ def run_minq(args, world, rank, local):
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": f"{args.workload} decode bs=1 after a {prompt_len}-token "
                                    f"prefill (KV length {prompt_len}..{prompt_len + W + K})",
-                       "model": arch, "quant": cfg.dtype, "global_batch": world,
+                       "model": arch, "layers": cfg.n_layers, "quant": cfg.dtype, "global_batch": world,
                        "parallelism": f"replicas x{world}",
                        "cache_flush": "inputs > L2: 3.8 GB of weights streamed per step"
                        if arch == "qwen3-4b" else "inputs > L2",

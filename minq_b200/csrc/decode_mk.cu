@@ -68,20 +68,24 @@ constexpr int kMkThreads = kMkConsumers + 32 * kMkProducers;
 constexpr int kMkSlot = 16384;                 // bytes per ring slot
 constexpr int kMkS = 8;                        // ring slots (a multiple of kMkProducers)
 static_assert(kMkS % kMkProducers == 0, "each producer warp owns its own slots");
-constexpr int kMkCK = 32;                      // blocks per projection chunk (8 groups of 4)
-// Row slots per lane (rows 4k + 2*half + h of a pass): enough for the most
-// rows of each format whose box fits a 16 KB slot (Q4_0: 25 single / 12
-// pairs, Q8_0: 14 single / 7 pairs).
-template <int DT, bool DUAL>
-struct MkAccN {
-  static constexpr int value = DUAL ? (DT == MINQ_Q4_0 ? 3 : 2) : (DT == MINQ_Q4_0 ? 7 : 4);
-};
-__host__ __device__ constexpr int mk_acc(int dt, bool dual) {
-  return dual ? (dt == MINQ_Q4_0 ? 3 : 2) : (dt == MINQ_Q4_0 ? 7 : 4);
-}
+// Projection inputs are staged as exact fixed-point planes: per 32-column
+// block, m = rint(x * 2^(kMkFx - e)) with 2^(e-1) <= max|x| < 2^e, written
+// as kMkNP signed base-256 digits (plane p holds digit p of every column), so
+// that the block dot with the weight codes is a sum of exact integer dp4a
+// products. kMkNP = 4 keeps 31 bits of the block maximum, more than the 24 of
+// an f32 product, so a block whose largest input is 2^7 times its typical one
+// still sees f32-grade inputs.
+constexpr int kMkNP = 4;
+constexpr int kMkFx = 8 * kMkNP - 2;           // |m| <= 2^kMkFx
+// Words of one staged block: 8 * kMkNP plane words (Q4_0: [word j][plane]
+// [low / high nibble columns]; Q8_0: [word j][plane]), then kMkNP Q4_0
+// offset corrections; a multiple of 4 words for 16-byte loads.
+constexpr int kMkRecW = (9 * kMkNP + 3) & ~3;
+// Row slots per consumer thread in one pass (rows (16 k + warp) R + lane / ck).
+constexpr int kMkRS = 2;
 constexpr int kMkMiscOff = 256;                // small reductions and flags
 constexpr int kMkCtaOff = 768;                 // the CTA's plan (MkCta)
-constexpr int kMkRedOff = 1024;                // projection pass reduction 2 x [8][32][2]
+constexpr int kMkRedOff = 1024;                // projection pass reduction 2 x [128][2]
 constexpr int kMkRopeOff = 5120;               // cos | sin of this position's RoPE row
 constexpr int kMkScrOff = 5632;                // x / attention scratch, then the ring
 
@@ -90,38 +94,72 @@ __device__ __forceinline__ float4 ldcg4(const float* p) {
   return __ldcg(reinterpret_cast<const float4*>(p));
 }
 
-// Packed partial dot of one lane's 8 columns of a block (see qmatvec_tma.cu):
-// Q8_0: x of the 8 columns in order; Q4_0: (x_even - x_odd/16, x_odd/16) of
-// the 4 column pairs, with b = lo + 16*hi the raw code byte.
+// 4-way byte dot products with 32-bit accumulate: unsigned codes (Q4_0
+// nibbles times 16) or signed codes (Q8_0) against signed plane digits.
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// Low bytes of four ints packed into one word (a in byte 0).
+__device__ __forceinline__ uint32_t pack_lo_bytes(int a, int b, int c, int d) {
+  const uint32_t ab = __byte_perm((uint32_t)a, (uint32_t)b, 0x0040);
+  const uint32_t cd = __byte_perm((uint32_t)c, (uint32_t)d, 0x0040);
+  return __byte_perm(ab, cd, 0x5410);
+}
+
+// Block dot of one row block (quantize.rs:252-280: sum over the block of
+// code * x, times the scale d) against the staged planes xw of the same
+// columns, before the block's power-of-two input scale: exact integer sums
+// per plane, combined in f32. Q4_0 codes enter as 16 * nibble; the block's
+// -8 offset is the staged correction (-128 * digit sum per plane), which
+// also starts each plane's sum.
 template <int DT>
-__device__ __forceinline__ float2 mk_dot8(uint32_t c0, uint32_t c1, const float4& xa,
-                                          const float4& xb) {
-  float2 a, s;
+__device__ __forceinline__ float mk_block_dot(const unsigned char* blk, const uint32_t (&xw)[kMkRecW]) {
+  const float d = *reinterpret_cast<const float*>(blk);
+  const uint32_t* cw = reinterpret_cast<const uint32_t*>(blk + 4);
+  int s[kMkNP];
   if (DT == MINQ_Q8_0) {
-    const uint32_t w0 = c0 ^ 0x80808080u, w1 = c1 ^ 0x80808080u;
-    const float2 k = make_float2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
-    a = __fadd2_rn(bytes_to_float2(w0, 0, 1), k);
-    s = __fmul2_rn(a, make_float2(xa.x, xa.y));
-    a = __fadd2_rn(bytes_to_float2(w0, 2, 3), k);
-    s = __ffma2_rn(a, make_float2(xa.z, xa.w), s);
-    a = __fadd2_rn(bytes_to_float2(w1, 0, 1), k);
-    s = __ffma2_rn(a, make_float2(xb.x, xb.y), s);
-    a = __fadd2_rn(bytes_to_float2(w1, 2, 3), k);
-    s = __ffma2_rn(a, make_float2(xb.z, xb.w), s);
+#pragma unroll
+    for (int q = 0; q < kMkNP; ++q) s[q] = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t w = cw[j];
+#pragma unroll
+      for (int q = 0; q < kMkNP; ++q) s[q] = dp4a_ss(w, xw[j * kMkNP + q], s[q]);
+    }
   } else {
-    const uint32_t lo = c0 & 0x0F0F0F0Fu;
-    const float2 kl = make_float2(-8388616.0f, -8388616.0f);  // -(2^23 + 8)
-    const float2 kb = make_float2(-8388744.0f, -8388744.0f);  // -(2^23 + 136)
-    a = __fadd2_rn(bytes_to_float2(lo, 0, 1), kl);
-    s = __fmul2_rn(a, make_float2(xa.x, xa.y));
-    a = __fadd2_rn(bytes_to_float2(lo, 2, 3), kl);
-    s = __ffma2_rn(a, make_float2(xa.z, xa.w), s);
-    a = __fadd2_rn(bytes_to_float2(c0, 0, 1), kb);
-    s = __ffma2_rn(a, make_float2(xb.x, xb.y), s);
-    a = __fadd2_rn(bytes_to_float2(c0, 2, 3), kb);
-    s = __ffma2_rn(a, make_float2(xb.z, xb.w), s);
+#pragma unroll
+    for (int q = 0; q < kMkNP; ++q) s[q] = (int)xw[8 * kMkNP + q];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t w = cw[j];
+      const uint32_t hi = w & 0xF0F0F0F0u;          // 16 * high nibbles: odd columns
+      const uint32_t lo = (w << 4) & 0xF0F0F0F0u;   // 16 * low nibbles: even columns
+#pragma unroll
+      for (int q = 0; q < kMkNP; ++q) {
+        s[q] = dp4a_us(lo, xw[j * 2 * kMkNP + 2 * q], s[q]);
+        s[q] = dp4a_us(hi, xw[j * 2 * kMkNP + 2 * q + 1], s[q]);
+      }
+    }
   }
-  return s;
+  // sum_q 256^q s[q] in f32: pairs of planes combine exactly in 32 bits
+  float f;
+  if (kMkNP == 4) {
+    const int hi = s[3] * 256 + s[2], lo = s[1] * 256 + s[0];
+    f = fmaf((float)hi, 65536.0f, (float)lo);
+  } else {
+    f = (float)s[kMkNP - 1];
+#pragma unroll
+    for (int q = kMkNP - 2; q >= 0; --q) f = fmaf(f, 256.0f, (float)s[q]);
+  }
+  return f * d;
 }
 
 // Balanced contiguous share [begin, begin + cnt) of `units` for this CTA.
@@ -207,7 +245,7 @@ __device__ void mk_cta_plan(const MkParams& p, int L, MkCta* c) {
     if (ph == 1) continue;
     const MkMat& m = mk_mat(p, ph);
     c->sh[ph] = mk_mat_share(m);
-    c->tiles[ph] = c->sh[ph].passes * m.nchunks;
+    c->tiles[ph] = c->sh[ph].passes * m.ntiles;
   }
   int kh = 0, t0 = 0, t1 = 0;
   bool last = false;
@@ -261,12 +299,6 @@ __device__ bool mk_wait_empty(const MkParams& p, const MkFeed& f, int it) {
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-// Producer: copy the next tile into its slot with the warp's 32 lanes, then
-// have the slot's full barrier track the copies (cp.async.mbarrier.arrive).
-// Projection tiles: lane l copies 16-byte pieces l, l + 32, ... of each row
-// chunk (40 pieces for Q4_0, 72 for Q8_0), the up rows of the gate/up phase
-// after the gate rows. Attention tiles: pieces l, l + 32, ... of K and of V.
-// Returns false when every tile is issued (or on abort).
 // Advance the iterator past phases without tiles; false past the last layer.
 __device__ __forceinline__ bool mk_feed_settle(const MkParams& p, MkFeed& f, const MkCta* cta) {
   while (f.li < p.n_layers && f.idx >= cta->tiles[f.ph]) {
@@ -284,7 +316,7 @@ __device__ __forceinline__ bool mk_feed_settle(const MkParams& p, MkFeed& f, con
 
 // Step the iterator over one tile without copying it.
 __device__ __forceinline__ void mk_feed_skip(const MkParams& p, MkFeed& f, const MkCta* cta) {
-  if (f.ph != 1 && ++f.c == mk_mat(p, f.ph).nchunks) {
+  if (f.ph != 1 && ++f.c == mk_mat(p, f.ph).ntiles) {
     f.c = 0;
     if (++f.j < cta->sh[f.ph].passes) mk_feed_pass(f, cta->sh[f.ph]);
   }
@@ -295,14 +327,13 @@ __device__ __forceinline__ void mk_feed_skip(const MkParams& p, MkFeed& f, const
 // Producer warp: copy the current tile into its slot with the warp's 32
 // lanes, then have the slot's full barrier track the copies
 // (cp.async.mbarrier.arrive). Projection tiles: the rows x 16-byte pieces of
-// the row chunk (40 pieces for Q4_0, 72 for Q8_0) flattened over the lanes,
+// the row chunk (ck blocks: 1.25 ck pieces for Q4_0, 2.25 ck for Q8_0)
+// flattened over the lanes,
 // the up rows of the gate/up phase after the gate rows. Attention tiles: the
 // pieces of K and of V. False on abort.
 template <int DT>
 __device__ bool mk_issue(const MkParams& p, MkFeed& f, const MkCta* cta, int L) {
   constexpr int BB = DT == MINQ_Q8_0 ? kQ8Bytes : kQ4Bytes;
-  constexpr int PITCH = kMkCK * BB;
-  constexpr int PPR = PITCH / 16;  // pieces of a full row chunk
   const int lane = threadIdx.x & 31;
   if (!mk_wait_empty(p, f, f.issued)) return false;
   const int slot = f.issued % kMkS;
@@ -313,9 +344,13 @@ __device__ bool mk_issue(const MkParams& p, MkFeed& f, const MkCta* cta, int L) 
     const int p0 = (cta->t0 + f.idx) * tp, np = min(tp, L - p0);
     const size_t off = (size_t)f.li * p.cache_layer_stride + (size_t)cta->kh * p.max_seq * hd +
                        (size_t)p0 * hd;
-    const int pieces = np * hd / 4;  // 16-byte pieces of K (and of V)
+    // K row r's 16-byte chunk c lands at chunk c ^ (r mod 16) of the row (16
+    // <= the chunks per row), so the consumer's lane r reads chunk c of its
+    // row where every lane reads chunk c of q without a bank conflict
+    const int nch = hd / 4, pieces = np * nch;  // 16-byte pieces of K (and of V)
     for (int i = lane; i < pieces; i += 32) {
-      cp_async16(dst + i * 16, p.kc + off + i * 4);
+      const int r = i / nch, c = i - r * nch;
+      cp_async16(dst + (r * nch + (c ^ (r & 15))) * 16, p.kc + off + i * 4);
       cp_async16(dst + tp * hd * 4 + i * 16, p.vc + off + i * 4);
     }
   } else {
@@ -323,16 +358,17 @@ __device__ bool mk_issue(const MkParams& p, MkFeed& f, const MkCta* cta, int L) 
     const MkMat& m = mk_mat(p, f.ph);
     const uint8_t* w0 = f.ph == 0 ? lp.w_qkv : f.ph == 2 ? lp.w_o : dual ? lp.w_gate : lp.w_down;
     const int nb = m.cols / kBlock;
-    const int ppr = min(kMkCK, nb - f.c * kMkCK) * BB / 16;  // pieces per row (nb % 4 == 0)
     const size_t row_bytes = (size_t)nb * BB;
-    const size_t first = (size_t)(cta->sh[f.ph].rb + f.pr0) * row_bytes + (size_t)f.c * PITCH;
-    const int n = f.n, total = (dual ? 2 : 1) * n * ppr;
+    const size_t first = (size_t)(cta->sh[f.ph].rb + f.pr0) * row_bytes + (size_t)f.c * m.tb * BB;
+    const int ppr = min(m.tb, nb - f.c * m.tb) * BB / 16;  // pieces per tile row
+    const uint32_t magic = ((1u << 20) + ppr - 1) / ppr;    // i / ppr == (i * magic) >> 20, i < 2^14
+    const int pitch = m.pitch, n = f.n, total = (dual ? 2 : 1) * n * ppr;
     for (int i = lane; i < total; i += 32) {
-      const int r = ppr == PPR ? i / PPR : i / ppr;  // constant divisor for full chunks
+      const int r = (int)(((uint32_t)i * magic) >> 20);
       const int pc = i - r * ppr;
       const bool up = dual && r >= n;
       const int row = up ? r - n : r;
-      cp_async16(dst + (up ? m.up_off : 0) + row * PITCH + pc * 16,
+      cp_async16(dst + (up ? m.up_off : 0) + row * pitch + pc * 16,
                  (up ? lp.w_up : w0) + first + (size_t)row * row_bytes + pc * 16);
     }
   }
@@ -421,22 +457,73 @@ __device__ bool mk_grid_sync(const MkParams& p, unsigned long long target, int* 
   return *reinterpret_cast<volatile int*>(flag) != 0;
 }
 
-// Stage the phase input in shared memory: xs = src (n floats, n % 8 == 0),
-// times rmsnorm(src) * gain when gain is set (tensor.rs:219-227), in the
-// Q4_0 pair layout when q4. Each thread transforms the groups of 8 it loaded
-// itself, so only the sum of squares needs a block-wide step.
+// Stage the lm_head input in shared memory: xs = rmsnorm(src) * gain
+// (tensor.rs:219-227), n floats, n % 8 == 0.
 __device__ void mk_stage_x(const MkParams& p, float* xs, const float* src, int n,
-                           const float* gain, bool q4, float* misc) {
+                           const float* gain, float* misc) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int ng = n >> 3;
   float4* xs4 = reinterpret_cast<float4*>(xs);
+  float ss = 0.0f;
+  for (int gi = tid; gi < ng; gi += kMkConsumers) {
+    const float4 a = ldcg4(src + 8 * gi), b = ldcg4(src + 8 * gi + 4);
+    xs4[2 * gi] = a;
+    xs4[2 * gi + 1] = b;
+    ss = fmaf(a.x, a.x, ss);
+    ss = fmaf(a.y, a.y, ss);
+    ss = fmaf(a.z, a.z, ss);
+    ss = fmaf(a.w, a.w, ss);
+    ss = fmaf(b.x, b.x, ss);
+    ss = fmaf(b.y, b.y, ss);
+    ss = fmaf(b.z, b.z, ss);
+    ss = fmaf(b.w, b.w, ss);
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) misc[warp] = ss;
+  mk_sync();
+  float v = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kMkCW; ++w) v += misc[w];
+  const float inv = 1.0f / sqrtf(v / (float)n + p.eps);
+  const float4* g4 = reinterpret_cast<const float4*>(gain);
+  for (int gi = tid; gi < ng; gi += kMkConsumers) {
+    float4 a = xs4[2 * gi], b = xs4[2 * gi + 1];
+    const float4 ga = g4[2 * gi], gb = g4[2 * gi + 1];
+    a.x = a.x * inv * ga.x; a.y = a.y * inv * ga.y; a.z = a.z * inv * ga.z; a.w = a.w * inv * ga.w;
+    b.x = b.x * inv * gb.x; b.y = b.y * inv * gb.y; b.z = b.z * inv * gb.z; b.w = b.w * inv * gb.w;
+    xs4[2 * gi] = a;
+    xs4[2 * gi + 1] = b;
+  }
+  mk_sync();
+}
+
+// Stage a projection input as fixed-point planes: v = src (n floats, n % 32
+// == 0), times rmsnorm(src) * gain when gain is set (tensor.rs:219-227, the
+// same f32 operations as the reference), then per 32-column block b:
+// e = exponent of max|v| (2^(e-1) <= max < 2^e), m = rint(v * 2^(kMkFx - e))
+// (|m| <= 2^kMkFx), split into kMkNP signed base-256 digits
+// (m = sum_q 256^q d_q, d_q in [-128, 127]). xp gets kMkRecW words per block
+// (see mk_block_dot for their order) and xsb the block's scale 2^(e - kMkFx)
+// (over 16 for Q4_0, whose codes enter as 16 * nibble). Thread t stages the 8
+// columns 8 (t mod 4) .. + 7 of block t / 4, so the four threads of a block
+// are adjacent lanes.
+template <int DT>
+__device__ void mk_stage_planes(const MkParams& p, uint32_t* xp, float* xsb, const float* src,
+                                int n, const float* gain, float* misc) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ng = n >> 3;
+  const float4 zero = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  float4 a0 = zero, b0 = zero;  // group tid, loaded once
+  if (tid < ng) {
+    a0 = ldcg4(src + 8 * tid);
+    b0 = ldcg4(src + 8 * tid + 4);
+  }
   float inv = 1.0f;
   if (gain) {
     float ss = 0.0f;
     for (int gi = tid; gi < ng; gi += kMkConsumers) {
-      const float4 a = ldcg4(src + 8 * gi), b = ldcg4(src + 8 * gi + 4);
-      xs4[2 * gi] = a;
-      xs4[2 * gi + 1] = b;
+      const float4 a = gi == tid ? a0 : ldcg4(src + 8 * gi);
+      const float4 b = gi == tid ? b0 : ldcg4(src + 8 * gi + 4);
       ss = fmaf(a.x, a.x, ss);
       ss = fmaf(a.y, a.y, ss);
       ss = fmaf(a.z, a.z, ss);
@@ -455,123 +542,140 @@ __device__ void mk_stage_x(const MkParams& p, float* xs, const float* src, int n
     inv = 1.0f / sqrtf(v / (float)n + p.eps);
   }
   const float4* g4 = reinterpret_cast<const float4*>(gain);
-  for (int gi = tid; gi < ng; gi += kMkConsumers) {
-    float4 a, b;
-    if (gain) {
-      a = xs4[2 * gi];
-      b = xs4[2 * gi + 1];
+  for (int base = 0; base < ng; base += kMkConsumers) {  // every lane runs every round
+    const int gi = base + tid;
+    const bool act = gi < ng;
+    float4 a = a0, b = b0;
+    if (base > 0) {
+      a = act ? ldcg4(src + 8 * gi) : zero;
+      b = act ? ldcg4(src + 8 * gi + 4) : zero;
+    }
+    if (gain && act) {
       const float4 ga = g4[2 * gi], gb = g4[2 * gi + 1];
       a.x = a.x * inv * ga.x; a.y = a.y * inv * ga.y; a.z = a.z * inv * ga.z; a.w = a.w * inv * ga.w;
       b.x = b.x * inv * gb.x; b.y = b.y * inv * gb.y; b.z = b.z * inv * gb.z; b.w = b.w * inv * gb.w;
-    } else {
-      a = ldcg4(src + 8 * gi);
-      b = ldcg4(src + 8 * gi + 4);
     }
-    if (q4) {
-      const float o0 = a.y * 0.0625f, o1 = a.w * 0.0625f, o2 = b.y * 0.0625f,
-                  o3 = b.w * 0.0625f;
-      xs4[2 * gi] = make_float4(a.x - o0, a.z - o1, b.x - o2, b.z - o3);
-      xs4[2 * gi + 1] = make_float4(o0, o1, o2, o3);
-    } else {
-      xs4[2 * gi] = a;
-      xs4[2 * gi + 1] = b;
+    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    float mx = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(v[i]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    // e from the exponent field; tiny blocks (< 2^-91) clamp to e = -90
+    const int e = max((int)((__float_as_uint(mx) >> 23) & 0xFFu) - 126, -90);
+    const float scale = __uint_as_float((uint32_t)(127 + kMkFx - e) << 23);  // 2^(kMkFx - e)
+    int r[kMkNP][8];   // r[0] = m, r[q+1] = floor((r[q] + 128) / 256); digit q = low byte of r[q]
+    int dsum[kMkNP];   // sum of the digits d_q = r[q] - 256 r[q+1] (last: r[q])
+#pragma unroll
+    for (int q = 0; q < kMkNP; ++q) dsum[q] = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      r[0][i] = __float2int_rn(v[i] * scale);
+#pragma unroll
+      for (int q = 1; q < kMkNP; ++q) r[q][i] = (r[q - 1][i] + 128) >> 8;
+#pragma unroll
+      for (int q = 0; q < kMkNP; ++q)
+        dsum[q] += q + 1 < kMkNP ? r[q][i] - 256 * r[q + 1][i] : r[q][i];
+    }
+    uint32_t w[2 * kMkNP];
+#pragma unroll
+    for (int q = 0; q < kMkNP; ++q) {
+      if (DT == MINQ_Q4_0) {  // word j = t mod 4: even columns (low nibbles), odd (high)
+        w[2 * q] = pack_lo_bytes(r[q][0], r[q][2], r[q][4], r[q][6]);
+        w[2 * q + 1] = pack_lo_bytes(r[q][1], r[q][3], r[q][5], r[q][7]);
+      } else {                // words 2 (t mod 4) and 2 (t mod 4) + 1, plane-minor
+        w[q] = pack_lo_bytes(r[q][0], r[q][1], r[q][2], r[q][3]);
+        w[kMkNP + q] = pack_lo_bytes(r[q][4], r[q][5], r[q][6], r[q][7]);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < kMkNP; ++q) {
+      dsum[q] += __shfl_xor_sync(0xffffffffu, dsum[q], 1);
+      dsum[q] += __shfl_xor_sync(0xffffffffu, dsum[q], 2);
+    }
+    if (act) {
+      uint32_t* rec = xp + (size_t)(gi >> 2) * kMkRecW;
+      uint2* dst = reinterpret_cast<uint2*>(rec + (gi & 3) * 2 * kMkNP);
+#pragma unroll
+      for (int q = 0; q < kMkNP; ++q) dst[q] = make_uint2(w[2 * q], w[2 * q + 1]);
+      if ((gi & 3) == 0) {
+#pragma unroll
+        for (int q = 0; q < kMkNP; ++q)
+          rec[8 * kMkNP + q] = DT == MINQ_Q4_0 ? (uint32_t)(-128 * dsum[q]) : 0u;
+        xsb[gi >> 2] = __uint_as_float((uint32_t)(127 + e - kMkFx - (DT == MINQ_Q4_0 ? 4 : 0)) << 23);
+      }
     }
   }
   mk_sync();
 }
 
-// One projection phase. epi(row, v0, v1) gets the finished row (v1 = up for
-// the dual gate/up form).
+// One projection phase. A pass of n rows is 2n "virtual rows" for the dual
+// gate/up form (gate rows, then up rows at m.up_off in the slot). Thread
+// (warp w, lane l) takes the virtual rows (16 k + w) R + l / ck (R = 32 / ck,
+// k < kMkRS) and in every tile the blocks b, b + ck, ... (b = l mod ck) of
+// them, accumulating its block dots in registers over the pass; a pass ends
+// with a reduction over the ck lanes of each row and epi(row, v0, v1) (v1 =
+// up for the dual form) on the finished rows.
 template <int DT, bool DUAL, class Epi>
-__device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const float* xs, MkFeed& f,
-                               const MkCta* cta, int L, float* red, int& it, Epi epi) {
+__device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const uint32_t* xp,
+                               const float* xsb, MkFeed& f, const MkCta* cta, int L, float* red,
+                               int& it, Epi epi) {
   constexpr int BB = DT == MINQ_Q8_0 ? kQ8Bytes : kQ4Bytes;
-  constexpr int PITCH = kMkCK * BB;
-  constexpr int kMkAcc = MkAccN<DT, DUAL>::value;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int grp = warp & 7, rs = warp >> 3;
-  const int h = lane >> 4, bi = (lane >> 2) & 3, sub = lane & 3;
-  const int nb = m.cols / kBlock;
+  const int ck = m.ck, pitch = m.pitch, nb = m.cols / kBlock;
+  const int R = 32 / ck, rr = lane / ck, bl = lane - rr * ck;
   int rb, cnt;
   mk_share(m.rows, &rb, &cnt);
   const int passes = (cnt + m.nr - 1) / m.nr;
   for (int j = 0; j < passes; ++j) {
     const int pr0 = (int)(((long long)cnt * j) / passes);
     const int n = (int)(((long long)cnt * (j + 1)) / passes) - pr0;
-    float acc[kMkAcc], acc1[DUAL ? kMkAcc : 1];
+    const int nv = DUAL ? 2 * n : n;
+    int off[kMkRS];  // slot offset of each row slot's row (-1: none)
 #pragma unroll
-    for (int k = 0; k < kMkAcc; ++k) {
-      acc[k] = 0.0f;
-      if (DUAL) acc1[k] = 0.0f;
+    for (int k = 0; k < kMkRS; ++k) {
+      const int v = (16 * k + warp) * R + rr;
+      const bool up = DUAL && v >= n;
+      off[k] = v < nv ? (up ? m.up_off : 0) + (up ? v - n : v) * pitch + bl * BB : -1;
     }
-    for (int c = 0; c < m.nchunks; ++c, ++it) {
+    float acc[kMkRS];
+#pragma unroll
+    for (int k = 0; k < kMkRS; ++k) acc[k] = 0.0f;
+    for (int c = 0; c < m.ntiles; ++c, ++it) {
       const unsigned char* tile = mk_next_tile(p, f, it);
-      if (c * kMkCK + 4 * grp < nb) {  // nb % 4 == 0: the group is whole or absent
-        const int bl = 4 * grp + bi;
-        const int bg = c * kMkCK + bl;
-        const float4 xa = *reinterpret_cast<const float4*>(xs + 32 * bg + 8 * sub);
-        const float4 xb = *reinterpret_cast<const float4*>(xs + 32 * bg + 8 * sub + 4);
-        const unsigned char* bp = tile + (size_t)(2 * rs + h) * PITCH + bl * BB;
-        // all of the lane's code words and scales first (rows past the pass
-        // read nothing and count as zero), then the arithmetic: the loads of
-        // every row slot are in flight together
-        constexpr int NW = DT == MINQ_Q8_0 ? 2 : 1;
-        constexpr int NM = DUAL ? 2 : 1;
-        uint32_t cw[kMkAcc][NM][NW];
-        float dd[kMkAcc][NM];
+      const int g0 = c * m.tb, nbk = min(m.tb, nb - g0);
+      for (int u = off[0] >= 0 ? bl : nbk; u < nbk; u += ck) {  // this lane's blocks, if it has rows
+        const int g = g0 + u;
+        uint32_t xw[kMkRecW];
+        const uint4* rec = reinterpret_cast<const uint4*>(xp + (size_t)g * kMkRecW);
 #pragma unroll
-        for (int k = 0; k < kMkAcc; ++k) {
-          const bool ok = 4 * k + 2 * rs + h < n;
-#pragma unroll
-          for (int mm = 0; mm < NM; ++mm) {
-            const unsigned char* blk = bp + (size_t)(4 * k) * PITCH + (mm ? m.up_off : 0);
-            const uint32_t* wp = reinterpret_cast<const uint32_t*>(blk + 4 + 4 * NW * sub);
-            dd[k][mm] = ok ? *reinterpret_cast<const float*>(blk) : 0.0f;
-#pragma unroll
-            for (int w = 0; w < NW; ++w) cw[k][mm][w] = ok ? wp[w] : 0u;
-          }
+        for (int i = 0; i < kMkRecW / 4; ++i) {
+          const uint4 v = rec[i];
+          xw[4 * i] = v.x;
+          xw[4 * i + 1] = v.y;
+          xw[4 * i + 2] = v.z;
+          xw[4 * i + 3] = v.w;
         }
+        const float sb = xsb[g];
+        const unsigned char* tb_ = tile + (u - bl) * BB;
 #pragma unroll
-        for (int k = 0; k < kMkAcc; ++k) {
-          const float2 part = mk_dot8<DT>(cw[k][0][0], NW == 2 ? cw[k][0][NW - 1] : 0u, xa, xb);
-          acc[k] = fmaf(dd[k][0], part.x + part.y, acc[k]);
-          if (DUAL) {
-            const float2 part1 =
-                mk_dot8<DT>(cw[k][NM - 1][0], NW == 2 ? cw[k][NM - 1][NW - 1] : 0u, xa, xb);
-            acc1[k] = fmaf(dd[k][NM - 1], part1.x + part1.y, acc1[k]);
-          }
-        }
+        for (int k = 0; k < kMkRS; ++k)
+          if (off[k] >= 0) acc[k] = fmaf(mk_block_dot<DT>(tb_ + off[k], xw), sb, acc[k]);
       }
       mk_release(f, it);
     }
-    // sum over the 16 lanes of each half (4 blocks x 4 column slices), then
-    // over the 8 groups in a fixed order; passes alternate between two
-    // buffers so one barrier per pass suffices
-    float* rb_ = red + (j & 1) * 512;
+    // virtual rows -> red[row][half] (two buffers, alternating by pass, so
+    // one barrier a pass)
+    float* rb_ = red + (j & 1) * 256;
 #pragma unroll
-    for (int k = 0; k < kMkAcc; ++k) {
-      float v = acc[k], v1 = DUAL ? acc1[k] : 0.0f;
-#pragma unroll
-      for (int o = 1; o < 16; o <<= 1) {
-        v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (DUAL) v1 += __shfl_xor_sync(0xffffffffu, v1, o);
-      }
-      const int row = 4 * k + 2 * rs + h;
-      if ((lane & 15) == 0) {
-        rb_[(grp * 32 + row) * 2] = v;
-        if (DUAL) rb_[(grp * 32 + row) * 2 + 1] = v1;
-      }
+    for (int k = 0; k < kMkRS; ++k) {
+      float v = acc[k];
+      for (int o = ck >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      const int vr = (16 * k + warp) * R + rr;
+      if (bl == 0 && vr < nv) rb_[DUAL && vr >= n ? (vr - n) * 2 + 1 : vr * 2] = v;
     }
     mk_sync();
-    if (tid < n) {
-      float v0 = 0.0f, v1 = 0.0f;
-#pragma unroll
-      for (int g = 0; g < 8; ++g) {
-        v0 += rb_[(g * 32 + tid) * 2];
-        if (DUAL) v1 += rb_[(g * 32 + tid) * 2 + 1];
-      }
-      epi(rb + pr0 + tid, v0, v1);
-    }
+    for (int t = tid; t < n; t += kMkConsumers) epi(rb + pr0 + t, rb_[t * 2], rb_[t * 2 + 1]);
   }
 }
 
@@ -620,250 +724,254 @@ __device__ void mk_head_prep(const MkParams& p, const float* src, const float* g
   }
 }
 
-// Shared-memory layout of the attention phase (in the scratch region).
-struct MkAttnSmem {
-  float* qs;    // [G][hd]   RoPE'd (and normed) query heads
-  float* knew;  // [hd]      the new position's key (last split)
-  float* vnew;  // [hd]
-  float* sc;    // [G][32]   scores of the tile
-  float* pp;    // [G][32]   softmax numerators of the tile
-  float* corr;  // [G]       rescale of the running output
-};
-
-// One step of attend (model.rs:223-248: s = q.k / sqrt(hd), softmax over
-// positions, o = sum p v) over up to 32 positions held in shared memory:
-// positions j < base1 are rows j of (k0, v0) (j < n0), positions j >= base1
-// rows j - base1 of (k1, v1) (j - base1 < n1). As an online softmax: (A)
-// warp w scores positions w and w + 16 for every head, (B) warp g < G
-// updates head g's running max m and sum l and forms the numerators, (C)
-// every thread rescales and accumulates its outputs (head, dim) =
-// (idx / hd, idx % hd) for idx = tid, tid + 512. m, l live in warp g's lanes
-// (replicated); o in the owning thread.
+// One tile of the online softmax of every query head of the kv head, run by
+// one warp (model.rs:223-248: s = q.k / sqrt(hd), softmax over positions,
+// o = sum p v). Scores: lane (h, j) = (lane / TP, lane mod TP) takes position
+// j of the tile for the heads g = h, h + HS, ... (HS = 32 / TP lanes per
+// position), reading K row j in the producer's swizzled chunk order while
+// every lane reads the same chunk of q. The running max m[g] and sum l[g]
+// are replicated in all lanes; lane l owns output dims DPL l .. DPL l + DPL - 1
+// of every head. Ks points at the swizzled K rows (or, with swz = false, at
+// plain rows: the new position).
 template <int DPL, int GM>
-__device__ void mk_attn_step(const MkParams& p, const MkAttnSmem& a, const float (&q)[GM][DPL],
-                             const float* k0, const float* v0, int n0, const float* k1,
-                             const float* v1, int n1, int base1, float& m, float& l,
-                             float (&o)[2]) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int G = p.G, hd = p.hd;
-  // (A) scores
-  float sv[2][GM];
+__device__ __forceinline__ void mk_attn_tile(const float* qs, int G, const float* Ks, bool swz,
+                                             const float* V, int np, float scale, float (&m)[GM],
+                                             float (&l)[GM], float (&o)[GM][DPL]) {
+  constexpr int HD = 32 * DPL, NCH = HD / 4, TP = 2048 / HD, HS = 32 / TP, GL = (GM + HS - 1) / HS;
+  const int lane = threadIdx.x & 31, h = lane / TP, j = lane - h * TP;
+  float s[GL];
 #pragma unroll
-  for (int rep = 0; rep < 2; ++rep) {
-    const int j = warp + 16 * rep;
-    const bool t1 = j >= base1;
-    const int r = t1 ? j - base1 : j;
-    const bool ok = r < (t1 ? n1 : n0);
-    const float* kr = (t1 ? k1 : k0) + (ok ? r : 0) * hd;
-    float kv[DPL];
+  for (int k = 0; k < GL; ++k) s[k] = 0.0f;
+  if (j < np) {
+    const float* kr = Ks + j * HD;
+    const int sw = swz ? (j & 15) : 0;  // the producer's K chunk swizzle
+    float a[GL][4];  // four independent partial sums per head
 #pragma unroll
-    for (int e = 0; e < DPL; ++e) kv[e] = ok ? kr[DPL * lane + e] : 0.0f;
+    for (int k = 0; k < GL; ++k) a[k][0] = a[k][1] = a[k][2] = a[k][3] = 0.0f;
+#pragma unroll 4
+    for (int c = 0; c < NCH; ++c) {
+      const float4 kv = *reinterpret_cast<const float4*>(kr + 4 * (c ^ sw));
+#pragma unroll
+      for (int k = 0; k < GL; ++k) {
+        if (h + HS * k < G) {
+          const float4 qv = *reinterpret_cast<const float4*>(qs + (h + HS * k) * HD + 4 * c);
+          a[k][0] = fmaf(qv.x, kv.x, a[k][0]);
+          a[k][1] = fmaf(qv.y, kv.y, a[k][1]);
+          a[k][2] = fmaf(qv.z, kv.z, a[k][2]);
+          a[k][3] = fmaf(qv.w, kv.w, a[k][3]);
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < GL; ++k) s[k] = (a[k][0] + a[k][1]) + (a[k][2] + a[k][3]);
+  }
+  // per head: tile max and sum over the TP lanes of its half, new running
+  // max, rescale of the running sums and outputs, numerators p
+  float pr[GL];
+#pragma unroll
+  for (int k = 0; k < GL; ++k) {
+    const float sv = j < np ? s[k] * scale : -INFINITY;
+    float mt = sv;
+#pragma unroll
+    for (int o_ = TP / 2; o_ > 0; o_ >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o_));
+    s[k] = sv;
+    pr[k] = mt;  // tile max of head h + HS k (finite: np >= 1)
+  }
+#pragma unroll
+  for (int g = 0; g < GM; ++g) {
+    if (g < G) {
+      const float mt = __shfl_sync(0xffffffffu, pr[g / HS], (g % HS) * TP);
+      const float mn = fmaxf(m[g], mt);
+      const float c = m[g] == -INFINITY ? 0.0f : expf(m[g] - mn);
+      m[g] = mn;
+      l[g] *= c;
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) o[g][e] *= c;
+    }
+  }
+  // numerators with each lane's own head max, and their sums
+#pragma unroll
+  for (int k = 0; k < GL; ++k) {
+    float mk = -INFINITY;
+#pragma unroll
+    for (int g = 0; g < GM; ++g)
+      if (g / HS == k && g % HS == h) mk = m[g];
+    const bool valid = h + HS * k < G && s[k] != -INFINITY;
+    const float e = valid ? expf(s[k] - mk) : 0.0f;
+    float sum = e;
+#pragma unroll
+    for (int o_ = TP / 2; o_ > 0; o_ >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o_);
+    pr[k] = e;
+    s[k] = sum;  // this tile's sum of numerators for head h + HS k
+  }
+#pragma unroll
+  for (int g = 0; g < GM; ++g)
+    if (g < G) l[g] += __shfl_sync(0xffffffffu, s[g / HS], (g % HS) * TP);
+#pragma unroll 4
+  for (int jj = 0; jj < np; ++jj) {
+    const float* vr = V + jj * HD + DPL * lane;
+    float v[DPL];
+    if (DPL == 4) {
+      const float4 v4 = *reinterpret_cast<const float4*>(vr);
+      v[0] = v4.x;
+      v[1] = v4.y;
+      v[2] = v4.z;
+      v[3] = v4.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) v[e] = vr[e];
+    }
 #pragma unroll
     for (int g = 0; g < GM; ++g) {
-      sv[rep][g] = 0.0f;
+      if (g < G) {
+        const float pj = __shfl_sync(0xffffffffu, pr[g / HS], (g % HS) * TP + jj);
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) sv[rep][g] = fmaf(q[g][e], kv[e], sv[rep][g]);
-    }
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-    for (int rep = 0; rep < 2; ++rep)
-#pragma unroll
-      for (int g = 0; g < GM; ++g) sv[rep][g] += __shfl_xor_sync(0xffffffffu, sv[rep][g], off);
-  if (lane < GM && lane < G) {
-#pragma unroll
-    for (int rep = 0; rep < 2; ++rep) {
-      float v = sv[rep][0];
-#pragma unroll
-      for (int g = 1; g < GM; ++g) v = lane == g ? sv[rep][g] : v;
-      a.sc[lane * 32 + warp + 16 * rep] = v * p.scale;
-    }
-  }
-  mk_sync();
-  // (B) online softmax per head
-  if (warp < G) {
-    const bool t1 = lane >= base1;
-    const bool ok = (t1 ? lane - base1 : lane) < (t1 ? n1 : n0);
-    const float s_ = ok ? a.sc[warp * 32 + lane] : -INFINITY;
-    const float mt = warp_max(s_);
-    const float mn = fmaxf(m, mt);
-    const float c = m == -INFINITY ? 0.0f : expf(m - mn);
-    const float pr = s_ == -INFINITY ? 0.0f : expf(s_ - mn);
-    l = fmaf(l, c, warp_sum(pr));
-    m = mn;
-    a.pp[warp * 32 + lane] = pr;
-    if (lane == 0) a.corr[warp] = c;
-  }
-  mk_sync();
-  // (C) o = o * corr + sum_j p_j v_j
-#pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int idx = tid + kMkConsumers * u;
-    if (idx < G * hd) {
-      const int g = idx / hd, d = idx - g * hd;
-      const float* pg = a.pp + g * 32;
-      const float* va = v0 + d;
-      const float* vb = v1 + d;
-      float acc = o[u] * a.corr[g], acc2 = 0.0f;
-      int j = 0;
-#pragma unroll 4
-      for (; j + 1 < n0; j += 2) {
-        acc = fmaf(pg[j], va[j * hd], acc);
-        acc2 = fmaf(pg[j + 1], va[(j + 1) * hd], acc2);
+        for (int e = 0; e < DPL; ++e) o[g][e] = fmaf(pj, v[e], o[g][e]);
       }
-      if (j < n0) acc = fmaf(pg[j], va[j * hd], acc);
-      pg += base1;
-#pragma unroll 4
-      for (j = 0; j + 1 < n1; j += 2) {
-        acc = fmaf(pg[j], vb[j * hd], acc);
-        acc2 = fmaf(pg[j + 1], vb[(j + 1) * hd], acc2);
-      }
-      if (j < n1) acc = fmaf(pg[j], vb[j * hd], acc);
-      o[u] = acc + acc2;
     }
   }
 }
 
-template <int DT, int DPL, int GM>
+// Attention phase of one CTA: kv head kh, history tiles [t0, t1) of TP
+// positions (swizzled K rows, then V rows, in the slot) and, in the head's
+// last split, the new position. The query heads form HG = ceil(G / 2) pairs;
+// warp w serves pair w mod HG on the tiles t0 + w / HG, t0 + w / HG + 16 / HG,
+// ... (every warp still waits for and releases every tile in order), the new
+// position going to the warps next in that order; the warp states then merge
+// into this split's partial (o, m, l) per head. The last split of the
+// head to arrive (a counter per head) merges all of the head's split
+// partials into the attention output; the others go on to the grid barrier.
+template <int DT, int DPL>
 __device__ void mk_consume_attn(const MkParams& p, int li, int L, float* scr, MkFeed& f,
                                 const MkCta* cta, const float* rope_cs, int* misc_i, int& it) {
   int kh, t0, t1;
   bool last;
   if (!mk_attn_item(p, L, &kh, &t0, &t1, &last)) return;
+  constexpr int HD = 32 * DPL, TP = 2048 / HD;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int G = p.G, hd = p.hd, tp = 2048 / hd;
-  MkAttnSmem a;
-  a.qs = scr;
-  a.knew = a.qs + G * hd;
-  a.vnew = a.knew + hd;
-  a.sc = a.vnew + hd;
-  a.pp = a.sc + 32 * G;
-  a.corr = a.pp + 32 * G;
+  constexpr int HPW = 2;  // query heads per warp
+  const int G = p.G, HG = (G + HPW - 1) / HPW, WPG = kMkCW / HG;
+  const int g0 = (warp % HG) * HPW, gw = min(HPW, G - g0), slot = warp / HG;
+  const bool served = warp < HG * WPG;
+  float* qs = scr;                     // [G][hd] RoPE'd (and normed) query heads
+  float* knew = qs + G * HD;           // [hd] the new position's key (last split)
+  float* vnew = knew + HD;             // [hd]
+  float* wst = vnew + HD;              // [16][HPW][hd + 2] per-warp o, m, l
+  float* fw = wst + kMkCW * HPW * (HD + 2);  // merge: [ns][G] (max, sum), then weights
   const MkLayerPtrs& lp = p.layers[li];
-  const size_t head_off = (size_t)li * p.cache_layer_stride + (size_t)kh * p.max_seq * hd;
+  const size_t head_off = (size_t)li * p.cache_layer_stride + (size_t)kh * p.max_seq * HD;
   // q heads (q_norm, RoPE at position L); the last split also builds the new
   // k (k_norm, RoPE) and v and appends them to the cache
   if (warp < G) {
-    mk_head_prep(p, p.qkv_out + (size_t)(kh * G + warp) * hd, lp.q_norm, true, rope_cs,
-                 a.qs + warp * hd);
+    mk_head_prep(p, p.qkv_out + (size_t)(kh * G + warp) * HD, lp.q_norm, true, rope_cs,
+                 qs + warp * HD);
   } else if (last && warp == G) {
-    mk_head_prep(p, p.qkv_out + p.qd + (size_t)kh * hd, lp.k_norm, true, rope_cs, a.knew);
+    mk_head_prep(p, p.qkv_out + p.qd + (size_t)kh * HD, lp.k_norm, true, rope_cs, knew);
     __syncwarp();
-    for (int i = lane; i < hd; i += 32) p.kc[head_off + (size_t)L * hd + i] = a.knew[i];
+    for (int i = lane; i < HD; i += 32) p.kc[head_off + (size_t)L * HD + i] = knew[i];
   } else if (last && warp == G + 1) {
-    for (int i = lane; i < hd; i += 32) {
-      const float v = ldcg(p.qkv_out + p.qd + p.kvd + (size_t)kh * hd + i);
-      a.vnew[i] = v;
-      p.vc[head_off + (size_t)L * hd + i] = v;
+    for (int i = lane; i < HD; i += 32) {
+      const float v = ldcg(p.qkv_out + p.qd + p.kvd + (size_t)kh * HD + i);
+      vnew[i] = v;
+      p.vc[head_off + (size_t)L * HD + i] = v;
     }
   }
   mk_sync();
-  float q[GM][DPL];
+  float m[HPW], l[HPW], o[HPW][DPL];
 #pragma unroll
-  for (int g = 0; g < GM; ++g)
+  for (int g = 0; g < HPW; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.0f;
 #pragma unroll
-    for (int e = 0; e < DPL; ++e) q[g][e] = g < G ? a.qs[g * hd + DPL * lane + e] : 0.0f;
-  float m = -INFINITY, l = 0.0f, o[2] = {0.0f, 0.0f};
-  // two 16-position tiles per step for head_dim 128, one 32-position tile for 64
-  const int per_step = 32 / tp;
-  for (int t = t0; t < t1; t += per_step) {
-    const float* ka = reinterpret_cast<const float*>(mk_next_tile(p, f, it));
-    const int na = min(tp, L - t * tp);
-    const float* kb = ka;
-    int nb_ = 0;
-    if (per_step == 2 && t + 1 < t1) {
-      kb = reinterpret_cast<const float*>(mk_next_tile(p, f, it + 1));
-      nb_ = min(tp, L - (t + 1) * tp);
-    }
-    mk_attn_step<DPL, GM>(p, a, q, ka, ka + tp * hd, na, kb, kb + tp * hd, nb_, tp, m, l, o);
+    for (int e = 0; e < DPL; ++e) o[g][e] = 0.0f;
+  }
+  for (int t = t0; t < t1; ++t, ++it) {
+    const float* kt = reinterpret_cast<const float*>(mk_next_tile(p, f, it));
+    if (served && (t - t0) % WPG == slot)
+      mk_attn_tile<DPL, HPW>(qs + g0 * HD, gw, kt, true, kt + TP * HD, min(TP, L - t * TP),
+                             p.scale, m, l, o);
     mk_release(f, it);
-    ++it;
-    if (nb_ > 0) {
-      mk_release(f, it);
-      ++it;
-    }
   }
-  if (last) mk_attn_step<DPL, GM>(p, a, q, a.knew, a.vnew, 1, a.knew, a.vnew, 0, 32, m, l, o);
-  // this split's partial: unnormalised o, running max m and sum l per head
-  const int item = blockIdx.x;
-  float* part = p.part + (size_t)item * G * (hd + 2);  // [G][hd + 2]: o, m, l
+  if (served && last && (t1 - t0) % WPG == slot)
+    mk_attn_tile<DPL, HPW>(qs + g0 * HD, gw, knew, false, vnew, 1, p.scale, m, l, o);
 #pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int idx = tid + kMkConsumers * u;
-    if (idx < G * hd) {
-      const int g = idx / hd, d = idx - g * hd;
-      part[g * (hd + 2) + d] = o[u];
+  for (int g = 0; g < HPW; ++g) {
+    if (served && g < gw) {
+      float* w = wst + (warp * HPW + g) * (HD + 2);
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) w[DPL * lane + e] = o[g][e];
+      if (lane == 0) {
+        w[HD] = m[g];
+        w[HD + 1] = l[g];
+      }
     }
   }
-  if (warp < G && lane == 0) {
-    part[warp * (hd + 2) + hd] = m;
-    part[warp * (hd + 2) + hd + 1] = l;
+  mk_sync();
+  // this split's partial: unnormalised o, max m and sum l per head
+  float* part = p.part + (size_t)blockIdx.x * G * (HD + 2);  // [G][hd + 2]
+  for (int idx = tid; idx < G * HD; idx += kMkConsumers) {
+    const int g = idx / HD, d = idx - g * HD;
+    const int wg = g / HPW, gl = g - HPW * wg;  // warps wg, wg + HG, ... hold head g as gl
+    float M = -INFINITY;
+    for (int w = wg; w < HG * WPG; w += HG) M = fmaxf(M, wst[(w * HPW + gl) * (HD + 2) + HD]);
+    float O = 0.0f, Ls = 0.0f;
+    for (int w = wg; w < HG * WPG; w += HG) {
+      const float* ws = wst + (w * HPW + gl) * (HD + 2);
+      const float mw = ws[HD];
+      if (mw == -INFINITY) continue;
+      const float fr = expf(mw - M);
+      O = fmaf(fr, ws[d], O);
+      Ls = fmaf(fr, ws[HD + 1], Ls);
+    }
+    part[g * (HD + 2) + d] = O;
+    if (d == 0) {
+      part[g * (HD + 2) + HD] = M;
+      part[g * (HD + 2) + HD + 1] = Ls;
+    }
   }
-  // every split of this kv head waits for the others (an arrival counter per
-  // head, reset after the next grid barrier), then merges its own slice of
-  // the head's G * hd outputs from all splits' partials
+  // arrival at the head's counter; the last split merges
   const int ns = mk_nsplit(p, L);
-  const int sp = item - kh * ns;
   __threadfence();
   mk_sync();
   if (tid == 0) {
-    atomicAdd(p.head_ctr + kh, 1);
-    const uint64_t tw = global_timer_ns();
-    for (;;) {
-      int v;
-      asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p.head_ctr + kh) : "memory");
-      if (v >= ns) break;
-      if (*reinterpret_cast<volatile int*>(p.abort_flag)) break;
-      if (global_timer_ns() - tw > kWaitLimitNs) {
-        atomicOr(p.status, kDeviceTimeout);
-        atomicExch(p.abort_flag, 1);
-        break;
-      }
+    const int old = atomicAdd(p.head_ctr + kh, 1);
+    const int is_last = old == ns - 1;
+    if (is_last) {
+      __threadfence();
+      p.head_ctr[kh] = 0;  // next used after later grid barriers
     }
-    __threadfence();
+    misc_i[2] = is_last;
   }
   mk_sync();
-  const int GH = G * hd;
-  const int o0 = (int)((long long)GH * sp / ns), o1 = (int)((long long)GH * (sp + 1) / ns);
-  const int nout = o1 - o0;
-  const int g0 = o0 / hd, ng = (o1 - 1) / hd - g0 + 1;  // heads the slice touches
-  const float* hp = p.part + (size_t)kh * ns * G * (hd + 2);
-  float* mm = scr;             // [ns][ng] split maxima, then weights
-  float* ll = mm + ns * ng;    // [ns][ng]
-  float* inv = ll + ns * ng;   // [ng]
-  float* vals = inv + ng;      // [ns][nout] weighted partial outputs
-  for (int i = tid; i < ns * ng; i += kMkConsumers) {
-    const int s_ = i / ng, gg = i - s_ * ng;
-    const float* e = hp + ((size_t)s_ * G + g0 + gg) * (hd + 2);
-    mm[i] = ldcg(e + hd);
-    ll[i] = ldcg(e + hd + 1);
+  if (!misc_i[2]) return;
+  const float* hp = p.part + (size_t)kh * ns * G * (HD + 2);
+  for (int i = tid; i < ns * G; i += kMkConsumers) {  // every split's (max, sum), in parallel
+    const float* e = hp + (size_t)i * (HD + 2);
+    fw[2 * i] = ldcg(e + HD);
+    fw[2 * i + 1] = ldcg(e + HD + 1);
   }
   mk_sync();
-  if (tid < ng) {
+  float* wgt = fw + 2 * ns * G;  // [ns][G] weights, then [G] 1 / sum
+  if (tid < G) {
     float M = -INFINITY;
-    for (int s_ = 0; s_ < ns; ++s_) M = fmaxf(M, mm[s_ * ng + tid]);
+    for (int s_ = 0; s_ < ns; ++s_) M = fmaxf(M, fw[2 * (s_ * G + tid)]);
     float Ls = 0.0f;
     for (int s_ = 0; s_ < ns; ++s_) {
-      const float ms = mm[s_ * ng + tid];
-      const float f = ms == -INFINITY ? 0.0f : expf(ms - M);
-      Ls = fmaf(ll[s_ * ng + tid], f, Ls);
-      mm[s_ * ng + tid] = f;
+      const float ms = fw[2 * (s_ * G + tid)];
+      const float fs = ms == -INFINITY ? 0.0f : expf(ms - M);
+      Ls = fmaf(fw[2 * (s_ * G + tid) + 1], fs, Ls);
+      wgt[s_ * G + tid] = fs;
     }
-    inv[tid] = 1.0f / Ls;
+    wgt[ns * G + tid] = 1.0f / Ls;
   }
   mk_sync();
-  for (int i = tid; i < ns * nout; i += kMkConsumers) {
-    const int s_ = i / nout, oi = i - s_ * nout;
-    const int g = (o0 + oi) / hd, d = (o0 + oi) - g * hd;
-    vals[i] = ldcg(hp + ((size_t)s_ * G + g) * (hd + 2) + d) * mm[s_ * ng + g - g0];
-  }
-  mk_sync();
-  for (int oi = tid; oi < nout; oi += kMkConsumers) {
-    const int g = (o0 + oi) / hd, d = (o0 + oi) - g * hd;
+  for (int idx = tid; idx < G * HD; idx += kMkConsumers) {
+    const int g = idx / HD, d = idx - g * HD;
     float O = 0.0f;
-    for (int s_ = 0; s_ < ns; ++s_) O += vals[s_ * nout + oi];
-    p.att[(size_t)(kh * G + g) * hd + d] = O * inv[g - g0];
+#pragma unroll 6
+    for (int s_ = 0; s_ < ns; ++s_)
+      O = fmaf(wgt[s_ * G + g], ldcg(hp + ((size_t)s_ * G + g) * (HD + 2) + d), O);
+    p.att[(size_t)(kh * G + g) * HD + d] = O * wgt[ns * G + g];
   }
 }
 
@@ -924,7 +1032,9 @@ __device__ void mk_consumers(const MkParams& p, unsigned char* sm, MkFeed& f, co
   int* misc_i = reinterpret_cast<int*>(sm + kMkMiscOff + 160);     // flags
   unsigned long long* best_s = reinterpret_cast<unsigned long long*>(sm + kMkMiscOff + 256);
   float* red = reinterpret_cast<float*>(sm + kMkRedOff);
-  float* xs = reinterpret_cast<float*>(sm + kMkScrOff);
+  float* xs = reinterpret_cast<float*>(sm + kMkScrOff);  // attention scratch / lm_head input
+  uint32_t* xp = reinterpret_cast<uint32_t*>(sm + kMkScrOff);  // staged projection input
+  float* xsb = reinterpret_cast<float*>(xp + (size_t)(max(max(p.H, p.I), p.qd) >> 5) * kMkRecW);
   const int G = gridDim.x;
   int it = 0, nbar = 0;
   bool ok = !*reinterpret_cast<volatile int*>(p.abort_flag);
@@ -937,49 +1047,42 @@ __device__ void mk_consumers(const MkParams& p, unsigned char* sm, MkFeed& f, co
     for (int i = threadIdx.x; i < 2 * half; i += kMkConsumers)
       rope_cs[i] = i < half ? p.rope_cos[(size_t)L * half + i] : p.rope_sin[(size_t)L * half + i - half];
   }
-  constexpr bool Q4 = DT == MINQ_Q4_0;
   for (int li = 0; li < p.n_layers && ok; ++li) {
     const MkLayerPtrs& lp = p.layers[li];
     // P1: q|k|v
-    mk_stage_x(p, xs, xsrc, p.H, lp.attn_norm, Q4, misc);
+    mk_stage_planes<DT>(p, xp, xsb, xsrc, p.H, lp.attn_norm, misc);
     const float* bias = lp.bias_qkv;
-    mk_consume_mat<DT, false>(p, p.qkv, xs, f, cta, L, red, it, [&](int row, float v, float) {
+    mk_consume_mat<DT, false>(p, p.qkv, xp, xsb, f, cta, L, red, it, [&](int row, float v, float) {
       p.qkv_out[row] = bias ? v + bias[row] : v;
     });
     if (!(ok = barrier())) break;
     // P2: attention
-    if (p.hd == 128) {
-      if (p.G <= 4) mk_consume_attn<DT, 4, 4>(p, li, L, xs, f, cta, rope_cs, misc_i, it);
-      else mk_consume_attn<DT, 4, 8>(p, li, L, xs, f, cta, rope_cs, misc_i, it);
-    } else {
-      if (p.G <= 4) mk_consume_attn<DT, 2, 4>(p, li, L, xs, f, cta, rope_cs, misc_i, it);
-      else mk_consume_attn<DT, 2, 8>(p, li, L, xs, f, cta, rope_cs, misc_i, it);
-    }
+    if (p.hd == 128) mk_consume_attn<DT, 4>(p, li, L, xs, f, cta, rope_cs, misc_i, it);
+    else mk_consume_attn<DT, 2>(p, li, L, xs, f, cta, rope_cs, misc_i, it);
     if (!(ok = barrier())) break;
-    // P3: x = x + W_o att (every split is past its head's counter now)
-    if (blockIdx.x < (unsigned)p.nkv && threadIdx.x == 0) p.head_ctr[blockIdx.x] = 0;
-    mk_stage_x(p, xs, p.att, p.qd, nullptr, Q4, misc);
+    // P3: x = x + W_o att
+    mk_stage_planes<DT>(p, xp, xsb, p.att, p.qd, nullptr, misc);
     const float* res = xsrc;
-    mk_consume_mat<DT, false>(p, p.o, xs, f, cta, L, red, it, [&](int row, float v, float) {
+    mk_consume_mat<DT, false>(p, p.o, xp, xsb, f, cta, L, red, it, [&](int row, float v, float) {
       p.x[row] = ldcg(res + row) + v;
     });
     xsrc = p.x;
     if (!(ok = barrier())) break;
     // P4: h = silu(gate) * up
-    mk_stage_x(p, xs, p.x, p.H, lp.ffn_norm, Q4, misc);
-    mk_consume_mat<DT, true>(p, p.gu, xs, f, cta, L, red, it, [&](int row, float g, float u) {
+    mk_stage_planes<DT>(p, xp, xsb, p.x, p.H, lp.ffn_norm, misc);
+    mk_consume_mat<DT, true>(p, p.gu, xp, xsb, f, cta, L, red, it, [&](int row, float g, float u) {
       p.h[row] = silu(g) * u;
     });
     if (!(ok = barrier())) break;
     // P5: x = x + W_down h
-    mk_stage_x(p, xs, p.h, p.I, nullptr, Q4, misc);
-    mk_consume_mat<DT, false>(p, p.down, xs, f, cta, L, red, it, [&](int row, float v, float) {
+    mk_stage_planes<DT>(p, xp, xsb, p.h, p.I, nullptr, misc);
+    mk_consume_mat<DT, false>(p, p.down, xp, xsb, f, cta, L, red, it, [&](int row, float v, float) {
       p.x[row] = ldcg(p.x + row) + v;
     });
     if (!(ok = barrier())) break;
   }
   if (ok && p.want_logits) {
-    mk_stage_x(p, xs, p.x, p.H, p.final_norm, false, misc);
+    mk_stage_x(p, xs, p.x, p.H, p.final_norm, misc);
     mk_lm_head(p, xs, best_s);
     ok = barrier();
     if (ok && blockIdx.x == 0) {
@@ -1040,35 +1143,91 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
 
 // ---------------------------------------------------------------- host
 
-MkMat mk_plan_mat(int dtype, bool dual, uint64_t rows, uint64_t cols, int grid) {
-  MkMat m{};
-  const int pitch = kMkCK * block_bytes(dtype);
-  int nr_max = 0;
-  for (int nr = 1; nr <= 4 * mk_acc(dtype, dual); ++nr) {
-    const size_t box = ((size_t)nr * pitch + 127) & ~(size_t)127;
-    if ((dual ? 2 : 1) * box <= (size_t)kMkSlot) nr_max = nr;
+// Consumer issue cost of a plan for one CTA's share of `cnt` rows: per warp
+// the most block dots any of its lanes computes (the warp issues that many);
+// per SM sub-partition (warp w runs on w mod 4) the sum over its warps, but
+// at least twice its busiest warp (one warp alone issues at about half the
+// rate); the plan costs the busiest sub-partition.
+static long mk_plan_cost(const MkMat& m, int cnt, bool dual) {
+  const int nb = m.cols / kBlock, R = 32 / m.ck;
+  long sub[4] = {0, 0, 0, 0}, top[4] = {0, 0, 0, 0};
+  const int passes = (cnt + m.nr - 1) / m.nr;
+  for (int w = 0; w < kMkCW; ++w) {
+    long warp_cost = 0;
+    for (int j = 0; j < passes; ++j) {
+      const int n = (int)((long long)cnt * (j + 1) / passes - (long long)cnt * j / passes);
+      const int nv = dual ? 2 * n : n;
+      long lane_max = 0;
+      for (int lane = 0; lane < 32; ++lane) {
+        const int rr = lane / m.ck, bl = lane % m.ck;
+        int rows_here = 0;
+        for (int k = 0; k < kMkRS; ++k) rows_here += (16 * k + w) * R + rr < nv;
+        long blocks = 0;
+        for (int c = 0; c < m.ntiles; ++c) {
+          const int nbk = std::min(m.tb, nb - c * m.tb);
+          blocks += nbk > bl ? (nbk - bl + m.ck - 1) / m.ck : 0;
+        }
+        lane_max = std::max(lane_max, rows_here * blocks);
+      }
+      warp_cost += lane_max;
+    }
+    sub[w % 4] += warp_cost;
+    top[w % 4] = std::max(top[w % 4], warp_cost);
   }
+  long cost = 0;
+  for (int i = 0; i < 4; ++i) cost = std::max(cost, std::max(sub[i], 2 * top[i]));
+  return cost;
+}
+
+MkMat mk_plan_mat(int dtype, bool dual, uint64_t rows, uint64_t cols, int grid) {
+  const int nb = (int)(cols / kBlock), bb = block_bytes(dtype), halves = dual ? 2 : 1;
   const uint64_t rmax = (rows + grid - 1) / grid;
-  const uint64_t passes = (rmax + nr_max - 1) / nr_max;
-  m.rows = (int)rows;
-  m.cols = (int)cols;
-  m.nr = (int)((rmax + passes - 1) / passes);
-  m.nchunks = (int)((cols / kBlock + kMkCK - 1) / kMkCK);
-  m.up_off = dual ? (int)(((size_t)m.nr * pitch + 127) & ~(size_t)127) : 0;
-  return m;
+  auto box = [](size_t b) { return (b + 127) & ~(size_t)127; };
+  // For each lanes-per-row width ck: rows per pass as many as the consumer
+  // row slots (and the 128 of the reduction buffer) take and one slot holds
+  // at one block per lane, passes balanced, then as many blocks per tile row
+  // (a multiple of 4, so rows stay 16-byte aligned) as the slot holds. Keep
+  // the plan with the least consumer issue cost, then the fewest tiles.
+  MkMat best{};
+  long best_cost = -1;
+  uint64_t best_tiles = ~0ull;
+  for (int ck = 32; ck >= 4; ck >>= 1) {
+    int nr_max = 0;
+    for (int nr = 1; nr <= std::min(128, 16 * (32 / ck) * kMkRS / halves); ++nr)
+      if (halves * box((size_t)nr * ck * bb) <= (size_t)kMkSlot) nr_max = nr;
+    if (nr_max == 0) continue;
+    const uint64_t passes = (rmax + nr_max - 1) / nr_max;
+    const int nr = (int)((rmax + passes - 1) / passes);
+    int tb = 4;
+    while (tb + 4 <= nb && halves * box((size_t)nr * (tb + 4) * bb) <= (size_t)kMkSlot) tb += 4;
+    MkMat m{};
+    m.rows = (int)rows;
+    m.cols = (int)cols;
+    m.nr = nr;
+    m.ck = ck;
+    m.tb = tb;
+    m.ntiles = (nb + tb - 1) / tb;
+    m.pitch = tb * bb;
+    m.up_off = dual ? (int)box((size_t)nr * m.pitch) : 0;
+    const long cost = mk_plan_cost(m, (int)rmax, dual);
+    const uint64_t tiles = passes * (uint64_t)m.ntiles;
+    if (best_cost < 0 || cost < best_cost || (cost == best_cost && tiles < best_tiles)) {
+      best_cost = cost;
+      best_tiles = tiles;
+      best = m;
+    }
+  }
+  return best;
 }
 
 size_t mk_scratch_bytes(int H, int I, int qd, int G, int hd, int nsplit) {
-  const size_t xs = (size_t)std::max({H, I, qd}) * 4;
-  // attention: q heads, new k and v, scores / numerators / rescales of a
-  // tile; then, in the CTA merging a kv head, every split's partial
-  // (o, max, sum) plus a weight per split and head
-  // merge of a slice of one kv head's outputs: (max, sum) per split and
-  // head, 1 / sum per head, weighted partials per split and output
-  const size_t splits = (size_t)nsplit;
-  const size_t slice = ((size_t)G * hd + splits - 1) / splits + 1;
-  const size_t att = std::max((size_t)G * hd + 2 * hd + 2 * 32 * G + G,
-                              2 * splits * G + G + splits * slice) * 4;
+  // staged projection input (planes + one scale per block), or the lm_head input
+  const size_t xs = std::max((size_t)(std::max({H, I, qd}) / kBlock) * (kMkRecW * 4 + 4),
+                             (size_t)H * 4);
+  // attention: q heads, new k and v, the 16 warps' (o, m, l), then the
+  // merge's split weights and 1 / sum per head
+  const size_t att = ((size_t)G * hd + 2 * hd + (size_t)kMkCW * 2 * (hd + 2) +
+                      3 * (size_t)nsplit * G + G) * 4;
   return (std::max(xs, att) + 127) & ~(size_t)127;
 }
 

@@ -12,11 +12,14 @@ namespace minq {
 
 // Plan of one projection phase, the same for every layer.
 struct MkMat {
-  int rows;     // output rows (gate/up row pairs for the dual phase)
+  int rows;       // output rows (gate/up row pairs for the dual phase)
   int cols;
-  int nr;       // max rows per pass
-  int nchunks;  // 32-block column chunks per row
-  int up_off;   // dual: offset of the up rows in a ring slot
+  int nr;         // max rows per pass
+  int ck;         // consumer lanes per row (32, 16, 8 or 4): lane l takes blocks l, l + ck, ...
+  int tb;         // blocks per tile row, a multiple of 4 (the last tile of a row may hold fewer)
+  int ntiles;     // tiles per pass: ceil(cols / 32 / tb)
+  int pitch;      // bytes of one tile row in a ring slot (tb blocks)
+  int up_off;     // dual: offset of the up rows in a ring slot
 };
 
 // Per-layer weights and vectors (device array).

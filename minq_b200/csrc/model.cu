@@ -268,6 +268,8 @@ minq_status setup_megakernel(minq_model* m) {
   k.o = mk_plan_mat(dt, false, H, qd, grid);
   k.gu = mk_plan_mat(dt, true, I, H, grid);
   k.down = mk_plan_mat(dt, false, H, I, grid);
+  for (const MkMat* mm : {&k.qkv, &k.o, &k.gu, &k.down})
+    if (mm->nr == 0) return MINQ_OK;  // no tile plan fits a ring slot
   // history splits per kv head: up to one CTA each, as many as the merge
   // buffer in shared memory allows
   k.nsplit = std::max(1, grid / (int)nkv);

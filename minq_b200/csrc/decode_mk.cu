@@ -81,13 +81,11 @@ constexpr int kMkFx = 8 * kMkNP - 2;           // |m| <= 2^kMkFx
 // [low / high nibble columns]; Q8_0: [word j][plane]), then kMkNP Q4_0
 // offset corrections; a multiple of 4 words for 16-byte loads.
 constexpr int kMkRecW = (9 * kMkNP + 3) & ~3;
-// Row slots per consumer thread in one pass (rows (16 k + warp) R + lane / ck).
-constexpr int kMkRS = 2;
 constexpr int kMkMiscOff = 256;                // small reductions and flags
 constexpr int kMkCtaOff = 768;                 // the CTA's plan (MkCta)
-constexpr int kMkRedOff = 1024;                // projection pass reduction 2 x [128][2]
-constexpr int kMkRopeOff = 5120;               // cos | sin of this position's RoPE row
-constexpr int kMkScrOff = 5632;                // x / attention scratch, then the ring
+constexpr int kMkRedOff = 1024;                // projection row sums, 2048 floats
+constexpr int kMkRopeOff = 9216;               // cos | sin of this position's RoPE row
+constexpr int kMkScrOff = 9728;                // x / attention scratch, then the ring
 
 __device__ __forceinline__ float ldcg(const float* p) { return __ldcg(p); }
 __device__ __forceinline__ float4 ldcg4(const float* p) {
@@ -213,19 +211,17 @@ __device__ __forceinline__ void cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-// Rows of this CTA in a projection and its passes of at most m.nr rows.
+// Rows [rb, rb + cnt) of this CTA in a projection: cnt * nb contiguous
+// blocks of the row-major matrix, streamed as tiles of kMkTileBlocks blocks
+// (the last one shorter), gate and up tiles alternating in the dual phase.
 struct MkShare {
-  int rb, cnt, passes;
+  int rb, cnt;
 };
-__device__ __forceinline__ MkShare mk_mat_share(const MkMat& m) {
-  MkShare s;
-  mk_share(m.rows, &s.rb, &s.cnt);
-  s.passes = (s.cnt + m.nr - 1) / m.nr;
-  return s;
-}
-__device__ __forceinline__ int mk_pass_row(const MkShare& s, int j) {
-  return (int)(((long long)s.cnt * j) / s.passes);
-}
+template <int DT>
+struct MkTile {
+  // blocks per tile: a whole number of blocks and of 16-byte pieces, <= a slot
+  static constexpr int blocks = DT == MINQ_Q8_0 ? 452 : 816;
+};
 
 // This CTA's plan for the launch (the same for every layer), computed once
 // into shared memory: row shares of the four projections and the attention
@@ -240,12 +236,14 @@ __device__ __forceinline__ const MkMat& mk_mat(const MkParams& p, int ph) {
   return ph == 0 ? p.qkv : ph == 2 ? p.o : ph == 3 ? p.gu : p.down;
 }
 
+template <int DT>
 __device__ void mk_cta_plan(const MkParams& p, int L, MkCta* c) {
   for (int ph = 0; ph < 5; ++ph) {
     if (ph == 1) continue;
     const MkMat& m = mk_mat(p, ph);
-    c->sh[ph] = mk_mat_share(m);
-    c->tiles[ph] = c->sh[ph].passes * m.ntiles;
+    mk_share(m.rows, &c->sh[ph].rb, &c->sh[ph].cnt);
+    const long long blocks = (long long)c->sh[ph].cnt * (m.cols / kBlock);
+    c->tiles[ph] = (ph == 3 ? 2 : 1) * (int)((blocks + MkTile<DT>::blocks - 1) / MkTile<DT>::blocks);
   }
   int kh = 0, t0 = 0, t1 = 0;
   bool last = false;
@@ -263,14 +261,7 @@ struct MkFeed {
   uint64_t* empty;  // [kMkS]: every consumer warp released the slot
   int li, ph, idx;  // next tile to issue: layer, phase, index in the phase
   int issued;       // tiles issued so far (slot = issued % kMkS)
-  int j, c;         // projection pass and chunk of the next tile
-  int pr0, n;       // rows of that pass
 };
-
-__device__ __forceinline__ void mk_feed_pass(MkFeed& f, const MkShare& sh) {
-  f.pr0 = mk_pass_row(sh, f.j);
-  f.n = mk_pass_row(sh, f.j + 1) - f.pr0;
-}
 
 // Producer wait until slot `it % kMkS` may be refilled; false on abort or
 // timeout. Lane 0 decides and the warp follows it.
@@ -307,30 +298,21 @@ __device__ __forceinline__ bool mk_feed_settle(const MkParams& p, MkFeed& f, con
       f.ph = 0;
       ++f.li;
     }
-    f.j = 0;
-    f.c = 0;
-    if (f.ph != 1) mk_feed_pass(f, cta->sh[f.ph]);
   }
   return f.li < p.n_layers;
 }
 
 // Step the iterator over one tile without copying it.
-__device__ __forceinline__ void mk_feed_skip(const MkParams& p, MkFeed& f, const MkCta* cta) {
-  if (f.ph != 1 && ++f.c == mk_mat(p, f.ph).ntiles) {
-    f.c = 0;
-    if (++f.j < cta->sh[f.ph].passes) mk_feed_pass(f, cta->sh[f.ph]);
-  }
+__device__ __forceinline__ void mk_feed_skip(MkFeed& f) {
   ++f.idx;
   ++f.issued;
 }
 
 // Producer warp: copy the current tile into its slot with the warp's 32
 // lanes, then have the slot's full barrier track the copies
-// (cp.async.mbarrier.arrive). Projection tiles: the rows x 16-byte pieces of
-// the row chunk (ck blocks: 1.25 ck pieces for Q4_0, 2.25 ck for Q8_0)
-// flattened over the lanes,
-// the up rows of the gate/up phase after the gate rows. Attention tiles: the
-// pieces of K and of V. False on abort.
+// (cp.async.mbarrier.arrive). Projection tiles: a contiguous run of the
+// CTA's blocks (gate and up alternating in the gate/up phase). Attention
+// tiles: the pieces of K (swizzled) and of V. False on abort.
 template <int DT>
 __device__ bool mk_issue(const MkParams& p, MkFeed& f, const MkCta* cta, int L) {
   constexpr int BB = DT == MINQ_Q8_0 ? kQ8Bytes : kQ4Bytes;
@@ -356,25 +338,20 @@ __device__ bool mk_issue(const MkParams& p, MkFeed& f, const MkCta* cta, int L) 
   } else {
     const bool dual = f.ph == 3;
     const MkMat& m = mk_mat(p, f.ph);
-    const uint8_t* w0 = f.ph == 0 ? lp.w_qkv : f.ph == 2 ? lp.w_o : dual ? lp.w_gate : lp.w_down;
-    const int nb = m.cols / kBlock;
-    const size_t row_bytes = (size_t)nb * BB;
-    const size_t first = (size_t)(cta->sh[f.ph].rb + f.pr0) * row_bytes + (size_t)f.c * m.tb * BB;
-    const int ppr = min(m.tb, nb - f.c * m.tb) * BB / 16;  // pieces per tile row
-    const uint32_t magic = ((1u << 20) + ppr - 1) / ppr;    // i / ppr == (i * magic) >> 20, i < 2^14
-    const int pitch = m.pitch, n = f.n, total = (dual ? 2 : 1) * n * ppr;
-    for (int i = lane; i < total; i += 32) {
-      const int r = (int)(((uint32_t)i * magic) >> 20);
-      const int pc = i - r * ppr;
-      const bool up = dual && r >= n;
-      const int row = up ? r - n : r;
-      cp_async16(dst + (up ? m.up_off : 0) + row * pitch + pc * 16,
-                 (up ? lp.w_up : w0) + first + (size_t)row * row_bytes + pc * 16);
-    }
+    const MkShare& sh = cta->sh[f.ph];
+    const int nb = m.cols / kBlock, up = dual ? (f.idx & 1) : 0, k = dual ? f.idx >> 1 : f.idx;
+    const uint8_t* w = f.ph == 0 ? lp.w_qkv : f.ph == 2 ? lp.w_o : dual ? (up ? lp.w_up : lp.w_gate)
+                                                                         : lp.w_down;
+    const long long g0 = (long long)k * MkTile<DT>::blocks;
+    const int nblk = (int)min((long long)MkTile<DT>::blocks, (long long)sh.cnt * nb - g0);
+    const unsigned char* src = w + ((size_t)sh.rb * nb + (size_t)g0) * BB;
+    const int pieces = nblk * BB / 16;  // rows are 16-byte multiples (nb % 4 == 0)
+#pragma unroll 4
+    for (int i = lane; i < pieces; i += 32) cp_async16(dst + i * 16, src + (size_t)i * 16);
   }
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&f.full[slot]))
                : "memory");
-  mk_feed_skip(p, f, cta);
+  mk_feed_skip(f);
   return true;
 }
 
@@ -388,7 +365,7 @@ __device__ void mk_producer(const MkParams& p, MkFeed& f, const MkCta* cta, int 
       if (f.issued % kMkProducers == k) {
         if (!mk_issue<DT>(p, f, cta, L)) break;
       } else {
-        mk_feed_skip(p, f, cta);
+        mk_feed_skip(f);
       }
     }
   }
@@ -609,73 +586,85 @@ __device__ void mk_stage_planes(const MkParams& p, uint32_t* xp, float* xsb, con
   mk_sync();
 }
 
-// One projection phase. A pass of n rows is 2n "virtual rows" for the dual
-// gate/up form (gate rows, then up rows at m.up_off in the slot). Thread
-// (warp w, lane l) takes the virtual rows (16 k + w) R + l / ck (R = 32 / ck,
-// k < kMkRS) and in every tile the blocks b, b + ck, ... (b = l mod ck) of
-// them, accumulating its block dots in registers over the pass; a pass ends
-// with a reduction over the ck lanes of each row and epi(row, v0, v1) (v1 =
-// up for the dual form) on the finished rows.
+// One projection phase over the CTA's rows [rb, rb + cnt). Every consumer
+// thread owns one column block for the whole phase: warps form T = 16 / WG
+// groups of WG = ceil(nb / 32) (nb blocks per row), warp wc of a group takes
+// blocks 32 wc + lane, and its staged input planes stay in registers. Group
+// r processes the tiles tt = r mod T (a tile is a run of the CTA's row-major
+// blocks), so T tiles are in work at once; for each row of its tile a warp
+// sums its lanes' block dots and writes red[tile parity][half][row][wc] (a
+// row spans at most two tiles, which differ in parity: one writer per
+// entry). epi(row, v0, v1) (v1 = up for the dual gate/up form) gets the rows
+// summed over parity and wc in a fixed order.
 template <int DT, bool DUAL, class Epi>
 __device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const uint32_t* xp,
                                const float* xsb, MkFeed& f, const MkCta* cta, int L, float* red,
                                int& it, Epi epi) {
   constexpr int BB = DT == MINQ_Q8_0 ? kQ8Bytes : kQ4Bytes;
+  constexpr int TB = MkTile<DT>::blocks;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int ck = m.ck, pitch = m.pitch, nb = m.cols / kBlock;
-  const int R = 32 / ck, rr = lane / ck, bl = lane - rr * ck;
+  const int nb = m.cols / kBlock, WG = (nb + 31) >> 5, T = kMkCW / WG;
+  const int grp = warp / WG, wc = warp - grp * WG, col = 32 * wc + lane;
+  const bool in_grp = grp < T, has_col = in_grp && col < nb;
   int rb, cnt;
   mk_share(m.rows, &rb, &cnt);
-  const int passes = (cnt + m.nr - 1) / m.nr;
-  for (int j = 0; j < passes; ++j) {
-    const int pr0 = (int)(((long long)cnt * j) / passes);
-    const int n = (int)(((long long)cnt * (j + 1)) / passes) - pr0;
-    const int nv = DUAL ? 2 * n : n;
-    int off[kMkRS];  // slot offset of each row slot's row (-1: none)
+  const int halves = DUAL ? 2 : 1;
+  // this thread's column: staged planes and scale, kept for the phase
+  uint32_t xw[kMkRecW];
+  float sb = 0.0f;
+  {
+    const uint4* rec = reinterpret_cast<const uint4*>(xp + (size_t)(has_col ? col : 0) * kMkRecW);
 #pragma unroll
-    for (int k = 0; k < kMkRS; ++k) {
-      const int v = (16 * k + warp) * R + rr;
-      const bool up = DUAL && v >= n;
-      off[k] = v < nv ? (up ? m.up_off : 0) + (up ? v - n : v) * pitch + bl * BB : -1;
+    for (int i = 0; i < kMkRecW / 4; ++i) {
+      const uint4 v = rec[i];
+      xw[4 * i] = v.x;
+      xw[4 * i + 1] = v.y;
+      xw[4 * i + 2] = v.z;
+      xw[4 * i + 3] = v.w;
     }
-    float acc[kMkRS];
+    if (has_col) sb = xsb[col];
+  }
+  const int plane = halves * cnt * WG;  // floats per tile parity
+  for (int i = tid; i < 2 * plane; i += kMkConsumers) red[i] = 0.0f;
+  mk_sync();
+  const int total = cnt * nb;  // < 2^16 for every eligible shape
+  const int per = (total + TB - 1) / TB;  // tiles per matrix
+  for (int tt = 0; tt < halves * per; ++tt, ++it) {
+    const unsigned char* tile = mk_next_tile(p, f, it);
+    if (in_grp && tt % T == grp) {
+      const int half = DUAL ? (tt & 1) : 0, k = DUAL ? tt >> 1 : tt;
+      const int g0 = k * TB, g1 = min(g0 + TB, total);
+      const int r_lo = g0 / nb, r_hi = (g1 - 1) / nb;
+      float* rr = red + (k & 1) * plane + half * cnt * WG + wc;
+      const unsigned char* base = tile - (size_t)g0 * BB;  // block g at base + g * BB
+      for (int R = r_lo; R <= r_hi; R += 2) {  // two rows at a time for ILP
+        const int ga = R * nb + col, gb = ga + nb;
+        float va = 0.0f, vb = 0.0f;
+        if (col < nb && ga >= g0 && ga < g1) va = mk_block_dot<DT>(base + (size_t)ga * BB, xw) * sb;
+        if (col < nb && R + 1 <= r_hi && gb < g1)
+          vb = mk_block_dot<DT>(base + (size_t)gb * BB, xw) * sb;
 #pragma unroll
-    for (int k = 0; k < kMkRS; ++k) acc[k] = 0.0f;
-    for (int c = 0; c < m.ntiles; ++c, ++it) {
-      const unsigned char* tile = mk_next_tile(p, f, it);
-      const int g0 = c * m.tb, nbk = min(m.tb, nb - g0);
-      for (int u = off[0] >= 0 ? bl : nbk; u < nbk; u += ck) {  // this lane's blocks, if it has rows
-        const int g = g0 + u;
-        uint32_t xw[kMkRecW];
-        const uint4* rec = reinterpret_cast<const uint4*>(xp + (size_t)g * kMkRecW);
-#pragma unroll
-        for (int i = 0; i < kMkRecW / 4; ++i) {
-          const uint4 v = rec[i];
-          xw[4 * i] = v.x;
-          xw[4 * i + 1] = v.y;
-          xw[4 * i + 2] = v.z;
-          xw[4 * i + 3] = v.w;
+        for (int o = 16; o > 0; o >>= 1) {
+          va += __shfl_xor_sync(0xffffffffu, va, o);
+          vb += __shfl_xor_sync(0xffffffffu, vb, o);
         }
-        const float sb = xsb[g];
-        const unsigned char* tb_ = tile + (u - bl) * BB;
-#pragma unroll
-        for (int k = 0; k < kMkRS; ++k)
-          if (off[k] >= 0) acc[k] = fmaf(mk_block_dot<DT>(tb_ + off[k], xw), sb, acc[k]);
+        if (lane == 0) {
+          rr[(size_t)R * WG] = va;
+          if (R + 1 <= r_hi) rr[(size_t)(R + 1) * WG] = vb;
+        }
       }
-      mk_release(f, it);
     }
-    // virtual rows -> red[row][half] (two buffers, alternating by pass, so
-    // one barrier a pass)
-    float* rb_ = red + (j & 1) * 256;
-#pragma unroll
-    for (int k = 0; k < kMkRS; ++k) {
-      float v = acc[k];
-      for (int o = ck >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      const int vr = (16 * k + warp) * R + rr;
-      if (bl == 0 && vr < nv) rb_[DUAL && vr >= n ? (vr - n) * 2 + 1 : vr * 2] = v;
-    }
-    mk_sync();
-    for (int t = tid; t < n; t += kMkConsumers) epi(rb + pr0 + t, rb_[t * 2], rb_[t * 2 + 1]);
+    mk_release(f, it);
+  }
+  mk_sync();
+  for (int t = tid; t < cnt; t += kMkConsumers) {
+    float v0 = 0.0f, v1 = 0.0f;
+    for (int q = 0; q < 2; ++q)
+      for (int w = 0; w < WG; ++w) {
+        v0 += red[q * plane + (size_t)t * WG + w];
+        if (DUAL) v1 += red[q * plane + ((size_t)cnt + t) * WG + w];
+      }
+    epi(rb + t, v0, v1);
   }
 }
 
@@ -1113,7 +1102,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
   const uint32_t tok = *reinterpret_cast<volatile const uint32_t*>(p.d_tok);
   const unsigned long long bbase = *reinterpret_cast<volatile const unsigned long long*>(p.bar_base);
   MkCta* cta = reinterpret_cast<MkCta*>(sm + kMkCtaOff);
-  if (threadIdx.x == 0) mk_cta_plan(p, L, cta);
+  if (threadIdx.x == 0) mk_cta_plan<DT>(p, L, cta);
   __syncthreads();
   MkFeed f;
   f.ring = sm + kMkScrOff + (size_t)p.scratch_bytes;
@@ -1123,9 +1112,6 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
   f.ph = 0;
   f.idx = 0;
   f.issued = 0;
-  f.j = 0;
-  f.c = 0;
-  mk_feed_pass(f, cta->sh[0]);
   if (threadIdx.x == 0) {
     for (int s = 0; s < kMkS; ++s) {
       mbar_init(&f.full[s], 32);     // the issuing producer warp's lanes (cp.async.mbarrier.arrive)
@@ -1143,81 +1129,17 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
 
 // ---------------------------------------------------------------- host
 
-// Consumer issue cost of a plan for one CTA's share of `cnt` rows: per warp
-// the most block dots any of its lanes computes (the warp issues that many);
-// per SM sub-partition (warp w runs on w mod 4) the sum over its warps, but
-// at least twice its busiest warp (one warp alone issues at about half the
-// rate); the plan costs the busiest sub-partition.
-static long mk_plan_cost(const MkMat& m, int cnt, bool dual) {
-  const int nb = m.cols / kBlock, R = 32 / m.ck;
-  long sub[4] = {0, 0, 0, 0}, top[4] = {0, 0, 0, 0};
-  const int passes = (cnt + m.nr - 1) / m.nr;
-  for (int w = 0; w < kMkCW; ++w) {
-    long warp_cost = 0;
-    for (int j = 0; j < passes; ++j) {
-      const int n = (int)((long long)cnt * (j + 1) / passes - (long long)cnt * j / passes);
-      const int nv = dual ? 2 * n : n;
-      long lane_max = 0;
-      for (int lane = 0; lane < 32; ++lane) {
-        const int rr = lane / m.ck, bl = lane % m.ck;
-        int rows_here = 0;
-        for (int k = 0; k < kMkRS; ++k) rows_here += (16 * k + w) * R + rr < nv;
-        long blocks = 0;
-        for (int c = 0; c < m.ntiles; ++c) {
-          const int nbk = std::min(m.tb, nb - c * m.tb);
-          blocks += nbk > bl ? (nbk - bl + m.ck - 1) / m.ck : 0;
-        }
-        lane_max = std::max(lane_max, rows_here * blocks);
-      }
-      warp_cost += lane_max;
-    }
-    sub[w % 4] += warp_cost;
-    top[w % 4] = std::max(top[w % 4], warp_cost);
-  }
-  long cost = 0;
-  for (int i = 0; i < 4; ++i) cost = std::max(cost, std::max(sub[i], 2 * top[i]));
-  return cost;
-}
-
 MkMat mk_plan_mat(int dtype, bool dual, uint64_t rows, uint64_t cols, int grid) {
-  const int nb = (int)(cols / kBlock), bb = block_bytes(dtype), halves = dual ? 2 : 1;
-  const uint64_t rmax = (rows + grid - 1) / grid;
-  auto box = [](size_t b) { return (b + 127) & ~(size_t)127; };
-  // For each lanes-per-row width ck: rows per pass as many as the consumer
-  // row slots (and the 128 of the reduction buffer) take and one slot holds
-  // at one block per lane, passes balanced, then as many blocks per tile row
-  // (a multiple of 4, so rows stay 16-byte aligned) as the slot holds. Keep
-  // the plan with the least consumer issue cost, then the fewest tiles.
-  MkMat best{};
-  long best_cost = -1;
-  uint64_t best_tiles = ~0ull;
-  for (int ck = 32; ck >= 4; ck >>= 1) {
-    int nr_max = 0;
-    for (int nr = 1; nr <= std::min(128, 16 * (32 / ck) * kMkRS / halves); ++nr)
-      if (halves * box((size_t)nr * ck * bb) <= (size_t)kMkSlot) nr_max = nr;
-    if (nr_max == 0) continue;
-    const uint64_t passes = (rmax + nr_max - 1) / nr_max;
-    const int nr = (int)((rmax + passes - 1) / passes);
-    int tb = 4;
-    while (tb + 4 <= nb && halves * box((size_t)nr * (tb + 4) * bb) <= (size_t)kMkSlot) tb += 4;
-    MkMat m{};
-    m.rows = (int)rows;
-    m.cols = (int)cols;
-    m.nr = nr;
-    m.ck = ck;
-    m.tb = tb;
-    m.ntiles = (nb + tb - 1) / tb;
-    m.pitch = tb * bb;
-    m.up_off = dual ? (int)box((size_t)nr * m.pitch) : 0;
-    const long cost = mk_plan_cost(m, (int)rmax, dual);
-    const uint64_t tiles = passes * (uint64_t)m.ntiles;
-    if (best_cost < 0 || cost < best_cost || (cost == best_cost && tiles < best_tiles)) {
-      best_cost = cost;
-      best_tiles = tiles;
-      best = m;
-    }
-  }
-  return best;
+  const uint64_t nb = cols / kBlock, wg = (nb + 31) / 32, rmax = (rows + grid - 1) / grid;
+  const uint64_t tile = dtype == MINQ_Q8_0 ? MkTile<MINQ_Q8_0>::blocks : MkTile<MINQ_Q4_0>::blocks;
+  MkMat m{};
+  // a row must span at most two tiles (the consumer's row sums by tile parity)
+  if (nb == 0 || nb > tile || wg > (uint64_t)kMkCW || 2 * (dual ? 2 : 1) * rmax * wg > 2048 ||
+      rmax * nb >= (1u << 16))
+    return m;
+  m.rows = (int)rows;
+  m.cols = (int)cols;
+  return m;
 }
 
 size_t mk_scratch_bytes(int H, int I, int qd, int G, int hd, int nsplit) {

@@ -10,16 +10,11 @@
 
 namespace minq {
 
-// Plan of one projection phase, the same for every layer.
+// One projection phase, the same for every layer: rows (gate/up row pairs
+// for the dual phase) x cols of 32-column blocks.
 struct MkMat {
-  int rows;       // output rows (gate/up row pairs for the dual phase)
+  int rows;
   int cols;
-  int nr;         // max rows per pass
-  int ck;         // consumer lanes per row (32, 16, 8 or 4): lane l takes blocks l, l + ck, ...
-  int tb;         // blocks per tile row, a multiple of 4 (the last tile of a row may hold fewer)
-  int ntiles;     // tiles per pass: ceil(cols / 32 / tb)
-  int pitch;      // bytes of one tile row in a ring slot (tb blocks)
-  int up_off;     // dual: offset of the up rows in a ring slot
 };
 
 // Per-layer weights and vectors (device array).
@@ -69,6 +64,10 @@ struct MkParams {
   int scratch_bytes;           // x / attention scratch in shared memory
 };
 
+// The projection plan, or rows == 0 when the consumer's row sums (2 x halves
+// x rows per CTA x column warps <= 2048 floats), its column warps (cols / 32
+// blocks <= 512, and at most one tile of blocks, so a row spans at most two
+// tiles) or its 16-bit block indices do not take the shape.
 MkMat mk_plan_mat(int dtype, bool dual, uint64_t rows, uint64_t cols, int grid);
 // Shared-memory scratch: the staged input vector, or the attention state
 // and the partials of up to nsplit history splits.

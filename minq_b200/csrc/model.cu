@@ -269,7 +269,7 @@ minq_status setup_megakernel(minq_model* m) {
   k.gu = mk_plan_mat(dt, true, I, H, grid);
   k.down = mk_plan_mat(dt, false, H, I, grid);
   for (const MkMat* mm : {&k.qkv, &k.o, &k.gu, &k.down})
-    if (mm->nr == 0) return MINQ_OK;  // no tile plan fits a ring slot
+    if (mm->rows == 0) return MINQ_OK;  // the consumer's row sums do not take the shape
   // history splits per kv head: up to one CTA each, as many as the merge
   // buffer in shared memory allows
   k.nsplit = std::max(1, grid / (int)nkv);

@@ -408,23 +408,26 @@ __device__ __forceinline__ void mk_sync() { named_barrier_sync(1, kMkConsumers);
 __device__ bool mk_grid_sync(const MkParams& p, unsigned long long target, int* flag) {
   mk_sync();
   if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(p.bar_ctr, 1ull);
+    // arrival: a release add (the CTA's writes, ordered before by the named
+    // barrier, become visible with it), no round trip for a return value
+    asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(p.bar_ctr) : "memory");
     int ok = 1;
     const uint64_t t0 = global_timer_ns();
-    for (;;) {
+    for (uint32_t n = 1;; ++n) {
       unsigned long long v;
       asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p.bar_ctr) : "memory");
       if (v >= target) break;
-      if (*reinterpret_cast<volatile int*>(p.abort_flag)) {
-        ok = 0;
-        break;
-      }
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
-        atomicOr(p.status, kDeviceTimeout);
-        atomicExch(p.abort_flag, 1);
-        ok = 0;
-        break;
+      if ((n & 15) == 0) {  // the abort flag and the time limit, now and then
+        if (*reinterpret_cast<volatile int*>(p.abort_flag)) {
+          ok = 0;
+          break;
+        }
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+          atomicOr(p.status, kDeviceTimeout);
+          atomicExch(p.abort_flag, 1);
+          ok = 0;
+          break;
+        }
       }
     }
     __threadfence();
@@ -490,17 +493,21 @@ __device__ void mk_stage_planes(const MkParams& p, uint32_t* xp, float* xsb, con
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int ng = n >> 3;
   const float4 zero = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-  float4 a0 = zero, b0 = zero;  // group tid, loaded once
-  if (tid < ng) {
-    a0 = ldcg4(src + 8 * tid);
-    b0 = ldcg4(src + 8 * tid + 4);
+  // every load first (n <= 16384: at most four rounds of 512 groups of 8)
+  constexpr int MR = 4;
+  float4 va[MR], vb[MR];
+#pragma unroll
+  for (int r = 0; r < MR; ++r) {
+    const int gi = tid + r * kMkConsumers;
+    va[r] = gi < ng ? ldcg4(src + 8 * gi) : zero;
+    vb[r] = gi < ng ? ldcg4(src + 8 * gi + 4) : zero;
   }
   float inv = 1.0f;
   if (gain) {
     float ss = 0.0f;
-    for (int gi = tid; gi < ng; gi += kMkConsumers) {
-      const float4 a = gi == tid ? a0 : ldcg4(src + 8 * gi);
-      const float4 b = gi == tid ? b0 : ldcg4(src + 8 * gi + 4);
+#pragma unroll
+    for (int r = 0; r < MR; ++r) {
+      const float4 a = va[r], b = vb[r];
       ss = fmaf(a.x, a.x, ss);
       ss = fmaf(a.y, a.y, ss);
       ss = fmaf(a.z, a.z, ss);
@@ -519,14 +526,12 @@ __device__ void mk_stage_planes(const MkParams& p, uint32_t* xp, float* xsb, con
     inv = 1.0f / sqrtf(v / (float)n + p.eps);
   }
   const float4* g4 = reinterpret_cast<const float4*>(gain);
-  for (int base = 0; base < ng; base += kMkConsumers) {  // every lane runs every round
-    const int gi = base + tid;
+#pragma unroll
+  for (int rd = 0; rd < MR; ++rd) {
+    if (rd * kMkConsumers >= ng) break;  // the same for every thread
+    const int gi = tid + rd * kMkConsumers;
     const bool act = gi < ng;
-    float4 a = a0, b = b0;
-    if (base > 0) {
-      a = act ? ldcg4(src + 8 * gi) : zero;
-      b = act ? ldcg4(src + 8 * gi + 4) : zero;
-    }
+    float4 a = va[rd], b = vb[rd];
     if (gain && act) {
       const float4 ga = g4[2 * gi], gb = g4[2 * gi + 1];
       a.x = a.x * inv * ga.x; a.y = a.y * inv * ga.y; a.z = a.z * inv * ga.z; a.w = a.w * inv * ga.w;
@@ -594,12 +599,13 @@ __device__ void mk_stage_planes(const MkParams& p, uint32_t* xp, float* xsb, con
 // blocks), so T tiles are in work at once; for each row of its tile a warp
 // sums its lanes' block dots and writes red[tile parity][half][row][wc] (a
 // row spans at most two tiles, which differ in parity: one writer per
-// entry). epi(row, v0, v1) (v1 = up for the dual gate/up form) gets the rows
-// summed over parity and wc in a fixed order.
-template <int DT, bool DUAL, class Epi>
+// entry). epi(row, v0, v1, pre) (v1 = up for the dual gate/up form) gets
+// the rows summed over parity and wc in a fixed order, and pre = pre_ld(row),
+// loaded when the phase starts (thread t < cnt takes row rb + t).
+template <int DT, bool DUAL, class Pre, class Epi>
 __device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const uint32_t* xp,
                                const float* xsb, MkFeed& f, const MkCta* cta, int L, float* red,
-                               int& it, Epi epi) {
+                               int& it, Pre pre_ld, Epi epi) {
   constexpr int BB = DT == MINQ_Q8_0 ? kQ8Bytes : kQ4Bytes;
   constexpr int TB = MkTile<DT>::blocks;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -624,6 +630,7 @@ __device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const uint32_t
     }
     if (has_col) sb = xsb[col];
   }
+  const float pre = tid < cnt ? pre_ld(rb + tid) : 0.0f;  // cnt <= 512
   const int plane = halves * cnt * WG;  // floats per tile parity
   for (int i = tid; i < 2 * plane; i += kMkConsumers) red[i] = 0.0f;
   mk_sync();
@@ -657,14 +664,15 @@ __device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const uint32_t
     mk_release(f, it);
   }
   mk_sync();
-  for (int t = tid; t < cnt; t += kMkConsumers) {
+  if (tid < cnt) {
+    const int t = tid;
     float v0 = 0.0f, v1 = 0.0f;
     for (int q = 0; q < 2; ++q)
       for (int w = 0; w < WG; ++w) {
         v0 += red[q * plane + (size_t)t * WG + w];
         if (DUAL) v1 += red[q * plane + ((size_t)cnt + t) * WG + w];
       }
-    epi(rb + t, v0, v1);
+    epi(rb + t, v0, v1, pre);
   }
 }
 
@@ -846,7 +854,7 @@ __device__ void mk_consume_attn(const MkParams& p, int li, int L, float* scr, Mk
   float* knew = qs + G * HD;           // [hd] the new position's key (last split)
   float* vnew = knew + HD;             // [hd]
   float* wst = vnew + HD;              // [16][HPW][hd + 2] per-warp o, m, l
-  float* fw = wst + kMkCW * HPW * (HD + 2);  // merge: [ns][G] (max, sum), then weights
+  float* fw = wst + kMkCW * HPW * (HD + 2);  // merge: weights and the splits' partials
   const MkLayerPtrs& lp = p.layers[li];
   const size_t head_off = (size_t)li * p.cache_layer_stride + (size_t)kh * p.max_seq * HD;
   // q heads (q_norm, RoPE at position L); the last split also builds the new
@@ -933,22 +941,25 @@ __device__ void mk_consume_attn(const MkParams& p, int li, int L, float* scr, Mk
   }
   mk_sync();
   if (!misc_i[2]) return;
+  // every split's partial of this head into shared memory in one round of
+  // loads, then the weights, then the outputs
   const float* hp = p.part + (size_t)kh * ns * G * (HD + 2);
-  for (int i = tid; i < ns * G; i += kMkConsumers) {  // every split's (max, sum), in parallel
-    const float* e = hp + (size_t)i * (HD + 2);
-    fw[2 * i] = ldcg(e + HD);
-    fw[2 * i + 1] = ldcg(e + HD + 1);
-  }
+  float* wgt = fw;                       // [ns][G] weights, then [G] 1 / sum
+  float* stg = fw + ((ns * G + G + 1) & ~1);  // [ns][G][hd + 2] partials (8-byte aligned)
+  const int nf2 = ns * G * (HD + 2) / 2;  // float2 pieces (hd + 2 is even)
+  const float2* hp2 = reinterpret_cast<const float2*>(hp);
+  float2* stg2 = reinterpret_cast<float2*>(stg);
+#pragma unroll 4
+  for (int i = tid; i < nf2; i += kMkConsumers) stg2[i] = __ldcg(hp2 + i);
   mk_sync();
-  float* wgt = fw + 2 * ns * G;  // [ns][G] weights, then [G] 1 / sum
   if (tid < G) {
     float M = -INFINITY;
-    for (int s_ = 0; s_ < ns; ++s_) M = fmaxf(M, fw[2 * (s_ * G + tid)]);
+    for (int s_ = 0; s_ < ns; ++s_) M = fmaxf(M, stg[(s_ * G + tid) * (HD + 2) + HD]);
     float Ls = 0.0f;
     for (int s_ = 0; s_ < ns; ++s_) {
-      const float ms = fw[2 * (s_ * G + tid)];
-      const float fs = ms == -INFINITY ? 0.0f : expf(ms - M);
-      Ls = fmaf(fw[2 * (s_ * G + tid) + 1], fs, Ls);
+      const float* e = stg + (s_ * G + tid) * (HD + 2);
+      const float fs = e[HD] == -INFINITY ? 0.0f : expf(e[HD] - M);
+      Ls = fmaf(e[HD + 1], fs, Ls);
       wgt[s_ * G + tid] = fs;
     }
     wgt[ns * G + tid] = 1.0f / Ls;
@@ -957,9 +968,7 @@ __device__ void mk_consume_attn(const MkParams& p, int li, int L, float* scr, Mk
   for (int idx = tid; idx < G * HD; idx += kMkConsumers) {
     const int g = idx / HD, d = idx - g * HD;
     float O = 0.0f;
-#pragma unroll 6
-    for (int s_ = 0; s_ < ns; ++s_)
-      O = fmaf(wgt[s_ * G + g], ldcg(hp + ((size_t)s_ * G + g) * (HD + 2) + d), O);
+    for (int s_ = 0; s_ < ns; ++s_) O = fmaf(wgt[s_ * G + g], stg[(s_ * G + g) * (HD + 2) + d], O);
     p.att[(size_t)(kh * G + g) * HD + d] = O * wgt[ns * G + g];
   }
 }
@@ -1041,9 +1050,9 @@ __device__ void mk_consumers(const MkParams& p, unsigned char* sm, MkFeed& f, co
     // P1: q|k|v
     mk_stage_planes<DT>(p, xp, xsb, xsrc, p.H, lp.attn_norm, misc);
     const float* bias = lp.bias_qkv;
-    mk_consume_mat<DT, false>(p, p.qkv, xp, xsb, f, cta, L, red, it, [&](int row, float v, float) {
-      p.qkv_out[row] = bias ? v + bias[row] : v;
-    });
+    mk_consume_mat<DT, false>(
+        p, p.qkv, xp, xsb, f, cta, L, red, it, [&](int row) { return bias ? bias[row] : 0.0f; },
+        [&](int row, float v, float, float b) { p.qkv_out[row] = bias ? v + b : v; });
     if (!(ok = barrier())) break;
     // P2: attention
     if (p.hd == 128) mk_consume_attn<DT, 4>(p, li, L, xs, f, cta, rope_cs, misc_i, it);
@@ -1052,22 +1061,22 @@ __device__ void mk_consumers(const MkParams& p, unsigned char* sm, MkFeed& f, co
     // P3: x = x + W_o att
     mk_stage_planes<DT>(p, xp, xsb, p.att, p.qd, nullptr, misc);
     const float* res = xsrc;
-    mk_consume_mat<DT, false>(p, p.o, xp, xsb, f, cta, L, red, it, [&](int row, float v, float) {
-      p.x[row] = ldcg(res + row) + v;
-    });
+    mk_consume_mat<DT, false>(
+        p, p.o, xp, xsb, f, cta, L, red, it, [&](int row) { return ldcg(res + row); },
+        [&](int row, float v, float, float r) { p.x[row] = r + v; });
     xsrc = p.x;
     if (!(ok = barrier())) break;
     // P4: h = silu(gate) * up
     mk_stage_planes<DT>(p, xp, xsb, p.x, p.H, lp.ffn_norm, misc);
-    mk_consume_mat<DT, true>(p, p.gu, xp, xsb, f, cta, L, red, it, [&](int row, float g, float u) {
-      p.h[row] = silu(g) * u;
-    });
+    mk_consume_mat<DT, true>(
+        p, p.gu, xp, xsb, f, cta, L, red, it, [&](int) { return 0.0f; },
+        [&](int row, float g, float u, float) { p.h[row] = silu(g) * u; });
     if (!(ok = barrier())) break;
     // P5: x = x + W_down h
     mk_stage_planes<DT>(p, xp, xsb, p.h, p.I, nullptr, misc);
-    mk_consume_mat<DT, false>(p, p.down, xp, xsb, f, cta, L, red, it, [&](int row, float v, float) {
-      p.x[row] = ldcg(p.x + row) + v;
-    });
+    mk_consume_mat<DT, false>(
+        p, p.down, xp, xsb, f, cta, L, red, it, [&](int row) { return ldcg(p.x + row); },
+        [&](int row, float v, float, float r) { p.x[row] = r + v; });
     if (!(ok = barrier())) break;
   }
   if (ok && p.want_logits) {
@@ -1135,7 +1144,7 @@ MkMat mk_plan_mat(int dtype, bool dual, uint64_t rows, uint64_t cols, int grid) 
   MkMat m{};
   // a row must span at most two tiles (the consumer's row sums by tile parity)
   if (nb == 0 || nb > tile || wg > (uint64_t)kMkCW || 2 * (dual ? 2 : 1) * rmax * wg > 2048 ||
-      rmax * nb >= (1u << 16))
+      rmax * nb >= (1u << 16) || rmax > (uint64_t)kMkConsumers)
     return m;
   m.rows = (int)rows;
   m.cols = (int)cols;
@@ -1147,9 +1156,9 @@ size_t mk_scratch_bytes(int H, int I, int qd, int G, int hd, int nsplit) {
   const size_t xs = std::max((size_t)(std::max({H, I, qd}) / kBlock) * (kMkRecW * 4 + 4),
                              (size_t)H * 4);
   // attention: q heads, new k and v, the 16 warps' (o, m, l), then the
-  // merge's split weights and 1 / sum per head
+  // merge's split weights, 1 / sum per head and every split's partial
   const size_t att = ((size_t)G * hd + 2 * hd + (size_t)kMkCW * 2 * (hd + 2) +
-                      3 * (size_t)nsplit * G + G) * 4;
+                      (size_t)nsplit * G + G + 2 + (size_t)nsplit * G * (hd + 2)) * 4;
   return (std::max(xs, att) + 127) & ~(size_t)127;
 }
 

@@ -234,6 +234,25 @@ void minq_cache_free(minq_cache* c);
 minq_status minq_forward(minq_model* m, minq_cache* c, const uint32_t* tokens, size_t n,
                          float* logits_out, uint32_t* argmax_out);
 
+/* Batched decode step for the `batch` sequences of a cache created with
+ * minq_cache_new(m, batch, ...) (batch <= 64): `tokens` (host, n == batch
+ * ids) holds one token per sequence; every sequence runs Model::forward_token
+ * (model.rs:273-318) at the cache's common position, which then advances by
+ * one. `logits_out` (host, batch x vocab floats, or NULL) and `argmax_out`
+ * (host, batch ids, or NULL) get each sequence's results. Replaces the
+ * reference's per-sequence loop over Model::forward (64 independent
+ * sequences, data-sharded by the caller); the weights are read once per step
+ * for all sequences. Errors as minq_forward, plus MINQ_ERR_ARG when n !=
+ * batch. */
+minq_status minq_forward_batch(minq_model* m, minq_cache* c, const uint32_t* tokens, size_t n,
+                               float* logits_out, uint32_t* argmax_out);
+
+/* Greedy continuation of a batched cache on the device: n_steps batched
+ * steps, each feeding every sequence its previous argmax (no host
+ * synchronisation); `d_tokens_out` (device, n_steps x batch ids, or NULL). */
+minq_status minq_forward_batch_device(minq_model* m, minq_cache* c, size_t n_steps,
+                                      uint32_t* d_tokens_out);
+
 /* Same as minq_forward with device-resident token ids and outputs on the
  * model's stream (no host synchronisation): used to measure the kernels
  * without host copies and to chain decode steps. */

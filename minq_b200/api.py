@@ -299,6 +299,25 @@ class Model:
         check(lib().minq_decode_steps(self._h, cache._h, n,
                                       C.c_void_p(d_tokens_out) if d_tokens_out else None))
 
+    def forward_batch(self, tokens, cache: "KVCache", logits: bool = True):
+        """One batched step: tokens[b] (one per sequence of a batch cache) through
+        Model::forward_token (model.rs:273-318) at the cache's position. Returns
+        (argmax [batch], logits [batch, vocab] or None), host arrays."""
+        toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32).reshape(-1))
+        am = np.zeros(toks.size, dtype=np.uint32)
+        out = np.empty((toks.size, self.config.vocab_size), dtype=np.float32) if logits else None
+        check(lib().minq_forward_batch(self._h, cache._h, toks.ctypes.data_as(C.c_void_p),
+                                       toks.size,
+                                       out.ctypes.data_as(C.c_void_p) if logits else None,
+                                       am.ctypes.data_as(C.c_void_p)))
+        return am, out
+
+    def forward_batch_steps(self, cache: "KVCache", n: int, d_tokens_out: int | None = None):
+        """Greedy continuation of a batch cache on the device: n batched steps,
+        every sequence fed its previous argmax; no host synchronisation."""
+        check(lib().minq_forward_batch_device(self._h, cache._h, n,
+                                              C.c_void_p(d_tokens_out) if d_tokens_out else None))
+
     def forward_device(self, d_tokens, n: int, cache: "KVCache", d_logits=None, d_argmax=None):
         """Device-resident variant (no host synchronisation) on the model's stream."""
         check(lib().minq_forward_device(self._h, cache._h, C.c_void_p(d_tokens), n,

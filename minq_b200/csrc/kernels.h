@@ -43,6 +43,19 @@ minq_status launch_argmax(const float* x, size_t n, unsigned long long* part, in
                           uint32_t* out, cudaStream_t s);
 int argmax_parts_capacity();
 
+// qmatmul.cu: Y[b] = W X[b] for up to kQmmMaxB inputs (see qmatmul.cu);
+// w1 (dual) = up rows with a SwiGLU epilogue, else bias / residual; norm_w
+// applies the input RMSNorm first (xn_scratch: B x cols floats); part (up to
+// part_floats) holds the column slices' partials.
+constexpr int kQmmMaxB = 64;
+minq_status launch_qmatmul(int dtype, const void* w0, const void* w1, size_t rows, int cols,
+                           int B, const float* x, size_t x_stride, const float* norm_w, float eps,
+                           float* xn_scratch, const float* bias, const float* residual, float* y,
+                           size_t y_stride, float* part, size_t part_floats, cudaStream_t s);
+minq_status launch_embed_batch(const float* embed, const uint32_t* d_tok, size_t vocab, int hidden,
+                               int B, float* x, cudaStream_t s);
+minq_status launch_argmax_rows(const float* x, size_t n, int B, uint32_t* out, cudaStream_t s);
+
 // attention.cu
 size_t attn_workspace_bytes(size_t batch, size_t nh, size_t len, size_t hd_max);
 minq_status launch_attention(const float* q, const float* k, const float* v, size_t batch,

@@ -120,6 +120,18 @@ struct minq_cache {
   int* d_pos = nullptr;        // device copy of `len` read by graph-captured steps
   bool d_pos_valid = false;
   cudaGraphExec_t step[2] = {nullptr, nullptr};  // [0]: no logits, [1]: logits + argmax
+  // activations of the batched step (minq_forward_batch), allocated on first use
+  float* bx = nullptr;     // [batch][H] residual stream
+  float* bqkv = nullptr;   // [batch][qd + 2 kvd]
+  float* bq = nullptr;     // [batch][qd] RoPE'd queries
+  float* batt = nullptr;   // [batch][qd]
+  float* bh = nullptr;     // [batch][I]
+  float* blog = nullptr;   // [batch][vocab]
+  float* bxn = nullptr;    // [batch][H] RMSNorm'd inputs
+  float* bpart = nullptr;  // column-slice partials of the batched matvec
+  size_t bpart_floats = 0;
+  uint32_t* btok = nullptr;  // [batch] token ids
+  uint32_t* barg = nullptr;  // [batch] argmax ids
 };
 
 namespace minq {
@@ -564,6 +576,85 @@ minq_status forward_token(minq_model* m, minq_cache* c, const uint32_t* d_tok, s
   return MINQ_OK;
 }
 
+// model.rs:273-318 for the `batch` sequences of cache c, one token each
+// (c->btok), all at position c->len: the same steps as forward_token with
+// every projection a batched matvec (weights read once for the batch).
+static minq_status forward_batch_step(minq_model* m, minq_cache* c, bool want_logits) {
+  const minq_config& cfg = m->cfg;
+  const int H = (int)cfg.hidden_size, hd = (int)cfg.head_dim, nh = (int)cfg.n_heads,
+            nkv = (int)cfg.n_kv_heads, B = (int)c->batch;
+  const uint64_t qd = (uint64_t)nh * hd, kvd = (uint64_t)nkv * hd, I = cfg.intermediate_size;
+  const uint64_t qkv_rows = qd + 2 * kvd, V = cfg.vocab_size;
+  const float eps = cfg.rms_norm_eps;
+  const int pos = (int)c->len;
+  cudaStream_t s = m->stream;
+  const size_t seq_stride = (size_t)nkv * c->max_seq * hd, head_stride = c->max_seq * hd;
+  const size_t layer_elems = c->batch * seq_stride;
+  MINQ_TRY(launch_embed_batch(m->embed, c->btok, V, H, B, c->bx, s));
+  for (uint64_t li = 0; li < cfg.n_layers; ++li) {
+    const DevLayer& L = m->layers[li];
+    MINQ_TRY(launch_qmatmul(L.qkv.tag, L.qkv.ptr, nullptr, qkv_rows, H, B, c->bx, H, L.attn_norm,
+                            eps, c->bxn, L.bias_qkv, nullptr, c->bqkv, qkv_rows, c->bpart,
+                            c->bpart_floats, s));
+    float* kc = c->k + li * layer_elems;
+    float* vc = c->v + li * layer_elems;
+    MINQ_TRY(launch_rope_append(c->bqkv, c->bqkv + qd, c->bqkv + qd + kvd, qkv_rows, qkv_rows,
+                                L.q_norm, L.k_norm, eps, m->rope_cos, m->rope_sin, c->batch, nh,
+                                nkv, hd, pos, c->bq, kc, vc, seq_stride, head_stride, hd, s));
+    MINQ_TRY(launch_attention(c->bq, kc, vc, c->batch, nh, nkv, hd, pos + 1, seq_stride,
+                              head_stride, hd, c->batt, c->ws, c->ws_bytes, s));
+    MINQ_TRY(launch_qmatmul(L.o.tag, L.o.ptr, nullptr, H, (int)qd, B, c->batt, qd, nullptr, eps,
+                            nullptr, nullptr, c->bx, c->bx, H, c->bpart, c->bpart_floats,
+                            s));  // x += o
+    MINQ_TRY(launch_qmatmul(L.gate.tag, L.gate.ptr, L.up.ptr, I, H, B, c->bx, H, L.ffn_norm, eps,
+                            c->bxn, nullptr, nullptr, c->bh, I, c->bpart, c->bpart_floats,
+                            s));  // silu(gate) * up
+    MINQ_TRY(launch_qmatmul(L.down.tag, L.down.ptr, nullptr, H, (int)I, B, c->bh, I, nullptr, eps,
+                            nullptr, nullptr, c->bx, c->bx, H, c->bpart, c->bpart_floats,
+                            s));  // x += down
+  }
+  if (want_logits) {
+    MINQ_TRY(launch_qmatmul(m->lm_head.tag, m->lm_head.ptr, nullptr, V, H, B, c->bx, H,
+                            m->final_norm, eps, c->bxn, nullptr, nullptr, c->blog, V, c->bpart,
+                            c->bpart_floats, s));
+    MINQ_TRY(launch_argmax_rows(c->blog, V, B, c->barg, s));
+  }
+  return MINQ_OK;
+}
+
+// The batched step's activations (first use) and its shape requirements.
+static minq_status batch_ready(minq_model* m, minq_cache* c) {
+  const minq_config& cfg = m->cfg;
+  if (c->batch > (size_t)kQmmMaxB)
+    return fail(MINQ_ERR_ARG, "minq_forward_batch takes at most 64 sequences per cache");
+  if (cfg.hidden_size % 32 || cfg.intermediate_size % 32 || (cfg.n_heads * cfg.head_dim) % 32)
+    return fail(MINQ_ERR_SHAPE, "the batched step needs 32-column blocks");
+  for (const DevLayer& L : m->layers)
+    if (L.qkv.tag < 0 || L.gate.tag == MINQ_F32 || L.gate.tag != L.up.tag)
+      return fail(MINQ_ERR_SHAPE,
+                  "the batched step needs quantized q|k|v and gate/up projections of one dtype");
+  if (c->bx) return MINQ_OK;
+  const size_t B = c->batch, H = cfg.hidden_size, I = cfg.intermediate_size,
+               qd = cfg.n_heads * cfg.head_dim, kvd = cfg.n_kv_heads * cfg.head_dim,
+               V = cfg.vocab_size;
+  auto alloc = [&](void** dst, size_t bytes) -> minq_status {  // owned by the cache
+    MINQ_CUDA_TRY(cudaMalloc(dst, bytes ? bytes : 16));
+    return MINQ_OK;
+  };
+  MINQ_TRY(alloc(reinterpret_cast<void**>(&c->bx), B * H * 4));
+  MINQ_TRY(alloc(reinterpret_cast<void**>(&c->bqkv), B * (qd + 2 * kvd) * 4));
+  MINQ_TRY(alloc(reinterpret_cast<void**>(&c->bq), B * qd * 4));
+  MINQ_TRY(alloc(reinterpret_cast<void**>(&c->batt), B * qd * 4));
+  MINQ_TRY(alloc(reinterpret_cast<void**>(&c->bh), B * I * 4));
+  MINQ_TRY(alloc(reinterpret_cast<void**>(&c->blog), B * V * 4));
+  MINQ_TRY(alloc(reinterpret_cast<void**>(&c->bxn), B * H * 4));
+  c->bpart_floats = 4 * B * std::max({H, qd + 2 * kvd, I});
+  MINQ_TRY(alloc(reinterpret_cast<void**>(&c->bpart), c->bpart_floats * 4));
+  MINQ_TRY(alloc(reinterpret_cast<void**>(&c->btok), B * 4));
+  MINQ_TRY(alloc(reinterpret_cast<void**>(&c->barg), B * 4));
+  return MINQ_OK;
+}
+
 // Capture one decode step (with or without logits) of cache `c` as a graph.
 static minq_status capture_step(minq_model* m, minq_cache* c, bool logits, cudaGraphExec_t* out) {
   cudaGraph_t g = nullptr;
@@ -912,6 +1003,10 @@ void minq_cache_free(minq_cache* c) {
   cudaFree(c->v);
   cudaFree(c->ws);
   cudaFree(c->d_pos);
+  for (void* b : {(void*)c->bx, (void*)c->bqkv, (void*)c->bq, (void*)c->batt, (void*)c->bh,
+                  (void*)c->blog, (void*)c->bxn, (void*)c->bpart, (void*)c->btok,
+                  (void*)c->barg})
+    cudaFree(b);
   delete c;
 }
 
@@ -989,6 +1084,62 @@ minq_status minq_decode_steps(minq_model* m, minq_cache* c, size_t n_steps,
       MINQ_CUDA_TRY(cudaMemcpyAsync(d_tokens_out + i, m->d_tok, 4, cudaMemcpyDeviceToDevice,
                                     m->stream));
   }
+  return MINQ_OK;
+}
+
+minq_status minq_forward_batch(minq_model* m, minq_cache* c, const uint32_t* tokens, size_t n,
+                               float* logits_out, uint32_t* argmax_out) {
+  if (!m || !c) return fail(MINQ_ERR_ARG, "null argument");
+  if (c->m != m) return fail(MINQ_ERR_ARG, "cache belongs to another model");
+  if (n == 0 || !tokens) return fail(MINQ_ERR_MODEL, "empty token sequence");
+  if (n != c->batch) return fail(MINQ_ERR_ARG, "one token per sequence of the cache");
+  if (!m->shape_error.empty()) return fail(MINQ_ERR_SHAPE, m->shape_error);
+  MINQ_CUDA_TRY(cudaSetDevice(m->device));
+  if (c->len >= m->cfg.max_seq_len)  // model.rs:260-265
+    return fail(MINQ_ERR_MODEL,
+                "sequence exceeds max_seq_len (" + std::to_string(m->cfg.max_seq_len) + ")");
+  if (c->len >= c->max_seq)
+    return fail(MINQ_ERR_MODEL,
+                "sequence exceeds the cache capacity (" + std::to_string(c->max_seq) + ")");
+  for (size_t i = 0; i < n; ++i)
+    if (tokens[i] >= m->cfg.vocab_size)  // Tensor::row (tensor.rs:73-78)
+      return fail(MINQ_ERR_SHAPE, "row index " + std::to_string(tokens[i]) +
+                                      " out of bounds for " + std::to_string(m->cfg.vocab_size) +
+                                      " rows");
+  MINQ_TRY(batch_ready(m, c));
+  MINQ_CUDA_TRY(cudaMemcpyAsync(c->btok, tokens, n * 4, cudaMemcpyHostToDevice, m->stream));
+  const bool want = logits_out || argmax_out;
+  MINQ_TRY(forward_batch_step(m, c, want));
+  c->len += 1;
+  c->d_pos_valid = false;
+  if (logits_out)
+    MINQ_CUDA_TRY(cudaMemcpyAsync(logits_out, c->blog, n * m->cfg.vocab_size * 4,
+                                  cudaMemcpyDeviceToHost, m->stream));
+  if (argmax_out)
+    MINQ_CUDA_TRY(cudaMemcpyAsync(argmax_out, c->barg, n * 4, cudaMemcpyDeviceToHost, m->stream));
+  MINQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  return take_device_status();
+}
+
+minq_status minq_forward_batch_device(minq_model* m, minq_cache* c, size_t n_steps,
+                                      uint32_t* d_tokens_out) {
+  if (!m || !c) return fail(MINQ_ERR_ARG, "null argument");
+  if (c->m != m) return fail(MINQ_ERR_ARG, "cache belongs to another model");
+  if (!m->shape_error.empty()) return fail(MINQ_ERR_SHAPE, m->shape_error);
+  if (c->len == 0 || !c->bx) return fail(MINQ_ERR_MODEL, "decode continuation needs a prefilled cache");
+  MINQ_CUDA_TRY(cudaSetDevice(m->device));
+  for (size_t i = 0; i < n_steps; ++i) {
+    if (c->len >= m->cfg.max_seq_len || c->len >= c->max_seq)
+      return fail(MINQ_ERR_MODEL, "sequence exceeds the cache capacity");
+    MINQ_CUDA_TRY(cudaMemcpyAsync(c->btok, c->barg, c->batch * 4, cudaMemcpyDeviceToDevice,
+                                  m->stream));
+    MINQ_TRY(forward_batch_step(m, c, true));
+    c->len += 1;
+    if (d_tokens_out)
+      MINQ_CUDA_TRY(cudaMemcpyAsync(d_tokens_out + i * c->batch, c->barg, c->batch * 4,
+                                    cudaMemcpyDeviceToDevice, m->stream));
+  }
+  c->d_pos_valid = false;
   return MINQ_OK;
 }
 

@@ -1,0 +1,108 @@
+"""The batched decode step (minq_forward_batch: B independent sequences, one
+token each per step, the weights read once per step) against the CPU oracle
+run sequence by sequence, on small models shaped like the batched
+configurations (LLaMA-style untied Q4_0 lm_head; Qwen-style Q8_0 with q|k|v
+bias and a tied f32 lm_head).
+
+Tolerances as in test_gpu_model.py: logits max-abs < 1e-3 (model.rs:932-940),
+greedy tokens identical."""
+import numpy as np
+import pytest
+
+from minq_b200.minq_format import ModelConfig, quantize_tensor_rule
+from minq_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def _cfg_dict(c):
+    return {k: getattr(c, k) for k in c.__dataclass_fields__}
+
+
+def _records(cfg, dtype, orc, seed, qk_norm, bias, tied):
+    dt = 1 if dtype == "q8_0" else 2
+    out = []
+    for n, t, s, d in synth.random_model_records(cfg, seed, qk_norm=qk_norm, with_bias=bias):
+        if tied and n == "lm_head.weight":
+            continue
+        if quantize_tensor_rule(n, s):
+            out.append((n, dt, s, orc.quantize(dt, d)))
+        else:
+            out.append((n, t, s, d))
+    return out
+
+
+CASES = [
+    # name, dtype, hidden, inter, heads, kv heads, head_dim, vocab, qk_norm, bias, tied, batch
+    ("q4_llama_untied_b5", "q4_0", 256, 512, 8, 2, 64, 300, False, False, False, 5),
+    ("q8_qwen_bias_tied_b3", "q8_0", 256, 384, 4, 2, 64, 257, True, True, True, 3),
+    ("q4_hd128_b9", "q4_0", 512, 768, 8, 2, 128, 200, True, False, False, 9),
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
+def test_batched_step_matches_oracle_per_sequence(mq, orc, case):
+    name, dtype, H, I, nh, nkv, hd, V, qkn, bias, tied, B = case
+    cfg = ModelConfig(H, I, 2, nh, nkv, hd, V, 64, 1e6, 1e-6, bias, dtype)
+    recs = _records(cfg, dtype, orc, 21, qkn, bias, tied)
+    model = mq.Model.from_tensors(cfg, recs)
+    om = orc.Model.from_tensors(_cfg_dict(cfg), {n: (t, s, d) for n, t, s, d in recs})
+    plen, ndec = 6, 4
+    rng = np.random.default_rng(5)
+    prompts = [list(rng.integers(0, V, plen)) for _ in range(B)]
+    cache = model.new_cache(batch=B)
+    # prompts through batched steps, one position per step
+    for i in range(plen):
+        am, logits = model.forward_batch([p[i] for p in prompts], cache)
+    ref_logits, ref_tokens = [], []
+    for p in prompts:
+        oc = om.new_cache()
+        ref_logits.append(om.forward(p, oc))
+        toks, _ = orc.greedy_generate(om, p, ndec + 1)
+        ref_tokens.append(toks)
+    for b in range(B):
+        assert np.abs(logits[b] - ref_logits[b]).max() < 1e-3, b
+        assert int(am[b]) == ref_tokens[b][0]
+    got = [[int(am[b])] for b in range(B)]
+    for _ in range(ndec):
+        am, _ = model.forward_batch([g[-1] for g in got], cache, logits=False)
+        for b in range(B):
+            got[b].append(int(am[b]))
+    assert got == [t[: ndec + 1] for t in ref_tokens]
+
+
+def test_batched_device_continuation_matches_host_steps(mq, orc):
+    import torch
+    cfg = ModelConfig(256, 512, 2, 8, 2, 64, 300, 64, 1e6, 1e-6, False, "q4_0")
+    recs = _records(cfg, "q4_0", orc, 3, False, False, False)
+    model = mq.Model.from_tensors(cfg, recs)
+    B = 4
+    rng = np.random.default_rng(9)
+    first = list(rng.integers(0, 300, B))
+    c1, c2 = model.new_cache(batch=B), model.new_cache(batch=B)
+    a1, _ = model.forward_batch(first, c1, logits=False)
+    a2, _ = model.forward_batch(first, c2, logits=False)
+    host = [list(a1)]
+    for _ in range(5):
+        a1, _ = model.forward_batch(host[-1], c1, logits=False)
+        host.append(list(a1))
+    out = torch.zeros(5 * B, dtype=torch.int32, device="cuda")
+    model.forward_batch_steps(c2, 5, out.data_ptr())
+    torch.cuda.synchronize()
+    dev = out.cpu().numpy().reshape(5, B)
+    assert [list(map(int, r)) for r in dev] == [list(map(int, r)) for r in host[1:]]
+
+
+def test_batched_step_errors(mq, orc):
+    from minq_b200._lib import MinqError
+    cfg = ModelConfig(128, 256, 1, 2, 2, 64, 100, 8, 1e6, 1e-6, False, "q4_0")
+    model = mq.Model.from_tensors(cfg, _records(cfg, "q4_0", orc, 1, False, False, False))
+    cache = model.new_cache(batch=2)
+    with pytest.raises(MinqError):
+        model.forward_batch([1, 2, 3], cache)       # one token per sequence
+    with pytest.raises(MinqError):
+        model.forward_batch([1, 100], cache)        # token >= vocab
+    for i in range(8):
+        model.forward_batch([1, 2], cache, logits=False)
+    with pytest.raises(MinqError):
+        model.forward_batch([1, 2], cache)          # max_seq_len reached

@@ -206,6 +206,20 @@ minq_status minq_model_config(const minq_model* m, minq_config* out);
 minq_status minq_model_weight_bytes(const minq_model* m, uint64_t* out);
 void minq_model_free(minq_model* m);
 
+/* Tensor-parallel decode over `world` GPUs (one process or thread per GPU,
+ * each holding the whole model): minq_tp_unique_id (on one rank) makes the
+ * NCCL id (128 bytes) that the caller hands to every rank; minq_tp_init then
+ * keeps this rank's query / kv heads (q|k|v rows, o_proj columns) and
+ * intermediate rows (gate/up rows, down_proj columns) and joins the NCCL
+ * communicator. Afterwards minq_forward / minq_decode_steps (called by every
+ * rank with the same tokens, in the same order) all-reduce the o_proj and
+ * down_proj partial sums (2 per layer, hidden_size floats each); caches
+ * created afterwards hold this rank's kv heads. Requires quantized
+ * projections and n_heads, n_kv_heads divisible by world, intermediate_size
+ * by 32 * world. */
+minq_status minq_tp_unique_id(void* id_out);
+minq_status minq_tp_init(minq_model* m, int rank, int world, const void* unique_id);
+
 /* KVCache::new / reset (model.rs:117-130). The cache is preallocated in HBM
  * for `max_seq` positions (0 = config.max_seq_len) and `batch` independent
  * sequences (1 for the reference's single-sequence API). */

@@ -98,6 +98,8 @@ SIGNATURES = {
     "minq_forward_device": (I, [P, P, P, S, P, P]),
     "minq_decode_steps": (I, [P, P, S, P]),
     "minq_forward_batch": (I, [P, P, P, S, P, P]),
+    "minq_tp_unique_id": (I, [P]),
+    "minq_tp_init": (I, [P, C.c_int, C.c_int, P]),
     "minq_forward_batch_device": (I, [P, P, S, P]),
     "minq_model_set_graphs": (I, [P, I]),
     "minq_generate": (I, [P, P, S, S, P, S, TOKEN_CB, P, P, C.POINTER(GenStats)]),

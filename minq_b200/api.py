@@ -299,6 +299,13 @@ class Model:
         check(lib().minq_decode_steps(self._h, cache._h, n,
                                       C.c_void_p(d_tokens_out) if d_tokens_out else None))
 
+    def tp_init(self, rank: int, world: int, unique_id: bytes) -> None:
+        """Keep this rank's share of a tensor-parallel split over `world` GPUs and
+        join the NCCL communicator named by `unique_id` (tp_unique_id()); every
+        rank then calls forward / decode_steps with the same tokens."""
+        buf = C.create_string_buffer(bytes(unique_id), 128)
+        check(lib().minq_tp_init(self._h, rank, world, buf))
+
     def forward_batch(self, tokens, cache: "KVCache", logits: bool = True):
         """One batched step: tokens[b] (one per sequence of a batch cache) through
         Model::forward_token (model.rs:273-318) at the cache's position. Returns
@@ -323,6 +330,13 @@ class Model:
         check(lib().minq_forward_device(self._h, cache._h, C.c_void_p(d_tokens), n,
                                         C.c_void_p(d_logits) if d_logits else None,
                                         C.c_void_p(d_argmax) if d_argmax else None))
+
+
+def tp_unique_id() -> bytes:
+    """A fresh NCCL unique id (128 bytes) for Model.tp_init."""
+    buf = C.create_string_buffer(128)
+    check(lib().minq_tp_unique_id(buf))
+    return buf.raw
 
 
 class KVCache:

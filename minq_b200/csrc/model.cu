@@ -30,6 +30,7 @@
 
 #include "common.cuh"
 #include "decode_mk.h"
+#include "nccl_dl.h"
 #include "kernels.h"
 #include "minq_format.h"
 
@@ -73,6 +74,12 @@ using minq::DevTensor;
 struct minq_model {
   minq_config cfg{};
   int device = 0;
+  // tensor parallelism (minq_tp_init): this rank's query / kv heads and
+  // intermediate rows; the full counts on a single GPU
+  int tp_rank = 0, tp_world = 1;
+  void* tp_comm = nullptr;  // ncclComm_t
+  int nh_l = 0, nkv_l = 0;
+  uint64_t I_l = 0;
   cudaStream_t stream = nullptr;
   bool finished = false;
   bool use_graphs = true;
@@ -481,6 +488,9 @@ minq_status model_finish(minq_model* m) {
   if (!device_status_word()) return fail(MINQ_ERR_CUDA, "cannot allocate the device status word");
   if (m->shape_error.empty()) MINQ_TRY(setup_megakernel(m));
   MINQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  m->nh_l = (int)c.n_heads;
+  m->nkv_l = (int)c.n_kv_heads;
+  m->I_l = c.intermediate_size;
   m->finished = true;
   return MINQ_OK;
 }
@@ -507,6 +517,15 @@ minq_status linear(minq_model* m, const DevLinear& l, const float* x, const floa
 
 }  // namespace
 
+// x = sum over the tensor-parallel ranks of x (in place, on the model stream).
+static minq_status tp_allreduce_x(minq_model* m) {
+  const NcclApi& nc = nccl_api();
+  const ncclResult_t r = nc.AllReduce(m->x, m->x, m->cfg.hidden_size, ncclFloat, ncclSum,
+                                      static_cast<ncclComm_t>(m->tp_comm), m->stream);
+  if (r != ncclSuccess) return fail(MINQ_ERR_NCCL, std::string("ncclAllReduce: ") + nc.GetErrorString(r));
+  return MINQ_OK;
+}
+
 // model.rs:273-318 for one token. The token id is read from `d_tok`. In
 // graph mode the position comes from c->d_pos (device) and the attention
 // grid is sized for the cache capacity; otherwise `pos` is used. Logits (and
@@ -514,11 +533,14 @@ minq_status linear(minq_model* m, const DevLinear& l, const float* x, const floa
 minq_status forward_token(minq_model* m, minq_cache* c, const uint32_t* d_tok, size_t pos,
                           bool want_logits, float* d_logits, uint32_t* d_argmax, bool graph) {
   const minq_config& cfg = m->cfg;
-  const int H = (int)cfg.hidden_size, hd = (int)cfg.head_dim, nh = (int)cfg.n_heads,
-            nkv = (int)cfg.n_kv_heads;
-  const uint64_t qd = (uint64_t)nh * hd, kvd = (uint64_t)nkv * hd, I = cfg.intermediate_size;
+  const int H = (int)cfg.hidden_size, hd = (int)cfg.head_dim, nh = m->nh_l, nkv = m->nkv_l;
+  const uint64_t qd = (uint64_t)nh * hd, kvd = (uint64_t)nkv * hd, I = m->I_l;
   const float eps = cfg.rms_norm_eps;
   cudaStream_t s = m->stream;
+  // tensor parallel: o_proj and down_proj give partial sums of x's update;
+  // rank 0 adds the residual, then an all-reduce sums the ranks into x
+  const bool tp = m->tp_world > 1;
+  const float* res = tp && m->tp_rank != 0 ? nullptr : m->x;
   const size_t seq_stride = (size_t)nkv * c->max_seq * hd, head_stride = c->max_seq * hd,
                pos_stride = hd;
   const size_t layer_elems = c->batch * seq_stride;
@@ -545,7 +567,8 @@ minq_status forward_token(minq_model* m, minq_cache* c, const uint32_t* d_tok, s
     MINQ_TRY(launch_attention(m->q_rot, kc, vc, 1, nh, nkv, hd, (int)pos + 1, seq_stride,
                               head_stride, pos_stride, m->att, c->ws, c->ws_bytes, s, dpos,
                               (int)c->max_seq));
-    MINQ_TRY(linear(m, L.o, m->att, nullptr, nullptr, m->x, m->x));  // x += o
+    MINQ_TRY(linear(m, L.o, m->att, nullptr, nullptr, res, m->x));  // x += o
+    if (tp) MINQ_TRY(tp_allreduce_x(m));
     // MLP sub-layer: h = silu(gate(rmsnorm(x))) * up(rmsnorm(x)); x += down(h)
     if (L.gate.tag != MINQ_F32 && L.gate.tag == L.up.tag) {
       MINQ_TRY(launch_qmatvec(L.gate.tag, L.gate.ptr, L.up.ptr, I, H, m->x, L.ffn_norm, eps,
@@ -556,7 +579,8 @@ minq_status forward_token(minq_model* m, minq_cache* c, const uint32_t* d_tok, s
       MINQ_TRY(linear(m, L.up, m->xn, nullptr, nullptr, nullptr, m->ubuf));
       MINQ_TRY(launch_swiglu(m->gbuf, m->ubuf, m->hbuf, I, s));
     }
-    MINQ_TRY(linear(m, L.down, m->hbuf, nullptr, nullptr, m->x, m->x));  // x += down
+    MINQ_TRY(linear(m, L.down, m->hbuf, nullptr, nullptr, res, m->x));  // x += down
+    if (tp) MINQ_TRY(tp_allreduce_x(m));
   }
   if (want_logits) {
     const uint64_t V = cfg.vocab_size;
@@ -625,6 +649,7 @@ static minq_status forward_batch_step(minq_model* m, minq_cache* c, bool want_lo
 // The batched step's activations (first use) and its shape requirements.
 static minq_status batch_ready(minq_model* m, minq_cache* c) {
   const minq_config& cfg = m->cfg;
+  if (m->tp_world > 1) return fail(MINQ_ERR_ARG, "the batched step runs on one GPU");
   if (c->batch > (size_t)kQmmMaxB)
     return fail(MINQ_ERR_ARG, "minq_forward_batch takes at most 64 sequences per cache");
   if (cfg.hidden_size % 32 || cfg.intermediate_size % 32 || (cfg.n_heads * cfg.head_dim) % 32)
@@ -894,9 +919,146 @@ void minq_model_free(minq_model* m) {
   if (!m) return;
   cudaSetDevice(m->device);
   if (m->stream) cudaStreamSynchronize(m->stream);
+  if (m->tp_comm) nccl_api().CommDestroy(static_cast<ncclComm_t>(m->tp_comm));
   for (void* p : m->allocs) cudaFree(p);
   if (m->stream) cudaStreamDestroy(m->stream);
   delete m;
+}
+
+// ---------------------------------------------------------------------------
+// C ABI: tensor parallelism
+
+minq_status minq_tp_unique_id(void* id_out) {
+  if (!id_out) return fail(MINQ_ERR_ARG, "null argument");
+  const NcclApi& nc = nccl_api();
+  if (!nc.ok) return fail(MINQ_ERR_NCCL, "libnccl.so.2 could not be loaded");
+  ncclUniqueId id;
+  const ncclResult_t r = nc.GetUniqueId(&id);
+  if (r != ncclSuccess) return fail(MINQ_ERR_NCCL, std::string("ncclGetUniqueId: ") + nc.GetErrorString(r));
+  std::memcpy(id_out, &id, sizeof(id));
+  return MINQ_OK;
+}
+
+namespace {
+
+// Rows [r0, r1) of a quantized linear as a new device matrix.
+minq_status tp_rows(minq_model* m, DevLinear* l, uint64_t r0, uint64_t r1) {
+  const size_t rb = l->nbytes / l->rows;
+  void* p;
+  MINQ_TRY(dmalloc(m, &p, (r1 - r0) * rb));
+  MINQ_CUDA_TRY(cudaMemcpyAsync(p, static_cast<const char*>(l->ptr) + r0 * rb, (r1 - r0) * rb,
+                                cudaMemcpyDeviceToDevice, m->stream));
+  l->ptr = p;
+  l->rows = r1 - r0;
+  l->nbytes = (r1 - r0) * rb;
+  l->tm_ok = false;
+  return MINQ_OK;
+}
+
+// Columns [c0, c1) (block aligned) of a quantized linear as a new matrix.
+minq_status tp_cols(minq_model* m, DevLinear* l, uint64_t c0, uint64_t c1) {
+  const size_t rb = l->nbytes / l->rows, bb = rb / (l->cols / 32);
+  const size_t nrb = (c1 - c0) / 32 * bb;
+  void* p;
+  MINQ_TRY(dmalloc(m, &p, l->rows * nrb));
+  MINQ_CUDA_TRY(cudaMemcpy2DAsync(p, nrb, static_cast<const char*>(l->ptr) + c0 / 32 * bb, rb, nrb,
+                                  l->rows, cudaMemcpyDeviceToDevice, m->stream));
+  l->ptr = p;
+  l->cols = c1 - c0;
+  l->nbytes = l->rows * nrb;
+  l->tm_ok = false;
+  return MINQ_OK;
+}
+
+// Rows [r0, r1) of q, k and v of the fused matrix (and its bias) as a new
+// fused matrix.
+minq_status tp_qkv(minq_model* m, DevLayer* L, uint64_t q0, uint64_t q1, uint64_t k0, uint64_t k1,
+                   uint64_t v0, uint64_t v1) {
+  DevLinear& l = L->qkv;
+  const size_t rb = l.nbytes / l.rows, n = (q1 - q0) + (k1 - k0) + (v1 - v0);
+  void* p;
+  MINQ_TRY(dmalloc(m, &p, n * rb));
+  char* d = static_cast<char*>(p);
+  const char* src = static_cast<const char*>(l.ptr);
+  size_t at = 0;
+  for (auto [a, b] : {std::pair<uint64_t, uint64_t>{q0, q1}, {k0, k1}, {v0, v1}}) {
+    MINQ_CUDA_TRY(cudaMemcpyAsync(d + at * rb, src + a * rb, (b - a) * rb,
+                                  cudaMemcpyDeviceToDevice, m->stream));
+    at += b - a;
+  }
+  if (L->bias_qkv) {
+    void* bp;
+    MINQ_TRY(dmalloc(m, &bp, n * 4));
+    float* bd = static_cast<float*>(bp);
+    at = 0;
+    for (auto [a, b] : {std::pair<uint64_t, uint64_t>{q0, q1}, {k0, k1}, {v0, v1}}) {
+      MINQ_CUDA_TRY(cudaMemcpyAsync(bd + at, L->bias_qkv + a, (b - a) * 4,
+                                    cudaMemcpyDeviceToDevice, m->stream));
+      at += b - a;
+    }
+    L->bias_qkv = bd;
+  }
+  l.ptr = p;
+  l.rows = n;
+  l.nbytes = n * rb;
+  l.tm_ok = false;
+  return MINQ_OK;
+}
+
+}  // namespace
+
+minq_status minq_tp_init(minq_model* m, int rank, int world, const void* unique_id) {
+  if (!m || !unique_id) return fail(MINQ_ERR_ARG, "null argument");
+  if (!m->finished) return fail(MINQ_ERR_MODEL, "model not finished");
+  if (world < 1 || rank < 0 || rank >= world) return fail(MINQ_ERR_ARG, "bad rank / world");
+  if (m->tp_world > 1) return fail(MINQ_ERR_ARG, "tensor parallelism already set up");
+  if (!m->shape_error.empty()) return fail(MINQ_ERR_SHAPE, m->shape_error);
+  const minq_config& c = m->cfg;
+  const uint64_t hd = c.head_dim, nh = c.n_heads, nkv = c.n_kv_heads, I = c.intermediate_size;
+  if (nh % world || nkv % world || I % (32ull * world) || (nh / world * hd) % 32)
+    return fail(MINQ_ERR_SHAPE, "heads and intermediate rows must split evenly over the ranks "
+                                "in 32-column blocks");
+  for (const DevLayer& L : m->layers)
+    if (L.qkv.tag < 0 || L.o.tag == MINQ_F32 || L.down.tag == MINQ_F32 || L.gate.tag == MINQ_F32 ||
+        L.up.tag == MINQ_F32)
+      return fail(MINQ_ERR_SHAPE, "tensor parallelism needs quantized projections");
+  const NcclApi& nc = nccl_api();
+  if (!nc.ok) return fail(MINQ_ERR_NCCL, "libnccl.so.2 could not be loaded");
+  MINQ_CUDA_TRY(cudaSetDevice(m->device));
+  ncclUniqueId id;
+  std::memcpy(&id, unique_id, sizeof(id));
+  ncclComm_t comm = nullptr;
+  const ncclResult_t r = nc.CommInitRank(&comm, world, id, rank);
+  if (r != ncclSuccess) return fail(MINQ_ERR_NCCL, std::string("ncclCommInitRank: ") + nc.GetErrorString(r));
+  // this rank's heads and intermediate rows (the SURVEY's c5 split: q/k/v rows
+  // by head, gate/up rows, o_proj / down_proj columns)
+  const uint64_t nhl = nh / world, nkvl = nkv / world, Il = I / world, qd = nh * hd, kvd = nkv * hd;
+  const uint64_t q0 = rank * nhl * hd, k0 = rank * nkvl * hd, i0 = rank * Il;
+  for (DevLayer& L : m->layers) {
+    MINQ_TRY(tp_qkv(m, &L, q0, q0 + nhl * hd, qd + k0, qd + k0 + nkvl * hd, qd + kvd + k0,
+                    qd + kvd + k0 + nkvl * hd));
+    MINQ_TRY(tp_cols(m, &L.o, q0, q0 + nhl * hd));
+    MINQ_TRY(tp_rows(m, &L.gate, i0, i0 + Il));
+    MINQ_TRY(tp_rows(m, &L.up, i0, i0 + Il));
+    MINQ_TRY(tp_cols(m, &L.down, i0, i0 + Il));
+    MINQ_TRY(prepare_map(&L.qkv, false, true));
+    MINQ_TRY(prepare_map(&L.o, false, false));
+    MINQ_TRY(prepare_map(&L.down, false, false));
+    if (L.gate.tag == L.up.tag) {
+      MINQ_TRY(prepare_map(&L.gate, true, true));
+      MINQ_TRY(prepare_map(&L.up, true, true));
+    }
+  }
+  MINQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  m->tp_comm = comm;
+  m->tp_rank = rank;
+  m->tp_world = world;
+  m->nh_l = (int)nhl;
+  m->nkv_l = (int)nkvl;
+  m->I_l = Il;
+  m->mk.ok = false;       // the decode megakernel runs on one GPU
+  m->use_graphs = false;  // steps launch eagerly (the all-reduces on the model stream)
+  return MINQ_OK;
 }
 
 // ---------------------------------------------------------------------------
@@ -912,11 +1074,11 @@ minq_status minq_cache_new(minq_model* m, size_t batch, size_t max_seq, minq_cac
   c->m = m;
   c->batch = batch;
   c->max_seq = max_seq;
-  const size_t per_layer = batch * m->cfg.n_kv_heads * max_seq * m->cfg.head_dim;
+  const size_t per_layer = batch * (size_t)m->nkv_l * max_seq * m->cfg.head_dim;
   const size_t bytes = m->cfg.n_layers * per_layer * sizeof(float);
   cudaError_t e = cudaMalloc(&c->k, bytes ? bytes : 16);
   if (e == cudaSuccess) e = cudaMalloc(&c->v, bytes ? bytes : 16);
-  c->ws_bytes = attn_workspace_bytes(batch, m->cfg.n_heads, max_seq, m->cfg.head_dim);
+  c->ws_bytes = attn_workspace_bytes(batch, (size_t)m->nh_l, max_seq, m->cfg.head_dim);
   if (e == cudaSuccess) e = cudaMalloc(&c->ws, c->ws_bytes);
   if (e == cudaSuccess) e = cudaMalloc(&c->d_pos, 16);
   if (e != cudaSuccess) {
@@ -958,7 +1120,7 @@ static minq_status cache_copy(const minq_cache* c, size_t layer, size_t start, s
   if (layer >= cfg.n_layers) return fail(MINQ_ERR_SHAPE, "layer out of range");
   if (start + n > c->max_seq) return fail(MINQ_ERR_SHAPE, "positions exceed cache capacity");
   if (n == 0) return MINQ_OK;
-  const size_t hd = cfg.head_dim, nkv = cfg.n_kv_heads;
+  const size_t hd = cfg.head_dim, nkv = (size_t)c->m->nkv_l;
   const size_t per_layer = c->batch * nkv * c->max_seq * hd;
   MINQ_CUDA_TRY(cudaSetDevice(c->m->device));
   for (int which = 0; which < 2; ++which) {

@@ -54,6 +54,10 @@ WORKLOADS = {
     "qwen3-4b-q4_0": ("qwen3-4b", 2048),
     "qwen2-0.5b-q8_0": ("qwen2-0.5b", 128),
 }
+# Long-context tensor-parallel decode: the Qwen3-4B shape in Q8_0 with the KV
+# cache pre-filled (N(0, 1)) at 32768 positions, greedy decode split over the
+# ranks (heads and intermediate rows; NCCL all-reduce after o_proj / down_proj).
+TP_WORKLOAD = "qwen3-4b-q8_0-tp32k"
 
 
 def parse():
@@ -62,7 +66,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["minq", "reference"], default="minq")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="qwen3-4b-q4_0")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + [TP_WORKLOAD],
+                    default="qwen3-4b-q4_0")
     ap.add_argument("--prompt", type=int, default=None, help="prefill length override")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -457,11 +462,104 @@ def run_minq(args, world, rank, local):
     del cache, model
 
 
+def run_tp(args, world, rank, local):
+    """One greedy sequence of the long-context workload, tensor-parallel over
+    the `world` ranks (single GPU: the decode megakernel)."""
+    import torch
+    import minq_b200 as mq
+    from minq_b200 import synth
+    from dataclasses import replace
+    torch.cuda.set_device(local)
+    ctx, K, W = 32768, args.steps, args.warmup
+    cfg0, qk_norm, tied = synth.ARCH["qwen3-4b"]
+    cfg = replace(cfg0, dtype="q8_0", max_seq_len=ctx + W + 2 * K + 16)
+    model = build_model(mq, synth, cfg, qk_norm, tied, args.seed)  # every rank: the same weights
+    if world > 1:
+        import torch.distributed as dist
+        uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(mq.tp_unique_id()), dtype=torch.uint8))
+        dist.broadcast(uid, 0)
+        model.tp_init(rank, world, bytes(uid.cpu().numpy().tobytes()))
+    cache = model.new_cache()
+    nkv_l = cfg.n_kv_heads // world
+    g = torch.Generator(device="cuda").manual_seed(args.seed + 7)
+    for li in range(cfg.n_layers):  # the KV history (model.rs:103-114 public fields)
+        k = torch.randn(ctx, nkv_l * cfg.head_dim, device="cuda", generator=g)
+        v = torch.randn(ctx, nkv_l * cfg.head_dim, device="cuda", generator=g)
+        cache.write_device(li, 0, k.data_ptr(), v.data_ptr(), ctx)
+        del k, v
+    cache.set_len(ctx)
+    stream = torch.cuda.ExternalStream(model.stream)
+    model.forward_argmax([1], cache)
+    model.decode_steps(cache, W)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(physical_gpu_index(local))
+    clocks.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    model.decode_steps(cache, K)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    ms_max = max_over_ranks(world, ev0.elapsed_time(ev1))
+    # e2e: the public call with host buffers (token in, logits + argmax out)
+    V = cfg.vocab_size
+    h_tok = np.zeros(1, dtype=np.uint32)
+    h_tok[0] = model.forward_argmax([1], cache)
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(K):
+        tok, _ = model.forward_argmax([int(h_tok[0])], cache, logits=True)
+        h_tok[0] = tok
+    e2e_ms = max_over_ranks(world, 1000.0 * (time.perf_counter() - t0))
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    peak = peaks.get("hbm_gbs") or 6650.0
+    # per-GPU algorithmic bytes of a step: this rank's share of the quantized
+    # weights and of the K/V history, the replicated f32 lm_head
+    lm = 4.0 * V * cfg.hidden_size
+    per_gpu = (model.weight_bytes - lm) / world + lm + \
+        2 * 4 * cfg.n_kv_heads * cfg.head_dim * (ctx + W + K / 2) * cfg.n_layers / world
+    gbs = per_gpu / (ms_max / K * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": "decode tok/s", "value": K / (ms_max / 1000.0), "unit": "tok/s",
+            "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_max / K,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": f"{TP_WORKLOAD}: Qwen3-4B shape, Q8_0, KV pre-filled at "
+                                   f"{ctx} positions, 1 sequence",
+                       "parallelism": f"tp{world}" if world > 1 else "single GPU",
+                       "cache_flush": "inputs > L2"},
+            "e2e": {"value": K / (e2e_ms / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": 4,
+                    "d2h_bytes_per_step": 4 * V + 4},
+            "gpu_launches": None,
+            "roofline": {"bound": "hbm", "kernel": "decode step (per GPU)", "achieved": gbs,
+                         "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                         "traffic": None, "per_launch_bytes": per_gpu},
+            "cpu_baseline": None,
+            "clocks": clk,
+        }), flush=True)
+    del cache, model
+
+
 def main():
     args = parse()
     world, rank, local = dist_init()
     try:
-        if args.impl == "reference":
+        if args.workload == TP_WORKLOAD:
+            run_tp(args, world, rank, local)
+        elif args.impl == "reference":
             run_reference(args, world, rank)
         else:
             run_minq(args, world, rank, local)

@@ -235,6 +235,10 @@ minq_status minq_cache_write(minq_cache* c, size_t layer, size_t start, size_t n
                              const float* k, const float* v);
 minq_status minq_cache_read(const minq_cache* c, size_t layer, size_t start, size_t n, float* k,
                             float* v);
+/* minq_cache_write from device memory (the same [n, n_kv*head_dim] layout,
+ * this rank's kv heads after minq_tp_init): the long-context pre-fill. */
+minq_status minq_cache_write_device(minq_cache* c, size_t layer, size_t start, size_t n,
+                                    const float* d_k, const float* d_v);
 minq_status minq_cache_set_len(minq_cache* c, size_t len);
 void minq_cache_free(minq_cache* c);
 

@@ -347,6 +347,12 @@ class KVCache:
         self._h = C.c_void_p()
         check(lib().minq_cache_new(model._h, batch, max_seq, C.byref(self._h)))
 
+    def write_device(self, layer: int, start: int, k_ptr: int, v_ptr: int, n: int) -> None:
+        """Pre-fill positions [start, start+n) of one layer from device memory
+        ([n, n_kv*head_dim] f32 each, this rank's kv heads)."""
+        check(lib().minq_cache_write_device(self._h, layer, start, n, C.c_void_p(k_ptr),
+                                            C.c_void_p(v_ptr)))
+
     def __del__(self):
         h = getattr(self, "_h", None)
         if h and not sys.is_finalizing():

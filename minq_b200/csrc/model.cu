@@ -1115,7 +1115,8 @@ minq_status minq_cache_set_len(minq_cache* c, size_t len) {
 }
 
 static minq_status cache_copy(const minq_cache* c, size_t layer, size_t start, size_t n,
-                              float* host_k, float* host_v, bool to_device) {
+                              float* host_k, float* host_v, bool to_device,
+                              cudaMemcpyKind in_kind = cudaMemcpyHostToDevice) {
   const minq_config& cfg = c->m->cfg;
   if (layer >= cfg.n_layers) return fail(MINQ_ERR_SHAPE, "layer out of range");
   if (start + n > c->max_seq) return fail(MINQ_ERR_SHAPE, "positions exceed cache capacity");
@@ -1131,8 +1132,7 @@ static minq_status cache_copy(const minq_cache* c, size_t layer, size_t start, s
       float* d = dev + h * c->max_seq * hd + start * hd;
       float* hp = host + h * hd;
       if (to_device)
-        MINQ_CUDA_TRY(cudaMemcpy2D(d, hd * 4, hp, nkv * hd * 4, hd * 4, n,
-                                   cudaMemcpyHostToDevice));
+        MINQ_CUDA_TRY(cudaMemcpy2D(d, hd * 4, hp, nkv * hd * 4, hd * 4, n, in_kind));
       else
         MINQ_CUDA_TRY(cudaMemcpy2D(hp, nkv * hd * 4, d, hd * 4, hd * 4, n,
                                    cudaMemcpyDeviceToHost));
@@ -1146,6 +1146,14 @@ minq_status minq_cache_write(minq_cache* c, size_t layer, size_t start, size_t n
   if (!c) return fail(MINQ_ERR_ARG, "null cache");
   MINQ_CUDA_TRY(cudaStreamSynchronize(c->m->stream));
   return cache_copy(c, layer, start, n, const_cast<float*>(k), const_cast<float*>(v), true);
+}
+
+minq_status minq_cache_write_device(minq_cache* c, size_t layer, size_t start, size_t n,
+                                    const float* d_k, const float* d_v) {
+  if (!c) return fail(MINQ_ERR_ARG, "null cache");
+  MINQ_CUDA_TRY(cudaStreamSynchronize(c->m->stream));
+  return cache_copy(c, layer, start, n, const_cast<float*>(d_k), const_cast<float*>(d_v), true,
+                    cudaMemcpyDeviceToDevice);
 }
 
 minq_status minq_cache_read(const minq_cache* c, size_t layer, size_t start, size_t n, float* k,

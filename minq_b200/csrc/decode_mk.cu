@@ -257,6 +257,7 @@ __device__ void mk_cta_plan(const MkParams& p, int L, MkCta* c) {
 
 struct MkFeed {
   unsigned char* ring;
+  const MkLayerPtrs* lps;  // the per-layer pointers, copied to shared memory
   uint64_t* full;   // [kMkS]: the producer lanes' copies of the slot's tile landed
   uint64_t* empty;  // [kMkS]: every consumer warp released the slot
   int li, ph, idx;  // next tile to issue: layer, phase, index in the phase
@@ -320,7 +321,7 @@ __device__ bool mk_issue(const MkParams& p, MkFeed& f, const MkCta* cta, int L) 
   if (!mk_wait_empty(p, f, f.issued)) return false;
   const int slot = f.issued % kMkS;
   unsigned char* dst = f.ring + (size_t)slot * kMkSlot;
-  const MkLayerPtrs& lp = p.layers[f.li];
+  const MkLayerPtrs& lp = f.lps[f.li];
   if (f.ph == 1) {
     const int hd = p.hd, tp = 2048 / hd;
     const int p0 = (cta->t0 + f.idx) * tp, np = min(tp, L - p0);
@@ -855,7 +856,7 @@ __device__ void mk_consume_attn(const MkParams& p, int li, int L, float* scr, Mk
   float* vnew = knew + HD;             // [hd]
   float* wst = vnew + HD;              // [16][HPW][hd + 2] per-warp o, m, l
   float* fw = wst + kMkCW * HPW * (HD + 2);  // merge: weights and the splits' partials
-  const MkLayerPtrs& lp = p.layers[li];
+  const MkLayerPtrs& lp = f.lps[li];
   const size_t head_off = (size_t)li * p.cache_layer_stride + (size_t)kh * p.max_seq * HD;
   // q heads (q_norm, RoPE at position L); the last split also builds the new
   // k (k_norm, RoPE) and v and appends them to the cache
@@ -1046,7 +1047,7 @@ __device__ void mk_consumers(const MkParams& p, unsigned char* sm, MkFeed& f, co
       rope_cs[i] = i < half ? p.rope_cos[(size_t)L * half + i] : p.rope_sin[(size_t)L * half + i - half];
   }
   for (int li = 0; li < p.n_layers && ok; ++li) {
-    const MkLayerPtrs& lp = p.layers[li];
+    const MkLayerPtrs& lp = f.lps[li];
     // P1: q|k|v
     mk_stage_planes<DT>(p, xp, xsb, xsrc, p.H, lp.attn_norm, misc);
     const float* bias = lp.bias_qkv;
@@ -1115,6 +1116,15 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
   __syncthreads();
   MkFeed f;
   f.ring = sm + kMkScrOff + (size_t)p.scratch_bytes;
+  // the per-layer pointers after the ring (one copy for the launch)
+  MkLayerPtrs* lps = reinterpret_cast<MkLayerPtrs*>(f.ring + (size_t)kMkS * kMkSlot);
+  {
+    const uint64_t* src = reinterpret_cast<const uint64_t*>(p.layers);
+    uint64_t* dst = reinterpret_cast<uint64_t*>(lps);
+    const int words = p.n_layers * (int)(sizeof(MkLayerPtrs) / 8);
+    for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+  }
+  f.lps = lps;
   f.full = reinterpret_cast<uint64_t*>(sm);
   f.empty = f.full + kMkS;
   f.li = 0;
@@ -1162,8 +1172,9 @@ size_t mk_scratch_bytes(int H, int I, int qd, int G, int hd, int nsplit) {
   return (std::max(xs, att) + 127) & ~(size_t)127;
 }
 
-size_t mk_smem_bytes(size_t scratch_bytes) {
-  const size_t total = kMkScrOff + scratch_bytes + (size_t)kMkS * kMkSlot;
+size_t mk_smem_bytes(size_t scratch_bytes, int n_layers) {
+  const size_t total = kMkScrOff + scratch_bytes + (size_t)kMkS * kMkSlot +
+                       (size_t)n_layers * sizeof(MkLayerPtrs);
   return total <= 227 * 1024 ? total : 0;
 }
 

@@ -31,6 +31,8 @@ struct MkLayerPtrs {
   const float* k_norm;    // may be null
 };
 
+static_assert(sizeof(MkLayerPtrs) % 8 == 0, "copied as 8-byte words");
+
 struct MkParams {
   const MkLayerPtrs* layers;   // [n_layers]
   int n_layers;
@@ -73,7 +75,7 @@ MkMat mk_plan_mat(int dtype, bool dual, uint64_t rows, uint64_t cols, int grid);
 // and the partials of up to nsplit history splits.
 size_t mk_scratch_bytes(int H, int I, int qd, int G, int hd, int nsplit);
 // Shared memory of the launch, or 0 when it does not fit one SM.
-size_t mk_smem_bytes(size_t scratch_bytes);
+size_t mk_smem_bytes(size_t scratch_bytes, int n_layers);
 minq_status launch_decode_mk(const MkParams& p, int dtype, int grid, size_t smem,
                              cudaStream_t s);
 

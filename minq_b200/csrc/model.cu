@@ -294,7 +294,7 @@ minq_status setup_megakernel(minq_model* m) {
   k.nsplit = std::max(1, grid / (int)nkv);
   for (;;) {
     k.scratch = (int)mk_scratch_bytes((int)H, (int)I, (int)qd, (int)G, (int)hd, k.nsplit);
-    k.smem = mk_smem_bytes(k.scratch);
+    k.smem = mk_smem_bytes(k.scratch, (int)c.n_layers);
     if (k.smem != 0 || k.nsplit == 1) break;
     --k.nsplit;
   }

@@ -58,6 +58,10 @@ WORKLOADS = {
 # cache pre-filled (N(0, 1)) at 32768 positions, greedy decode split over the
 # ranks (heads and intermediate rows; NCCL all-reduce after o_proj / down_proj).
 TP_WORKLOAD = "qwen3-4b-q8_0-tp32k"
+# Isolated GQA decode attention (32 query / 8 kv heads, head_dim 128): RoPE +
+# append + attend over L+1 positions for B sequences, swept over
+# L in {512, 2048, 8192, 32768} x B in {1, 8, 64}.
+ATTN_WORKLOAD = "attn-gqa32-8-hd128"
 
 
 def parse():
@@ -66,7 +70,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["minq", "reference"], default="minq")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + [TP_WORKLOAD],
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + [TP_WORKLOAD, ATTN_WORKLOAD],
                     default="qwen3-4b-q4_0")
     ap.add_argument("--prompt", type=int, default=None, help="prefill length override")
     ap.add_argument("--seed", type=int, default=1234)
@@ -553,11 +557,93 @@ def run_tp(args, world, rank, local):
     del cache, model
 
 
+def run_attn(args, world, rank, local):
+    """The decode-attention op (minq_attn_decode) over the sweep; the line's
+    value is the B = 8, L = 8192 point, `sweep` holds every point. Each
+    point's K/V history (N(0, 1), 2*4*B*8*128*(L+1) bytes) exceeds L2 from
+    L = 8192 at B = 8; smaller points are timed with an L2 flush between
+    calls."""
+    import torch
+    from minq_b200 import _lib
+    torch.cuda.set_device(local)
+    L_ = _lib.lib()
+    nh, nkv, hd, eps = 32, 8, 128, 1e-6
+    P = lambda t: C.c_void_p(t.data_ptr()) if t is not None else None
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    peak = peaks.get("hbm_gbs") or 6650.0
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    s = torch.cuda.current_stream()
+    sweep = []
+    for B in (1, 8, 64):
+        for L in (512, 2048, 8192, 32768):
+            ms_ = L + 1
+            g = torch.Generator(device="cuda").manual_seed(B * 100003 + L)
+            kc = torch.randn((B, nkv, ms_, hd), device="cuda", generator=g)
+            vc = torch.randn((B, nkv, ms_, hd), device="cuda", generator=g)
+            q = torch.randn((B, nh, hd), device="cuda", generator=g)
+            kn = torch.randn((B, nkv, hd), device="cuda", generator=g)
+            vn = torch.randn((B, nkv, hd), device="cuda", generator=g)
+            pos = torch.arange(ms_, dtype=torch.float32, device="cuda")[:, None]
+            inv = 1.0 / (1e6 ** (torch.arange(0, hd, 2, device="cuda", dtype=torch.float32) / hd))
+            cs, sn = torch.cos(pos * inv).contiguous(), torch.sin(pos * inv).contiguous()
+            out = torch.empty((B, nh, hd), device="cuda")
+            wsb = L_.minq_attn_workspace_bytes(B, nh, L + 1)
+            ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device="cuda")
+            big = 8.0 * B * nkv * hd * (L + 1) > 4 * (126 << 20)
+
+            def call():
+                _lib.check(L_.minq_attn_decode(
+                    P(q), P(kn), P(vn), None, None, eps, P(cs), P(sn), B, nh, nkv, hd, L, P(kc),
+                    P(vc), nkv * ms_ * hd, ms_ * hd, hd, P(out), P(ws), wsb,
+                    C.c_void_p(s.cuda_stream)))
+            for _ in range(max(3, args.warmup)):
+                call()
+            torch.cuda.synchronize()
+            tot, n = 0.0, max(8, args.steps // 4)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            for _ in range(n):
+                if not big:
+                    flush.zero_()
+                e0.record(s)
+                call()
+                e1.record(s)
+                torch.cuda.synchronize()
+                tot += e0.elapsed_time(e1)
+            us = 1000.0 * tot / n
+            byts = 8.0 * B * nkv * hd * (L + 1) + 4.0 * B * (2 * nh + 4 * nkv) * hd
+            sweep.append({"B": B, "L": L, "us": round(us, 2), "GB_s": round(byts / us / 1e3, 1),
+                          "frac": round(byts / us / 1e3 / peak, 3)})
+            del kc, vc, q, kn, vn, out, ws
+            torch.cuda.empty_cache()
+    head = next(x for x in sweep if x["B"] == 8 and x["L"] == 8192)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "decode attention GB/s", "value": head["GB_s"], "unit": "GB/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": head["us"] / 1000.0, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{ATTN_WORKLOAD}: RoPE + append + attend, B = 8, L = 8192",
+                       "cache_flush": "256 MB buffer written between calls below 4 x L2"},
+            "roofline": {"bound": "hbm", "kernel": "attn_tma_kernel + attn_combine_kernel",
+                         "achieved": head["GB_s"], "peak": peak, "unit": "GB/s",
+                         "frac": head["frac"], "traffic": None},
+            "sweep": sweep, "cpu_baseline": None,
+        }), flush=True)
+
+
 def main():
     args = parse()
     world, rank, local = dist_init()
     try:
-        if args.workload == TP_WORKLOAD:
+        if args.workload == ATTN_WORKLOAD:
+            if rank == 0:
+                run_attn(args, world, rank, local)
+        elif args.workload == TP_WORKLOAD:
             run_tp(args, world, rank, local)
         elif args.impl == "reference":
             run_reference(args, world, rank)

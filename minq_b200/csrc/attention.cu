@@ -237,7 +237,10 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
 template <int HD>
 struct TmaAttnCfg {
   static constexpr int TP = (2048 / HD) < 32 ? (2048 / HD) : 32;  // positions per tile
-  static constexpr int S = 8;                                       // ring depth
+  // ring depth: a multiple of the 4 consumer warps (warp w takes tiles w,
+  // w + 4, ...), so each slot is only ever used by one warp and its parity
+  // waits see consecutive phases; 4 slots keep two CTAs per SM resident
+  static constexpr int S = 4;
   static constexpr int TILE_FLOATS = TP * HD;
 };
 
@@ -246,6 +249,7 @@ __global__ void __launch_bounds__(160) attn_tma_kernel(AttnParams p) {
   using CFG = TmaAttnCfg<HD>;
   constexpr int TP = CFG::TP, S = CFG::S, TF = CFG::TILE_FLOATS;
   constexpr int NWC = 4;                       // consumer warps
+  static_assert(S % NWC == 0, "every ring slot must belong to one consumer warp");
   constexpr int EPL = 8;
   constexpr int LPP = HD / EPL;
   constexpr int PPS = 32 / LPP;

@@ -1056,8 +1056,8 @@ minq_status minq_tp_init(minq_model* m, int rank, int world, const void* unique_
   m->nh_l = (int)nhl;
   m->nkv_l = (int)nkvl;
   m->I_l = Il;
-  m->mk.ok = false;       // the decode megakernel runs on one GPU
-  m->use_graphs = false;  // steps launch eagerly (the all-reduces on the model stream)
+  m->mk.ok = false;  // the decode megakernel runs on one GPU; graph-captured
+                     // steps record the all-reduces with the kernels
   return MINQ_OK;
 }
 

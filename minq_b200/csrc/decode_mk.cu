@@ -37,13 +37,15 @@
 //
 // Every consumer warp waits for and releases every slot in order (a warp
 // that skipped slots could reach a slot two phases early, where a parity wait
-// cannot tell the phases apart): in projections each warp owns one 4-block
-// group of every chunk and a quarter of the rows; in attention the 16 warps
-// cooperate on each step of up to 32 positions (scores, softmax, p v).
+// cannot tell the phases apart): in projections a group of warps owning one
+// column block per thread computes a whole tile while the other groups take
+// the next tiles; in attention each warp takes one tile of positions for a
+// pair of query heads (scores, online softmax, p v).
 //
-// The quantized dot products are those of the streaming matvec: exact code ->
-// float conversion (byte permute into 2^23 + code), packed f32x2 FMAs, the
-// block scale applied once per block (quantize.rs:252-280). Cross-CTA data
+// The quantized block dots (quantize.rs:252-280) are integer dp4a products of
+// the weight codes with the input staged as fixed-point byte planes per
+// 32-column block, combined in f32 and scaled once per block by the weight
+// scale and the block's power-of-two input scale. Cross-CTA data
 // (x, q|k|v, attention output, h, split partials) is read with ld.global.cg
 // so no stale L1 line is used after a barrier.
 #include <cuda.h>
@@ -72,10 +74,11 @@ static_assert(kMkS % kMkProducers == 0, "each producer warp owns its own slots")
 // block, m = rint(x * 2^(kMkFx - e)) with 2^(e-1) <= max|x| < 2^e, written
 // as kMkNP signed base-256 digits (plane p holds digit p of every column), so
 // that the block dot with the weight codes is a sum of exact integer dp4a
-// products. kMkNP = 4 keeps 31 bits of the block maximum, more than the 24 of
-// an f32 product, so a block whose largest input is 2^7 times its typical one
-// still sees f32-grade inputs.
-constexpr int kMkNP = 4;
+// products. kMkNP = 3 keeps 23 bits of the block maximum (an input's error
+// is at most 2^-23 of the block's largest magnitude, about one f32 rounding
+// of that element); each further plane would add 8 bits for 8 more dp4a per
+// block, and the dp4a count bounds the projection phases.
+constexpr int kMkNP = 3;
 constexpr int kMkFx = 8 * kMkNP - 2;           // |m| <= 2^kMkFx
 // Words of one staged block: 8 * kMkNP plane words (Q4_0: [word j][plane]
 // [low / high nibble columns]; Q8_0: [word j][plane]), then kMkNP Q4_0
@@ -90,6 +93,40 @@ constexpr int kMkScrOff = 9728;                // x / attention scratch, then th
 __device__ __forceinline__ float ldcg(const float* p) { return __ldcg(p); }
 __device__ __forceinline__ float4 ldcg4(const float* p) {
   return __ldcg(reinterpret_cast<const float4*>(p));
+}
+
+// Shared-memory loads by 32-bit shared address: the ring slots and the
+// staged inputs are reached through pointers whose address space the
+// compiler cannot always see, and a generic load to shared memory takes the
+// slower L1 path. Volatile keeps them after the mbarrier waits (also volatile).
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float lds_f32(uint32_t a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float2 lds_f32x2(uint32_t a) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float4 lds_f32x4(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint4 lds_u32x4(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(a));
+  return v;
 }
 
 // 4-way byte dot products with 32-bit accumulate: unsigned codes (Q4_0
@@ -119,16 +156,15 @@ __device__ __forceinline__ uint32_t pack_lo_bytes(int a, int b, int c, int d) {
 // -8 offset is the staged correction (-128 * digit sum per plane), which
 // also starts each plane's sum.
 template <int DT>
-__device__ __forceinline__ float mk_block_dot(const unsigned char* blk, const uint32_t (&xw)[kMkRecW]) {
-  const float d = *reinterpret_cast<const float*>(blk);
-  const uint32_t* cw = reinterpret_cast<const uint32_t*>(blk + 4);
+__device__ __forceinline__ float mk_block_dot(uint32_t blk, const uint32_t (&xw)[kMkRecW]) {
+  const float d = lds_f32(blk);  // blk: shared address of the block
   int s[kMkNP];
   if (DT == MINQ_Q8_0) {
 #pragma unroll
     for (int q = 0; q < kMkNP; ++q) s[q] = 0;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const uint32_t w = cw[j];
+      const uint32_t w = lds_u32(blk + 4 + 4 * j);
 #pragma unroll
       for (int q = 0; q < kMkNP; ++q) s[q] = dp4a_ss(w, xw[j * kMkNP + q], s[q]);
     }
@@ -137,7 +173,7 @@ __device__ __forceinline__ float mk_block_dot(const unsigned char* blk, const ui
     for (int q = 0; q < kMkNP; ++q) s[q] = (int)xw[8 * kMkNP + q];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const uint32_t w = cw[j];
+      const uint32_t w = lds_u32(blk + 4 + 4 * j);
       const uint32_t hi = w & 0xF0F0F0F0u;          // 16 * high nibbles: odd columns
       const uint32_t lo = (w << 4) & 0xF0F0F0F0u;   // 16 * low nibbles: even columns
 #pragma unroll
@@ -431,7 +467,9 @@ __device__ bool mk_grid_sync(const MkParams& p, unsigned long long target, int* 
         }
       }
     }
-    __threadfence();
+    // no trailing fence: the acquire load that saw the last arrival orders
+    // this CTA's later reads after every CTA's released writes, and the named
+    // barrier below extends that order to the CTA's other threads
     *reinterpret_cast<volatile int*>(flag) = ok;
   }
   mk_sync();
@@ -620,10 +658,10 @@ __device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const uint32_t
   uint32_t xw[kMkRecW];
   float sb = 0.0f;
   {
-    const uint4* rec = reinterpret_cast<const uint4*>(xp + (size_t)(has_col ? col : 0) * kMkRecW);
+    const uint32_t rec = smem_u32(xp) + (uint32_t)(has_col ? col : 0) * kMkRecW * 4;
 #pragma unroll
     for (int i = 0; i < kMkRecW / 4; ++i) {
-      const uint4 v = rec[i];
+      const uint4 v = lds_u32x4(rec + 16 * i);
       xw[4 * i] = v.x;
       xw[4 * i + 1] = v.y;
       xw[4 * i + 2] = v.z;
@@ -644,13 +682,13 @@ __device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const uint32_t
       const int g0 = k * TB, g1 = min(g0 + TB, total);
       const int r_lo = g0 / nb, r_hi = (g1 - 1) / nb;
       float* rr = red + (k & 1) * plane + half * cnt * WG + wc;
-      const unsigned char* base = tile - (size_t)g0 * BB;  // block g at base + g * BB
+      const uint32_t base = smem_u32(tile) - (uint32_t)(g0 * BB);  // block g at base + g * BB
       for (int R = r_lo; R <= r_hi; R += 2) {  // two rows at a time for ILP
         const int ga = R * nb + col, gb = ga + nb;
         float va = 0.0f, vb = 0.0f;
-        if (col < nb && ga >= g0 && ga < g1) va = mk_block_dot<DT>(base + (size_t)ga * BB, xw) * sb;
+        if (col < nb && ga >= g0 && ga < g1) va = mk_block_dot<DT>(base + (uint32_t)(ga * BB), xw) * sb;
         if (col < nb && R + 1 <= r_hi && gb < g1)
-          vb = mk_block_dot<DT>(base + (size_t)gb * BB, xw) * sb;
+          vb = mk_block_dot<DT>(base + (uint32_t)(gb * BB), xw) * sb;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
           va += __shfl_xor_sync(0xffffffffu, va, o);
@@ -732,27 +770,27 @@ __device__ void mk_head_prep(const MkParams& p, const float* src, const float* g
 // of every head. Ks points at the swizzled K rows (or, with swz = false, at
 // plain rows: the new position).
 template <int DPL, int GM>
-__device__ __forceinline__ void mk_attn_tile(const float* qs, int G, const float* Ks, bool swz,
-                                             const float* V, int np, float scale, float (&m)[GM],
-                                             float (&l)[GM], float (&o)[GM][DPL]) {
+__device__ __forceinline__ void mk_attn_tile(uint32_t qs, int G, uint32_t Ks, bool swz, uint32_t V,
+                                             int np, float scale, float (&m)[GM], float (&l)[GM],
+                                             float (&o)[GM][DPL]) {
   constexpr int HD = 32 * DPL, NCH = HD / 4, TP = 2048 / HD, HS = 32 / TP, GL = (GM + HS - 1) / HS;
   const int lane = threadIdx.x & 31, h = lane / TP, j = lane - h * TP;
   float s[GL];
 #pragma unroll
   for (int k = 0; k < GL; ++k) s[k] = 0.0f;
   if (j < np) {
-    const float* kr = Ks + j * HD;
+    const uint32_t kr = Ks + (uint32_t)(j * HD * 4);
     const int sw = swz ? (j & 15) : 0;  // the producer's K chunk swizzle
     float a[GL][4];  // four independent partial sums per head
 #pragma unroll
     for (int k = 0; k < GL; ++k) a[k][0] = a[k][1] = a[k][2] = a[k][3] = 0.0f;
 #pragma unroll 4
     for (int c = 0; c < NCH; ++c) {
-      const float4 kv = *reinterpret_cast<const float4*>(kr + 4 * (c ^ sw));
+      const float4 kv = lds_f32x4(kr + (uint32_t)(16 * (c ^ sw)));
 #pragma unroll
       for (int k = 0; k < GL; ++k) {
         if (h + HS * k < G) {
-          const float4 qv = *reinterpret_cast<const float4*>(qs + (h + HS * k) * HD + 4 * c);
+          const float4 qv = lds_f32x4(qs + (uint32_t)(((h + HS * k) * HD + 4 * c) * 4));
           a[k][0] = fmaf(qv.x, kv.x, a[k][0]);
           a[k][1] = fmaf(qv.y, kv.y, a[k][1]);
           a[k][2] = fmaf(qv.z, kv.z, a[k][2]);
@@ -807,17 +845,18 @@ __device__ __forceinline__ void mk_attn_tile(const float* qs, int G, const float
     if (g < G) l[g] += __shfl_sync(0xffffffffu, s[g / HS], (g % HS) * TP);
 #pragma unroll 4
   for (int jj = 0; jj < np; ++jj) {
-    const float* vr = V + jj * HD + DPL * lane;
+    const uint32_t vr = V + (uint32_t)((jj * HD + DPL * lane) * 4);
     float v[DPL];
     if (DPL == 4) {
-      const float4 v4 = *reinterpret_cast<const float4*>(vr);
+      const float4 v4 = lds_f32x4(vr);
       v[0] = v4.x;
       v[1] = v4.y;
       v[2] = v4.z;
       v[3] = v4.w;
     } else {
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) v[e] = vr[e];
+      const float2 v2 = lds_f32x2(vr);
+      v[0] = v2.x;
+      v[DPL - 1] = v2.y;
     }
 #pragma unroll
     for (int g = 0; g < GM; ++g) {
@@ -886,12 +925,13 @@ __device__ void mk_consume_attn(const MkParams& p, int li, int L, float* scr, Mk
   for (int t = t0; t < t1; ++t, ++it) {
     const float* kt = reinterpret_cast<const float*>(mk_next_tile(p, f, it));
     if (served && (t - t0) % WPG == slot)
-      mk_attn_tile<DPL, HPW>(qs + g0 * HD, gw, kt, true, kt + TP * HD, min(TP, L - t * TP),
-                             p.scale, m, l, o);
+      mk_attn_tile<DPL, HPW>(smem_u32(qs + g0 * HD), gw, smem_u32(kt), true,
+                             smem_u32(kt + TP * HD), min(TP, L - t * TP), p.scale, m, l, o);
     mk_release(f, it);
   }
   if (served && last && (t1 - t0) % WPG == slot)
-    mk_attn_tile<DPL, HPW>(qs + g0 * HD, gw, knew, false, vnew, 1, p.scale, m, l, o);
+    mk_attn_tile<DPL, HPW>(smem_u32(qs + g0 * HD), gw, smem_u32(knew), false, smem_u32(vnew), 1,
+                           p.scale, m, l, o);
 #pragma unroll
   for (int g = 0; g < HPW; ++g) {
     if (served && g < gw) {

@@ -683,21 +683,29 @@ __device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const uint32_t
       const int r_lo = g0 / nb, r_hi = (g1 - 1) / nb;
       float* rr = red + (k & 1) * plane + half * cnt * WG + wc;
       const uint32_t base = smem_u32(tile) - (uint32_t)(g0 * BB);  // block g at base + g * BB
-      for (int R = r_lo; R <= r_hi; R += 2) {  // two rows at a time for ILP
-        const int ga = R * nb + col, gb = ga + nb;
-        float va = 0.0f, vb = 0.0f;
-        if (col < nb && ga >= g0 && ga < g1) va = mk_block_dot<DT>(base + (uint32_t)(ga * BB), xw) * sb;
-        if (col < nb && R + 1 <= r_hi && gb < g1)
-          vb = mk_block_dot<DT>(base + (uint32_t)(gb * BB), xw) * sb;
+      for (int R = r_lo; R <= r_hi; R += 4) {  // four rows at a time for ILP
+        float v[4];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          va += __shfl_xor_sync(0xffffffffu, va, o);
-          vb += __shfl_xor_sync(0xffffffffu, vb, o);
+        for (int k = 0; k < 4; ++k) {
+          const int g = (R + k) * nb + col;
+          v[k] = col < nb && R + k <= r_hi && g >= g0 && g < g1
+                     ? mk_block_dot<DT>(base + (uint32_t)(g * BB), xw) * sb
+                     : 0.0f;
         }
-        if (lane == 0) {
-          rr[(size_t)R * WG] = va;
-          if (R + 1 <= r_hi) rr[(size_t)(R + 1) * WG] = vb;
-        }
+        // transposed warp sum of the four rows: the upper half-warp keeps
+        // rows 2, 3 and sends rows 0, 1, then lanes with bit 3 set keep the
+        // odd row; the lanes 0, 8, 16, 24 end with rows R .. R + 3
+        const bool u16 = lane & 16, u8 = lane & 8;
+        float a0 = u16 ? v[2] : v[0], a1 = u16 ? v[3] : v[1];
+        a0 += __shfl_xor_sync(0xffffffffu, u16 ? v[0] : v[2], 16);
+        a1 += __shfl_xor_sync(0xffffffffu, u16 ? v[1] : v[3], 16);
+        float s = u8 ? a1 : a0;
+        s += __shfl_xor_sync(0xffffffffu, u8 ? a0 : a1, 8);
+        s += __shfl_xor_sync(0xffffffffu, s, 4);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        const int k = ((lane >> 4) << 1) | ((lane >> 3) & 1);
+        if ((lane & 7) == 0 && R + k <= r_hi) rr[(size_t)(R + k) * WG] = s;
       }
     }
     mk_release(f, it);
@@ -760,110 +768,107 @@ __device__ void mk_head_prep(const MkParams& p, const float* src, const float* g
   }
 }
 
-// One tile of the online softmax of every query head of the kv head, run by
-// one warp (model.rs:223-248: s = q.k / sqrt(hd), softmax over positions,
-// o = sum p v). Scores: lane (h, j) = (lane / TP, lane mod TP) takes position
-// j of the tile for the heads g = h, h + HS, ... (HS = 32 / TP lanes per
-// position), reading K row j in the producer's swizzled chunk order while
-// every lane reads the same chunk of q. The running max m[g] and sum l[g]
-// are replicated in all lanes; lane l owns output dims DPL l .. DPL l + DPL - 1
-// of every head. Ks points at the swizzled K rows (or, with swz = false, at
-// plain rows: the new position).
-template <int DPL, int GM>
-__device__ __forceinline__ void mk_attn_tile(uint32_t qs, int G, uint32_t Ks, bool swz, uint32_t V,
-                                             int np, float scale, float (&m)[GM], float (&l)[GM],
-                                             float (&o)[GM][DPL]) {
-  constexpr int HD = 32 * DPL, NCH = HD / 4, TP = 2048 / HD, HS = 32 / TP, GL = (GM + HS - 1) / HS;
-  const int lane = threadIdx.x & 31, h = lane / TP, j = lane - h * TP;
-  float s[GL];
+// One tile of the online softmax of a pair of query heads of the kv head,
+// run by one warp (model.rs:223-248: s = q.k / sqrt(hd), softmax over
+// positions, o = sum p v). Lane l owns dims DPL l .. DPL l + DPL - 1 and
+// keeps those of both heads' queries in registers (q); for 16 positions at a
+// time it forms the partial products with each K row, and one transposed
+// warp sum of the 32 partials (16 positions x 2 heads) leaves lane l with
+// the score of position l mod 16 for head l / 16. The running max m and sum
+// l are replicated in every lane, o[g] holds the lane's dims of head g; only
+// heads g < gw are live. Ks: K rows in the producer's swizzled chunk order
+// (swz) or plain (the new position); V: plain rows. np >= 1 positions.
+template <int DPL>
+__device__ __forceinline__ void mk_attn_tile(const float (&q)[2][DPL], int gw, uint32_t Ks,
+                                             bool swz, uint32_t V, int np, float scale,
+                                             float (&m)[2], float (&l)[2], float (&o)[2][DPL]) {
+  constexpr int HD = 32 * DPL;
+  const int lane = threadIdx.x & 31, hl = lane >> 4, jl = lane & 15;
+  for (int j0 = 0; j0 < np; j0 += 16) {
+    float v[32];  // v[16 g + j]: this lane's partial of head g at position j0 + j
 #pragma unroll
-  for (int k = 0; k < GL; ++k) s[k] = 0.0f;
-  if (j < np) {
-    const uint32_t kr = Ks + (uint32_t)(j * HD * 4);
-    const int sw = swz ? (j & 15) : 0;  // the producer's K chunk swizzle
-    float a[GL][4];  // four independent partial sums per head
+    for (int j = 0; j < 16; ++j) {
+      float k[DPL];
 #pragma unroll
-    for (int k = 0; k < GL; ++k) a[k][0] = a[k][1] = a[k][2] = a[k][3] = 0.0f;
-#pragma unroll 4
-    for (int c = 0; c < NCH; ++c) {
-      const float4 kv = lds_f32x4(kr + (uint32_t)(16 * (c ^ sw)));
-#pragma unroll
-      for (int k = 0; k < GL; ++k) {
-        if (h + HS * k < G) {
-          const float4 qv = lds_f32x4(qs + (uint32_t)(((h + HS * k) * HD + 4 * c) * 4));
-          a[k][0] = fmaf(qv.x, kv.x, a[k][0]);
-          a[k][1] = fmaf(qv.y, kv.y, a[k][1]);
-          a[k][2] = fmaf(qv.z, kv.z, a[k][2]);
-          a[k][3] = fmaf(qv.w, kv.w, a[k][3]);
+      for (int e = 0; e < DPL; ++e) k[e] = 0.0f;
+      const int jj = j0 + j;
+      if (jj < np) {
+        const int sw = swz ? (jj & 15) : 0;
+        const uint32_t row = Ks + (uint32_t)(jj * HD * 4);
+        if constexpr (DPL == 4) {
+          const float4 k4 = lds_f32x4(row + (uint32_t)(16 * (lane ^ sw)));
+          k[0] = k4.x;
+          k[1] = k4.y;
+          k[2] = k4.z;
+          k[3] = k4.w;
+        } else {
+          const float2 k2 = lds_f32x2(row + (uint32_t)(16 * ((lane >> 1) ^ sw) + 8 * (lane & 1)));
+          k[0] = k2.x;
+          k[1] = k2.y;
         }
       }
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        float a = 0.0f;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) a = fmaf(q[g][e], k[e], a);
+        v[16 * g + j] = a;
+      }
     }
+    // transposed warp sum: at the level of lane bit b the lanes with bit b
+    // set keep the upper half of their values and send the lower half
 #pragma unroll
-    for (int k = 0; k < GL; ++k) s[k] = (a[k][0] + a[k][1]) + (a[k][2] + a[k][3]);
-  }
-  // per head: tile max and sum over the TP lanes of its half, new running
-  // max, rescale of the running sums and outputs, numerators p
-  float pr[GL];
+    for (int lv = 0; lv < 5; ++lv) {
+      const int b = 16 >> lv, n = 16 >> lv;
+      const bool up = (lane & b) != 0;
 #pragma unroll
-  for (int k = 0; k < GL; ++k) {
-    const float sv = j < np ? s[k] * scale : -INFINITY;
-    float mt = sv;
+      for (int i = 0; i < n; ++i) {
+        const float keep = up ? v[i + n] : v[i], send = up ? v[i] : v[i + n];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, b);
+      }
+    }
+    const bool valid = j0 + jl < np && hl < gw;
+    const float sc = valid ? v[0] * scale : -INFINITY;
+    float mt = sc;  // tile max of head hl over the 16 lanes of its half-warp
 #pragma unroll
-    for (int o_ = TP / 2; o_ > 0; o_ >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o_));
-    s[k] = sv;
-    pr[k] = mt;  // tile max of head h + HS k (finite: np >= 1)
-  }
+    for (int o_ = 8; o_ > 0; o_ >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o_));
+    const float mtg[2] = {__shfl_sync(0xffffffffu, mt, 0), __shfl_sync(0xffffffffu, mt, 16)};
 #pragma unroll
-  for (int g = 0; g < GM; ++g) {
-    if (g < G) {
-      const float mt = __shfl_sync(0xffffffffu, pr[g / HS], (g % HS) * TP);
-      const float mn = fmaxf(m[g], mt);
+    for (int g = 0; g < 2; ++g) {
+      const float mn = fmaxf(m[g], mtg[g]);
       const float c = m[g] == -INFINITY ? 0.0f : expf(m[g] - mn);
       m[g] = mn;
       l[g] *= c;
 #pragma unroll
       for (int e = 0; e < DPL; ++e) o[g][e] *= c;
     }
-  }
-  // numerators with each lane's own head max, and their sums
+    const float pr = valid ? expf(sc - (hl ? m[1] : m[0])) : 0.0f;
+    float ps = pr;
 #pragma unroll
-  for (int k = 0; k < GL; ++k) {
-    float mk = -INFINITY;
-#pragma unroll
-    for (int g = 0; g < GM; ++g)
-      if (g / HS == k && g % HS == h) mk = m[g];
-    const bool valid = h + HS * k < G && s[k] != -INFINITY;
-    const float e = valid ? expf(s[k] - mk) : 0.0f;
-    float sum = e;
-#pragma unroll
-    for (int o_ = TP / 2; o_ > 0; o_ >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o_);
-    pr[k] = e;
-    s[k] = sum;  // this tile's sum of numerators for head h + HS k
-  }
-#pragma unroll
-  for (int g = 0; g < GM; ++g)
-    if (g < G) l[g] += __shfl_sync(0xffffffffu, s[g / HS], (g % HS) * TP);
+    for (int o_ = 8; o_ > 0; o_ >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o_);
+    l[0] += __shfl_sync(0xffffffffu, ps, 0);
+    l[1] += __shfl_sync(0xffffffffu, ps, 16);
+    const int nj = min(16, np - j0);
 #pragma unroll 4
-  for (int jj = 0; jj < np; ++jj) {
-    const uint32_t vr = V + (uint32_t)((jj * HD + DPL * lane) * 4);
-    float v[DPL];
-    if (DPL == 4) {
-      const float4 v4 = lds_f32x4(vr);
-      v[0] = v4.x;
-      v[1] = v4.y;
-      v[2] = v4.z;
-      v[3] = v4.w;
-    } else {
-      const float2 v2 = lds_f32x2(vr);
-      v[0] = v2.x;
-      v[DPL - 1] = v2.y;
-    }
+    for (int j = 0; j < nj; ++j) {
+      const uint32_t vr = V + (uint32_t)(((j0 + j) * HD + DPL * lane) * 4);
+      float vv[DPL];
+      if constexpr (DPL == 4) {
+        const float4 v4 = lds_f32x4(vr);
+        vv[0] = v4.x;
+        vv[1] = v4.y;
+        vv[2] = v4.z;
+        vv[3] = v4.w;
+      } else {
+        const float2 v2 = lds_f32x2(vr);
+        vv[0] = v2.x;
+        vv[1] = v2.y;
+      }
+      const float p0 = __shfl_sync(0xffffffffu, pr, j), p1 = __shfl_sync(0xffffffffu, pr, 16 + j);
 #pragma unroll
-    for (int g = 0; g < GM; ++g) {
-      if (g < G) {
-        const float pj = __shfl_sync(0xffffffffu, pr[g / HS], (g % HS) * TP + jj);
-#pragma unroll
-        for (int e = 0; e < DPL; ++e) o[g][e] = fmaf(pj, v[e], o[g][e]);
+      for (int e = 0; e < DPL; ++e) {
+        o[0][e] = fmaf(p0, vv[e], o[0][e]);
+        o[1][e] = fmaf(p1, vv[e], o[1][e]);
       }
     }
   }
@@ -873,8 +878,8 @@ __device__ __forceinline__ void mk_attn_tile(uint32_t qs, int G, uint32_t Ks, bo
 // positions (swizzled K rows, then V rows, in the slot) and, in the head's
 // last split, the new position. The query heads form HG = ceil(G / 2) pairs;
 // warp w serves pair w mod HG on the tiles t0 + w / HG, t0 + w / HG + 16 / HG,
-// ... (every warp still waits for and releases every tile in order), the new
-// position going to the warps next in that order; the warp states then merge
+// ..., the new position going to the warps next in that order; the warp
+// states then merge
 // into this split's partial (o, m, l) per head. The last split of the
 // head to arrive (a counter per head) merges all of the head's split
 // partials into the attention output; the others go on to the grid barrier.
@@ -922,16 +927,39 @@ __device__ void mk_consume_attn(const MkParams& p, int li, int L, float* scr, Mk
 #pragma unroll
     for (int e = 0; e < DPL; ++e) o[g][e] = 0.0f;
   }
-  for (int t = t0; t < t1; ++t, ++it) {
-    const float* kt = reinterpret_cast<const float*>(mk_next_tile(p, f, it));
-    if (served && (t - t0) % WPG == slot)
-      mk_attn_tile<DPL, HPW>(smem_u32(qs + g0 * HD), gw, smem_u32(kt), true,
-                             smem_u32(kt + TP * HD), min(TP, L - t * TP), p.scale, m, l, o);
-    mk_release(f, it);
+  // this warp's two query heads, its lane's dims, in registers
+  float q[HPW][DPL];
+#pragma unroll
+  for (int g = 0; g < HPW; ++g)
+#pragma unroll
+    for (int e = 0; e < DPL; ++e)
+      q[g][e] = served && g < gw ? qs[(g0 + g) * HD + DPL * lane + e] : 0.0f;
+  // The tiles go in rounds of at most kMkS: a warp waits only for the tiles
+  // it computes and releases the round's other tiles at once (lane i the
+  // round's tile i). The consumer sync closing a round means that every
+  // warp has released every earlier tile before a release of the next
+  // round's tiles (each empty barrier takes one tile's releases at a time),
+  // and that the tile a slot held before the one waited on was complete
+  // (a full barrier is never waited on two phases ahead).
+  const int ntile = t1 - t0;
+  for (int r0 = 0; r0 < ntile; r0 += kMkS) {
+    const int rn = min(kMkS, ntile - r0);
+    {
+      const int i = r0 + lane;
+      if (lane < rn && !(served && i % WPG == slot)) mbar_arrive(&f.empty[(it + i) % kMkS]);
+    }
+    for (int i = r0; i < r0 + rn; ++i) {
+      if (!served || i % WPG != slot) continue;
+      const uint32_t kt = smem_u32(mk_next_tile(p, f, it + i));
+      mk_attn_tile<DPL>(q, gw, kt, true, kt + (uint32_t)(TP * HD * 4), min(TP, L - (t0 + i) * TP),
+                        p.scale, m, l, o);
+      mk_release(f, it + i);
+    }
+    mk_sync();
   }
-  if (served && last && (t1 - t0) % WPG == slot)
-    mk_attn_tile<DPL, HPW>(smem_u32(qs + g0 * HD), gw, smem_u32(knew), false, smem_u32(vnew), 1,
-                           p.scale, m, l, o);
+  it += ntile;
+  if (served && last && ntile % WPG == slot)
+    mk_attn_tile<DPL>(q, gw, smem_u32(knew), false, smem_u32(vnew), 1, p.scale, m, l, o);
 #pragma unroll
   for (int g = 0; g < HPW; ++g) {
     if (served && g < gw) {

@@ -35,12 +35,14 @@
 //     (f32::total_cmp order, ties to the lowest index, sampler.rs:10-17),
 //     the token and the position written back for the next step.
 //
-// Every consumer warp waits for and releases every slot in order (a warp
-// that skipped slots could reach a slot two phases early, where a parity wait
-// cannot tell the phases apart): in projections a group of warps owning one
-// column block per thread computes a whole tile while the other groups take
-// the next tiles; in attention each warp takes one tile of positions for a
-// pair of query heads (scores, online softmax, p v).
+// Only the warps that compute a tile wait for it and release it: in
+// projections a group of warps owning one column block per thread computes
+// a whole tile while the other groups take the next tiles; in attention each
+// warp takes one tile of positions for a pair of query heads (scores, online
+// softmax, p v). A consumer first waits until the slot's tag (written by the
+// producer once the slot's previous tile was released) names its tile, so
+// its parity wait on the full barrier can never match an older phase, and
+// the releases of a tile add up to the empty barrier's count.
 //
 // The quantized block dots (quantize.rs:252-280) are integer dp4a products of
 // the weight codes with the input staged as fixed-point byte planes per
@@ -85,6 +87,7 @@ constexpr int kMkFx = 8 * kMkNP - 2;           // |m| <= 2^kMkFx
 // offset corrections; a multiple of 4 words for 16-byte loads.
 constexpr int kMkRecW = (9 * kMkNP + 3) & ~3;
 constexpr int kMkMiscOff = 256;                // small reductions and flags
+static_assert(kMkS * (16 + 4) <= kMkMiscOff, "ring barriers and slot tags precede the misc area");
 constexpr int kMkCtaOff = 768;                 // the CTA's plan (MkCta)
 constexpr int kMkRedOff = 1024;                // projection row sums, 2048 floats
 constexpr int kMkRopeOff = 9216;               // cos | sin of this position's RoPE row
@@ -295,7 +298,8 @@ struct MkFeed {
   unsigned char* ring;
   const MkLayerPtrs* lps;  // the per-layer pointers, copied to shared memory
   uint64_t* full;   // [kMkS]: the producer lanes' copies of the slot's tile landed
-  uint64_t* empty;  // [kMkS]: every consumer warp released the slot
+  uint64_t* empty;  // [kMkS]: the warps computing the slot's tile released it
+  int* tag;         // [kMkS]: the tile last issued into the slot
   int li, ph, idx;  // next tile to issue: layer, phase, index in the phase
   int issued;       // tiles issued so far (slot = issued % kMkS)
 };
@@ -356,6 +360,9 @@ __device__ bool mk_issue(const MkParams& p, MkFeed& f, const MkCta* cta, int L) 
   const int lane = threadIdx.x & 31;
   if (!mk_wait_empty(p, f, f.issued)) return false;
   const int slot = f.issued % kMkS;
+  // the slot now takes tile f.issued: its previous tile was computed and
+  // released, so a consumer that sees this tag waits on the right phase
+  if (lane == 0) st_release_shared(&f.tag[slot], f.issued);
   unsigned char* dst = f.ring + (size_t)slot * kMkSlot;
   const MkLayerPtrs& lp = f.lps[f.li];
   if (f.ph == 1) {
@@ -416,6 +423,21 @@ __device__ void mk_producer(const MkParams& p, MkFeed& f, const MkCta* cta, int 
 __device__ const unsigned char* mk_next_tile(const MkParams& p, const MkFeed& f, int it) {
   const int s = it % kMkS;
   const uint32_t parity = (uint32_t)(it / kMkS) & 1u;
+  // first the slot's tag: once it names this tile, the slot's previous tile
+  // was complete, so the parity wait below cannot match an older phase
+  if (ld_acquire_shared(&f.tag[s]) != it) {
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t n = 1; ld_acquire_shared(&f.tag[s]) != it; ++n) {
+      if ((n & 15) == 0) {
+        if (*reinterpret_cast<volatile int*>(p.abort_flag)) return f.ring + (size_t)s * kMkSlot;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+          atomicOr(p.status, kDeviceTimeout);
+          atomicExch(p.abort_flag, 1);
+          return f.ring + (size_t)s * kMkSlot;
+        }
+      }
+    }
+  }
   if (!mbar_try_wait(&f.full[s], parity)) {
     const uint64_t t0 = global_timer_ns();
     for (;;) {
@@ -431,12 +453,12 @@ __device__ const unsigned char* mk_next_tile(const MkParams& p, const MkFeed& f,
   return f.ring + (size_t)s * kMkSlot;
 }
 
-// The warp is done with tile `it`.
-__device__ __forceinline__ void mk_release(const MkFeed& f, int it) {
+// The warp is done with tile `it`; the warps computing a tile release it
+// with counts that add up to kMkCW.
+__device__ __forceinline__ void mk_release(const MkFeed& f, int it, uint32_t count) {
   __syncwarp();
-  if ((threadIdx.x & 31) == 0) mbar_arrive(&f.empty[it % kMkS]);
+  if ((threadIdx.x & 31) == 0) mbar_arrive_count(&f.empty[it % kMkS], count);
 }
-
 // ---------------------------------------------------------------- consumers
 
 __device__ __forceinline__ void mk_sync() { named_barrier_sync(1, kMkConsumers); }
@@ -675,41 +697,50 @@ __device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const uint32_t
   mk_sync();
   const int total = cnt * nb;  // < 2^16 for every eligible shape
   const int per = (total + TB - 1) / TB;  // tiles per matrix
-  for (int tt = 0; tt < halves * per; ++tt, ++it) {
-    const unsigned char* tile = mk_next_tile(p, f, it);
-    if (in_grp && tt % T == grp) {
-      const int half = DUAL ? (tt & 1) : 0, k = DUAL ? tt >> 1 : tt;
-      const int g0 = k * TB, g1 = min(g0 + TB, total);
-      const int r_lo = g0 / nb, r_hi = (g1 - 1) / nb;
-      float* rr = red + (k & 1) * plane + half * cnt * WG + wc;
-      const uint32_t base = smem_u32(tile) - (uint32_t)(g0 * BB);  // block g at base + g * BB
-      for (int R = r_lo; R <= r_hi; R += 4) {  // four rows at a time for ILP
-        float v[4];
+  // tile tt of the phase at `tile`, computed by this warp's group
+  auto work = [&](const unsigned char* tile, int tt) {
+    const int half = DUAL ? (tt & 1) : 0, k = DUAL ? tt >> 1 : tt;
+    const int g0 = k * TB, g1 = min(g0 + TB, total);
+    const int r_lo = g0 / nb, r_hi = (g1 - 1) / nb;
+    float* rr = red + (k & 1) * plane + half * cnt * WG + wc;
+    const uint32_t base = smem_u32(tile) - (uint32_t)(g0 * BB);  // block g at base + g * BB
+    for (int R = r_lo; R <= r_hi; R += 4) {  // four rows at a time for ILP
+      float v[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int g = (R + k) * nb + col;
-          v[k] = col < nb && R + k <= r_hi && g >= g0 && g < g1
-                     ? mk_block_dot<DT>(base + (uint32_t)(g * BB), xw) * sb
-                     : 0.0f;
-        }
-        // transposed warp sum of the four rows: the upper half-warp keeps
-        // rows 2, 3 and sends rows 0, 1, then lanes with bit 3 set keep the
-        // odd row; the lanes 0, 8, 16, 24 end with rows R .. R + 3
-        const bool u16 = lane & 16, u8 = lane & 8;
-        float a0 = u16 ? v[2] : v[0], a1 = u16 ? v[3] : v[1];
-        a0 += __shfl_xor_sync(0xffffffffu, u16 ? v[0] : v[2], 16);
-        a1 += __shfl_xor_sync(0xffffffffu, u16 ? v[1] : v[3], 16);
-        float s = u8 ? a1 : a0;
-        s += __shfl_xor_sync(0xffffffffu, u8 ? a0 : a1, 8);
-        s += __shfl_xor_sync(0xffffffffu, s, 4);
-        s += __shfl_xor_sync(0xffffffffu, s, 2);
-        s += __shfl_xor_sync(0xffffffffu, s, 1);
-        const int k = ((lane >> 4) << 1) | ((lane >> 3) & 1);
-        if ((lane & 7) == 0 && R + k <= r_hi) rr[(size_t)(R + k) * WG] = s;
+      for (int k = 0; k < 4; ++k) {
+        const int g = (R + k) * nb + col;
+        v[k] = col < nb && R + k <= r_hi && g >= g0 && g < g1
+                   ? mk_block_dot<DT>(base + (uint32_t)(g * BB), xw) * sb
+                   : 0.0f;
       }
+      // transposed warp sum of the four rows: the upper half-warp keeps
+      // rows 2, 3 and sends rows 0, 1, then lanes with bit 3 set keep the
+      // odd row; the lanes 0, 8, 16, 24 end with rows R .. R + 3
+      const bool u16 = lane & 16, u8 = lane & 8;
+      float a0 = u16 ? v[2] : v[0], a1 = u16 ? v[3] : v[1];
+      a0 += __shfl_xor_sync(0xffffffffu, u16 ? v[0] : v[2], 16);
+      a1 += __shfl_xor_sync(0xffffffffu, u16 ? v[1] : v[3], 16);
+      float s = u8 ? a1 : a0;
+      s += __shfl_xor_sync(0xffffffffu, u8 ? a0 : a1, 8);
+      s += __shfl_xor_sync(0xffffffffu, s, 4);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      const int k = ((lane >> 4) << 1) | ((lane >> 3) & 1);
+      if ((lane & 7) == 0 && R + k <= r_hi) rr[(size_t)(R + k) * WG] = s;
     }
-    mk_release(f, it);
+  };
+  // Group g computes the tiles g, g + T, ...: its warps wait only for those
+  // (tag, then full barrier) and release them with counts adding up to
+  // kMkCW; the other warps never touch them.
+  const int ntl = halves * per;
+  if (in_grp) {
+    const uint32_t cnt_rel = wc == 0 ? (uint32_t)(kMkCW - WG + 1) : 1u;
+    for (int tt = grp; tt < ntl; tt += T) {
+      work(mk_next_tile(p, f, it + tt), tt);
+      mk_release(f, it + tt, cnt_rel);
+    }
   }
+  it += ntl;
   mk_sync();
   if (tid < cnt) {
     const int t = tid;
@@ -934,28 +965,18 @@ __device__ void mk_consume_attn(const MkParams& p, int li, int L, float* scr, Mk
 #pragma unroll
     for (int e = 0; e < DPL; ++e)
       q[g][e] = served && g < gw ? qs[(g0 + g) * HD + DPL * lane + e] : 0.0f;
-  // The tiles go in rounds of at most kMkS: a warp waits only for the tiles
-  // it computes and releases the round's other tiles at once (lane i the
-  // round's tile i). The consumer sync closing a round means that every
-  // warp has released every earlier tile before a release of the next
-  // round's tiles (each empty barrier takes one tile's releases at a time),
-  // and that the tile a slot held before the one waited on was complete
-  // (a full barrier is never waited on two phases ahead).
+  // A tile is computed by the HG warps of its slot (one per head pair):
+  // they alone wait for it (tag, then full barrier) and release it, the
+  // pair-0 warp with the count that brings the releases to kMkCW.
   const int ntile = t1 - t0;
-  for (int r0 = 0; r0 < ntile; r0 += kMkS) {
-    const int rn = min(kMkS, ntile - r0);
-    {
-      const int i = r0 + lane;
-      if (lane < rn && !(served && i % WPG == slot)) mbar_arrive(&f.empty[(it + i) % kMkS]);
-    }
-    for (int i = r0; i < r0 + rn; ++i) {
-      if (!served || i % WPG != slot) continue;
+  if (served) {
+    const uint32_t cnt_rel = warp % HG == 0 ? (uint32_t)(kMkCW - HG + 1) : 1u;
+    for (int i = slot; i < ntile; i += WPG) {
       const uint32_t kt = smem_u32(mk_next_tile(p, f, it + i));
       mk_attn_tile<DPL>(q, gw, kt, true, kt + (uint32_t)(TP * HD * 4), min(TP, L - (t0 + i) * TP),
                         p.scale, m, l, o);
-      mk_release(f, it + i);
+      mk_release(f, it + i, cnt_rel);
     }
-    mk_sync();
   }
   it += ntile;
   if (served && last && ntile % WPG == slot)
@@ -1195,6 +1216,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
   f.lps = lps;
   f.full = reinterpret_cast<uint64_t*>(sm);
   f.empty = f.full + kMkS;
+  f.tag = reinterpret_cast<int*>(f.empty + kMkS);
   f.li = 0;
   f.ph = 0;
   f.idx = 0;
@@ -1202,7 +1224,8 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
   if (threadIdx.x == 0) {
     for (int s = 0; s < kMkS; ++s) {
       mbar_init(&f.full[s], 32);     // the issuing producer warp's lanes (cp.async.mbarrier.arrive)
-      mbar_init(&f.empty[s], kMkCW);  // every consumer warp
+      mbar_init(&f.empty[s], kMkCW);  // kMkCW counts from the warps that compute the tile
+      f.tag[s] = -1;
     }
     mbar_fence_init();
   }

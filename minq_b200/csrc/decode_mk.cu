@@ -915,8 +915,9 @@ __device__ __forceinline__ void mk_attn_tile(const float (&q)[2][DPL], int gw, u
 // head to arrive (a counter per head) merges all of the head's split
 // partials into the attention output; the others go on to the grid barrier.
 template <int DT, int DPL>
-__device__ void mk_consume_attn(const MkParams& p, int li, int L, float* scr, MkFeed& f,
-                                const MkCta* cta, const float* rope_cs, int* misc_i, int& it) {
+__device__ void mk_consume_attn(const MkParams& p, int li, int L, unsigned hbase, float* scr,
+                                MkFeed& f, const MkCta* cta, const float* rope_cs, int* misc_i,
+                                int& it) {
   int kh, t0, t1;
   bool last;
   if (!mk_attn_item(p, L, &kh, &t0, &t1, &last)) return;
@@ -1016,50 +1017,67 @@ __device__ void mk_consume_attn(const MkParams& p, int li, int L, float* scr, Mk
       part[g * (HD + 2) + HD + 1] = Ls;
     }
   }
-  // arrival at the head's counter; the last split merges
+  // arrival at the head's counter: a release add once the CTA's partial is
+  // written (the named barrier orders every thread's writes before it);
+  // then every split of the head waits for the head's other splits
+  // (bounded) and merges its own slice of the head's outputs
   const int ns = mk_nsplit(p, L);
-  __threadfence();
   mk_sync();
   if (tid == 0) {
-    const int old = atomicAdd(p.head_ctr + kh, 1);
-    const int is_last = old == ns - 1;
-    if (is_last) {
-      __threadfence();
-      p.head_ctr[kh] = 0;  // next used after later grid barriers
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.head_ctr + kh) : "memory");
+    const unsigned target = hbase + (unsigned)(li + 1) * (unsigned)ns;
+    int ok = 1;
+    const uint64_t tw = global_timer_ns();
+    for (uint32_t n = 1;; ++n) {
+      unsigned v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.head_ctr + kh) : "memory");
+      if ((int)(v - target) >= 0) break;
+      if ((n & 15) == 0) {
+        if (*reinterpret_cast<volatile int*>(p.abort_flag)) {
+          ok = 0;
+          break;
+        }
+        if (global_timer_ns() - tw > kWaitLimitNs) {
+          atomicOr(p.status, kDeviceTimeout);
+          atomicExch(p.abort_flag, 1);
+          ok = 0;
+          break;
+        }
+      }
     }
-    misc_i[2] = is_last;
+    misc_i[2] = ok;
   }
   mk_sync();
-  if (!misc_i[2]) return;
-  // every split's partial of this head into shared memory in one round of
-  // loads, then the weights, then the outputs
+  if (!misc_i[2]) return;  // aborting: the launch reports the error
+  // split sp merges outputs [o0, o1) of the head (o = g * hd + d): every
+  // split's (m, l, o) of them into shared memory in one round of loads,
+  // then per output the softmax weights of the splits and the sum
+  const int sp = blockIdx.x - kh * ns, no = G * HD;
+  const int o0 = (int)((long long)no * sp / ns), o1 = (int)((long long)no * (sp + 1) / ns);
+  const int n_o = o1 - o0;
   const float* hp = p.part + (size_t)kh * ns * G * (HD + 2);
-  float* wgt = fw;                       // [ns][G] weights, then [G] 1 / sum
-  float* stg = fw + ((ns * G + G + 1) & ~1);  // [ns][G][hd + 2] partials (8-byte aligned)
-  const int nf2 = ns * G * (HD + 2) / 2;  // float2 pieces (hd + 2 is even)
-  const float2* hp2 = reinterpret_cast<const float2*>(hp);
-  float2* stg2 = reinterpret_cast<float2*>(stg);
-#pragma unroll 4
-  for (int i = tid; i < nf2; i += kMkConsumers) stg2[i] = __ldcg(hp2 + i);
-  mk_sync();
-  if (tid < G) {
-    float M = -INFINITY;
-    for (int s_ = 0; s_ < ns; ++s_) M = fmaxf(M, stg[(s_ * G + tid) * (HD + 2) + HD]);
-    float Ls = 0.0f;
-    for (int s_ = 0; s_ < ns; ++s_) {
-      const float* e = stg + (s_ * G + tid) * (HD + 2);
-      const float fs = e[HD] == -INFINITY ? 0.0f : expf(e[HD] - M);
-      Ls = fmaf(e[HD + 1], fs, Ls);
-      wgt[s_ * G + tid] = fs;
-    }
-    wgt[ns * G + tid] = 1.0f / Ls;
+  float* sm_m = fw;               // [ns][n_o] each
+  float* sm_l = sm_m + ns * n_o;
+  float* sm_o = sm_l + ns * n_o;
+  for (int i = tid; i < ns * n_o; i += kMkConsumers) {
+    const int s_ = i / n_o, j = i - s_ * n_o, od = o0 + j, g = od / HD, d = od - g * HD;
+    const float* e = hp + ((size_t)s_ * G + g) * (HD + 2);
+    sm_m[i] = __ldcg(e + HD);
+    sm_l[i] = __ldcg(e + HD + 1);
+    sm_o[i] = __ldcg(e + d);
   }
   mk_sync();
-  for (int idx = tid; idx < G * HD; idx += kMkConsumers) {
-    const int g = idx / HD, d = idx - g * HD;
-    float O = 0.0f;
-    for (int s_ = 0; s_ < ns; ++s_) O = fmaf(wgt[s_ * G + g], stg[(s_ * G + g) * (HD + 2) + d], O);
-    p.att[(size_t)(kh * G + g) * HD + d] = O * wgt[ns * G + g];
+  for (int j = tid; j < n_o; j += kMkConsumers) {
+    float M = -INFINITY;
+    for (int s_ = 0; s_ < ns; ++s_) M = fmaxf(M, sm_m[s_ * n_o + j]);
+    float Ls = 0.0f, O = 0.0f;
+    for (int s_ = 0; s_ < ns; ++s_) {
+      const float mw = sm_m[s_ * n_o + j];
+      const float fs = mw == -INFINITY ? 0.0f : expf(mw - M);
+      Ls = fmaf(sm_l[s_ * n_o + j], fs, Ls);
+      O = fmaf(sm_o[s_ * n_o + j], fs, O);
+    }
+    p.att[(size_t)kh * no + o0 + j] = O * (1.0f / Ls);
   }
 }
 
@@ -1115,7 +1133,7 @@ __device__ void mk_lm_head(const MkParams& p, const float* xs, unsigned long lon
 template <int DT>
 __device__ void mk_consumers(const MkParams& p, unsigned char* sm, MkFeed& f, const MkCta* cta,
                              int L,
-                             uint32_t tok, unsigned long long bbase) {
+                             uint32_t tok, unsigned long long bbase, unsigned hbase) {
   float* misc = reinterpret_cast<float*>(sm + kMkMiscOff);         // [0..32]: reductions
   int* misc_i = reinterpret_cast<int*>(sm + kMkMiscOff + 160);     // flags
   unsigned long long* best_s = reinterpret_cast<unsigned long long*>(sm + kMkMiscOff + 256);
@@ -1145,8 +1163,8 @@ __device__ void mk_consumers(const MkParams& p, unsigned char* sm, MkFeed& f, co
         [&](int row, float v, float, float b) { p.qkv_out[row] = bias ? v + b : v; });
     if (!(ok = barrier())) break;
     // P2: attention
-    if (p.hd == 128) mk_consume_attn<DT, 4>(p, li, L, xs, f, cta, rope_cs, misc_i, it);
-    else mk_consume_attn<DT, 2>(p, li, L, xs, f, cta, rope_cs, misc_i, it);
+    if (p.hd == 128) mk_consume_attn<DT, 4>(p, li, L, hbase, xs, f, cta, rope_cs, misc_i, it);
+    else mk_consume_attn<DT, 2>(p, li, L, hbase, xs, f, cta, rope_cs, misc_i, it);
     if (!(ok = barrier())) break;
     // P3: x = x + W_o att
     mk_stage_planes<DT>(p, xp, xsb, p.att, p.qd, nullptr, misc);
@@ -1191,6 +1209,7 @@ __device__ void mk_consumers(const MkParams& p, unsigned char* sm, MkFeed& f, co
   if (ok && blockIdx.x == 0 && threadIdx.x == 0) {
     *p.d_pos = L + 1;
     *p.bar_base = bbase + (unsigned long long)nbar * G;
+    *p.head_base = hbase + (unsigned)p.n_layers * (unsigned)mk_nsplit(p, L);
   }
 }
 
@@ -1200,6 +1219,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
   const int L = *reinterpret_cast<volatile const int*>(p.d_pos);
   const uint32_t tok = *reinterpret_cast<volatile const uint32_t*>(p.d_tok);
   const unsigned long long bbase = *reinterpret_cast<volatile const unsigned long long*>(p.bar_base);
+  const unsigned hbase = *reinterpret_cast<volatile const unsigned*>(p.head_base);
   MkCta* cta = reinterpret_cast<MkCta*>(sm + kMkCtaOff);
   if (threadIdx.x == 0) mk_cta_plan<DT>(p, L, cta);
   __syncthreads();
@@ -1234,7 +1254,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     mk_producer<DT>(p, f, cta, L);
     return;
   }
-  mk_consumers<DT>(p, sm, f, cta, L, tok, bbase);
+  mk_consumers<DT>(p, sm, f, cta, L, tok, bbase, hbase);
 }
 
 // ---------------------------------------------------------------- host
@@ -1257,9 +1277,10 @@ size_t mk_scratch_bytes(int H, int I, int qd, int G, int hd, int nsplit) {
   const size_t xs = std::max((size_t)(std::max({H, I, qd}) / kBlock) * (kMkRecW * 4 + 4),
                              (size_t)H * 4);
   // attention: q heads, new k and v, the 16 warps' (o, m, l), then the
-  // merge's split weights, 1 / sum per head and every split's partial
+  // merge's (m, l, o) of every split for this split's slice of the head's
+  // G * hd outputs (ns * ceil(G * hd / ns) <= G * hd + ns of each)
   const size_t att = ((size_t)G * hd + 2 * hd + (size_t)kMkCW * 2 * (hd + 2) +
-                      (size_t)nsplit * G + G + 2 + (size_t)nsplit * G * (hd + 2)) * 4;
+                      3 * ((size_t)G * hd + nsplit)) * 4;
   return (std::max(xs, att) + 127) & ~(size_t)127;
 }
 

@@ -54,7 +54,8 @@ struct MkParams {
   float* h;                    // [I]
   float* logits;               // [vocab]
   float* part;                 // [nkv * nsplit][G][hd + 2]
-  int* head_ctr;               // [nkv]
+  unsigned* head_ctr;          // [nkv] monotonic: + history splits per layer
+  unsigned* head_base;         // head counters' value at the start of the next launch
   unsigned long long* argmax_part;  // [grid]
   uint32_t* d_tok;             // in: this token; out: its argmax
   int* d_pos;                  // in: history length; out: + 1
@@ -72,7 +73,7 @@ struct MkParams {
 // tiles) or its 16-bit block indices do not take the shape.
 MkMat mk_plan_mat(int dtype, bool dual, uint64_t rows, uint64_t cols, int grid);
 // Shared-memory scratch: the staged input vector, or the attention state
-// and the partials of up to nsplit history splits.
+// and one head's split partials for a slice of its outputs.
 size_t mk_scratch_bytes(int H, int I, int qd, int G, int hd, int nsplit);
 // Shared memory of the launch, or 0 when it does not fit one SM.
 size_t mk_smem_bytes(size_t scratch_bytes, int n_layers);

@@ -110,7 +110,8 @@ struct minq_model {
     minq::MkMat qkv{}, o{}, gu{}, down{};
     minq::MkLayerPtrs* layers = nullptr;
     float* part = nullptr;
-    int* head_ctr = nullptr;
+    unsigned* head_ctr = nullptr;
+    unsigned* head_base = nullptr;
     unsigned long long* argmax_part = nullptr;
     unsigned long long* bar = nullptr;  // [0] counter, [1] base
     int* abort_flag = nullptr;
@@ -317,8 +318,9 @@ minq_status setup_megakernel(minq_model* m) {
   MINQ_TRY(dmalloc(m, &p, nkv * 4 + 4 + 2 * 8 + (size_t)grid * 8 + 64));
   k.bar = static_cast<unsigned long long*>(p);                         // 2 u64
   k.argmax_part = k.bar + 2;                                           // grid u64
-  k.head_ctr = reinterpret_cast<int*>(k.argmax_part + grid);           // nkv
-  k.abort_flag = k.head_ctr + nkv;                                     // 1
+  k.head_ctr = reinterpret_cast<unsigned*>(k.argmax_part + grid);      // nkv
+  k.abort_flag = reinterpret_cast<int*>(k.head_ctr + nkv);             // 1
+  k.head_base = reinterpret_cast<unsigned*>(k.abort_flag + 1);         // 1 (in the slack)
   MINQ_CUDA_TRY(cudaMemset(p, 0, nkv * 4 + 4 + 2 * 8 + (size_t)grid * 8 + 64));
   k.ok = true;
   return MINQ_OK;
@@ -745,6 +747,7 @@ static minq_status run_megakernel(minq_model* m, minq_cache* c, bool logits) {
   p.logits = m->logits;
   p.part = k.part;
   p.head_ctr = k.head_ctr;
+  p.head_base = k.head_base;
   p.argmax_part = k.argmax_part;
   p.d_tok = m->d_tok;
   p.d_pos = c->d_pos;

@@ -45,13 +45,24 @@ int argmax_parts_capacity();
 
 // qmatmul.cu: Y[b] = W X[b] for up to kQmmMaxB inputs (see qmatmul.cu);
 // w1 (dual) = up rows with a SwiGLU epilogue, else bias / residual; norm_w
-// applies the input RMSNorm first (xn_scratch: B x cols floats); part (up to
-// part_floats) holds the column slices' partials.
+// applies the input RMSNorm first; xn_scratch (xn_floats floats, at least
+// B x cols) holds the prepared inputs; part (up to part_floats) holds the
+// column slices' partials. From kQmmTcMinB quantized inputs on, the product
+// runs on the tensor cores (qmatmul_tc.cu).
 constexpr int kQmmMaxB = 64;
+constexpr int kQmmTcMinB = 16;
 minq_status launch_qmatmul(int dtype, const void* w0, const void* w1, size_t rows, int cols,
                            int B, const float* x, size_t x_stride, const float* norm_w, float eps,
-                           float* xn_scratch, const float* bias, const float* residual, float* y,
-                           size_t y_stride, float* part, size_t part_floats, cudaStream_t s);
+                           float* xn_scratch, size_t xn_floats, const float* bias,
+                           const float* residual, float* y, size_t y_stride, float* part,
+                           size_t part_floats, cudaStream_t s);
+// qmatmul_tc.cu: whether the tensor-core form takes the shape, and the launch.
+bool qmatmul_tc_takes(int dtype, int cols, int B, size_t xp_floats);
+minq_status launch_qmatmul_tc(int dtype, const void* w0, const void* w1, size_t rows, int cols,
+                              int B, const float* x, size_t x_stride, const float* norm_w, float eps,
+                              float* xp, size_t xp_floats, const float* bias, const float* residual,
+                              float* y, size_t y_stride, float* part, size_t part_floats,
+                              cudaStream_t s);
 minq_status launch_embed_batch(const float* embed, const uint32_t* d_tok, size_t vocab, int hidden,
                                int B, float* x, cudaStream_t s);
 minq_status launch_argmax_rows(const float* x, size_t n, int B, uint32_t* out, cudaStream_t s);

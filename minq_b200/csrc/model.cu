@@ -135,7 +135,8 @@ struct minq_cache {
   float* batt = nullptr;   // [batch][qd]
   float* bh = nullptr;     // [batch][I]
   float* blog = nullptr;   // [batch][vocab]
-  float* bxn = nullptr;    // [batch][H] RMSNorm'd inputs
+  float* bxn = nullptr;    // prepared projection inputs: [batch][max(H, qd, I)] floats
+  size_t bxn_floats = 0;
   float* bpart = nullptr;  // column-slice partials of the batched matvec
   size_t bpart_floats = 0;
   uint32_t* btok = nullptr;  // [batch] token ids
@@ -620,8 +621,8 @@ static minq_status forward_batch_step(minq_model* m, minq_cache* c, bool want_lo
   for (uint64_t li = 0; li < cfg.n_layers; ++li) {
     const DevLayer& L = m->layers[li];
     MINQ_TRY(launch_qmatmul(L.qkv.tag, L.qkv.ptr, nullptr, qkv_rows, H, B, c->bx, H, L.attn_norm,
-                            eps, c->bxn, L.bias_qkv, nullptr, c->bqkv, qkv_rows, c->bpart,
-                            c->bpart_floats, s));
+                            eps, c->bxn, c->bxn_floats, L.bias_qkv, nullptr, c->bqkv, qkv_rows,
+                            c->bpart, c->bpart_floats, s));
     float* kc = c->k + li * layer_elems;
     float* vc = c->v + li * layer_elems;
     MINQ_TRY(launch_rope_append(c->bqkv, c->bqkv + qd, c->bqkv + qd + kvd, qkv_rows, qkv_rows,
@@ -630,19 +631,19 @@ static minq_status forward_batch_step(minq_model* m, minq_cache* c, bool want_lo
     MINQ_TRY(launch_attention(c->bq, kc, vc, c->batch, nh, nkv, hd, pos + 1, seq_stride,
                               head_stride, hd, c->batt, c->ws, c->ws_bytes, s));
     MINQ_TRY(launch_qmatmul(L.o.tag, L.o.ptr, nullptr, H, (int)qd, B, c->batt, qd, nullptr, eps,
-                            nullptr, nullptr, c->bx, c->bx, H, c->bpart, c->bpart_floats,
-                            s));  // x += o
+                            c->bxn, c->bxn_floats, nullptr, c->bx, c->bx, H, c->bpart,
+                            c->bpart_floats, s));  // x += o
     MINQ_TRY(launch_qmatmul(L.gate.tag, L.gate.ptr, L.up.ptr, I, H, B, c->bx, H, L.ffn_norm, eps,
-                            c->bxn, nullptr, nullptr, c->bh, I, c->bpart, c->bpart_floats,
-                            s));  // silu(gate) * up
+                            c->bxn, c->bxn_floats, nullptr, nullptr, c->bh, I, c->bpart,
+                            c->bpart_floats, s));  // silu(gate) * up
     MINQ_TRY(launch_qmatmul(L.down.tag, L.down.ptr, nullptr, H, (int)I, B, c->bh, I, nullptr, eps,
-                            nullptr, nullptr, c->bx, c->bx, H, c->bpart, c->bpart_floats,
-                            s));  // x += down
+                            c->bxn, c->bxn_floats, nullptr, c->bx, c->bx, H, c->bpart,
+                            c->bpart_floats, s));  // x += down
   }
   if (want_logits) {
     MINQ_TRY(launch_qmatmul(m->lm_head.tag, m->lm_head.ptr, nullptr, V, H, B, c->bx, H,
-                            m->final_norm, eps, c->bxn, nullptr, nullptr, c->blog, V, c->bpart,
-                            c->bpart_floats, s));
+                            m->final_norm, eps, c->bxn, c->bxn_floats, nullptr, nullptr, c->blog, V,
+                            c->bpart, c->bpart_floats, s));
     MINQ_TRY(launch_argmax_rows(c->blog, V, B, c->barg, s));
   }
   return MINQ_OK;
@@ -674,7 +675,8 @@ static minq_status batch_ready(minq_model* m, minq_cache* c) {
   MINQ_TRY(alloc(reinterpret_cast<void**>(&c->batt), B * qd * 4));
   MINQ_TRY(alloc(reinterpret_cast<void**>(&c->bh), B * I * 4));
   MINQ_TRY(alloc(reinterpret_cast<void**>(&c->blog), B * V * 4));
-  MINQ_TRY(alloc(reinterpret_cast<void**>(&c->bxn), B * H * 4));
+  c->bxn_floats = B * std::max({H, qd, I});
+  MINQ_TRY(alloc(reinterpret_cast<void**>(&c->bxn), c->bxn_floats * 4));
   c->bpart_floats = 4 * B * std::max({H, qd + 2 * kvd, I});
   MINQ_TRY(alloc(reinterpret_cast<void**>(&c->bpart), c->bpart_floats * 4));
   MINQ_TRY(alloc(reinterpret_cast<void**>(&c->btok), B * 4));

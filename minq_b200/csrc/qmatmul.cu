@@ -300,9 +300,13 @@ minq_status qmm_launch(QmmParams p, cudaStream_t s) {
 
 minq_status launch_qmatmul(int dtype, const void* w0, const void* w1, size_t rows, int cols,
                            int B, const float* x, size_t x_stride, const float* norm_w, float eps,
-                           float* xn_scratch, const float* bias, const float* residual, float* y,
-                           size_t y_stride, float* part, size_t part_floats, cudaStream_t s) {
+                           float* xn_scratch, size_t xn_floats, const float* bias,
+                           const float* residual, float* y, size_t y_stride, float* part,
+                           size_t part_floats, cudaStream_t s) {
   if (B < 1 || B > kQmmMaxB) return fail(MINQ_ERR_ARG, "batched matvec takes 1..64 inputs");
+  if (xn_scratch && qmatmul_tc_takes(dtype, cols, B, xn_floats))
+    return launch_qmatmul_tc(dtype, w0, w1, rows, cols, B, x, x_stride, norm_w, eps, xn_scratch,
+                             xn_floats, bias, residual, y, y_stride, part, part_floats, s);
   if (cols % kBlock != 0 || rows == 0) return fail(MINQ_ERR_SHAPE, "batched matvec shape");
   if (dtype != MINQ_Q8_0 && dtype != MINQ_Q4_0 && dtype != MINQ_F32)
     return fail(MINQ_ERR_ARG, "batched matvec dtype");

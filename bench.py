@@ -58,6 +58,9 @@ WORKLOADS = {
 # cache pre-filled (N(0, 1)) at 32768 positions, greedy decode split over the
 # ranks (heads and intermediate rows; NCCL all-reduce after o_proj / down_proj).
 TP_WORKLOAD = "qwen3-4b-q8_0-tp32k"
+# Batched decode: 64 independent greedy sequences of the LLaMA-3-8B shape in
+# Q4_0 (512-token prompts), data-sharded over the ranks with no collective.
+BATCH_WORKLOAD = "llama3-8b-q4_0-b64"
 # Isolated GQA decode attention (32 query / 8 kv heads, head_dim 128): RoPE +
 # append + attend over L+1 positions for B sequences, swept over
 # L in {512, 2048, 8192, 32768} x B in {1, 8, 64}.
@@ -70,7 +73,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["minq", "reference"], default="minq")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + [TP_WORKLOAD, ATTN_WORKLOAD],
+    ap.add_argument("--workload",
+                    choices=sorted(WORKLOADS) + [TP_WORKLOAD, ATTN_WORKLOAD, BATCH_WORKLOAD],
                     default="qwen3-4b-q4_0")
     ap.add_argument("--prompt", type=int, default=None, help="prefill length override")
     ap.add_argument("--seed", type=int, default=1234)
@@ -557,6 +561,91 @@ def run_tp(args, world, rank, local):
     del cache, model
 
 
+def run_batch(args, world, rank, local):
+    """64 independent greedy sequences of the LLaMA-3-8B shape in Q4_0, 64 /
+    world per rank (no collective): the prompts go through batched steps
+    (one token of every sequence per step), then batched decode steps with
+    each step's argmax fed back on the device."""
+    import torch
+    import minq_b200 as mq
+    from minq_b200 import synth
+    from dataclasses import replace
+    torch.cuda.set_device(local)
+    total, K, W = 64, args.steps, args.warmup
+    prompt = args.prompt or 512
+    if total % world:
+        raise SystemExit(f"{BATCH_WORKLOAD}: 64 sequences do not split over {world} ranks")
+    B = total // world
+    cfg0, qk_norm, tied = synth.ARCH["llama3-8b"]
+    cfg = replace(cfg0, max_seq_len=prompt + W + 2 * K + 16)
+    model = build_model(mq, synth, cfg, qk_norm, tied, args.seed)
+    cache = model.new_cache(batch=B)
+    rng = np.random.default_rng(args.seed + 100 + rank)
+    prompts = rng.integers(0, cfg.vocab_size, (B, prompt))
+    for i in range(prompt):
+        model.forward_batch(prompts[:, i].tolist(), cache, logits=False)
+    stream = torch.cuda.ExternalStream(model.stream)
+    model.forward_batch_steps(cache, W)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(physical_gpu_index(local))
+    clocks.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    model.forward_batch_steps(cache, K)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    ms_max = max_over_ranks(world, ev0.elapsed_time(ev1))
+    # e2e: the public batched call with host tokens in and host argmax out
+    toks = rng.integers(0, cfg.vocab_size, B).tolist()
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(K):
+        am, _ = model.forward_batch(toks, cache, logits=False)
+        toks = [int(t) for t in am]
+    e2e_ms = max_over_ranks(world, 1000.0 * (time.perf_counter() - t0))
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    # the step's algorithmic work per GPU: 2 flops per weight per sequence
+    # (every projection and the lm_head), on the tensor cores from 16 sequences
+    H, I, hd = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
+    qd, kvd = cfg.n_heads * hd, cfg.n_kv_heads * hd
+    params = cfg.n_layers * (H * (qd + 2 * kvd) + qd * H + 3 * I * H) + cfg.vocab_size * H
+    flops = 2.0 * params * B
+    tfs = flops / (ms_max / K * 1e-3) / 1e12
+    peak = peaks.get("bf16_tflops") or 1590.0
+    if rank == 0:
+        print(json.dumps({
+            "metric": "decode tok/s (batched)", "value": total * K / (ms_max / 1000.0),
+            "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16 x 2 (hi/lo split inputs), f32 accumulate",
+            "data": "synthetic",
+            "config": {"workload": f"{BATCH_WORKLOAD}: LLaMA-3-8B shape, Q4_0, 64 sequences, "
+                                   f"{prompt}-token prompts, {B} per GPU",
+                       "parallelism": f"data{world}" if world > 1 else "single GPU",
+                       "cache_flush": "inputs > L2"},
+            "e2e": {"value": total * K / (e2e_ms / 1000.0), "unit": "tok/s",
+                    "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B},
+            "gpu_launches": None,
+            "roofline": {"bound": "tensor" if B >= 16 else "hbm", "kernel": "batched step (per GPU)",
+                         "achieved": tfs, "peak": peak, "unit": "TFLOP/s", "frac": tfs / peak,
+                         "traffic": None, "per_launch_flops": flops},
+            "cpu_baseline": None,
+            "clocks": clk,
+        }), flush=True)
+    del cache, model
+
+
 def run_attn(args, world, rank, local):
     """The decode-attention op (minq_attn_decode) over the sweep; the line's
     value is the B = 8, L = 8192 point, `sweep` holds every point. Each
@@ -645,6 +734,8 @@ def main():
                 run_attn(args, world, rank, local)
         elif args.workload == TP_WORKLOAD:
             run_tp(args, world, rank, local)
+        elif args.workload == BATCH_WORKLOAD:
+            run_batch(args, world, rank, local)
         elif args.impl == "reference":
             run_reference(args, world, rank)
         else:

@@ -65,7 +65,9 @@ minq_status launch_qmatmul_tc(int dtype, const void* w0, const void* w1, size_t 
                               cudaStream_t s);
 minq_status launch_embed_batch(const float* embed, const uint32_t* d_tok, size_t vocab, int hidden,
                                int B, float* x, cudaStream_t s);
-minq_status launch_argmax_rows(const float* x, size_t n, int B, uint32_t* out, cudaStream_t s);
+// argmax of each of the B rows of x [B][n]; scratch: 32 u64 per row.
+minq_status launch_argmax_rows(const float* x, size_t n, int B, uint32_t* out,
+                               unsigned long long* scratch, cudaStream_t s);
 
 // attention.cu
 size_t attn_workspace_bytes(size_t batch, size_t nh, size_t len, size_t hd_max);

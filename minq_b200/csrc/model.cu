@@ -644,7 +644,9 @@ static minq_status forward_batch_step(minq_model* m, minq_cache* c, bool want_lo
     MINQ_TRY(launch_qmatmul(m->lm_head.tag, m->lm_head.ptr, nullptr, V, H, B, c->bx, H,
                             m->final_norm, eps, c->bxn, c->bxn_floats, nullptr, nullptr, c->blog, V,
                             c->bpart, c->bpart_floats, s));
-    MINQ_TRY(launch_argmax_rows(c->blog, V, B, c->barg, s));
+    // the lm_head's slice partials are consumed: bpart takes the argmax parts
+    MINQ_TRY(launch_argmax_rows(c->blog, V, B, c->barg,
+                                reinterpret_cast<unsigned long long*>(c->bpart), s));
   }
   return MINQ_OK;
 }

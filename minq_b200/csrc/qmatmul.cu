@@ -258,15 +258,20 @@ __global__ void embed_batch_kernel(const float* __restrict__ embed, const uint32
 }
 
 // argmax of each row of x [B][n] (sampler.rs:10-17: f32::total_cmp order,
-// ties to the lowest index).
-__global__ void __launch_bounds__(256) argmax_rows_kernel(const float* __restrict__ x, size_t n,
-                                                          uint32_t* out) {
+// ties to the lowest index): CTA (b, j) packs the best of part j of row b
+// (kArgParts parts, eight loads in flight per thread), then one warp per row
+// takes the best of the parts.
+constexpr int kArgParts = 32;
+__global__ void __launch_bounds__(256) argmax_rows_part_kernel(const float* __restrict__ x, size_t n,
+                                                               unsigned long long* part) {
   pdl_wait();
   pdl_launch_dependents();
   __shared__ unsigned long long red[8];
   const float* row = x + (size_t)blockIdx.x * n;
+  const size_t c0 = n * blockIdx.y / kArgParts, c1 = n * (blockIdx.y + 1) / kArgParts;
   unsigned long long best = 0;
-  for (size_t i = threadIdx.x; i < n; i += blockDim.x) {
+#pragma unroll 8
+  for (size_t i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
     const unsigned long long pk = argmax_pack(row[i], (uint32_t)i);
     best = pk > best ? pk : best;
   }
@@ -276,8 +281,17 @@ __global__ void __launch_bounds__(256) argmax_rows_kernel(const float* __restric
   if (threadIdx.x == 0) {
     for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
     best = red[0] > best ? red[0] : best;
-    out[blockIdx.x] = argmax_unpack_index(best);
+    part[(size_t)blockIdx.x * kArgParts + blockIdx.y] = best;
   }
+}
+
+__global__ void __launch_bounds__(32) argmax_rows_final_kernel(const unsigned long long* part,
+                                                              uint32_t* out) {
+  pdl_wait();
+  pdl_launch_dependents();
+  unsigned long long best = part[(size_t)blockIdx.x * kArgParts + threadIdx.x];
+  best = warp_max_u64(best);
+  if (threadIdx.x == 0) out[blockIdx.x] = argmax_unpack_index(best);
 }
 
 template <int DT, bool DUAL>
@@ -356,8 +370,13 @@ minq_status launch_embed_batch(const float* embed, const uint32_t* d_tok, size_t
   return MINQ_OK;
 }
 
-minq_status launch_argmax_rows(const float* x, size_t n, int B, uint32_t* out, cudaStream_t s) {
-  MINQ_CUDA_TRY(launch_k(argmax_rows_kernel, dim3((unsigned)B), dim3(256), 0, s, x, n, out));
+minq_status launch_argmax_rows(const float* x, size_t n, int B, uint32_t* out,
+                               unsigned long long* scratch, cudaStream_t s) {
+  static_assert(kArgParts == 32, "one warp reduces the parts");
+  MINQ_CUDA_TRY(launch_k(argmax_rows_part_kernel, dim3((unsigned)B, kArgParts), dim3(256), 0, s, x,
+                         n, scratch));
+  MINQ_CUDA_TRY(launch_k(argmax_rows_final_kernel, dim3((unsigned)B), dim3(32), 0, s,
+                         (const unsigned long long*)scratch, out));
   return MINQ_OK;
 }
 

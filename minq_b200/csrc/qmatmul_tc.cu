@@ -22,7 +22,8 @@
 // Work. A CTA of 8 warps takes 128 rows (64 rows of gate and of up for the
 // dual form) and a slice of the columns; a warp owns 16 rows and every input
 // (up to 8 n-tiles of 8). Chunks of 4 blocks of the CTA's rows and of the
-// inputs' columns are double-buffered in shared memory with cp.async. With
+// inputs' columns stream through a 4-deep ring in shared memory with
+// cp.async (three chunks in flight while one is computed). With
 // S > 1 column slices the partials go to the workspace and
 // qmm_reduce-style summation in slice order applies the epilogue.
 #include <cuda_bf16.h>
@@ -45,6 +46,8 @@ constexpr int kTcBpc = 4;                 // blocks per chunk
 constexpr int kTcKc = kTcBpc * kBlock;    // columns per chunk
 constexpr int kTcMaxB = 64;
 constexpr int kTcXPitch = kTcKc * 2 + 16;  // bytes per staged input row: ldmatrix rows on distinct banks
+constexpr int kTcStages = 2;              // chunk buffers (kTcStages - 1 chunks in flight)
+constexpr int kTcMinBlocks = 2;           // CTAs per SM (registers <= 128)
 
 // Column of a 32-column block at k-step s (0, 1), k-slot kap (0..15) of the
 // permuted order (see above).
@@ -70,7 +73,10 @@ struct TcParams {
 };
 
 // x[b] -> permuted x_hi / x_lo (bf16), optionally RMSNorm'd first with the
-// reference's f32 operations (x * inv * w); one CTA per input.
+// reference's f32 operations (x * inv * w). CTA (b, j) writes positions
+// [1024 j, 1024 j + 1024) of input b, four per thread; with the norm every
+// CTA of the input first sums the whole row's squares (float4 loads).
+constexpr int kTcPrepCols = 1024;
 __global__ void __launch_bounds__(256) tc_xprep_kernel(const float* __restrict__ x, size_t x_stride,
                                                       int n, const float* __restrict__ w, float eps,
                                                       __nv_bfloat16* __restrict__ xh,
@@ -82,7 +88,15 @@ __global__ void __launch_bounds__(256) tc_xprep_kernel(const float* __restrict__
   float inv = 1.0f;
   if (w) {
     float ss = 0.0f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(row[i], row[i], ss);
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < (n >> 2); i += blockDim.x) {
+      const float4 v = r4[i];
+      ss = fmaf(v.x, v.x, ss);
+      ss = fmaf(v.y, v.y, ss);
+      ss = fmaf(v.z, v.z, ss);
+      ss = fmaf(v.w, v.w, ss);
+    }
     ss = warp_sum(ss);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
@@ -96,13 +110,26 @@ __global__ void __launch_bounds__(256) tc_xprep_kernel(const float* __restrict__
   }
   __nv_bfloat16* oh = xh + (size_t)blockIdx.x * n;
   __nv_bfloat16* ol = xl + (size_t)blockIdx.x * n;
-  for (int p = threadIdx.x; p < n; p += blockDim.x) {
-    const int q = p & 31;
-    const int c = (p - q) + tc_col(q >> 4, q & 15);
-    const float v = w ? row[c] * inv * w[c] : row[c];
-    const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-    oh[p] = hi;
-    ol[p] = __float2bfloat16_rn(v - __bfloat162float(hi));
+  const int p0 = blockIdx.y * kTcPrepCols;
+  float v[4];
+  int pp[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int p = p0 + threadIdx.x + 256 * k;
+    pp[k] = p;
+    v[k] = 0.0f;
+    if (p < n) {
+      const int q = p & 31;
+      const int c = (p - q) + tc_col(q >> 4, q & 15);
+      v[k] = w ? row[c] * inv * w[c] : row[c];
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if (pp[k] >= n) continue;
+    const __nv_bfloat16 hi = __float2bfloat16_rn(v[k]);
+    oh[pp[k]] = hi;
+    ol[pp[k]] = __float2bfloat16_rn(v[k] - __bfloat162float(hi));
   }
 }
 
@@ -110,7 +137,9 @@ __device__ __forceinline__ void tc_cp16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 __device__ __forceinline__ void tc_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void tc_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void tc_wait_stages() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(kTcStages - 1) : "memory");
+}
 __device__ __forceinline__ void tc_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t tc_lds(uint32_t a) {
@@ -172,7 +201,7 @@ struct TcFmt {
 };
 
 template <int DT, bool DUAL>
-__global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(TcParams p) {
+__global__ void __launch_bounds__(kTcThreads, kTcMinBlocks) qmm_tc_kernel(TcParams p) {
   using F = TcFmt<DT>;
   constexpr int H2 = DUAL ? 2 : 1;
   constexpr int RPC = DUAL ? 64 : 128;  // rows of each matrix per CTA
@@ -187,9 +216,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(TcParams p) {
   const int NT = (p.B + 7) >> 3;
   const uint32_t sbase = smem_u32(sm);
   const size_t cols = (size_t)p.nb * kBlock;
-  // stage chunk c (blocks kb0 + 4c ..) into buffer c & 1
+  // stage chunk c (blocks kb0 + 4c ..) into buffer c mod kTcStages
   auto stage = [&](int c) {
-    const uint32_t buf = sbase + (uint32_t)((c & 1) * F::stage);
+    const uint32_t buf = sbase + (uint32_t)((c % kTcStages) * F::stage);
     const int kb = kb0 + c * kTcBpc;
     constexpr int ppr = F::wpitch / 16;  // 16-byte pieces per staged row
     for (int i = tid; i < 128 * ppr; i += kTcThreads) {
@@ -214,14 +243,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(TcParams p) {
   const int lrow = (DUAL ? 64 * h : 0) + 16 * rt + g;  // this lane's first staged row (+ 8: second)
   // ldmatrix row of this lane: matrix lane / 8 = (n-tile of the pair, k half)
   const int lm_n = 8 * ((lane >> 3) >> 1) + (lane & 7), lm_k = 8 * ((lane >> 3) & 1);
-  stage(0);
-  tc_commit();
-  for (int c = 0; c < nch; ++c) {
-    if (c + 1 < nch) stage(c + 1);
+#pragma unroll
+  for (int c = 0; c < kTcStages - 1; ++c) {
+    if (c < nch) stage(c);
     tc_commit();
-    tc_wait1();
+  }
+  for (int c = 0; c < nch; ++c) {
+    if (c + kTcStages - 1 < nch) stage(c + kTcStages - 1);
+    tc_commit();
+    tc_wait_stages();  // chunk c landed: at most kTcStages - 1 groups still pending
     __syncthreads();
-    const uint32_t buf = sbase + (uint32_t)((c & 1) * F::stage);
+    const uint32_t buf = sbase + (uint32_t)((c % kTcStages) * F::stage);
     const uint32_t wa = buf + (uint32_t)(lrow * F::wpitch), wb = wa + 8 * F::wpitch;
 #pragma unroll
     for (int bl = 0; bl < kTcBpc; ++bl) {
@@ -249,38 +281,32 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(TcParams p) {
       }
       const float d0 = __uint_as_float(tc_lds(wa + bl * F::bb));
       const float d1 = __uint_as_float(tc_lds(wb + bl * F::bb));
-      float cb[8][4];
 #pragma unroll
-      for (int n = 0; n < 8; ++n)
+      for (int np = 0; np < 4; ++np) {
+        if (2 * np >= NT) break;  // the same for the whole warp
+        float c0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, c1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) cb[n][i] = 0.0f;
+        for (int s = 0; s < 2; ++s)
 #pragma unroll
-      for (int s = 0; s < 2; ++s)
-#pragma unroll
-        for (int part = 0; part < 2; ++part) {
-          const uint32_t xb = buf + (uint32_t)(F::wbytes + part * F::xbytes) +
-                              (uint32_t)(lm_n * kTcXPitch + (bl * kBlock + 16 * s + lm_k) * 2);
-#pragma unroll
-          for (int np = 0; np < 4; ++np) {
-            if (2 * np < NT) {
-              uint32_t r[4];
-              tc_ldsm4(xb + (uint32_t)(16 * np * kTcXPitch), r);
-              tc_mma(cb[2 * np], a[s], r[0], r[1]);
-              if (2 * np + 1 < NT) tc_mma(cb[2 * np + 1], a[s], r[2], r[3]);
-            }
+          for (int part = 0; part < 2; ++part) {
+            uint32_t r[4];
+            tc_ldsm4(buf + (uint32_t)(F::wbytes + part * F::xbytes) +
+                         (uint32_t)((16 * np + lm_n) * kTcXPitch + (bl * kBlock + 16 * s + lm_k) * 2),
+                     r);
+            tc_mma(c0, a[s], r[0], r[1]);
+            tc_mma(c1, a[s], r[2], r[3]);
           }
-        }
-#pragma unroll
-      for (int n = 0; n < 8; ++n) {
-        if (n < NT) {
-          acc[n][0] = fmaf(d0, cb[n][0], acc[n][0]);
-          acc[n][1] = fmaf(d0, cb[n][1], acc[n][1]);
-          acc[n][2] = fmaf(d1, cb[n][2], acc[n][2]);
-          acc[n][3] = fmaf(d1, cb[n][3], acc[n][3]);
-        }
+        acc[2 * np][0] = fmaf(d0, c0[0], acc[2 * np][0]);
+        acc[2 * np][1] = fmaf(d0, c0[1], acc[2 * np][1]);
+        acc[2 * np][2] = fmaf(d1, c0[2], acc[2 * np][2]);
+        acc[2 * np][3] = fmaf(d1, c0[3], acc[2 * np][3]);
+        acc[2 * np + 1][0] = fmaf(d0, c1[0], acc[2 * np + 1][0]);
+        acc[2 * np + 1][1] = fmaf(d0, c1[1], acc[2 * np + 1][1]);
+        acc[2 * np + 1][2] = fmaf(d1, c1[2], acc[2 * np + 1][2]);
+        acc[2 * np + 1][3] = fmaf(d1, c1[3], acc[2 * np + 1][3]);
       }
     }
-    __syncthreads();  // buffer c & 1 is refilled two chunks later
+    __syncthreads();  // buffer c mod kTcStages is refilled from the next chunk on
   }
   tc_wait0();
   pdl_launch_dependents();
@@ -359,7 +385,7 @@ __global__ void __launch_bounds__(256) tc_reduce_kernel(TcParams p) {
 
 template <int DT, bool DUAL>
 minq_status tc_launch(const TcParams& p, unsigned tiles, cudaStream_t s) {
-  const size_t smem = 2 * (size_t)TcFmt<DT>::stage;
+  const size_t smem = (size_t)kTcStages * TcFmt<DT>::stage;
   auto k = qmm_tc_kernel<DT, DUAL>;
   MINQ_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(k), smem));
   MINQ_CUDA_TRY(launch_k(k, dim3(tiles, (unsigned)p.S), dim3(kTcThreads), smem, s, p));
@@ -389,8 +415,9 @@ minq_status launch_qmatmul_tc(int dtype, const void* w0, const void* w1, size_t 
     return fail(MINQ_ERR_ARG, "tensor-core batched matvec weights must be 16-byte aligned");
   __nv_bfloat16* xh = reinterpret_cast<__nv_bfloat16*>(xp);
   __nv_bfloat16* xl = xh + (size_t)B * cols;
-  MINQ_CUDA_TRY(launch_k(tc_xprep_kernel, dim3((unsigned)B), dim3(256), 0, s, x, x_stride, cols,
-                         norm_w, eps, xh, xl));
+  MINQ_CUDA_TRY(launch_k(tc_xprep_kernel,
+                         dim3((unsigned)B, (unsigned)((cols + kTcPrepCols - 1) / kTcPrepCols)),
+                         dim3(256), 0, s, x, x_stride, cols, norm_w, eps, xh, xl));
   TcParams p{};
   p.w0 = static_cast<const uint8_t*>(w0);
   p.w1 = static_cast<const uint8_t*>(w1);

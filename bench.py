@@ -45,8 +45,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 # byte, from ncu --set full captures (summaries and commands under profiles/):
 # three decode-shaped Q4_0 qmatvec launches (q/k/v, o_proj, gate/up), 47.72 MB
 # / 47.62 MB; one decode megakernel launch of a 12-layer cut of the Q4_0
-# model, 2.36884 GB / 2.36344 GB.
-NCU_TRAFFIC_RATIO = {"qmatvec": 1.002, "decode_mk": 1.002}
+# model, 2.37069 GB / 2.36344 GB.
+NCU_TRAFFIC_RATIO = {"qmatvec": 1.002, "decode_mk": 1.003}
 sys.path.insert(0, ROOT)
 
 WORKLOADS = {
@@ -577,6 +577,8 @@ def run_batch(args, world, rank, local):
         raise SystemExit(f"{BATCH_WORKLOAD}: 64 sequences do not split over {world} ranks")
     B = total // world
     cfg0, qk_norm, tied = synth.ARCH["llama3-8b"]
+    if args.layers:
+        cfg0 = replace(cfg0, n_layers=args.layers)
     cfg = replace(cfg0, max_seq_len=prompt + W + 2 * K + 16)
     model = build_model(mq, synth, cfg, qk_norm, tied, args.seed)
     cache = model.new_cache(batch=B)
@@ -593,9 +595,11 @@ def run_batch(args, world, rank, local):
     barrier(world)
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed_decode")
     ev0.record(stream)
     model.forward_batch_steps(cache, K)
     ev1.record(stream)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier(world)
     clk = clocks.stop()
@@ -632,6 +636,7 @@ def run_batch(args, world, rank, local):
             "data": "synthetic",
             "config": {"workload": f"{BATCH_WORKLOAD}: LLaMA-3-8B shape, Q4_0, 64 sequences, "
                                    f"{prompt}-token prompts, {B} per GPU",
+                       "layers": cfg.n_layers,
                        "parallelism": f"data{world}" if world > 1 else "single GPU",
                        "cache_flush": "inputs > L2"},
             "e2e": {"value": total * K / (e2e_ms / 1000.0), "unit": "tok/s",

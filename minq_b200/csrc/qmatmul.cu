@@ -1,5 +1,7 @@
 // Batched projections for B independent sequences (one token each) or B
-// tokens of one sequence: Y[b] = W X[b] for Q8_0 / Q4_0 / f32 weights, with
+// tokens of one sequence on the CUDA cores (one quantized input, or f32
+// weights; quantized projections of 2..64 inputs run on the tensor cores,
+// qmatmul_tc.cu): Y[b] = W X[b] for Q8_0 / Q4_0 / f32 weights, with
 // the input RMSNorm (tensor.rs:219-227) applied first and bias / residual /
 // SwiGLU after, the weights read once for all B inputs.
 //

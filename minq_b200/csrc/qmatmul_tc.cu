@@ -1,4 +1,4 @@
-// Tensor-core batched projections (the batched step at B >= 16 inputs):
+// Tensor-core batched projections (the batched step from 2 inputs on):
 // Y[b] = W X[b] for Q4_0 / Q8_0 weights with mma.sync m16n8k16 (bf16 in,
 // f32 accumulate), the input RMSNorm (tensor.rs:219-227) applied first and
 // bias / residual / SwiGLU after, the weights read once for all B inputs.

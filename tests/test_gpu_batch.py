@@ -37,7 +37,9 @@ CASES = [
     ("q4_llama_untied_b5", "q4_0", 256, 512, 8, 2, 64, 300, False, False, False, 5),
     ("q8_qwen_bias_tied_b3", "q8_0", 256, 384, 4, 2, 64, 257, True, True, True, 3),
     ("q4_hd128_b9", "q4_0", 512, 768, 8, 2, 128, 200, True, False, False, 9),
-    # from 16 inputs on the quantized projections run on the tensor cores
+    # one input: the quantized projections on the CUDA-core kernel (from two
+    # inputs on they run on the tensor cores)
+    ("q4_llama_untied_b1", "q4_0", 256, 512, 8, 2, 64, 300, False, False, False, 1),
     ("q4_llama_untied_b17_tc", "q4_0", 256, 512, 8, 2, 64, 300, False, False, False, 17),
     ("q8_qwen_bias_tied_b24_tc", "q8_0", 256, 384, 4, 2, 64, 257, True, True, True, 24),
     ("q4_hd128_b64_tc", "q4_0", 512, 768, 8, 2, 128, 200, True, False, False, 64),

@@ -296,7 +296,7 @@ def run_minq(args, world, rank, local):
     stream = torch.cuda.ExternalStream(model.stream)
     V = cfg.vocab_size
 
-    # ---- prefill (token-by-token on the device) ----
+    # ---- prefill (chunks of 64 prompt tokens, the last token as a decode step) ----
     prompt = np.random.default_rng(args.seed).integers(0, V, prompt_len).astype(np.uint32)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
@@ -456,7 +456,7 @@ def run_minq(args, world, rank, local):
                        if arch == "qwen3-4b" else "inputs > L2",
                        "weight_bytes": model.weight_bytes},
             "prefill": {"tokens": prompt_len, "tok_s": prompt_len / prefill_s,
-                        "mode": "token-by-token"},
+                        "mode": "chunks of 64 tokens (batched projections on the tensor cores, causal split-KV attention), then the last token as a decode step"},
             "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4,
                     "d2h_bytes_per_step": 4 * V + 4},
             "gpu_launches": int(launches),

@@ -42,6 +42,7 @@ struct AttnParams {
   const int* d_pos;      // if set: len = *d_pos + 1 and the split is derived on the device
   int ws_stride;         // split slots per (sequence, head) in the workspace
   int q_round;           // chunk granularity (positions)
+  int len_step;          // entry b attends over len + b * len_step positions
 };
 
 // Split of `len` positions into at most `cap` chunks of a multiple of `q`.
@@ -67,7 +68,7 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
 
   pdl_wait();
   pdl_launch_dependents();
-  int len = p.len, chunk = p.chunk, nsplit = p.nsplit;
+  int len = p.len + (int)blockIdx.z * p.len_step, chunk = p.chunk, nsplit = p.nsplit;
   if (p.d_pos) {
     len = *p.d_pos + 1;
     derive_split(len, gridDim.x, p.q_round, &chunk, &nsplit);
@@ -82,7 +83,7 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnParams p) {
   const int g0 = (blockIdx.y % qgroups) * 8;
   const int ng = min(GMAX, G - g0);
   const int t_begin = split * chunk;
-  const int t_end = min(len, t_begin + chunk);
+  const int t_end = max(t_begin, min(len, t_begin + chunk));  // empty past an entry's length
 
   const float* kb = p.k + b * p.seq_stride + kvh * p.head_stride;
   const float* vb = p.v + b * p.seq_stride + kvh * p.head_stride;
@@ -269,7 +270,7 @@ __global__ void __launch_bounds__(160) attn_tma_kernel(AttnParams p) {
 
   pdl_wait();  // K/V (this position) and q come from the previous kernel
   pdl_launch_dependents();
-  int len = p.len, chunk = p.chunk, nsplit = p.nsplit;
+  int len = p.len + (int)blockIdx.z * p.len_step, chunk = p.chunk, nsplit = p.nsplit;
   if (p.d_pos) {
     len = *p.d_pos + 1;
     derive_split(len, gridDim.x, p.q_round, &chunk, &nsplit);
@@ -284,7 +285,7 @@ __global__ void __launch_bounds__(160) attn_tma_kernel(AttnParams p) {
   const int g0 = (blockIdx.y % qgroups) * 8;
   const int ng = min(GMAX, G - g0);
   const int t_begin = split * chunk;
-  const int t_end = min(len, t_begin + chunk);
+  const int t_end = max(t_begin, min(len, t_begin + chunk));  // empty past an entry's length
   const int ntiles = (t_end - t_begin + TP - 1) / TP;
   const float* kb = p.k + b * p.seq_stride + kvh * p.head_stride;
   const float* vb = p.v + b * p.seq_stride + kvh * p.head_stride;
@@ -490,6 +491,7 @@ struct RopeParams {
   const float* cos_t;  // [max_seq, HD/2]
   const float* sin_t;
   int nh, nkv, hd, pos;
+  int pos_step;        // entry b takes position pos + b * pos_step
   const int* d_pos;    // if set, the position is read from the device
   float* q_out;        // [B, nh, HD]
   float* k_cache;
@@ -500,10 +502,10 @@ struct RopeParams {
 __global__ void rope_append_kernel(RopeParams p) {
   pdl_wait();
   pdl_launch_dependents();
-  const int pos = p.d_pos ? *p.d_pos : p.pos;
+  const int b = blockIdx.y;
+  const int pos = (p.d_pos ? *p.d_pos : p.pos) + b * p.pos_step;
   const int lane = threadIdx.x & 31;
   const int head = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int b = blockIdx.y;
   const int nheads = p.nh + 2 * p.nkv;
   if (head >= nheads) return;
   const int hd = p.hd, half = hd / 2;
@@ -576,6 +578,33 @@ static int pick_chunk(int len, size_t units) {
   return (int)c;
 }
 
+// Split plan of launch_attention: positions per split (chunk) and the
+// chunk granularity, for `batch` entries whose longest history is size_len.
+static void attn_split_plan(bool tma, size_t batch, int nh, int nkv, int hd, int size_len,
+                            int* chunk, int* q_round) {
+  const int qgroups = (nh / nkv + 7) / 8;
+  const size_t units = batch * nkv * qgroups;
+  if (tma) {
+    const int tp = std::min(32, 2048 / hd);
+    *q_round = 4 * tp;
+    const size_t target = (size_t)sm_count() * 2;
+    size_t c = ((size_t)size_len * units + target - 1) / target;
+    c = (c + *q_round - 1) / *q_round * *q_round;
+    *chunk = (int)std::min<size_t>(c, (size_t)((size_len + *q_round - 1) / *q_round * *q_round));
+  } else {
+    *q_round = 32;
+    *chunk = pick_chunk(size_len, units);
+  }
+}
+
+size_t attn_workspace_need(size_t batch, int nh, int nkv, int hd, int size_len, bool head_major) {
+  const bool tma = head_major && hd >= 16 && hd <= 256 && (hd & (hd - 1)) == 0;
+  int chunk = 0, q_round = 0;
+  attn_split_plan(tma, batch, nh, nkv, hd, size_len, &chunk, &q_round);
+  const size_t nsplit = ((size_t)size_len + chunk - 1) / chunk;
+  return nsplit > 1 ? batch * nh * nsplit * (hd + 2) * sizeof(float) : 0;
+}
+
 size_t attn_workspace_bytes(size_t batch, size_t nh, size_t len, size_t hd_max) {
   // Upper bound over every split choice: at most ceil(len / 32) splits.
   const size_t splits = (len + 31) / 32;
@@ -621,14 +650,17 @@ minq_status launch_attention(const float* q, const float* k, const float* v, siz
                              int nh, int nkv, int hd, int len, size_t seq_stride,
                              size_t head_stride, size_t pos_stride, float* out, void* ws,
                              size_t ws_bytes, cudaStream_t s, const int* d_pos, int cap_len,
-                             bool record_status) {
+                             bool record_status, int len_step) {
   if (!d_pos && len <= 0) return fail(MINQ_ERR_SHAPE, "attention over an empty history");
+  if (len_step < 0 || (len_step && d_pos))
+    return fail(MINQ_ERR_ARG, "per-entry history lengths take host positions");
   if (nkv <= 0 || nh % nkv != 0)
     return fail(MINQ_ERR_MODEL, "n_heads must be a multiple of n_kv_heads");
   const int G = nh / nkv;
   const int qgroups = (G + 7) / 8;
   const int gmax = G > 4 ? 8 : (G > 2 ? 4 : (G > 1 ? 2 : 1));
-  const int size_len = d_pos ? cap_len : len;  // sizes the grid
+  // sizes the grid: the longest entry
+  const int size_len = (d_pos ? cap_len : len) + (int)(batch - 1) * len_step;
   AttnParams p{};
   p.q = q;
   p.k = k;
@@ -639,6 +671,7 @@ minq_status launch_attention(const float* q, const float* k, const float* v, siz
   p.nh = nh;
   p.nkv = nkv;
   p.len = len;
+  p.len_step = len_step;
   p.status = record_status ? device_status_word() : nullptr;
   p.d_pos = d_pos;
   // The TMA path needs each KV head's positions contiguous (head-major
@@ -646,18 +679,7 @@ minq_status launch_attention(const float* q, const float* k, const float* v, siz
   const bool tma = hd >= 16 && hd <= 256 && (hd & (hd - 1)) == 0 && pos_stride == (size_t)hd &&
                    (uintptr_t)k % 16 == 0 && (uintptr_t)v % 16 == 0 &&
                    seq_stride % 4 == 0 && head_stride % 4 == 0;
-  const size_t units = batch * nkv * qgroups;
-  if (tma) {
-    const int tp = std::min(32, 2048 / hd);
-    p.q_round = 4 * tp;
-    const size_t target = (size_t)sm_count() * 2;
-    size_t c = ((size_t)size_len * units + target - 1) / target;
-    c = (c + p.q_round - 1) / p.q_round * p.q_round;
-    p.chunk = (int)std::min<size_t>(c, (size_t)((size_len + p.q_round - 1) / p.q_round * p.q_round));
-  } else {
-    p.q_round = 32;
-    p.chunk = pick_chunk(size_len, units);
-  }
+  attn_split_plan(tma, batch, nh, nkv, hd, size_len, &p.chunk, &p.q_round);
   p.nsplit = (size_len + p.chunk - 1) / p.chunk;  // grid (split slots)
   p.ws_stride = p.nsplit;
   p.scale = 1.0f / sqrtf((float)hd);
@@ -714,7 +736,7 @@ minq_status launch_rope_append(const float* q_in, const float* k_in, const float
                                const float* sin_t, size_t batch, int nh, int nkv, int hd,
                                int pos, float* q_out, float* k_cache, float* v_cache,
                                size_t seq_stride, size_t head_stride, size_t pos_stride,
-                               cudaStream_t s, const int* d_pos) {
+                               cudaStream_t s, const int* d_pos, int pos_step) {
   if (hd % 2 != 0 || hd > 256) return fail(MINQ_ERR_SHAPE, "head_dim must be even and <= 256");
   RopeParams p{};
   p.q_in = q_in;
@@ -731,6 +753,7 @@ minq_status launch_rope_append(const float* q_in, const float* k_in, const float
   p.nkv = nkv;
   p.hd = hd;
   p.pos = pos;
+  p.pos_step = pos_step;
   p.d_pos = d_pos;
   p.q_out = q_out;
   p.k_cache = k_cache;

@@ -73,20 +73,27 @@ minq_status launch_argmax_rows(const float* x, size_t n, int B, uint32_t* out,
 
 // attention.cu
 size_t attn_workspace_bytes(size_t batch, size_t nh, size_t len, size_t hd_max);
+// Exact workspace of one launch_attention call over `batch` entries whose
+// longest history is size_len (head_major: the model's cache layout with
+// 16-byte aligned K/V), 0 when it needs no split partials.
+size_t attn_workspace_need(size_t batch, int nh, int nkv, int hd, int size_len, bool head_major);
 minq_status launch_attention(const float* q, const float* k, const float* v, size_t batch,
                              int nh, int nkv, int hd, int len, size_t seq_stride,
                              size_t head_stride, size_t pos_stride, float* out, void* ws,
                              size_t ws_bytes, cudaStream_t s, const int* d_pos = nullptr,
-                             int cap_len = 0, bool record_status = true);
+                             int cap_len = 0, bool record_status = true, int len_step = 0);
 // record_status = false: bounded-wait timeouts are not recorded (and the
-// lazily allocated device status word is never touched).
+// lazily allocated device status word is never touched). len_step > 0
+// (host positions only): entry b attends over len + b * len_step positions,
+// e.g. the tokens of a prompt chunk over one cache (seq_stride 0).
 minq_status launch_rope_append(const float* q_in, const float* k_in, const float* v_in,
                                size_t q_in_bstride, size_t kv_in_bstride, const float* q_norm,
                                const float* k_norm, float eps, const float* cos_t,
                                const float* sin_t, size_t batch, int nh, int nkv, int hd,
                                int pos, float* q_out, float* k_cache, float* v_cache,
                                size_t seq_stride, size_t head_stride, size_t pos_stride,
-                               cudaStream_t s, const int* d_pos = nullptr);
+                               cudaStream_t s, const int* d_pos = nullptr, int pos_step = 0);
+// pos_step: entry b is rotated and appended at position pos + b * pos_step.
 
 // glue.cu
 minq_status launch_embed(const float* embed, const uint32_t* d_tok, size_t vocab, int hidden,

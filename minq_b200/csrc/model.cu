@@ -141,6 +141,19 @@ struct minq_cache {
   size_t bpart_floats = 0;
   uint32_t* btok = nullptr;  // [batch] token ids
   uint32_t* barg = nullptr;  // [batch] argmax ids
+  // activations of chunked prompt prefill (kPrefillChunk tokens of a batch-1
+  // cache per pass), allocated on first use
+  float* px = nullptr;     // [chunk][H]
+  float* pqkv = nullptr;   // [chunk][qd + 2 kvd]
+  float* pq = nullptr;     // [chunk][qd]
+  float* patt = nullptr;   // [chunk][qd]
+  float* ph = nullptr;     // [chunk][I]
+  float* pxn = nullptr;    // prepared projection inputs
+  size_t pxn_floats = 0;
+  float* ppart = nullptr;  // column-slice partials
+  size_t ppart_floats = 0;
+  void* pws = nullptr;     // attention split partials
+  size_t pws_bytes = 0;
 };
 
 namespace minq {
@@ -686,6 +699,95 @@ static minq_status batch_ready(minq_model* m, minq_cache* c) {
   return MINQ_OK;
 }
 
+// Chunked prompt prefill: kPrefillChunk prompt tokens of a batch-1 cache per
+// pass, the projections as batched matvecs over the chunk's tokens (tensor
+// cores from two tokens on), RoPE / cache append at consecutive positions,
+// and attention with causal per-token histories (token i of a chunk at
+// position p0 + i attends over p0 + i + 1 positions). The same steps as
+// forward_token (model.rs:273-318) for each token, without the lm_head: the
+// prompt's last token runs as a decode step, which also gives the logits.
+constexpr int kPrefillChunk = kQmmMaxB;
+
+// Whether the model takes chunked prefill (the batched step's shape rules,
+// one GPU), and its activations on first use.
+static minq_status prefill_ready(minq_model* m, minq_cache* c, bool* ok) {
+  *ok = false;
+  const minq_config& cfg = m->cfg;
+  const char* env = std::getenv("MINQ_CHUNKED_PREFILL");
+  if (env && env[0] == '0') return MINQ_OK;
+  if (m->tp_world > 1 || c->batch != 1) return MINQ_OK;
+  if (cfg.hidden_size % 32 || cfg.intermediate_size % 32 || (cfg.n_heads * cfg.head_dim) % 32)
+    return MINQ_OK;
+  for (const DevLayer& L : m->layers)
+    if (L.qkv.tag < 0 || L.gate.tag == MINQ_F32 || L.gate.tag != L.up.tag) return MINQ_OK;
+  *ok = true;
+  if (c->px) return MINQ_OK;
+  const size_t B = kPrefillChunk, H = cfg.hidden_size, I = cfg.intermediate_size,
+               qd = cfg.n_heads * cfg.head_dim, kvd = cfg.n_kv_heads * cfg.head_dim;
+  auto alloc = [&](void** dst, size_t bytes) -> minq_status {  // owned by the cache
+    MINQ_CUDA_TRY(cudaMalloc(dst, bytes ? bytes : 16));
+    return MINQ_OK;
+  };
+  MINQ_TRY(alloc(reinterpret_cast<void**>(&c->px), B * H * 4));
+  MINQ_TRY(alloc(reinterpret_cast<void**>(&c->pqkv), B * (qd + 2 * kvd) * 4));
+  MINQ_TRY(alloc(reinterpret_cast<void**>(&c->pq), B * qd * 4));
+  MINQ_TRY(alloc(reinterpret_cast<void**>(&c->patt), B * qd * 4));
+  MINQ_TRY(alloc(reinterpret_cast<void**>(&c->ph), B * I * 4));
+  c->pxn_floats = B * std::max({H, qd, I});
+  MINQ_TRY(alloc(reinterpret_cast<void**>(&c->pxn), c->pxn_floats * 4));
+  c->ppart_floats = 4 * B * std::max({H, qd + 2 * kvd, I});
+  MINQ_TRY(alloc(reinterpret_cast<void**>(&c->ppart), c->ppart_floats * 4));
+  // the attention's split partials for any chunk size at any history
+  size_t ws = 0;
+  for (size_t t = 1; t <= B; ++t)
+    ws = std::max(ws, attn_workspace_need(t, (int)cfg.n_heads, (int)cfg.n_kv_heads,
+                                          (int)cfg.head_dim, (int)c->max_seq, true));
+  c->pws_bytes = ws + 256;
+  MINQ_TRY(alloc(&c->pws, c->pws_bytes));
+  return MINQ_OK;
+}
+
+// T <= kPrefillChunk tokens (device ids) at positions c->len .. c->len + T - 1.
+static minq_status forward_chunk(minq_model* m, minq_cache* c, const uint32_t* d_toks, int T) {
+  const minq_config& cfg = m->cfg;
+  const int H = (int)cfg.hidden_size, hd = (int)cfg.head_dim, nh = (int)cfg.n_heads,
+            nkv = (int)cfg.n_kv_heads;
+  const uint64_t qd = (uint64_t)nh * hd, kvd = (uint64_t)nkv * hd, I = cfg.intermediate_size;
+  const uint64_t qkv_rows = qd + 2 * kvd, V = cfg.vocab_size;
+  const float eps = cfg.rms_norm_eps;
+  const int p0 = (int)c->len;
+  cudaStream_t s = m->stream;
+  const size_t layer_elems = (size_t)nkv * c->max_seq * hd, head_stride = c->max_seq * hd;
+  MINQ_TRY(launch_embed_batch(m->embed, d_toks, V, H, T, c->px, s));
+  for (uint64_t li = 0; li < cfg.n_layers; ++li) {
+    const DevLayer& L = m->layers[li];
+    MINQ_TRY(launch_qmatmul(L.qkv.tag, L.qkv.ptr, nullptr, qkv_rows, H, T, c->px, H, L.attn_norm,
+                            eps, c->pxn, c->pxn_floats, L.bias_qkv, nullptr, c->pqkv, qkv_rows,
+                            c->ppart, c->ppart_floats, s));
+    float* kc = c->k + li * layer_elems;
+    float* vc = c->v + li * layer_elems;
+    // token i: rotated at position p0 + i and appended there (one sequence:
+    // sequence stride 0), then attends over p0 + i + 1 positions
+    MINQ_TRY(launch_rope_append(c->pqkv, c->pqkv + qd, c->pqkv + qd + kvd, qkv_rows, qkv_rows,
+                                L.q_norm, L.k_norm, eps, m->rope_cos, m->rope_sin, (size_t)T, nh,
+                                nkv, hd, p0, c->pq, kc, vc, 0, head_stride, hd, s, nullptr, 1));
+    MINQ_TRY(launch_attention(c->pq, kc, vc, (size_t)T, nh, nkv, hd, p0 + 1, 0, head_stride, hd,
+                              c->patt, c->pws, c->pws_bytes, s, nullptr, 0, true, 1));
+    MINQ_TRY(launch_qmatmul(L.o.tag, L.o.ptr, nullptr, H, (int)qd, T, c->patt, qd, nullptr, eps,
+                            c->pxn, c->pxn_floats, nullptr, c->px, c->px, H, c->ppart,
+                            c->ppart_floats, s));  // x += o
+    MINQ_TRY(launch_qmatmul(L.gate.tag, L.gate.ptr, L.up.ptr, I, H, T, c->px, H, L.ffn_norm, eps,
+                            c->pxn, c->pxn_floats, nullptr, nullptr, c->ph, I, c->ppart,
+                            c->ppart_floats, s));  // silu(gate) * up
+    MINQ_TRY(launch_qmatmul(L.down.tag, L.down.ptr, nullptr, H, (int)I, T, c->ph, I, nullptr, eps,
+                            c->pxn, c->pxn_floats, nullptr, c->px, c->px, H, c->ppart,
+                            c->ppart_floats, s));  // x += down
+  }
+  c->len += (size_t)T;
+  c->d_pos_valid = false;
+  return MINQ_OK;
+}
+
 // Capture one decode step (with or without logits) of cache `c` as a graph.
 static minq_status capture_step(minq_model* m, minq_cache* c, bool logits, cudaGraphExec_t* out) {
   cudaGraph_t g = nullptr;
@@ -1182,7 +1284,8 @@ void minq_cache_free(minq_cache* c) {
   cudaFree(c->d_pos);
   for (void* b : {(void*)c->bx, (void*)c->bqkv, (void*)c->bq, (void*)c->batt, (void*)c->bh,
                   (void*)c->blog, (void*)c->bxn, (void*)c->bpart, (void*)c->btok,
-                  (void*)c->barg})
+                  (void*)c->barg, (void*)c->px, (void*)c->pqkv, (void*)c->pq, (void*)c->patt,
+                  (void*)c->ph, (void*)c->pxn, (void*)c->ppart, c->pws})
     cudaFree(b);
   delete c;
 }
@@ -1212,7 +1315,23 @@ static minq_status forward_impl(minq_model* m, minq_cache* c, const uint32_t* h_
                                   m->stream));
     toks = m->d_tokens;
   }
-  for (size_t i = 0; i < n; ++i) {
+  size_t i = 0;
+  bool chunked = false;
+  if (n >= 2 && c->len + n <= m->cfg.max_seq_len && c->len + n <= c->max_seq)
+    MINQ_TRY(prefill_ready(m, c, &chunked));
+  // a prompt with an out-of-range token goes token by token, so the valid
+  // tokens before it are processed and the error comes at that token
+  if (chunked && h_tokens)
+    for (size_t j = 0; j < n; ++j) chunked = chunked && h_tokens[j] < m->cfg.vocab_size;
+  if (chunked) {
+    // every token but the last in chunks; the last one below gives the logits
+    for (; i + 1 < n; i += kPrefillChunk) {
+      const int T = (int)std::min<size_t>(kPrefillChunk, n - 1 - i);
+      MINQ_TRY(forward_chunk(m, c, toks + i, T));
+    }
+    i = n - 1;
+  }
+  for (; i < n; ++i) {
     if (c->len >= m->cfg.max_seq_len)  // model.rs:260-265
       return fail(MINQ_ERR_MODEL,
                   "sequence exceeds max_seq_len (" + std::to_string(m->cfg.max_seq_len) + ")");

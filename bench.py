@@ -526,6 +526,13 @@ def run_tp(args, world, rank, local):
         tok, _ = model.forward_argmax([int(h_tok[0])], cache, logits=True)
         h_tok[0] = tok
     e2e_ms = max_over_ranks(world, 1000.0 * (time.perf_counter() - t0))
+    # this library's kernel launches of one step (eager; the timed steps run
+    # the same kernels)
+    from minq_b200 import _lib
+    n0 = _lib.lib().minq_kernel_launches()
+    model.forward_argmax([int(h_tok[0])], cache)
+    torch.cuda.synchronize()
+    launches_per_step = _lib.lib().minq_kernel_launches() - n0
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -551,7 +558,7 @@ def run_tp(args, world, rank, local):
                        "cache_flush": "inputs > L2"},
             "e2e": {"value": K / (e2e_ms / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": 4,
                     "d2h_bytes_per_step": 4 * V + 4},
-            "gpu_launches": None,
+            "gpu_launches": int(launches_per_step * K),
             "roofline": {"bound": "hbm", "kernel": "decode step (per GPU)", "achieved": gbs,
                          "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                          "traffic": None, "per_launch_bytes": per_gpu},
@@ -584,8 +591,12 @@ def run_batch(args, world, rank, local):
     cache = model.new_cache(batch=B)
     rng = np.random.default_rng(args.seed + 100 + rank)
     prompts = rng.integers(0, cfg.vocab_size, (B, prompt))
+    torch.cuda.synchronize()
+    tp0 = time.perf_counter()
     for i in range(prompt):
         model.forward_batch(prompts[:, i].tolist(), cache, logits=False)
+    torch.cuda.synchronize()
+    prefill_s = max_over_ranks(world, time.perf_counter() - tp0)
     stream = torch.cuda.ExternalStream(model.stream)
     model.forward_batch_steps(cache, W)
     torch.cuda.synchronize()
@@ -613,6 +624,13 @@ def run_batch(args, world, rank, local):
         am, _ = model.forward_batch(toks, cache, logits=False)
         toks = [int(t) for t in am]
     e2e_ms = max_over_ranks(world, 1000.0 * (time.perf_counter() - t0))
+    # this library's kernel launches of one step (an eager step; the timed
+    # device continuation replays the same kernels)
+    from minq_b200 import _lib
+    n0 = _lib.lib().minq_kernel_launches()
+    model.forward_batch(toks, cache, logits=False)
+    torch.cuda.synchronize()
+    launches_per_step = _lib.lib().minq_kernel_launches() - n0
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -641,7 +659,9 @@ def run_batch(args, world, rank, local):
                        "cache_flush": "inputs > L2"},
             "e2e": {"value": total * K / (e2e_ms / 1000.0), "unit": "tok/s",
                     "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B},
-            "gpu_launches": None,
+            "prefill": {"tokens": total * prompt, "tok_s": total * prompt / prefill_s,
+                        "mode": "batched steps, one prompt token of every sequence per step"},
+            "gpu_launches": int(launches_per_step * K),
             "roofline": {"bound": "tensor" if B >= 16 else "hbm", "kernel": "batched step (per GPU)",
                          "achieved": tfs, "peak": peak, "unit": "TFLOP/s", "frac": tfs / peak,
                          "traffic": None, "per_launch_flops": flops},

@@ -46,13 +46,13 @@ minq_status take_device_status();
     if (_s != MINQ_OK) return _s;          \
   } while (0)
 
-// Launch counter behind minq_kernel_launches().
+// Launch counter behind minq_kernel_launches(): launch_k counts every launch
+// it makes; the few launches made without it count themselves.
 void count_launch();
 
-// Check the last launch error (and count the launch).
+// Check the last launch error.
 #define MINQ_LAUNCH_CHECK(what)                                     \
   do {                                                              \
-    ::minq::count_launch();                                         \
     cudaError_t _e = cudaGetLastError();                            \
     if (_e != cudaSuccess) return ::minq::cuda_fail(_e, what);      \
   } while (0)
@@ -89,6 +89,7 @@ cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
   attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  count_launch();
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 

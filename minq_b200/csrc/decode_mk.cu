@@ -1309,6 +1309,7 @@ static minq_status mk_launch_inst(const MkParams& p, int grid, size_t smem, cuda
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  count_launch();
   MINQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, p));
   MINQ_LAUNCH_CHECK("decode_mk_kernel");
   return MINQ_OK;

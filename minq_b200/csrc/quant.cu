@@ -102,6 +102,7 @@ minq_status launch_quantize(int dtype, const float* x, size_t n, void* out, cuda
     quantize_kernel<MINQ_Q8_0><<<grid, 256, 0, s>>>(x, nb, (uint8_t*)out);
   else
     quantize_kernel<MINQ_Q4_0><<<grid, 256, 0, s>>>(x, nb, (uint8_t*)out);
+  count_launch();
   MINQ_LAUNCH_CHECK("quantize_kernel");
   return MINQ_OK;
 }
@@ -114,6 +115,7 @@ minq_status launch_dequantize(int dtype, const void* in, size_t nblocks, float* 
     dequantize_kernel<MINQ_Q8_0><<<grid, 256, 0, s>>>((const uint8_t*)in, nblocks, out);
   else
     dequantize_kernel<MINQ_Q4_0><<<grid, 256, 0, s>>>((const uint8_t*)in, nblocks, out);
+  count_launch();
   MINQ_LAUNCH_CHECK("dequantize_kernel");
   return MINQ_OK;
 }

@@ -72,7 +72,8 @@ def test_megakernel_matches_oracle_and_per_op_path(mq, orc, case):
     recs = _records(cfg, dtype, orc, 11, qkn, bias)
     mk, ops, om = _models(mq, orc, cfg, recs)
     prompt = list(np.random.default_rng(3).integers(0, V, plen))
-    # prefill: every prompt token through the megakernel, logits of the last
+    # prefill: the prompt in chunks, its last token through the megakernel
+    # (or the per-op step), logits of the last
     c_mk, c_ops, oc = mk.new_cache(), ops.new_cache(), om.new_cache()
     l_mk = mk.forward(prompt, c_mk)
     l_ops = ops.forward(prompt, c_ops)

@@ -539,15 +539,17 @@ __device__ void mk_stage_x(const MkParams& p, float* xs, const float* src, int n
 }
 
 // Stage a projection input as fixed-point planes: v = src (n floats, n % 32
-// == 0), times rmsnorm(src) * gain when gain is set (tensor.rs:219-227, the
-// same f32 operations as the reference), then per 32-column block b:
+// == 0), times gain when gain is set, then per 32-column block b:
 // e = exponent of max|v| (2^(e-1) <= max < 2^e), m = rint(v * 2^(kMkFx - e))
 // (|m| <= 2^kMkFx), split into kMkNP signed base-256 digits
 // (m = sum_q 256^q d_q, d_q in [-128, 127]). xp gets kMkRecW words per block
 // (see mk_block_dot for their order) and xsb the block's scale 2^(e - kMkFx)
 // (over 16 for Q4_0, whose codes enter as 16 * nibble). Thread t stages the 8
 // columns 8 (t mod 4) .. + 7 of block t / 4, so the four threads of a block
-// are adjacent lanes.
+// are adjacent lanes. With a gain, warp w also leaves its part of sum(src^2)
+// in misc[w]: RMSNorm (tensor.rs:219-227) is linear in the input, so its
+// scale 1 / rms multiplies each row's sum in the projection's epilogue and
+// the planes need not wait for the reduction.
 template <int DT>
 __device__ void mk_stage_planes(const MkParams& p, uint32_t* xp, float* xsb, const float* src,
                                 int n, const float* gain, float* misc) {
@@ -563,7 +565,6 @@ __device__ void mk_stage_planes(const MkParams& p, uint32_t* xp, float* xsb, con
     va[r] = gi < ng ? ldcg4(src + 8 * gi) : zero;
     vb[r] = gi < ng ? ldcg4(src + 8 * gi + 4) : zero;
   }
-  float inv = 1.0f;
   if (gain) {
     float ss = 0.0f;
 #pragma unroll
@@ -579,12 +580,7 @@ __device__ void mk_stage_planes(const MkParams& p, uint32_t* xp, float* xsb, con
       ss = fmaf(b.w, b.w, ss);
     }
     ss = warp_sum(ss);
-    if (lane == 0) misc[warp] = ss;
-    mk_sync();
-    float v = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kMkCW; ++w) v += misc[w];
-    inv = 1.0f / sqrtf(v / (float)n + p.eps);
+    if (lane == 0) misc[warp] = ss;  // read after the closing barrier
   }
   const float4* g4 = reinterpret_cast<const float4*>(gain);
 #pragma unroll
@@ -595,8 +591,8 @@ __device__ void mk_stage_planes(const MkParams& p, uint32_t* xp, float* xsb, con
     float4 a = va[rd], b = vb[rd];
     if (gain && act) {
       const float4 ga = g4[2 * gi], gb = g4[2 * gi + 1];
-      a.x = a.x * inv * ga.x; a.y = a.y * inv * ga.y; a.z = a.z * inv * ga.z; a.w = a.w * inv * ga.w;
-      b.x = b.x * inv * gb.x; b.y = b.y * inv * gb.y; b.z = b.z * inv * gb.z; b.w = b.w * inv * gb.w;
+      a.x *= ga.x; a.y *= ga.y; a.z *= ga.z; a.w *= ga.w;
+      b.x *= gb.x; b.y *= gb.y; b.z *= gb.z; b.w *= gb.w;
     }
     const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     float mx = 0.0f;
@@ -666,7 +662,7 @@ __device__ void mk_stage_planes(const MkParams& p, uint32_t* xp, float* xsb, con
 template <int DT, bool DUAL, class Pre, class Epi>
 __device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const uint32_t* xp,
                                const float* xsb, MkFeed& f, const MkCta* cta, int L, float* red,
-                               int& it, Pre pre_ld, Epi epi) {
+                               int& it, const float* norm_ss, int norm_n, Pre pre_ld, Epi epi) {
   constexpr int BB = DT == MINQ_Q8_0 ? kQ8Bytes : kQ4Bytes;
   constexpr int TB = MkTile<DT>::blocks;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -750,6 +746,14 @@ __device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const uint32_t
         v0 += red[q * plane + (size_t)t * WG + w];
         if (DUAL) v1 += red[q * plane + ((size_t)cnt + t) * WG + w];
       }
+    if (norm_ss) {  // the RMSNorm scale of the staged input (mk_stage_planes)
+      float ss = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kMkCW; ++w) ss += norm_ss[w];
+      const float inv = 1.0f / sqrtf(ss / (float)norm_n + p.eps);
+      v0 *= inv;
+      v1 *= inv;
+    }
     epi(rb + t, v0, v1, pre);
   }
 }
@@ -1159,7 +1163,8 @@ __device__ void mk_consumers(const MkParams& p, unsigned char* sm, MkFeed& f, co
     mk_stage_planes<DT>(p, xp, xsb, xsrc, p.H, lp.attn_norm, misc);
     const float* bias = lp.bias_qkv;
     mk_consume_mat<DT, false>(
-        p, p.qkv, xp, xsb, f, cta, L, red, it, [&](int row) { return bias ? bias[row] : 0.0f; },
+        p, p.qkv, xp, xsb, f, cta, L, red, it, misc, p.H,
+        [&](int row) { return bias ? bias[row] : 0.0f; },
         [&](int row, float v, float, float b) { p.qkv_out[row] = bias ? v + b : v; });
     if (!(ok = barrier())) break;
     // P2: attention
@@ -1170,20 +1175,21 @@ __device__ void mk_consumers(const MkParams& p, unsigned char* sm, MkFeed& f, co
     mk_stage_planes<DT>(p, xp, xsb, p.att, p.qd, nullptr, misc);
     const float* res = xsrc;
     mk_consume_mat<DT, false>(
-        p, p.o, xp, xsb, f, cta, L, red, it, [&](int row) { return ldcg(res + row); },
+        p, p.o, xp, xsb, f, cta, L, red, it, nullptr, 0, [&](int row) { return ldcg(res + row); },
         [&](int row, float v, float, float r) { p.x[row] = r + v; });
     xsrc = p.x;
     if (!(ok = barrier())) break;
     // P4: h = silu(gate) * up
     mk_stage_planes<DT>(p, xp, xsb, p.x, p.H, lp.ffn_norm, misc);
     mk_consume_mat<DT, true>(
-        p, p.gu, xp, xsb, f, cta, L, red, it, [&](int) { return 0.0f; },
+        p, p.gu, xp, xsb, f, cta, L, red, it, misc, p.H, [&](int) { return 0.0f; },
         [&](int row, float g, float u, float) { p.h[row] = silu(g) * u; });
     if (!(ok = barrier())) break;
     // P5: x = x + W_down h
     mk_stage_planes<DT>(p, xp, xsb, p.h, p.I, nullptr, misc);
     mk_consume_mat<DT, false>(
-        p, p.down, xp, xsb, f, cta, L, red, it, [&](int row) { return ldcg(p.x + row); },
+        p, p.down, xp, xsb, f, cta, L, red, it, nullptr, 0,
+        [&](int row) { return ldcg(p.x + row); },
         [&](int row, float v, float, float r) { p.x[row] = r + v; });
     if (!(ok = barrier())) break;
   }

@@ -65,6 +65,11 @@ BATCH_WORKLOAD = "llama3-8b-q4_0-b64"
 # append + attend over L+1 positions for B sequences, swept over
 # L in {512, 2048, 8192, 32768} x B in {1, 8, 64}.
 ATTN_WORKLOAD = "attn-gqa32-8-hd128"
+# Perplexity evaluation: the Qwen3-4B shape in Q4_0 over seeded synthetic
+# token ids in non-overlapping windows of 512 (the reference's protocol is
+# 10,000 tokens at context 512, i.e. 20 windows); one step = one window.
+PPL_WORKLOAD = "qwen3-4b-q4_0-ppl"
+PPL_CONTEXT = 512
 
 
 def parse():
@@ -74,7 +79,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["minq", "reference"], default="minq")
     ap.add_argument("--workload",
-                    choices=sorted(WORKLOADS) + [TP_WORKLOAD, ATTN_WORKLOAD, BATCH_WORKLOAD],
+                    choices=sorted(WORKLOADS) + [TP_WORKLOAD, ATTN_WORKLOAD, BATCH_WORKLOAD,
+                                                 PPL_WORKLOAD],
                     default="qwen3-4b-q4_0")
     ap.add_argument("--prompt", type=int, default=None, help="prefill length override")
     ap.add_argument("--seed", type=int, default=1234)
@@ -671,6 +677,160 @@ def run_batch(args, world, rank, local):
     del cache, model
 
 
+def _ppl_flops(cfg, n_pos, n_scored, context):
+    """Algorithmic flops of scoring: 2 per weight per swept position (every
+    projection), 2 per lm_head weight per scored position, and the causal
+    q.k and p.v products (2 * 2 * hd per head per attended position)."""
+    H, I, hd = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
+    qd, kvd = cfg.n_heads * hd, cfg.n_kv_heads * hd
+    proj = cfg.n_layers * (H * (qd + 2 * kvd) + qd * H + 3 * I * H)
+    attn = 0
+    left = n_pos
+    while left > 0:  # windows of `context` - 1 swept positions
+        t = min(context - 1, left)
+        attn += cfg.n_layers * cfg.n_heads * 4 * hd * t * (t + 1) // 2
+        left -= t
+    return 2.0 * proj * n_pos + 2.0 * cfg.vocab_size * H * n_scored + attn
+
+
+def run_ppl(args, world, rank, local):
+    """Perplexity evaluation (eval_ppl, ppl.rs:44-103) of the Qwen3-4B shape in
+    Q4_0: K windows of 512 synthetic token ids, the windows split over the
+    ranks (independent, no collective). The public call takes host token ids
+    and returns the mean nll; it synchronises per 64-position chunk to read
+    the chunk's f64 nll, so the device-timed value and e2e cover the same
+    work."""
+    from minq_b200 import synth
+    from dataclasses import replace
+    K, W, ctx = args.steps, args.warmup, PPL_CONTEXT
+    cfg0, qk_norm, tied = synth.ARCH["qwen3-4b"]
+    if args.layers:
+        cfg0 = replace(cfg0, n_layers=args.layers)
+    cfg = replace(cfg0, max_seq_len=ctx)
+    rng = np.random.default_rng(args.seed + 7)
+    tokens = rng.integers(0, cfg.vocab_size, K * ctx).astype(np.uint32)
+    scored_per_window = ctx - 2
+    # the reference arm: the oracle's eval_ppl on all host cores, one sample
+    # window of `cpu_ctx` tokens per step (about 10 s; scored positions / s)
+    cpu_ctx = 256
+
+    def cpu_line(om, orc, steps, warm):
+        for _ in range(warm):
+            om.eval_ppl(tokens[:cpu_ctx], cpu_ctx)
+        t0 = time.perf_counter()
+        for i in range(steps):
+            r = om.eval_ppl(tokens[i * cpu_ctx:(i + 1) * cpu_ctx], cpu_ctx)
+        el = time.perf_counter() - t0
+        return steps * (cpu_ctx - 2) / el, el, r
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        from oracle import oracle as orc
+        om = cpu_model(orc, synth, cfg, qk_norm, tied, args.seed)
+        steps = max(1, min(K, 2))
+        value, el, _ = cpu_line(om, orc, steps, 0)
+        line = {
+            "impl": "reference", "metric": "perplexity scored tok/s", "value": value,
+            "unit": "tok/s", "n_gpus": args.gpus, "steps": steps, "warmup": 0,
+            "ms_per_step": 1000 * el / steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32 (f64 log-sum-exp)", "data": "synthetic",
+            "config": {"workload": f"{PPL_WORKLOAD}: Qwen3-4B shape, Q4_0, windows of {ctx}",
+                       "cache_flush": "weights 3.8 GB > L2"},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": orc.max_threads(),
+                             "kind": "port",
+                             "sample": f"{steps} windows of {cpu_ctx} tokens "
+                                       f"({cpu_ctx - 2} scored each), {el:.1f} s"},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    import minq_b200 as mq
+    from minq_b200 import _lib
+    torch.cuda.set_device(local)
+    if K % world:
+        raise SystemExit(f"{PPL_WORKLOAD}: {K} windows do not split over {world} ranks")
+    kw = K // world
+    mine = tokens[rank * kw * ctx:(rank + 1) * kw * ctx]
+    model = build_model(mq, synth, cfg, qk_norm, tied, args.seed)
+    stream = torch.cuda.ExternalStream(model.stream)
+    warm = rng.integers(0, cfg.vocab_size, max(1, W) * ctx).astype(np.uint32)
+    mq.eval_ppl(model, warm, ctx)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(physical_gpu_index(local))
+    clocks.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    n0 = _lib.lib().minq_kernel_launches()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed_ppl")
+    t0 = time.perf_counter()
+    ev0.record(stream)
+    res = mq.eval_ppl(model, mine, ctx)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    wall_ms = 1000.0 * (time.perf_counter() - t0)
+    torch.cuda.nvtx.range_pop()
+    launches = _lib.lib().minq_kernel_launches() - n0
+    barrier(world)
+    clk = clocks.stop()
+    ms_max = max_over_ranks(world, ev0.elapsed_time(ev1))
+    e2e_ms = max_over_ranks(world, wall_ms)
+    scored = K * scored_per_window
+    assert res.scored_positions == kw * scored_per_window
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    flops = _ppl_flops(cfg, kw * (ctx - 1), kw * scored_per_window, ctx)
+    tfs = flops / (ms_max * 1e-3) / 1e12
+    peak = peaks.get("bf16_tflops") or 1590.0
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            from oracle import oracle as orc
+            om = cpu_model(orc, synth, cfg, qk_norm, tied, args.seed)
+            v, el, _ = cpu_line(om, orc, 1, 0)
+            cpu = {"value": v, "unit": "tok/s", "cores": orc.max_threads(), "kind": "port",
+                   "sample": f"one window of {cpu_ctx} tokens ({cpu_ctx - 2} scored) of the "
+                             f"same model, {el:.1f} s"}
+            del om
+        except Exception as e:  # the baseline must not sink the GPU number
+            cpu = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                   "sample": f"failed: {type(e).__name__}: {e}"}
+    if rank == 0:
+        print(json.dumps({
+            "metric": "perplexity scored tok/s", "value": scored / (ms_max / 1000.0),
+            "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": max(1, W),
+            "ms_per_step": ms_max / kw, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "projections bf16 x 2 (hi/lo split inputs) on the tensor cores, f32 "
+                     "accumulate; f32 lm_head; f64 log-sum-exp",
+            "data": "synthetic",
+            "config": {"workload": f"{PPL_WORKLOAD}: Qwen3-4B shape, Q4_0, {K} windows of "
+                                   f"{ctx} seeded token ids ({kw} per GPU)",
+                       "layers": cfg.n_layers, "context": ctx,
+                       "parallelism": f"data{world}" if world > 1 else "single GPU",
+                       "cache_flush": "inputs > L2: 3.8 GB of weights per 64-position chunk",
+                       "mean_nll_rank0": res.mean_nll},
+            "e2e": {"value": scored / (e2e_ms / 1000.0), "unit": "tok/s",
+                    "h2d_bytes_per_step": 4 * ctx, "d2h_bytes_per_step": 8 * scored_per_window},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "tensor", "kernel": "window (sweep + lm_head + nll)",
+                         "achieved": tfs, "peak": peak, "unit": "TFLOP/s", "frac": tfs / peak,
+                         "traffic": None, "per_launch_flops": flops / kw},
+            "cpu_baseline": cpu,
+            "clocks": clk,
+        }), flush=True)
+    del model
+
+
 def run_attn(args, world, rank, local):
     """The decode-attention op (minq_attn_decode) over the sweep; the line's
     value is the B = 8, L = 8192 point, `sweep` holds every point. Each
@@ -761,6 +921,8 @@ def main():
             run_tp(args, world, rank, local)
         elif args.workload == BATCH_WORKLOAD:
             run_batch(args, world, rank, local)
+        elif args.workload == PPL_WORKLOAD:
+            run_ppl(args, world, rank, local)
         elif args.impl == "reference":
             run_reference(args, world, rank)
         else:

@@ -74,12 +74,25 @@ typedef struct minq_gen_stats {
   double decode_secs;
 } minq_gen_stats;
 
+/* PplResult (ppl.rs:16-27). */
+typedef struct minq_ppl_result {
+  uint64_t total_tokens;     /* tokens in the input sequence */
+  uint64_t scored_positions; /* positions that contributed to the mean */
+  double mean_nll;           /* mean cross-entropy (natural log) */
+  double ppl;                /* exp(mean_nll) */
+} minq_ppl_result;
+
 typedef struct minq_model minq_model;
 typedef struct minq_cache minq_cache;
 
 /* Engine::generate's `on_token` callback (engine.rs:56); a non-zero return
  * aborts generation and is reported as MINQ_ERR_MODEL (engine.rs:73). */
 typedef int (*minq_token_cb)(uint32_t token, void* user);
+
+/* eval_ppl's `on_window(done, total, cumulative_ppl)` progress callback
+ * (ppl.rs:49), called after each window; cumulative_ppl is NaN while no
+ * position has been scored. */
+typedef void (*minq_ppl_window_cb)(size_t done, size_t total, double cumulative_ppl, void* user);
 
 const char* minq_last_error(void);
 int minq_abi_version(void);
@@ -298,6 +311,31 @@ minq_status minq_generate(minq_model* m, const uint32_t* prompt, size_t n_prompt
                           size_t max_tokens, const uint32_t* stop_tokens, size_t n_stop,
                           minq_token_cb on_token, void* user, uint32_t* tokens_out,
                           minq_gen_stats* stats);
+
+/* Model::forward_full_states (model.rs:337-424): the hidden state of every
+ * position of `tokens` (host, n ids) after the last decoder layer, before the
+ * final RMSNorm, into `states_out` (host, n x hidden_size floats, or NULL to
+ * run the sweep only). Runs on a scratch cache of n positions, chunk by chunk
+ * (64 positions per pass, causal), and leaves no state behind. Empty input ->
+ * MINQ_ERR_MODEL "empty token sequence"; n > max_seq_len -> MINQ_ERR_MODEL
+ * "sequence exceeds max_seq_len (N)"; token >= vocab -> MINQ_ERR_SHAPE; a
+ * model the chunked sweep does not take (tensor-parallel, f32 q|k|v or
+ * gate/up projections, dimensions not multiples of 32) -> MINQ_ERR_SHAPE. */
+minq_status minq_forward_full_states(minq_model* m, const uint32_t* tokens, size_t n,
+                                     float* states_out);
+
+/* eval_ppl (ppl.rs:44-103): split `tokens` (host, n ids) into
+ * non-overlapping windows of `context` tokens, sweep each window causally
+ * (as minq_forward_full_states), and score position t in 1 .. len - 2 of a
+ * window by the negative log-likelihood of window[t + 1] under the lm_head
+ * logits of its final-RMSNorm'd state (log-sum-exp in f64, ppl.rs:30-35),
+ * summed in f64 in position order. `on_window` (or NULL) is called after
+ * each window. n < 3, context < 3, context > max_seq_len, or no scorable
+ * position -> MINQ_ERR_MODEL with the reference's messages; token >= vocab
+ * -> MINQ_ERR_SHAPE when its window is reached; shapes the sweep does not
+ * take -> MINQ_ERR_SHAPE. */
+minq_status minq_eval_ppl(minq_model* m, const uint32_t* tokens, size_t n, size_t context,
+                          minq_ppl_window_cb on_window, void* user, minq_ppl_result* out);
 
 /* The model's CUDA stream (cudaStream_t as void*). */
 void* minq_model_stream(minq_model* m);

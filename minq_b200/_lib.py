@@ -56,7 +56,15 @@ class GenStats(C.Structure):
         return self.gen_tokens / max(self.decode_secs, 1e-9)
 
 
+class PplResult(C.Structure):
+    """minq_ppl_result == PplResult (ppl.rs:16-27)."""
+
+    _fields_ = [("total_tokens", C.c_uint64), ("scored_positions", C.c_uint64),
+                ("mean_nll", C.c_double), ("ppl", C.c_double)]
+
+
 TOKEN_CB = C.CFUNCTYPE(C.c_int, C.c_uint32, C.c_void_p)
+PPL_WINDOW_CB = C.CFUNCTYPE(None, C.c_size_t, C.c_size_t, C.c_double, C.c_void_p)
 
 P, S, I, U64P = C.c_void_p, C.c_size_t, C.c_int, C.POINTER(C.c_uint64)
 
@@ -104,6 +112,8 @@ SIGNATURES = {
     "minq_forward_batch_device": (I, [P, P, S, P]),
     "minq_model_set_graphs": (I, [P, I]),
     "minq_generate": (I, [P, P, S, S, P, S, TOKEN_CB, P, P, C.POINTER(GenStats)]),
+    "minq_forward_full_states": (I, [P, P, S, P]),
+    "minq_eval_ppl": (I, [P, P, S, S, PPL_WINDOW_CB, P, C.POINTER(PplResult)]),
 }
 
 _lib = None

@@ -27,10 +27,11 @@ from .minq_format import ModelConfig, TAG_F32, TAG_Q4_0, TAG_Q8_0, BLOCK_SIZE, B
 __all__ = [
     "MinqError", "ModelConfig", "QuantDtype", "QuantizedTensor", "quantize_q8_0",
     "quantize_q4_0", "dequantize_q8_0", "dequantize_q4_0", "argmax", "Model", "KVCache",
-    "Sampler", "Engine", "GenStats", "BLOCK_SIZE",
+    "Sampler", "Engine", "GenStats", "PplResult", "eval_ppl", "BLOCK_SIZE",
 ]
 
 GenStats = _lib.GenStats
+PplResult = _lib.PplResult
 
 
 def _torch():
@@ -299,6 +300,16 @@ class Model:
         check(lib().minq_decode_steps(self._h, cache._h, n,
                                       C.c_void_p(d_tokens_out) if d_tokens_out else None))
 
+    def forward_full_states(self, tokens) -> np.ndarray:
+        """Model::forward_full_states (model.rs:337-424): [n, hidden] f32 hidden
+        states after the last decoder layer, before the final RMSNorm; one
+        causal sweep, no cache kept."""
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32).reshape(-1))
+        out = np.empty((t.size, self.config.hidden_size), dtype=np.float32)
+        check(lib().minq_forward_full_states(self._h, t.ctypes.data_as(C.c_void_p), t.size,
+                                             out.ctypes.data_as(C.c_void_p)))
+        return out
+
     def tp_init(self, rank: int, world: int, unique_id: bytes) -> None:
         """Keep this rank's share of a tensor-parallel split over `world` GPUs and
         join the NCCL communicator named by `unique_id` (tp_unique_id()); every
@@ -387,6 +398,34 @@ class KVCache:
         check(lib().minq_cache_read(self._h, layer, start, n, k.ctypes.data_as(C.c_void_p),
                                     v.ctypes.data_as(C.c_void_p)))
         return k, v
+
+
+def eval_ppl(model: "Model", tokens, context: int,
+             on_window: Callable[[int, int, float], None] | None = None) -> "PplResult":
+    """eval_ppl (ppl.rs:44-103): non-overlapping windows of `context` tokens,
+    each swept causally on the GPU; position t in 1 .. len - 2 of a window
+    scores the next token by log-sum-exp (f64); `on_window(done, total,
+    cumulative_ppl)` after each window. Returns PplResult (total_tokens,
+    scored_positions, mean_nll, ppl). An exception raised by on_window is
+    re-raised after the call."""
+    t = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32).reshape(-1))
+    raised = []
+
+    def cb(done, total, ppl, _user):
+        if on_window is not None and not raised:
+            try:
+                on_window(int(done), int(total), float(ppl))
+            except BaseException as e:  # re-raised after the C call returns
+                raised.append(e)
+
+    ccb = _lib.PPL_WINDOW_CB(cb)
+    res = PplResult()
+    st = lib().minq_eval_ppl(model._h, t.ctypes.data_as(C.c_void_p), t.size, int(context), ccb,
+                             None, C.byref(res))
+    if raised:
+        raise raised[0]
+    check(st)
+    return res
 
 
 class Sampler:

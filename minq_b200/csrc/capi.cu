@@ -53,7 +53,7 @@ bool pdl_enabled() {
 }
 
 minq_status ensure_dynamic_smem(const void* kernel, size_t bytes) {
-  if (bytes <= 48 * 1024) return MINQ_OK;
+  if (bytes == 0) return MINQ_OK;
   static std::mutex mu;
   static std::map<std::pair<int, const void*>, size_t> done;
   int dev = 0;
@@ -61,6 +61,14 @@ minq_status ensure_dynamic_smem(const void* kernel, size_t bytes) {
   std::lock_guard<std::mutex> g(mu);
   size_t& cur = done[{dev, kernel}];
   if (cur >= bytes) return MINQ_OK;
+  // without the opt-in, static + dynamic shared memory must stay within
+  // 48 KB, so the kernel's static arrays count against that default
+  cudaFuncAttributes fa{};
+  MINQ_CUDA_TRY(cudaFuncGetAttributes(&fa, kernel));
+  if (fa.sharedSizeBytes + bytes <= 48 * 1024) {
+    cur = bytes;
+    return MINQ_OK;
+  }
   MINQ_CUDA_TRY(
       cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
   cur = bytes;

@@ -25,8 +25,9 @@ minq_status cuda_fail(cudaError_t e, const char* what);
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
-// Raise a kernel's dynamic shared-memory limit to at least `bytes` (cached
-// per device and kernel, so the attribute call happens once).
+// Raise a kernel's dynamic shared-memory limit to at least `bytes` when its
+// static plus `bytes` of dynamic shared memory exceed the 48 KB default
+// (cached per device and kernel, so the attribute call happens once).
 minq_status ensure_dynamic_smem(const void* kernel, size_t bytes);
 
 // Per-device status word that bounded device-side waits set on timeout

@@ -1,8 +1,9 @@
 // Small kernels of the forward step that are not fused into a matvec:
 // embedding row gather (model.rs:275), standalone RMSNorm (tensor.rs:219-227,
 // dense-f32 layers), bias/residual epilogue (tensor.rs:195 add_) and SwiGLU
-// (tensor.rs:203-215) after f32 matvecs, and the device-side position
-// counter of a graph-captured decode step.
+// (tensor.rs:203-215) after f32 matvecs, the device-side position
+// counter of a graph-captured decode step, and the per-position negative
+// log-likelihood of perplexity evaluation (ppl.rs:30-35).
 #include "common.cuh"
 
 namespace minq {
@@ -67,6 +68,47 @@ __global__ void advance_pos_kernel(int* pos, int by) {
   if (threadIdx.x == 0) *pos += by;
 }
 
+__device__ __forceinline__ double warp_sum_f64(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ppl.rs:30-35 for row blockIdx.x of logits [rows][V]: the f32 max (a fold
+// with f32::max, NaN ignored; the order of a max does not matter), then
+// sum_i exp((l_i - max) as f64) in f64, and nll = max + ln(sum) - l[target].
+// The f64 sum is a tree instead of the reference's left-to-right fold (a
+// relative difference of order 1e-16 per term). A target outside the row
+// (the host checks the tokens first) gives NaN rather than a read.
+__global__ void __launch_bounds__(1024) nll_rows_kernel(const float* __restrict__ logits, size_t V,
+                                                        const uint32_t* __restrict__ targets,
+                                                        double* __restrict__ out) {
+  __shared__ float smx[32];
+  __shared__ double ssum[32];
+  pdl_wait();
+  const float* row = logits + (size_t)blockIdx.x * V;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  float mx = -INFINITY;
+  for (size_t i = tid; i < V; i += blockDim.x) mx = fmaxf(mx, row[i]);
+  mx = warp_max(mx);
+  if (lane == 0) smx[warp] = mx;
+  __syncthreads();
+  mx = warp_max(lane < nw ? smx[lane] : -INFINITY);
+  double sum = 0.0;
+  for (size_t i = tid; i < V; i += blockDim.x) sum += exp((double)(row[i] - mx));
+  sum = warp_sum_f64(sum);
+  if (lane == 0) ssum[warp] = sum;
+  __syncthreads();
+  if (warp == 0) {
+    sum = warp_sum_f64(lane < nw ? ssum[lane] : 0.0);
+    if (lane == 0) {
+      const uint32_t t = targets[blockIdx.x];
+      out[blockIdx.x] = t < V ? (double)mx + log(sum) - (double)row[t] : (double)NAN;
+    }
+  }
+  pdl_launch_dependents();
+}
+
 static unsigned ew_grid(size_t n) {
   size_t g = (n + 255) / 256;
   size_t cap = (size_t)sm_count() * 8;
@@ -99,6 +141,15 @@ minq_status launch_epilogue(const float* acc, const float* bias, const float* re
 minq_status launch_swiglu(const float* g, const float* u, float* h, size_t n, cudaStream_t s) {
   MINQ_CUDA_TRY(launch_k(swiglu_kernel, dim3(ew_grid(n)), dim3(256), 0, s, g, u, h, n));
   MINQ_LAUNCH_CHECK("swiglu_kernel");
+  return MINQ_OK;
+}
+
+minq_status launch_nll_rows(const float* logits, size_t V, int rows, const uint32_t* targets,
+                            double* out, cudaStream_t s) {
+  if (rows <= 0) return MINQ_OK;
+  MINQ_CUDA_TRY(launch_k(nll_rows_kernel, dim3((unsigned)rows), dim3(1024), 0, s, logits, V,
+                         targets, out));
+  MINQ_LAUNCH_CHECK("nll_rows_kernel");
   return MINQ_OK;
 }
 

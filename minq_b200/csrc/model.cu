@@ -154,6 +154,9 @@ struct minq_cache {
   size_t ppart_floats = 0;
   void* pws = nullptr;     // attention split partials
   size_t pws_bytes = 0;
+  // perplexity scoring of a chunk: [chunk][vocab] logits, [chunk] f64 nll
+  float* plog = nullptr;
+  double* pnll = nullptr;
 };
 
 namespace minq {
@@ -709,12 +712,13 @@ static minq_status batch_ready(minq_model* m, minq_cache* c) {
 constexpr int kPrefillChunk = kQmmMaxB;
 
 // Whether the model takes chunked prefill (the batched step's shape rules,
-// one GPU), and its activations on first use.
-static minq_status prefill_ready(minq_model* m, minq_cache* c, bool* ok) {
+// one GPU), and its activations on first use. MINQ_CHUNKED_PREFILL=0 turns
+// chunked prompts off (use_env); the full-sequence sweep ignores it.
+static minq_status prefill_ready(minq_model* m, minq_cache* c, bool* ok, bool use_env = true) {
   *ok = false;
   const minq_config& cfg = m->cfg;
   const char* env = std::getenv("MINQ_CHUNKED_PREFILL");
-  if (env && env[0] == '0') return MINQ_OK;
+  if (use_env && env && env[0] == '0') return MINQ_OK;
   if (m->tp_world > 1 || c->batch != 1) return MINQ_OK;
   if (cfg.hidden_size % 32 || cfg.intermediate_size % 32 || (cfg.n_heads * cfg.head_dim) % 32)
     return MINQ_OK;
@@ -1285,7 +1289,8 @@ void minq_cache_free(minq_cache* c) {
   for (void* b : {(void*)c->bx, (void*)c->bqkv, (void*)c->bq, (void*)c->batt, (void*)c->bh,
                   (void*)c->blog, (void*)c->bxn, (void*)c->bpart, (void*)c->btok,
                   (void*)c->barg, (void*)c->px, (void*)c->pqkv, (void*)c->pq, (void*)c->patt,
-                  (void*)c->ph, (void*)c->pxn, (void*)c->ppart, c->pws})
+                  (void*)c->ph, (void*)c->pxn, (void*)c->ppart, c->pws, (void*)c->plog,
+                  (void*)c->pnll})
     cudaFree(b);
   delete c;
 }
@@ -1493,6 +1498,156 @@ minq_status minq_generate(minq_model* m, const uint32_t* prompt, size_t n_prompt
   minq_cache_free(c);
   if (stats) *stats = st;
   return rc;
+}
+
+// ---------------------------------------------------------------------------
+// C ABI: full-sequence states and perplexity (model.rs:337-424, ppl.rs:44-103)
+
+// Token ids to the device (m->d_tokens), after the common checks.
+static minq_status upload_tokens(minq_model* m, const uint32_t* h, size_t n) {
+  if (n > m->d_tokens_cap) {
+    void* p;
+    MINQ_TRY(dmalloc(m, &p, n * 4));
+    m->d_tokens = static_cast<uint32_t*>(p);
+    m->d_tokens_cap = n;
+  }
+  MINQ_CUDA_TRY(cudaMemcpyAsync(m->d_tokens, h, n * 4, cudaMemcpyHostToDevice, m->stream));
+  return MINQ_OK;
+}
+
+static minq_status check_rows(const minq_model* m, const uint32_t* t, size_t n) {
+  for (size_t i = 0; i < n; ++i)
+    if (t[i] >= m->cfg.vocab_size)  // Tensor::row (tensor.rs:73-78)
+      return fail(MINQ_ERR_SHAPE, "row index " + std::to_string(t[i]) + " out of bounds for " +
+                                      std::to_string(m->cfg.vocab_size) + " rows");
+  return MINQ_OK;
+}
+
+// A batch-1 scratch cache of max_seq positions with the chunk buffers (and,
+// for scoring, [chunk][vocab] logits and [chunk] nll).
+static minq_status sweep_cache(minq_model* m, size_t max_seq, bool scoring, minq_cache** out) {
+  minq_cache* c = nullptr;
+  MINQ_TRY(minq_cache_new(m, 1, max_seq, &c));
+  bool ok = false;
+  minq_status st = prefill_ready(m, c, &ok, false);
+  if (st == MINQ_OK && !ok)
+    st = fail(MINQ_ERR_SHAPE,
+              "the full-sequence sweep needs one GPU, quantized q|k|v and gate/up projections "
+              "and 32-column blocks");
+  if (st == MINQ_OK && scoring) {
+    const size_t V = m->cfg.vocab_size;
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&c->plog), kPrefillChunk * V * 4);
+    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&c->pnll), kPrefillChunk * 8);
+    if (e != cudaSuccess) st = cuda_fail(e, "cudaMalloc(perplexity buffers)");
+  }
+  if (st != MINQ_OK) {
+    minq_cache_free(c);
+    return st;
+  }
+  *out = c;
+  return MINQ_OK;
+}
+
+minq_status minq_forward_full_states(minq_model* m, const uint32_t* tokens, size_t n,
+                                     float* states_out) {
+  if (!m) return fail(MINQ_ERR_ARG, "null model");
+  if (!m->finished) return fail(MINQ_ERR_MODEL, "model not finished");
+  if (n == 0) return fail(MINQ_ERR_MODEL, "empty token sequence");  // model.rs:326-328
+  if (!tokens) return fail(MINQ_ERR_ARG, "null tokens");
+  if (n > m->cfg.max_seq_len)                                         // model.rs:331-336
+    return fail(MINQ_ERR_MODEL,
+                "sequence exceeds max_seq_len (" + std::to_string(m->cfg.max_seq_len) + ")");
+  if (!m->shape_error.empty()) return fail(MINQ_ERR_SHAPE, m->shape_error);
+  MINQ_TRY(check_rows(m, tokens, n));
+  MINQ_CUDA_TRY(cudaSetDevice(m->device));
+  MINQ_TRY(upload_tokens(m, tokens, n));
+  minq_cache* c = nullptr;
+  MINQ_TRY(sweep_cache(m, n, false, &c));
+  const size_t H = m->cfg.hidden_size;
+  minq_status st = MINQ_OK;
+  for (size_t i = 0; st == MINQ_OK && i < n; i += kPrefillChunk) {
+    const int T = (int)std::min<size_t>(kPrefillChunk, n - i);
+    st = forward_chunk(m, c, m->d_tokens + i, T);
+    if (st == MINQ_OK && states_out) {
+      const cudaError_t e = cudaMemcpyAsync(states_out + i * H, c->px, (size_t)T * H * 4,
+                                            cudaMemcpyDeviceToHost, m->stream);
+      if (e != cudaSuccess) st = cuda_fail(e, "cudaMemcpyAsync(states)");
+    }
+  }
+  if (st == MINQ_OK) {
+    const cudaError_t e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) st = cuda_fail(e, "cudaStreamSynchronize");
+  }
+  if (st == MINQ_OK) st = take_device_status();
+  minq_cache_free(c);
+  return st;
+}
+
+minq_status minq_eval_ppl(minq_model* m, const uint32_t* tokens, size_t n, size_t context,
+                          minq_ppl_window_cb on_window, void* user, minq_ppl_result* out) {
+  if (!m || !tokens || !out) return fail(MINQ_ERR_ARG, "null argument");
+  if (!m->finished) return fail(MINQ_ERR_MODEL, "model not finished");
+  if (n < 3)  // ppl.rs:51-68
+    return fail(MINQ_ERR_MODEL, "need at least 3 tokens to score, got " + std::to_string(n));
+  if (context < 3)
+    return fail(MINQ_ERR_MODEL, "context must be >= 3, got " + std::to_string(context));
+  if (context > m->cfg.max_seq_len)
+    return fail(MINQ_ERR_MODEL, "context " + std::to_string(context) + " exceeds max_seq_len (" +
+                                    std::to_string(m->cfg.max_seq_len) + ")");
+  if (!m->shape_error.empty()) return fail(MINQ_ERR_SHAPE, m->shape_error);
+  MINQ_CUDA_TRY(cudaSetDevice(m->device));
+  MINQ_TRY(upload_tokens(m, tokens, n));
+  minq_cache* c = nullptr;
+  MINQ_TRY(sweep_cache(m, context, true, &c));
+  const size_t H = m->cfg.hidden_size, V = m->cfg.vocab_size;
+  const size_t n_windows = (n + context - 1) / context;
+  cudaStream_t s = m->stream;
+  double nll_sum = 0.0, part[kPrefillChunk];
+  size_t count = 0;
+  minq_status st = MINQ_OK;
+  for (size_t w0 = 0, wi = 0; st == MINQ_OK && w0 < n; w0 += context, ++wi) {
+    const size_t len = std::min(context, n - w0);
+    // the reference's sweep of this window fails at an out-of-range row
+    // after the earlier windows have been reported
+    if ((st = check_rows(m, tokens + w0, len)) != MINQ_OK) break;
+    c->len = 0;
+    c->d_pos_valid = false;
+    // positions 0 .. len - 2: the last one predicts nothing (ppl.rs:75-82)
+    for (size_t i = 0; st == MINQ_OK && i + 1 < len; i += kPrefillChunk) {
+      const int T = (int)std::min<size_t>(kPrefillChunk, len - 1 - i);
+      if ((st = forward_chunk(m, c, m->d_tokens + w0 + i, T)) != MINQ_OK) break;
+      const int r0 = i == 0 ? 1 : 0;  // position 0 has no left context
+      const int R = T - r0;
+      if (R <= 0) continue;
+      // final RMSNorm fused into the lm_head over the chunk's scored rows
+      st = launch_qmatmul(m->lm_head.tag, m->lm_head.ptr, nullptr, V, (int)H, R, c->px + r0 * H,
+                          H, m->final_norm, m->cfg.rms_norm_eps, c->pxn, c->pxn_floats, nullptr,
+                          nullptr, c->plog, V, c->ppart, c->ppart_floats, s);
+      if (st == MINQ_OK)
+        st = launch_nll_rows(c->plog, V, R, m->d_tokens + w0 + i + r0 + 1, c->pnll, s);
+      if (st != MINQ_OK) break;
+      cudaError_t e = cudaMemcpyAsync(part, c->pnll, (size_t)R * 8, cudaMemcpyDeviceToHost, s);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+      if (e != cudaSuccess) {
+        st = cuda_fail(e, "perplexity chunk");
+        break;
+      }
+      for (int r = 0; r < R; ++r) nll_sum += part[r];  // position order, as ppl.rs:81
+      count += (size_t)R;
+    }
+    if (st == MINQ_OK && on_window)
+      on_window(wi + 1, n_windows, count ? std::exp(nll_sum / (double)count) : NAN, user);
+  }
+  if (st == MINQ_OK) st = take_device_status();
+  minq_cache_free(c);
+  if (st != MINQ_OK) return st;
+  if (count == 0)  // ppl.rs:93-97
+    return fail(MINQ_ERR_MODEL, "no scorable positions (sequence too short for context)");
+  out->total_tokens = n;
+  out->scored_positions = count;
+  out->mean_nll = nll_sum / (double)count;
+  out->ppl = std::exp(out->mean_nll);
+  return MINQ_OK;
 }
 
 }  // extern "C"

@@ -1035,4 +1035,50 @@ int orc_forward_full(void* hm, const uint32_t* toks, size_t n, float* logits) {
   return OK;
 }
 
+// ppl.rs:30-35: log-sum-exp in f64 over f32 differences from the f32 max.
+double orc_nll(const float* logits, size_t n, uint32_t target) {
+  float mx = -INFINITY;
+  for (size_t i = 0; i < n; ++i) mx = rmax(mx, logits[i]);
+  double s = 0.0;
+  for (size_t i = 0; i < n; ++i) s += std::exp((double)(logits[i] - mx));
+  return (double)mx + std::log(s) - (double)logits[target];
+}
+
+// ppl.rs:44-103: non-overlapping windows of `context` tokens, each one
+// forward_full_states sweep; position t in 1 .. len - 2 of a window scores
+// window[t + 1]; nll summed in f64 in position order. window_ppl (n_windows
+// doubles, or null) receives the cumulative ppl after each window (NaN while
+// nothing is scored), as the reference's on_window callback sees it.
+int orc_eval_ppl(void* hm, const uint32_t* toks, size_t n, size_t context, uint64_t* scored,
+                 double* mean_nll, double* ppl, double* window_ppl) {
+  Model* m = static_cast<Model*>(hm);
+  if (n < 3) return fail(E_MODEL, "need at least 3 tokens to score, got " + std::to_string(n));
+  if (context < 3) return fail(E_MODEL, "context must be >= 3, got " + std::to_string(context));
+  if (context > m->cfg.max_seq)
+    return fail(E_MODEL, "context " + std::to_string(context) + " exceeds max_seq_len (" +
+                             std::to_string(m->cfg.max_seq) + ")");
+  const size_t H = m->cfg.hidden, V = m->lm_head.rows;
+  std::vector<float> st, xn(H), logits(V);
+  double nll_sum = 0.0;
+  size_t count = 0, wi = 0;
+  for (size_t w0 = 0; w0 < n; w0 += context, ++wi) {
+    const size_t len = std::min(context, n - w0);
+    st.assign(len * H, 0.0f);
+    int rc = forward_full_states(*m, toks + w0, len, st.data());
+    if (rc) return rc;
+    for (size_t t = 1; t + 1 < len; ++t) {
+      rmsnorm(&st[t * H], m->final_norm.data(), m->cfg.eps, H, xn.data());
+      m->lm_head.matvec(xn.data(), logits.data());
+      nll_sum += orc_nll(logits.data(), V, toks[w0 + t + 1]);
+      count += 1;
+    }
+    if (window_ppl) window_ppl[wi] = count ? std::exp(nll_sum / (double)count) : NAN;
+  }
+  if (count == 0) return fail(E_MODEL, "no scorable positions (sequence too short for context)");
+  *scored = count;
+  *mean_nll = nll_sum / (double)count;
+  *ppl = std::exp(*mean_nll);
+  return OK;
+}
+
 }  // extern "C"

@@ -88,6 +88,8 @@ def lib():
             "orc_forward": (I, [P, P, P, S, P]),
             "orc_forward_full_states": (I, [P, P, S, P]),
             "orc_forward_full": (I, [P, P, S, P]),
+            "orc_nll": (C.c_double, [P, S, C.c_uint32]),
+            "orc_eval_ppl": (I, [P, P, S, S, P, P, P, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -104,6 +106,12 @@ def _p(a: np.ndarray):
 def _check(rc: int):
     if rc != 0:
         raise OracleError(rc, lib().orc_last_error().decode())
+
+
+def nll(logits, target: int) -> float:
+    """ppl.rs:30-35: log-sum-exp (f64) minus the target's logit."""
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    return float(lib().orc_nll(_p(x), x.size, target))
 
 
 def set_simd(on: bool) -> None:
@@ -301,6 +309,20 @@ class Model:
         out = np.zeros((t.size, self.config["hidden_size"]), dtype=np.float32)
         _check(lib().orc_forward_full_states(self._h, _p(t), t.size, _p(out)))
         return out
+
+    def eval_ppl(self, tokens, context: int) -> dict:
+        """ppl.rs:44-103: windows of `context` tokens, one full-states sweep
+        each; returns total_tokens, scored_positions, mean_nll, ppl and the
+        cumulative ppl after each window (what on_window receives)."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        nw = max(1, -(-t.size // max(1, context)))
+        win = np.full(nw, np.nan, dtype=np.float64)
+        scored = np.zeros(1, dtype=np.uint64)
+        mean, ppl = np.zeros(1, dtype=np.float64), np.zeros(1, dtype=np.float64)
+        _check(lib().orc_eval_ppl(self._h, _p(t), t.size, context, _p(scored), _p(mean), _p(ppl),
+                                  _p(win)))
+        return {"total_tokens": int(t.size), "scored_positions": int(scored[0]),
+                "mean_nll": float(mean[0]), "ppl": float(ppl[0]), "windows": win}
 
 
 class KVCache:

@@ -70,6 +70,9 @@ ATTN_WORKLOAD = "attn-gqa32-8-hd128"
 # 10,000 tokens at context 512, i.e. 20 windows); one step = one window.
 PPL_WORKLOAD = "qwen3-4b-q4_0-ppl"
 PPL_CONTEXT = 512
+# Device sampling: Sampler::sample on seeded logits over the Qwen vocabulary
+# (151,936), one draw per step, for four sampler settings.
+SAMPLER_WORKLOAD = "sampler-v151936"
 
 
 def parse():
@@ -80,7 +83,7 @@ def parse():
     ap.add_argument("--impl", choices=["minq", "reference"], default="minq")
     ap.add_argument("--workload",
                     choices=sorted(WORKLOADS) + [TP_WORKLOAD, ATTN_WORKLOAD, BATCH_WORKLOAD,
-                                                 PPL_WORKLOAD],
+                                                 PPL_WORKLOAD, SAMPLER_WORKLOAD],
                     default="qwen3-4b-q4_0")
     ap.add_argument("--prompt", type=int, default=None, help="prefill length override")
     ap.add_argument("--seed", type=int, default=1234)
@@ -831,6 +834,58 @@ def run_ppl(args, world, rank, local):
     del model
 
 
+def run_sampler(args):
+    """Device draws (minq_sampler_sample_device) on seeded N(0, 3^2) logits of
+    151,936 entries, timed with CUDA events over K draws per setting; the
+    line's value is the temperature 0.8 / top_k 40 / top_p 0.9 setting. The
+    CPU baseline is the oracle's Sampler::sample on the same logits."""
+    import torch
+    import minq_b200 as mq
+    n, K, W = 151936, args.steps, args.warmup
+    x = (np.random.default_rng(args.seed).standard_normal(n) * 3.0).astype(np.float32)
+    d = torch.from_numpy(x).cuda()
+    out = torch.zeros(1, dtype=torch.int32, device="cuda")
+    settings = {"t0.8_k40_p0.9": (0.8, 40, 0.9), "t1_nofilter": (1.0, 0, 1.0),
+                "t1_k0_p0.9": (1.0, 0, 0.9), "greedy": (0.0, 0, 1.0)}
+    res = {}
+    stream = torch.cuda.current_stream()
+    for name, (t, k, p) in settings.items():
+        smp = mq.Sampler(t, k, p, args.seed)
+        for _ in range(max(3, W)):
+            smp.sample_device(d, out)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(K):
+            smp.sample_device(d, out)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        res[name] = {"us_per_draw": 1000.0 * e0.elapsed_time(e1) / K}
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import oracle as orc
+        o = orc.Sampler(0.8, 40, 0.9, args.seed)
+        t0 = time.perf_counter()
+        nd = 0
+        while time.perf_counter() - t0 < min(args.cpu_seconds, 5.0) or nd < 3:
+            o.sample(x)
+            nd += 1
+        el = time.perf_counter() - t0
+        cpu = {"value": nd / el, "unit": "draws/s", "cores": 1, "kind": "port",
+               "sample": f"{nd} draws of the t0.8_k40_p0.9 setting, {el:.1f} s"}
+    us = res["t0.8_k40_p0.9"]["us_per_draw"]
+    print(json.dumps({
+        "metric": "device sampling draws/s", "value": 1e6 / us, "unit": "draws/s",
+        "n_gpus": 1, "steps": K, "warmup": max(3, W), "ms_per_step": us / 1000.0,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 probabilities, f64 sums", "data": "synthetic",
+        "config": {"workload": f"{SAMPLER_WORKLOAD}: Sampler::sample over 151936 logits",
+                   "settings": res, "cache_flush": "none: 0.6 MB of logits stay in L2, as "
+                   "after a decode step's lm_head"},
+        "cpu_baseline": cpu,
+    }), flush=True)
+
+
 def run_attn(args, world, rank, local):
     """The decode-attention op (minq_attn_decode) over the sweep; the line's
     value is the B = 8, L = 8192 point, `sweep` holds every point. Each
@@ -923,6 +978,9 @@ def main():
             run_batch(args, world, rank, local)
         elif args.workload == PPL_WORKLOAD:
             run_ppl(args, world, rank, local)
+        elif args.workload == SAMPLER_WORKLOAD:
+            if rank == 0:
+                run_sampler(args)
         elif args.impl == "reference":
             run_reference(args, world, rank)
         else:

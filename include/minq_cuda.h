@@ -84,6 +84,7 @@ typedef struct minq_ppl_result {
 
 typedef struct minq_model minq_model;
 typedef struct minq_cache minq_cache;
+typedef struct minq_sampler minq_sampler;
 
 /* Engine::generate's `on_token` callback (engine.rs:56); a non-zero return
  * aborts generation and is reported as MINQ_ERR_MODEL (engine.rs:73). */
@@ -336,6 +337,47 @@ minq_status minq_forward_full_states(minq_model* m, const uint32_t* tokens, size
  * take -> MINQ_ERR_SHAPE. */
 minq_status minq_eval_ppl(minq_model* m, const uint32_t* tokens, size_t n, size_t context,
                           minq_ppl_window_cb on_window, void* user, minq_ppl_result* out);
+
+/* Sampler::new (sampler.rs:32-40) on the current CUDA device: temperature
+ * (<= 0: greedy), top_k (0: off), top_p (>= 1: off) and the StdRng seed
+ * (rand 0.8 StdRng::seed_from_u64: ChaCha12 keyed by PCG32 outputs), whose
+ * state lives in device memory and advances once per non-greedy draw. */
+minq_status minq_sampler_new(float temperature, size_t top_k, float top_p, uint64_t seed,
+                             minq_sampler** out);
+void minq_sampler_free(minq_sampler* s);
+
+/* Sampler::sample (sampler.rs:47-109) on device logits (n floats) into
+ * d_token (device, one id), enqueued on `stream` (cudaStream_t, NULL: the
+ * legacy default stream) with no host synchronisation. Greedy samplers take
+ * the argmax (total_cmp, ties low). Otherwise softmax(logits / temperature),
+ * then one uniform draw: over the whole distribution without filters, else
+ * over the top_k most probable (ties at the boundary by lower index; the
+ * reference leaves their order unspecified) cut at the top_p cumulative
+ * mass, renormalised. Probabilities use the f64 exponential rounded to f32
+ * and f64 running sums, so a draw can differ from the reference's only when
+ * the uniform falls within rounding of a boundary, and then by a neighbouring
+ * token. n == 0 -> token 0; n > 4194304 -> MINQ_ERR_ARG. */
+minq_status minq_sampler_sample_device(minq_sampler* s, const float* d_logits, size_t n,
+                                       uint32_t* d_token, void* stream);
+
+/* The same with host logits and a host token (synchronous). */
+minq_status minq_sampler_sample(minq_sampler* s, const float* logits, size_t n,
+                                uint32_t* token_out);
+
+/* Diagnostic: the sampler's next n raw StdRng outputs (RngCore::next_u32),
+ * advancing its state; n <= 2^20. No reference counterpart. */
+minq_status minq_sampler_rng_u32(minq_sampler* s, size_t n, uint32_t* out);
+
+/* Engine::generate (engine.rs:52-88) with the given Sampler: prefill the
+ * prompt, then up to max_tokens steps, each token drawn on the device from
+ * the step's logits (no logits copy to the host; 4 bytes come back per token
+ * for on_token and the stop check). The sampler must live on the model's
+ * device. Errors as minq_generate. */
+minq_status minq_generate_sampled(minq_model* m, minq_sampler* s, const uint32_t* prompt,
+                                  size_t n_prompt, size_t max_tokens,
+                                  const uint32_t* stop_tokens, size_t n_stop,
+                                  minq_token_cb on_token, void* user, uint32_t* tokens_out,
+                                  minq_gen_stats* stats);
 
 /* The model's CUDA stream (cudaStream_t as void*). */
 void* minq_model_stream(minq_model* m);

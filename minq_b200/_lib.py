@@ -114,6 +114,12 @@ SIGNATURES = {
     "minq_generate": (I, [P, P, S, S, P, S, TOKEN_CB, P, P, C.POINTER(GenStats)]),
     "minq_forward_full_states": (I, [P, P, S, P]),
     "minq_eval_ppl": (I, [P, P, S, S, PPL_WINDOW_CB, P, C.POINTER(PplResult)]),
+    "minq_sampler_new": (I, [C.c_float, S, C.c_float, C.c_uint64, C.POINTER(C.c_void_p)]),
+    "minq_sampler_free": (None, [P]),
+    "minq_sampler_sample_device": (I, [P, P, S, P, P]),
+    "minq_sampler_sample": (I, [P, P, S, P]),
+    "minq_sampler_rng_u32": (I, [P, S, P]),
+    "minq_generate_sampled": (I, [P, P, P, S, S, P, S, TOKEN_CB, P, P, C.POINTER(GenStats)]),
 }
 
 _lib = None

@@ -429,21 +429,56 @@ def eval_ppl(model: "Model", tokens, context: int,
 
 
 class Sampler:
-    """sampler.rs:20-55. Only greedy decoding runs on this path (temperature
-    <= 0 or top_k == 1, the argmax short-circuit of sampler.rs:51-53)."""
+    """Sampler (sampler.rs:20-109): temperature (<= 0: greedy), top_k (0: off),
+    top_p (>= 1: off) and the StdRng seed. Greedy samplers take the argmax;
+    the others draw on the GPU (minq_sampler_*), with the RNG state in device
+    memory, created on the current device at the first draw."""
 
     def __init__(self, temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0,
                  seed: int = 0):
-        if not (temperature <= 0.0 or top_k == 1):
-            raise MinqError(_lib.ERR_MODEL, "only greedy sampling runs on the CUDA path")
         self.temperature, self.top_k, self.top_p, self.seed = temperature, top_k, top_p, seed
+        self._h = None
 
     @classmethod
     def greedy(cls) -> "Sampler":
         return cls(0.0, 0, 1.0, 0)
 
+    @property
+    def is_greedy(self) -> bool:
+        return self.temperature <= 0.0 or self.top_k == 1
+
+    def _handle(self):
+        if self._h is None:
+            h = C.c_void_p()
+            check(lib().minq_sampler_new(float(self.temperature), int(self.top_k),
+                                         float(self.top_p), int(self.seed), C.byref(h)))
+            self._h = h
+        return self._h
+
+    def __del__(self):
+        if getattr(self, "_h", None) is not None:
+            lib().minq_sampler_free(self._h)
+            self._h = None
+
     def sample(self, logits) -> int:
-        return argmax(logits)
+        """Sampler::sample on host logits (drawn on the GPU)."""
+        x = np.ascontiguousarray(np.asarray(logits, dtype=np.float32).reshape(-1))
+        out = np.zeros(1, dtype=np.uint32)
+        check(lib().minq_sampler_sample(self._handle(), x.ctypes.data_as(C.c_void_p), x.size,
+                                        out.ctypes.data_as(C.c_void_p)))
+        return int(out[0])
+
+    def sample_device(self, logits, out) -> None:
+        """Sampler::sample on a CUDA f32 tensor into a CUDA int32 tensor of one
+        element, on torch's current stream (no host synchronisation)."""
+        check(lib().minq_sampler_sample_device(self._handle(), _ptr(logits), logits.numel(),
+                                               _ptr(out), _stream_ptr()))
+
+    def rng_u32(self, n: int) -> np.ndarray:
+        """The next n raw StdRng outputs (diagnostic; advances the state)."""
+        out = np.zeros(n, dtype=np.uint32)
+        check(lib().minq_sampler_rng_u32(self._handle(), n, out.ctypes.data_as(C.c_void_p)))
+        return out
 
 
 class Engine:
@@ -471,9 +506,16 @@ class Engine:
 
         ccb = _lib.TOKEN_CB(cb)
         stats = GenStats()
-        st = lib().minq_generate(self.model._h, prompt.ctypes.data_as(C.c_void_p), prompt.size,
-                                 max_tokens, stop.ctypes.data_as(C.c_void_p) if stop.size else None,
-                                 stop.size, ccb, None, None, C.byref(stats))
+        stop_p = stop.ctypes.data_as(C.c_void_p) if stop.size else None
+        if self.sampler.is_greedy:
+            st = lib().minq_generate(self.model._h, prompt.ctypes.data_as(C.c_void_p),
+                                     prompt.size, max_tokens, stop_p, stop.size, ccb, None, None,
+                                     C.byref(stats))
+        else:  # tokens drawn on the GPU from each step's logits
+            st = lib().minq_generate_sampled(self.model._h, self.sampler._handle(),
+                                             prompt.ctypes.data_as(C.c_void_p), prompt.size,
+                                             max_tokens, stop_p, stop.size, ccb, None, None,
+                                             C.byref(stats))
         if err:
             raise err[0]
         check(st)

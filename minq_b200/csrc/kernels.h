@@ -104,6 +104,8 @@ minq_status launch_epilogue(const float* acc, const float* bias, const float* re
                             size_t n, cudaStream_t s);
 minq_status launch_swiglu(const float* g, const float* u, float* h, size_t n, cudaStream_t s);
 minq_status launch_advance_pos(int* pos, int by, cudaStream_t s);
+// sampler.cu: the device a sampler was created on
+int sampler_device(const minq_sampler* s);
 // per-row negative log-likelihood (ppl.rs:30-35) of logits [rows][V] at
 // targets[rows] (device), into out[rows] (f64)
 minq_status launch_nll_rows(const float* logits, size_t V, int rows, const uint32_t* targets,

@@ -1500,6 +1500,59 @@ minq_status minq_generate(minq_model* m, const uint32_t* prompt, size_t n_prompt
   return rc;
 }
 
+minq_status minq_generate_sampled(minq_model* m, minq_sampler* smp, const uint32_t* prompt,
+                                  size_t n_prompt, size_t max_tokens,
+                                  const uint32_t* stop_tokens, size_t n_stop,
+                                  minq_token_cb on_token, void* user, uint32_t* tokens_out,
+                                  minq_gen_stats* stats) {
+  if (!m || !smp) return fail(MINQ_ERR_ARG, "null argument");
+  if (n_prompt == 0) return fail(MINQ_ERR_MODEL, "empty prompt");  // engine.rs:58-60
+  if (sampler_device(smp) != m->device)
+    return fail(MINQ_ERR_ARG, "the sampler lives on another device than the model");
+  MINQ_CUDA_TRY(cudaSetDevice(m->device));
+  minq_cache* c = nullptr;
+  MINQ_TRY(minq_cache_new(m, 1, 0, &c));
+  uint32_t* d_tok = nullptr;
+  if (cudaMalloc(&d_tok, 16) != cudaSuccess) {
+    minq_cache_free(c);
+    return fail(MINQ_ERR_CUDA, "cudaMalloc(token)");
+  }
+  using clk = std::chrono::steady_clock;
+  minq_gen_stats st{};
+  st.prompt_tokens = n_prompt;
+  auto t0 = clk::now();
+  minq_status rc = minq_forward(m, c, prompt, n_prompt, nullptr, nullptr);
+  st.prefill_secs = std::chrono::duration<double>(clk::now() - t0).count();
+  auto t1 = clk::now();
+  for (size_t i = 0; rc == MINQ_OK && i < max_tokens; ++i) {
+    // Sampler::sample on the step's logits (engine.rs:72), on the device
+    rc = minq_sampler_sample_device(smp, m->logits, m->cfg.vocab_size, d_tok, m->stream);
+    uint32_t tok = 0;
+    if (rc == MINQ_OK) {
+      cudaError_t e = cudaMemcpyAsync(&tok, d_tok, 4, cudaMemcpyDeviceToHost, m->stream);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+      if (e != cudaSuccess) rc = cuda_fail(e, "sampled token");
+    }
+    if (rc != MINQ_OK) break;
+    if (tokens_out) tokens_out[i] = tok;
+    if (on_token && on_token(tok, user) != 0) {
+      rc = fail(MINQ_ERR_MODEL, "on_token callback aborted generation");
+      break;
+    }
+    st.gen_tokens += 1;
+    bool stop = false;
+    for (size_t k = 0; k < n_stop; ++k) stop |= stop_tokens[k] == tok;
+    if (stop) break;
+    rc = forward_impl(m, c, nullptr, d_tok, 1);  // logits of the next step
+  }
+  if (rc == MINQ_OK) rc = take_device_status();
+  st.decode_secs = std::chrono::duration<double>(clk::now() - t1).count();
+  cudaFree(d_tok);
+  minq_cache_free(c);
+  if (stats) *stats = st;
+  return rc;
+}
+
 // ---------------------------------------------------------------------------
 // C ABI: full-sequence states and perplexity (model.rs:337-424, ppl.rs:44-103)
 

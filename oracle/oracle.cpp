@@ -1081,4 +1081,149 @@ int orc_eval_ppl(void* hm, const uint32_t* toks, size_t n, size_t context, uint6
   return OK;
 }
 
+// ---------------------------------------------------------------------------
+// Sampler (sampler.rs:20-109) and its RNG. The reference's StdRng is rand
+// 0.8.8's, i.e. rand_chacha 0.3.1's ChaCha12Rng, seeded by rand_core 0.6.4's
+// SeedableRng::seed_from_u64; neither crate is in the reference tree, so
+// their published algorithms are restated here:
+// * seed_from_u64: a PCG32 (XSH-RR) generator with state s advanced as
+//   s = s * 6364136223846793005 + 11634580027462260723 before each output;
+//   eight outputs, little-endian, form the 32-byte seed;
+// * ChaCha12Rng::from_seed: key = the seed as eight little-endian words,
+//   64-bit block counter 0 (state words 12, 13), stream 0 (words 14, 15);
+//   each refill produces four consecutive 16-word blocks (64 words) and
+//   next_u32 returns them in order;
+// * gen::<f32>() (rand's Standard for f32): (next_u32() >> 8) * 2^-24.
+// The ChaCha block function is pinned by the ChaCha20 keystream test vectors
+// (all-zero key and nonce) in tests/test_oracle_sampler.py; the PCG
+// expansion, the word layout and the float conversion are not pinned by any
+// output of the reference.
+
+struct StdRng {
+  uint32_t key[8];
+  uint64_t block = 0;
+  uint32_t buf[64];
+  unsigned idx = 64;
+};
+
+inline uint32_t rotl32(uint32_t x, int r) { return (x << r) | (x >> (32 - r)); }
+
+void chacha_block(const uint32_t key[8], uint64_t ctr, uint64_t stream, int rounds,
+                  uint32_t out[16]) {
+  uint32_t s[16] = {0x61707865u, 0x3320646eu, 0x79622d32u, 0x6b206574u};
+  for (int i = 0; i < 8; ++i) s[4 + i] = key[i];
+  s[12] = (uint32_t)ctr;
+  s[13] = (uint32_t)(ctr >> 32);
+  s[14] = (uint32_t)stream;
+  s[15] = (uint32_t)(stream >> 32);
+  uint32_t x[16];
+  std::memcpy(x, s, sizeof(x));
+  auto qr = [&](int a, int b, int c, int d) {
+    x[a] += x[b]; x[d] = rotl32(x[d] ^ x[a], 16);
+    x[c] += x[d]; x[b] = rotl32(x[b] ^ x[c], 12);
+    x[a] += x[b]; x[d] = rotl32(x[d] ^ x[a], 8);
+    x[c] += x[d]; x[b] = rotl32(x[b] ^ x[c], 7);
+  };
+  for (int r = 0; r < rounds; r += 2) {
+    qr(0, 4, 8, 12); qr(1, 5, 9, 13); qr(2, 6, 10, 14); qr(3, 7, 11, 15);
+    qr(0, 5, 10, 15); qr(1, 6, 11, 12); qr(2, 7, 8, 13); qr(3, 4, 9, 14);
+  }
+  for (int i = 0; i < 16; ++i) out[i] = x[i] + s[i];
+}
+
+void std_rng_seed(StdRng& g, uint64_t seed) {
+  uint64_t st = seed;
+  for (int i = 0; i < 8; ++i) {
+    st = st * 6364136223846793005ull + 11634580027462260723ull;
+    const uint32_t xs = (uint32_t)(((st >> 18) ^ st) >> 27);
+    const unsigned rot = (unsigned)(st >> 59);
+    g.key[i] = (xs >> rot) | (xs << ((32 - rot) & 31));
+  }
+  g.block = 0;
+  g.idx = 64;
+}
+
+uint32_t std_rng_u32(StdRng& g) {
+  if (g.idx >= 64) {
+    for (int b = 0; b < 4; ++b) chacha_block(g.key, g.block + b, 0, 12, g.buf + 16 * b);
+    g.block += 4;
+    g.idx = 0;
+  }
+  return g.buf[g.idx++];
+}
+
+float std_rng_f32(StdRng& g) { return (float)(std_rng_u32(g) >> 8) * (1.0f / 16777216.0f); }
+
+struct Sampler {
+  float temperature;
+  size_t top_k;
+  float top_p;
+  StdRng rng;
+};
+
+// sampler.rs:47-109. The reference ranks the top-k survivors with
+// select_nth_unstable_by and a stable sort on probability, which leaves the
+// order of exactly equal probabilities at the top-k boundary unspecified;
+// here (and on the GPU) equal probabilities rank by lower index.
+uint32_t sampler_sample(Sampler& s, const float* logits, size_t n) {
+  if (n == 0) return 0;
+  if (s.temperature <= 0.0f || s.top_k == 1) return argmax(logits, n);
+  std::vector<float> probs(n);
+  for (size_t i = 0; i < n; ++i) probs[i] = logits[i] / s.temperature;
+  softmax(probs.data(), n);
+  if ((s.top_k == 0 || s.top_k >= n) && s.top_p >= 1.0f) {
+    float r = std_rng_f32(s.rng);
+    for (size_t i = 0; i < n; ++i) {
+      r -= probs[i];
+      if (r <= 0.0f) return (uint32_t)i;
+    }
+    return (uint32_t)(n - 1);
+  }
+  const size_t k = s.top_k == 0 ? n : std::min(s.top_k, n);
+  std::vector<uint32_t> ranked(n);
+  for (size_t i = 0; i < n; ++i) ranked[i] = (uint32_t)i;
+  auto before = [&](uint32_t a, uint32_t b) {
+    return probs[a] > probs[b] || (probs[a] == probs[b] && a < b);
+  };
+  if (k < n) {
+    std::nth_element(ranked.begin(), ranked.begin() + (k - 1), ranked.end(), before);
+    ranked.resize(k);
+  }
+  std::sort(ranked.begin(), ranked.end(), before);
+  size_t cutoff = k;
+  float cumulative = 0.0f;
+  for (size_t r = 0; r < ranked.size(); ++r) {
+    cumulative += probs[ranked[r]];
+    if (cumulative >= s.top_p) {
+      cutoff = r + 1;
+      break;
+    }
+  }
+  float total = 0.0f;
+  for (size_t r = 0; r < cutoff; ++r) total += probs[ranked[r]];
+  float rr = std_rng_f32(s.rng) * total;
+  for (size_t r = 0; r < cutoff; ++r) {
+    rr -= probs[ranked[r]];
+    if (rr <= 0.0f) return ranked[r];
+  }
+  return ranked[cutoff - 1];
+}
+
+void* orc_sampler_new(float temperature, size_t top_k, float top_p, uint64_t seed) {
+  Sampler* s = new Sampler{temperature, top_k, top_p, {}};
+  std_rng_seed(s->rng, seed);
+  return s;
+}
+void orc_sampler_free(void* s) { delete static_cast<Sampler*>(s); }
+uint32_t orc_sampler_sample(void* s, const float* logits, size_t n) {
+  return sampler_sample(*static_cast<Sampler*>(s), logits, n);
+}
+void orc_sampler_rng_u32(void* s, size_t n, uint32_t* out) {
+  for (size_t i = 0; i < n; ++i) out[i] = std_rng_u32(static_cast<Sampler*>(s)->rng);
+}
+void orc_chacha_block(const uint32_t* key, uint64_t ctr, uint64_t stream, int rounds,
+                      uint32_t* out) {
+  chacha_block(key, ctr, stream, rounds, out);
+}
+
 }  // extern "C"

@@ -90,6 +90,11 @@ def lib():
             "orc_forward_full": (I, [P, P, S, P]),
             "orc_nll": (C.c_double, [P, S, C.c_uint32]),
             "orc_eval_ppl": (I, [P, P, S, S, P, P, P, P]),
+            "orc_sampler_new": (P, [F, S, F, C.c_uint64]),
+            "orc_sampler_free": (None, [P]),
+            "orc_sampler_sample": (C.c_uint32, [P, P, S]),
+            "orc_sampler_rng_u32": (None, [P, S, P]),
+            "orc_chacha_block": (None, [P, C.c_uint64, C.c_uint64, I, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -323,6 +328,35 @@ class Model:
                                   _p(win)))
         return {"total_tokens": int(t.size), "scored_positions": int(scored[0]),
                 "mean_nll": float(mean[0]), "ppl": float(ppl[0]), "windows": win}
+
+
+class Sampler:
+    """sampler.rs:20-109 with rand 0.8's StdRng (ChaCha12, seed_from_u64)."""
+
+    def __init__(self, temperature: float, top_k: int, top_p: float, seed: int):
+        self._h = lib().orc_sampler_new(float(temperature), int(top_k), float(top_p), int(seed))
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().orc_sampler_free(self._h)
+            self._h = None
+
+    def sample(self, logits) -> int:
+        x = np.ascontiguousarray(logits, dtype=np.float32)
+        return int(lib().orc_sampler_sample(self._h, _p(x), x.size))
+
+    def rng_u32(self, n: int) -> np.ndarray:
+        out = np.zeros(n, dtype=np.uint32)
+        lib().orc_sampler_rng_u32(self._h, n, _p(out))
+        return out
+
+
+def chacha_block(key, counter: int, stream: int, rounds: int) -> np.ndarray:
+    """One ChaCha block (16 words) for a key of 8 words."""
+    k = np.ascontiguousarray(key, dtype=np.uint32)
+    out = np.zeros(16, dtype=np.uint32)
+    lib().orc_chacha_block(_p(k), counter, stream, rounds, _p(out))
+    return out
 
 
 class KVCache:

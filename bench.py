@@ -205,12 +205,15 @@ def build_model(mq, synth, cfg, qk_norm, tied, seed):
 
 
 def cpu_model(orc, synth, cfg, qk_norm, tied, seed):
-    """The same seeded model for the oracle: drawn on the GPU (plumbing), then
-    quantized on the host by the oracle's own quantizer (reference algorithm)."""
+    """The same seeded model for the oracle: drawn on the GPU (plumbing; on
+    the CPU where there is none), then quantized on the host by the oracle's
+    own quantizer (reference algorithm)."""
+    import torch
     from minq_b200.minq_format import quantize_tensor_rule, DTYPE_TAGS
     qtag = DTYPE_TAGS[cfg.dtype]
     tensors = {}
-    for name, tag, shape, data in synth.synth_records(cfg, seed, qk_norm, tied, device="cuda",
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    for name, tag, shape, data in synth.synth_records(cfg, seed, qk_norm, tied, device=dev,
                                                       quantize=lambda t, x: x):
         host = data.detach().cpu().numpy()
         if qtag and quantize_tensor_rule(name, shape):
@@ -282,6 +285,111 @@ def run_reference(args, world, rank):
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
+    print(json.dumps(line), flush=True)
+
+
+def _reference_line(args, metric, value, unit, steps, warmup, ms, scaling, dtype, config,
+                    cores, sample, higher=True):
+    return {"impl": "reference", "metric": metric, "value": value, "unit": unit,
+            "n_gpus": args.gpus, "steps": steps, "warmup": warmup, "ms_per_step": ms,
+            "higher_is_better": higher, "scaling": scaling, "vs_baseline": None, "dtype": dtype,
+            "data": "synthetic", "config": config,
+            "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def run_reference_workload(args, rank):
+    """The reference arm of the long-context, batched, attention and sampler
+    workloads: the reference's CPU algorithm (the oracle, AVX2 + OpenMP on all
+    host cores; its sampler on one core, as sampler.rs runs) on a bounded
+    sample of the same workload, rank 0 only."""
+    if rank != 0:
+        return
+    from oracle import oracle as orc
+    from minq_b200 import synth
+    from dataclasses import replace
+    K, W = max(1, min(args.steps, 3)), max(0, min(args.warmup, 1))
+    cores = orc.max_threads()
+    if args.workload in (TP_WORKLOAD, BATCH_WORKLOAD):
+        tp = args.workload == TP_WORKLOAD
+        arch = "qwen3-4b" if tp else "llama3-8b"
+        hist = args.prompt or (32768 if tp else 512)
+        cfg0, qk_norm, tied = synth.ARCH[arch]
+        if args.layers:
+            cfg0 = replace(cfg0, n_layers=args.layers)
+        cfg = replace(cfg0, max_seq_len=hist + W + K + 8, **({"dtype": "q8_0"} if tp else {}))
+        om = cpu_model(orc, synth, cfg, qk_norm, tied, args.seed)
+        oc = om.new_cache()
+        kvd = cfg.n_kv_heads * cfg.head_dim
+        rng = np.random.default_rng(args.seed)
+        k = rng.standard_normal((cfg.n_layers, hist, kvd), dtype=np.float32)
+        v = rng.standard_normal((cfg.n_layers, hist, kvd), dtype=np.float32)
+        oc.fill(k, v)
+        del k, v
+        tok = 1
+        for _ in range(W):
+            tok = orc.argmax(om.forward([tok], oc))
+        t0 = time.perf_counter()
+        for _ in range(K):
+            tok = orc.argmax(om.forward([tok], oc))
+        el = time.perf_counter() - t0
+        value = K / el  # one sequence-token per forward, for either workload
+        if tp:
+            metric, scaling = "decode tok/s", "strong"
+            config = {"workload": f"{TP_WORKLOAD}: Qwen3-4B shape, Q8_0, KV pre-filled at "
+                                  f"{hist} positions", "layers": cfg.n_layers}
+        else:
+            metric, scaling = "decode tok/s (batched)", "strong"
+            config = {"workload": f"{BATCH_WORKLOAD}: LLaMA-3-8B shape, Q4_0, 64 sequences, "
+                                  f"history {hist}; the reference decodes the sequences one "
+                                  f"forward at a time", "layers": cfg.n_layers}
+        line = _reference_line(args, metric, value, "tok/s", K, W, 1000 * el / K, scaling, "f32",
+                               config, cores, f"{K} decode tokens at KV history {hist} after "
+                               f"{W} warm-up, {el:.1f} s")
+    elif args.workload == ATTN_WORKLOAD:
+        B, L, nh, nkv, hd = 8, 8192, 32, 8, 128
+        rng = np.random.default_rng(args.seed)
+        ks = [rng.standard_normal((L + 1, nkv * hd), dtype=np.float32) for _ in range(B)]
+        vs = [rng.standard_normal((L + 1, nkv * hd), dtype=np.float32) for _ in range(B)]
+        qs = [rng.standard_normal(nh * hd, dtype=np.float32) for _ in range(B)]
+        for b in range(B if W else 0):
+            orc.attend(qs[b], ks[b], vs[b], L + 1, nh, nkv, hd)
+        t0 = time.perf_counter()
+        for _ in range(K):
+            for b in range(B):
+                orc.attend(qs[b], ks[b], vs[b], L + 1, nh, nkv, hd)
+        el = time.perf_counter() - t0
+        byts = 2.0 * 4 * B * nkv * hd * (L + 1)
+        value = byts * K / el / 1e9
+        line = _reference_line(args, "decode attention GB/s", value, "GB/s", K, W,
+                               1000 * el / K, "weak", "f32",
+                               {"workload": f"{ATTN_WORKLOAD}: RoPE + append + attend, B = 8, "
+                                            f"L = 8192"}, 1,
+                               f"{K} x attend (model.rs:223-248, single-threaded loops as in "
+                               f"the reference) over {B} sequences of {L + 1} positions, "
+                               f"{el:.1f} s")
+    elif args.workload == SAMPLER_WORKLOAD:
+        n = 151936
+        x = (np.random.default_rng(args.seed).standard_normal(n) * 3.0).astype(np.float32)
+        o = orc.Sampler(0.8, 40, 0.9, args.seed)
+        for _ in range(W):
+            o.sample(x)
+        t0 = time.perf_counter()
+        nd = 0
+        while nd < 3 or time.perf_counter() - t0 < 5.0:
+            o.sample(x)
+            nd += 1
+        el = time.perf_counter() - t0
+        line = _reference_line(args, "device sampling draws/s", nd / el, "draws/s", nd, W,
+                               1000 * el / nd, "weak", "f32 probabilities, f64 sums",
+                               {"workload": f"{SAMPLER_WORKLOAD}: Sampler::sample over 151936 "
+                                            f"logits"}, 1,
+                               f"{nd} draws of the temperature 0.8 / top_k 40 / top_p 0.9 "
+                               f"setting, {el:.1f} s")
+    else:
+        raise SystemExit(f"no reference arm for {args.workload}")
     print(json.dumps(line), flush=True)
 
 
@@ -969,7 +1077,10 @@ def main():
     args = parse()
     world, rank, local = dist_init()
     try:
-        if args.workload == ATTN_WORKLOAD:
+        if args.impl == "reference" and args.workload in (TP_WORKLOAD, BATCH_WORKLOAD,
+                                                          ATTN_WORKLOAD, SAMPLER_WORKLOAD):
+            run_reference_workload(args, rank)
+        elif args.workload == ATTN_WORKLOAD:
             if rank == 0:
                 run_attn(args, world, rank, local)
         elif args.workload == TP_WORKLOAD:

@@ -1143,8 +1143,8 @@ minq_status minq_tp_init(minq_model* m, int rank, int world, const void* unique_
   ncclComm_t comm = nullptr;
   const ncclResult_t r = nc.CommInitRank(&comm, world, id, rank);
   if (r != ncclSuccess) return fail(MINQ_ERR_NCCL, std::string("ncclCommInitRank: ") + nc.GetErrorString(r));
-  // this rank's heads and intermediate rows (the SURVEY's c5 split: q/k/v rows
-  // by head, gate/up rows, o_proj / down_proj columns)
+  // this rank's heads and intermediate rows (q/k/v rows by head, gate/up
+  // rows, o_proj / down_proj columns)
   const uint64_t nhl = nh / world, nkvl = nkv / world, Il = I / world, qd = nh * hd, kvd = nkv * hd;
   const uint64_t q0 = rank * nhl * hd, k0 = rank * nkvl * hd, i0 = rank * Il;
   for (DevLayer& L : m->layers) {

@@ -1,7 +1,7 @@
 // CPU ORACLE — TEST INFRASTRUCTURE ONLY.
 //
 // A C++17 restatement of minq's CPU forward path (kn1g78/minq, Rust), used as
-// the checker for the CUDA library and as the timed CPU baseline. Only the
+// the parity reference for the CUDA library and as the timed CPU baseline. Only the
 // test suite, `__graft_entry__.smoke()` and `bench.py`'s CPU legs load it; the
 // product library (minq_b200/libminq_cuda.so) never links or calls it.
 //

@@ -1,7 +1,7 @@
 """ctypes binding of the CPU oracle (oracle/liboracle.so).
 
 TEST INFRASTRUCTURE ONLY: imported by tests/, `__graft_entry__.smoke()` and
-the CPU legs of bench.py as the checker / CPU baseline. The product package
+the CPU legs of bench.py as the parity reference / CPU baseline. The product package
 `minq_b200` never imports this module.
 
 Function names follow the reference (kn1g78/minq, Rust) so the tests read

@@ -152,3 +152,43 @@ def test_oracle_sampler_matches_python_restatement(orc, t, top_k, top_p):
     us = (py_stdrng_u32(77, 64) >> 8).astype(np.float64) * 2.0 ** -24
     for d in range(64):
         assert s.sample(x) == py_sample(orc, x, t, top_k, top_p, np.float32(us[d])), d
+
+
+def _exact_draws(x, t, top_p, us):
+    """The sampling steps in exact (f64) cumulative arithmetic on f32
+    probabilities: the first position (index order without filters, rank
+    order with top_p) whose cumulative mass reaches u (u * the kept mass)."""
+    xt = x / np.float32(t)
+    e = np.exp((xt - xt.max()).astype(np.float64))
+    prob = (e / e.sum()).astype(np.float32).astype(np.float64)
+    if top_p >= 1.0:
+        cum = np.cumsum(prob)
+        return [int(min(np.searchsorted(cum, u), len(x) - 1)) for u in us], np.arange(len(x))
+    order = np.lexsort((np.arange(len(x)), -prob))
+    cum = np.cumsum(prob[order])
+    cutoff = int(np.searchsorted(cum, top_p)) + 1
+    toks = [int(order[min(np.searchsorted(cum[:cutoff], u * cum[cutoff - 1]), cutoff - 1)])
+            for u in us]
+    pos = np.empty(len(x), dtype=np.int64)
+    pos[order] = np.arange(len(x))
+    return toks, pos
+
+
+@pytest.mark.parametrize("n,scale,t,top_p", [(300, 8.0, 1.0, 1.0), (3000, 30.0, 1.0, 0.9),
+                                             (151936, 12.0, 0.8, 1.0), (151936, 30.0, 1.0, 0.9)])
+def test_reference_rounding_moves_large_vocabulary_draws_to_neighbours(orc, n, scale, t, top_p):
+    """On small vocabularies the reference's f32 steps draw what exact
+    arithmetic draws; over 151,936 entries its sequential f32 softmax sum
+    drops the terms below half an ulp of the running sum, so its draws land a
+    few positions away (index order without filters, rank order with top_p),
+    never far. The device sampler is checked against the exact steps there."""
+    x = _logits(n, 5, scale)
+    s = orc.Sampler(t, 0, top_p, 77)
+    ref = [s.sample(x) for _ in range(64)]
+    us = (py_stdrng_u32(77, 64) >> 8).astype(np.float64) * 2.0 ** -24
+    exact, pos = _exact_draws(x, t, top_p, us)
+    dist = [abs(int(pos[a]) - int(pos[b])) for a, b in zip(ref, exact)]
+    if n <= 3000:
+        assert ref == exact
+    else:
+        assert max(dist) <= 64 and sum(d > 0 for d in dist) > 0

@@ -135,6 +135,21 @@ minq_status minq_dequantize(minq_dtype dtype, const void* blocks, size_t nbytes,
 minq_status minq_qmatvec(minq_dtype dtype, const void* blocks, size_t rows, size_t cols,
                          const float* x, size_t x_len, float* y, void* stream);
 
+/* QuantizedTensor::matvec (quantize.rs:215-249) applied to `batch`
+ * independent inputs at once, as the reference's per-sequence loop over
+ * Linear::matvec (model.rs:57) would: y[b] = W x[b] for b < batch (1..64).
+ * x [batch][cols] and y [batch][rows] are device f32, `blocks` the
+ * row-major block layout (16-byte aligned). From 2 inputs on the product
+ * runs on the tensor cores (tcgen05, f32 accumulation of exact weight codes
+ * times a two-part bf16 split of x). `workspace` (device, 16-byte aligned)
+ * holds minq_qmatmul_workspace_bytes(batch, rows, cols) bytes. Errors as
+ * minq_qmatvec, plus MINQ_ERR_ARG for batch outside 1..64 or a small
+ * workspace. */
+size_t minq_qmatmul_workspace_bytes(size_t batch, size_t rows, size_t cols);
+minq_status minq_qmatmul(minq_dtype dtype, const void* blocks, size_t rows, size_t cols,
+                         const float* x, size_t batch, float* y, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
 /* tensor::matvec (tensor.rs:181-192) for a dense f32 [rows, cols] weight. */
 minq_status minq_matvec_f32(const float* w, size_t rows, size_t cols, const float* x,
                             size_t x_len, float* y, void* stream);

@@ -80,6 +80,8 @@ SIGNATURES = {
     "minq_quantize": (I, [I, P, S, P, P]),
     "minq_dequantize": (I, [I, P, S, P, S, P]),
     "minq_qmatvec": (I, [I, P, S, S, P, S, P, P]),
+    "minq_qmatmul_workspace_bytes": (S, [S, S, S]),
+    "minq_qmatmul": (I, [I, P, S, S, P, S, P, P, S, P]),
     "minq_matvec_f32": (I, [P, S, S, P, S, P, P]),
     "minq_argmax": (I, [P, S, P, P]),
     "minq_attn_workspace_bytes": (S, [S, S, S]),

@@ -171,6 +171,28 @@ class QuantizedTensor:
         torch = _torch()
         return self.matvec_device(_dev_tensor(x, torch.float32).reshape(-1)).cpu().numpy()
 
+    def matmul_device(self, x_dev, y_dev=None, ws_dev=None):
+        """matvec of each row of x_dev [batch, cols] (batch 1..64) in one
+        call: y_dev [batch, rows]."""
+        torch = _torch()
+        batch = int(x_dev.shape[0])
+        if y_dev is None:
+            y_dev = torch.empty(batch, self.rows, dtype=torch.float32, device="cuda")
+        nbytes = lib().minq_qmatmul_workspace_bytes(batch, self.rows, self.cols)
+        if ws_dev is None or ws_dev.numel() < nbytes:
+            ws_dev = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+        check(lib().minq_qmatmul(self.dtype, _ptr(self._dev), self.rows, self.cols, _ptr(x_dev),
+                                 batch, _ptr(y_dev), _ptr(ws_dev), ws_dev.numel(), _stream_ptr()))
+        return y_dev
+
+    def matmul(self, x) -> np.ndarray:
+        """quantize.rs:215 applied to every row of x [batch, cols]."""
+        torch = _torch()
+        xd = _dev_tensor(x, torch.float32)
+        if xd.dim() != 2 or xd.shape[1] != self.cols:
+            raise MinqError(_lib.ERR_SHAPE, f"matmul input must be [batch, {self.cols}]")
+        return self.matmul_device(xd.contiguous()).cpu().numpy()
+
 
 def matvec_f32(w, x) -> np.ndarray:
     """tensor.rs:181 — dense f32 matvec on the GPU."""

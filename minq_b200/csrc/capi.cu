@@ -253,6 +253,35 @@ minq_status minq_qmatvec(minq_dtype dtype, const void* blocks, size_t rows, size
                         nullptr, y, (cudaStream_t)stream);
 }
 
+size_t minq_qmatmul_workspace_bytes(size_t batch, size_t rows, size_t cols) {
+  // prepared inputs (x_hi + x_lo: batch x cols floats) and up to 16 column
+  // slices of partial sums (16 x batch x rows floats)
+  return 4 * batch * cols + 64 * batch * rows + 256;
+}
+
+minq_status minq_qmatmul(minq_dtype dtype, const void* blocks, size_t rows, size_t cols,
+                         const float* x, size_t batch, float* y, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  if (dtype != MINQ_Q8_0 && dtype != MINQ_Q4_0) return fail(MINQ_ERR_FORMAT, "unknown dtype");
+  if (cols % kBlock != 0) return fail(MINQ_ERR_SHAPE, "cols must be a multiple of 32");
+  if (cols > (1u << 30) || rows > (1u << 30)) return fail(MINQ_ERR_SHAPE, "matrix too large");
+  if (batch < 1 || batch > (size_t)kQmmMaxB) return fail(MINQ_ERR_ARG, "batch must be 1..64");
+  if (rows == 0) return MINQ_OK;
+  if (!blocks || !x || !y || !workspace) return fail(MINQ_ERR_ARG, "null pointer");
+  if (!aligned(blocks, 16) || !aligned(x, 16) || !aligned(workspace, 16))
+    return fail(MINQ_ERR_ARG, "blocks, x and workspace must be 16-byte aligned");
+  if (workspace_bytes < minq_qmatmul_workspace_bytes(batch, rows, cols))
+    return fail(MINQ_ERR_ARG, "workspace smaller than minq_qmatmul_workspace_bytes");
+  MINQ_TRY(require_device());
+  float* xp = static_cast<float*>(workspace);
+  const size_t xp_floats = batch * cols;
+  float* part = xp + xp_floats;
+  const size_t part_floats = 16 * batch * rows;
+  return launch_qmatmul(dtype, blocks, nullptr, rows, (int)cols, (int)batch, x, cols, nullptr,
+                        0.0f, xp, xp_floats, nullptr, nullptr, y, rows, part, part_floats,
+                        (cudaStream_t)stream);
+}
+
 minq_status minq_matvec_f32(const float* w, size_t rows, size_t cols, const float* x,
                             size_t x_len, float* y, void* stream) {
   if (x_len != cols)

@@ -65,6 +65,14 @@ minq_status launch_qmatmul_tc(int dtype, const void* w0, const void* w1, size_t 
                               float* xp, size_t xp_floats, const float* bias, const float* residual,
                               float* y, size_t y_stride, float* part, size_t part_floats,
                               cudaStream_t s);
+// qmatmul_umma.cu: the same product on the 5th-generation tensor cores
+// (tcgen05.mma, TMEM accumulators) for 1..64 quantized inputs.
+bool qmatmul_umma_takes(int dtype, int cols, int B, size_t xp_floats);
+minq_status launch_qmatmul_umma(int dtype, const void* w0, const void* w1, size_t rows, int cols,
+                                int B, const float* x, size_t x_stride, const float* norm_w,
+                                float eps, float* xp, size_t xp_floats, const float* bias,
+                                const float* residual, float* y, size_t y_stride, float* part,
+                                size_t part_floats, cudaStream_t s);
 minq_status launch_embed_batch(const float* embed, const uint32_t* d_tok, size_t vocab, int hidden,
                                int B, float* x, cudaStream_t s);
 // argmax of each of the B rows of x [B][n]; scratch: 32 u64 per row.

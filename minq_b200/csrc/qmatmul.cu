@@ -20,6 +20,8 @@
 // and applies the epilogue.
 #include <algorithm>
 
+#include <cstdlib>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "matvec_common.cuh"
@@ -314,12 +316,25 @@ minq_status qmm_launch(QmmParams p, cudaStream_t s) {
 
 }  // namespace
 
+// MINQ_TCGEN05=0 in the environment selects the mma.sync kernel for the
+// tensor-core batched projections (comparison runs); default: tcgen05.
+static bool umma_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("MINQ_TCGEN05");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 minq_status launch_qmatmul(int dtype, const void* w0, const void* w1, size_t rows, int cols,
                            int B, const float* x, size_t x_stride, const float* norm_w, float eps,
                            float* xn_scratch, size_t xn_floats, const float* bias,
                            const float* residual, float* y, size_t y_stride, float* part,
                            size_t part_floats, cudaStream_t s) {
   if (B < 1 || B > kQmmMaxB) return fail(MINQ_ERR_ARG, "batched matvec takes 1..64 inputs");
+  if (B >= kQmmTcMinB && xn_scratch && umma_enabled() && qmatmul_umma_takes(dtype, cols, B, xn_floats))
+    return launch_qmatmul_umma(dtype, w0, w1, rows, cols, B, x, x_stride, norm_w, eps, xn_scratch,
+                               xn_floats, bias, residual, y, y_stride, part, part_floats, s);
   if (xn_scratch && qmatmul_tc_takes(dtype, cols, B, xn_floats))
     return launch_qmatmul_tc(dtype, w0, w1, rows, cols, B, x, x_stride, norm_w, eps, xn_scratch,
                              xn_floats, bias, residual, y, y_stride, part, part_floats, s);

@@ -1,0 +1,749 @@
+// Batched quantized projections on the 5th-generation tensor cores:
+// Y[b] = W X[b] for Q4_0 / Q8_0 weights (quantize.rs:215-280, the
+// reference's QuantizedTensor::matvec run once per sequence) and 1..64
+// inputs, with tcgen05.mma accumulating in tensor memory (TMEM). The input
+// RMSNorm (tensor.rs:219-227) is applied while the inputs are prepared;
+// bias / residual / SwiGLU are applied after the sum.
+//
+// Operands. A = weight codes of 128 rows as exact bf16 (Q4_0: nibble - 8,
+// Q8_0: the i8 code), B = the inputs split into x_hi = bf16(x) and x_lo =
+// bf16(x - x_hi): both parts accumulate into the same TMEM tile, so a
+// block's sum_k code_k x_k carries the input to 2^-18 of |x| (16
+// significand bits of the split, then f32 accumulation). The block scale d
+// multiplies each 32-column block's sum once, in block order, into the
+// row's running f32 sum (acc += d * sum, quantize.rs:252-280), so every
+// block gets its own accumulator in TMEM and an epilogue pass.
+//
+// Data flow in one CTA (ROWS weight rows x one K slice, chunks of 4 blocks
+// = 128 columns):
+//   warp 0, lane 0   TMA: the chunk's raw weight rows (a 2-D box of the
+//                    row-major block stream, no swizzle) and the four
+//                    64-column x_hi / x_lo tiles (128-byte swizzle) into a
+//                    ring of stages; warp 0 also owns the TMEM allocation
+//   converter warps  raw codes -> bf16 A tiles in the K-major 128-byte
+//                    swizzled layout tcgen05 reads (one 64-column half
+//                    chunk per A buffer, two A buffers)
+//   warp 1, lane 0   tcgen05.mma: per block, (ROWS/128) accumulators of
+//                    128 x N f32, four MMAs each (two k steps x hi/lo),
+//                    then tcgen05.commit to the block's mbarrier
+//   epilogue warps   tcgen05.ld of their 32 lanes x 32 columns, acc +=
+//                    d * sum, release the accumulator; at the end bias /
+//                    residual / SwiGLU and the store (or the slice partial)
+// Every mbarrier wait is time-bounded (1 s); a timeout sets the device
+// status word and an abort flag that ends every role's loop, after which
+// the producer waits for its copies in flight, the MMA thread for its
+// MMAs, and warp 0 frees the TMEM.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "matvec_common.cuh"
+#include "pipeline.cuh"
+
+namespace minq {
+
+namespace {
+
+constexpr int kUmChunkBlocks = 4;  // blocks per staged chunk (128 columns)
+constexpr int kUmCtrlWarps = 4;    // warp 0 producer / TMEM, warp 1 MMA, warps 2-3 converters
+constexpr int kUmExtraConv = 4;    // more converter warps after the epilogue warps
+constexpr int kUmConvWarps = 2 + kUmExtraConv;
+constexpr int kUmMaxStages = 6;
+constexpr int kUmAccBufs = 2;      // TMEM accumulator sets (block g uses set g mod 2)
+constexpr size_t kUmSmemLimit = 227 * 1024;
+
+constexpr int pow2_at_least(int v) {
+  int p = 32;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+template <int DT, int N>
+struct UmGeom {
+  static constexpr int ROWS = DT == MINQ_Q8_0 ? 128 : 256;     // weight rows per CTA
+  static constexpr int bb = DT == MINQ_Q8_0 ? kQ8Bytes : kQ4Bytes;
+  static constexpr int raw_pitch = kUmChunkBlocks * bb;       // bytes of one row of a raw chunk
+  static constexpr int raw_bytes = ROWS * raw_pitch;
+  static constexpr int xsub_bytes = N * 128;                  // 64 bf16 columns x N inputs
+  static constexpr int x_bytes = 4 * xsub_bytes;              // {hi, lo} x {columns 0-63, 64-127}
+  static constexpr int stage_bytes = (x_bytes + raw_bytes + 1023) & ~1023;
+  static constexpr int a_bytes = ROWS * 128;                  // one A buffer: ROWS x 64 bf16
+  static constexpr int MACC = ROWS / 128;                     // accumulators per block
+  static constexpr int CW = N < 32 ? N : 32;                  // columns per epilogue warp
+  static constexpr int CG = N / CW;                           // column groups
+  static constexpr int EPI = 4 * MACC * CG;                   // epilogue warps
+  static constexpr int WARPS = kUmCtrlWarps + EPI + kUmExtraConv;
+  static constexpr int THREADS = 32 * WARPS;
+  static constexpr int TMEM_COLS = pow2_at_least(kUmAccBufs * MACC * N);
+  static constexpr int ITEMS = ROWS / 4;                      // converter items per half chunk
+  // dynamic shared memory for S stages: alignment slack, A buffers, ring, barriers
+  static constexpr size_t smem(int S) { return 1024 + 2 * (size_t)a_bytes + (size_t)S * stage_bytes + 256; }
+  static constexpr int max_stages() {
+    int s = kUmMaxStages;
+    while (s > 2 && smem(s) > kUmSmemLimit) --s;
+    return s;
+  }
+};
+
+struct UmParams {
+  size_t rows;      // rows of each matrix
+  int B;
+  int S;            // column slices
+  int slice_chunks; // chunks per slice
+  int nchunks;      // chunks of the whole row
+  int stages;
+  const float* bias;      // [rows] or null
+  const float* residual;  // [B][y_stride] or null (may alias y)
+  float* y;               // [B][y_stride]
+  size_t y_stride;
+  float* part;            // S > 1: [S][halves][B][rows]
+  int* status;
+};
+
+// ---------------------------------------------------------------------------
+// tcgen05 / TMEM building blocks (inline PTX, sm_100a)
+
+__device__ __forceinline__ void tc05_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc05_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major tile in the 128-byte swizzle
+// layout: rows of 128 bytes, 8-row groups 1024 bytes apart (stride byte
+// offset), descriptor version 1, layout type 2 (SWIZZLE_128B). The start
+// address may sit 32 / 64 / 96 bytes into the swizzle row to select a
+// 16-column k step; the 8-row group it belongs to must be 1024-byte aligned.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor of kind::f16: D f32, A and B bf16, both K-major,
+// M = 128, N columns.
+template <int N>
+__device__ __forceinline__ constexpr uint32_t um_idesc() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t dtmem, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(dtmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// The mbarrier tracks completion of every tcgen05 operation this thread
+// issued before (one arrival when they are done).
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 16 columns of f32 from TMEM (lane quarter of this warp).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// Wait for this thread's TMEM loads; the registers pass through the asm so
+// no use of them can be scheduled before the wait.
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ void sts_v4(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
+
+__device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) {
+  uint32_t u;
+  memcpy(&u, &v, 4);
+  return u;
+}
+__device__ __forceinline__ __nv_bfloat162 bits_bf2(uint32_t u) {
+  __nv_bfloat162 v;
+  memcpy(&v, &u, 4);
+  return v;
+}
+
+// Codes 2e, 2e + 1 of a Q4_0 code word w (byte e: low nibble = the even
+// column) as exact bf16 (code - 8): 0x4300 | n is bf16(128 + n), minus
+// bf16(136) = 0x4308. w4 = w >> 4 supplies the high nibbles.
+__device__ __forceinline__ uint32_t q4_pair_bf16(uint32_t w, uint32_t w4, int e) {
+  uint32_t v = __byte_perm(w, w4, (uint32_t)e | ((uint32_t)(4 + e) << 8));
+  v = (v & 0x000F000Fu) | 0x43004300u;
+  return bf2_bits(__hsub2(bits_bf2(v), bits_bf2(0x43084308u)));
+}
+
+// Codes (bytes) e, e + 1 of a Q8_0 code word as exact bf16.
+__device__ __forceinline__ uint32_t q8_pair_bf16(uint32_t w, int e) {
+  const float a = (float)(int8_t)((w >> (8 * e)) & 0xFFu);
+  const float b = (float)(int8_t)((w >> (8 * e + 8)) & 0xFFu);
+  return bf2_bits(__floats2bfloat162_rn(a, b));
+}
+
+// Bounded mbarrier wait shared by every role: returns false once the abort
+// flag is set (by any thread) or after 1 s, when it sets the flag and the
+// device status word.
+__device__ __forceinline__ bool um_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                        int* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 2000u)) return true;
+    if (*abort) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      *abort = 1;
+      if (status) atomicOr(status, kDeviceTimeout);
+      return false;
+    }
+  }
+}
+
+// The same for a whole warp: every lane waits, and the warp goes on only
+// if all of them saw the phase (an abort seen by one lane stops all).
+__device__ __forceinline__ bool um_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                             int* status) {
+  const bool ok = um_wait(bar, parity, abort, status);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// ---------------------------------------------------------------------------
+
+// x[b] -> x_hi / x_lo (bf16, natural column order), optionally RMSNorm'd
+// first with the reference's f32 operations (x * inv * w). CTA (b, j)
+// writes columns [1024 j, 1024 j + 1024) of input b, four per thread.
+constexpr int kUmPrepCols = 1024;
+__global__ void __launch_bounds__(256) um_xprep_kernel(const float* __restrict__ x, size_t x_stride,
+                                                      int n, const float* __restrict__ w, float eps,
+                                                      __nv_bfloat16* __restrict__ xh,
+                                                      __nv_bfloat16* __restrict__ xl) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ float red[9];
+  const float* row = x + (size_t)blockIdx.x * x_stride;
+  float inv = 1.0f;
+  if (w) {
+    float ss = 0.0f;
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < (n >> 2); i += blockDim.x) {
+      const float4 v = r4[i];
+      ss = fmaf(v.x, v.x, ss);
+      ss = fmaf(v.y, v.y, ss);
+      ss = fmaf(v.z, v.z, ss);
+      ss = fmaf(v.w, v.w, ss);
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float v = 0.0f;
+      for (int k = 0; k < (int)(blockDim.x >> 5); ++k) v += red[k];
+      red[8] = 1.0f / sqrtf(v / (float)n + eps);
+    }
+    __syncthreads();
+    inv = red[8];
+  }
+  const int c = blockIdx.y * kUmPrepCols + 4 * threadIdx.x;
+  if (c >= n) return;
+  float4 v = *reinterpret_cast<const float4*>(row + c);
+  if (w) {
+    const float4 g = *reinterpret_cast<const float4*>(w + c);
+    v.x = v.x * inv * g.x;
+    v.y = v.y * inv * g.y;
+    v.z = v.z * inv * g.z;
+    v.w = v.w * inv * g.w;
+  }
+  const __nv_bfloat162 h01 = __floats2bfloat162_rn(v.x, v.y);
+  const __nv_bfloat162 h23 = __floats2bfloat162_rn(v.z, v.w);
+  const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
+  const __nv_bfloat162 l01 = __floats2bfloat162_rn(v.x - f01.x, v.y - f01.y);
+  const __nv_bfloat162 l23 = __floats2bfloat162_rn(v.z - f23.x, v.w - f23.y);
+  const size_t o = (size_t)blockIdx.x * n + c;
+  uint2 hh, ll;
+  hh.x = bf2_bits(h01);
+  hh.y = bf2_bits(h23);
+  ll.x = bf2_bits(l01);
+  ll.y = bf2_bits(l23);
+  *reinterpret_cast<uint2*>(xh + o) = hh;
+  *reinterpret_cast<uint2*>(xl + o) = ll;
+}
+
+template <int DT, int N, bool DUAL>
+__global__ void __launch_bounds__(UmGeom<DT, N>::THREADS, 1)
+    qmm_umma_kernel(const __grid_constant__ CUtensorMap mw0, const __grid_constant__ CUtensorMap mw1,
+                    const __grid_constant__ CUtensorMap mxh, const __grid_constant__ CUtensorMap mxl,
+                    UmParams p) {
+  using G = UmGeom<DT, N>;
+  constexpr int ROWS = G::ROWS, MACC = G::MACC, CW = G::CW;
+  constexpr int HR = DUAL ? ROWS / 2 : ROWS;  // rows of each matrix in this CTA
+  extern __shared__ unsigned char um_sm[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int S = p.stages;
+
+  // shared memory: [align][A0][A1][stage 0..S-1: x tiles | raw][barriers]
+  const uint32_t base = (smem_u32(um_sm) + 1023u) & ~1023u;
+  unsigned char* gbase = um_sm + (base - smem_u32(um_sm));
+  const uint32_t abuf0 = base;
+  const uint32_t ring = base + 2 * G::a_bytes;
+  unsigned char* ctl = gbase + 2 * G::a_bytes + (size_t)S * G::stage_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ctl);
+  uint64_t* empty = full + kUmMaxStages;
+  uint64_t* afull = empty + kUmMaxStages;
+  uint64_t* aempty = afull + 2;
+  uint64_t* accfull = aempty + 2;
+  uint64_t* accempty = accfull + kUmAccBufs;
+  uint64_t* mma_done = accempty + kUmAccBufs;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int slice = blockIdx.y;
+  const int kc0 = slice * p.slice_chunks;
+  const int nch = min(p.nchunks, kc0 + p.slice_chunks) - kc0;
+  const size_t rb = (size_t)blockIdx.x * HR;  // first row of each matrix
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int i = 0; i < S; ++i) {
+        mbar_init(&full[i], 1);
+        mbar_init(&empty[i], 1 + G::EPI);
+      }
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&afull[i], kUmConvWarps);
+        mbar_init(&aempty[i], 1);
+      }
+      for (int i = 0; i < kUmAccBufs; ++i) {
+        mbar_init(&accfull[i], 1);
+        mbar_init(&accempty[i], G::EPI);
+      }
+      mbar_init(mma_done, 1);
+      *abort = 0;
+      mbar_fence_init();
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&mw0) : "memory");
+      if (DUAL) asm volatile("prefetch.tensormap [%0];" ::"l"(&mw1) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&mxh) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&mxl) : "memory");
+    }
+    __syncwarp();
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(G::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc05_fence_before();
+  __syncthreads();
+  tc05_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_wait();
+
+  if (warp == 0) {
+    // ---------------- producer
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      int issued = 0;
+      for (int cl = 0; cl < nch; ++cl) {
+        const int s = cl % S, w = cl / S;
+        if (w >= 1 && !um_wait(&empty[s], (uint32_t)((w - 1) & 1), abort, p.status)) break;
+        unsigned char* st = gbase + 2 * G::a_bytes + (size_t)s * G::stage_bytes;
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(G::x_bytes + G::raw_bytes));
+        const int kc = kc0 + cl;
+#pragma unroll
+        for (int part = 0; part < 2; ++part)
+#pragma unroll
+          for (int sh = 0; sh < 2; ++sh)
+            tma_load_2d_nohint(st + (part * 2 + sh) * G::xsub_bytes, part ? &mxl : &mxh,
+                               kc * 128 + sh * 64, 0, &full[s]);
+        unsigned char* raw = st + G::x_bytes;
+        tma_load_2d(raw, &mw0, kc * G::raw_pitch, (int)rb, &full[s], pol);
+        if (DUAL) tma_load_2d(raw + HR * G::raw_pitch, &mw1, kc * G::raw_pitch, (int)rb, &full[s], pol);
+        issued = cl + 1;
+      }
+      // copies still in flight land before the CTA may exit
+      for (int cl = max(0, issued - S); cl < issued; ++cl)
+        mbar_wait_timed(&full[cl % S], (uint32_t)((cl / S) & 1), p.status);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issue (one thread)
+    if (lane == 0) {
+      constexpr uint32_t idesc = um_idesc<N>();
+      for (int cl = 0; cl < nch; ++cl) {
+        const int s = cl % S, w = cl / S;
+        if (!um_wait(&full[s], (uint32_t)(w & 1), abort, p.status)) break;
+        const uint32_t xs = ring + (uint32_t)(s * G::stage_bytes);
+        bool ok = true;
+        for (int h = 0; h < 2 && ok; ++h) {
+          const int hh = 2 * cl + h, a = hh & 1, u = hh >> 1;
+          if (!um_wait(&afull[a], (uint32_t)(u & 1), abort, p.status)) { ok = false; break; }
+          tc05_fence_after();
+          const uint32_t ab = abuf0 + (uint32_t)(a * G::a_bytes);
+          for (int jj = 0; jj < 2; ++jj) {
+            const int g = 4 * cl + 2 * h + jj, t = g & (kUmAccBufs - 1), vv = g / kUmAccBufs;
+            if (vv >= 1 && !um_wait(&accempty[t], (uint32_t)((vv - 1) & 1), abort, p.status)) {
+              ok = false;
+              break;
+            }
+            tc05_fence_after();
+#pragma unroll
+            for (int m = 0; m < MACC; ++m) {
+              const uint32_t d = tmem + (uint32_t)((t * MACC + m) * N);
+#pragma unroll
+              for (int ks = 0; ks < 2; ++ks) {
+                const uint64_t ad = sw128_desc(ab + (uint32_t)(m * 16384 + jj * 64 + ks * 32));
+#pragma unroll
+                for (int part = 0; part < 2; ++part) {
+                  const uint64_t bd =
+                      sw128_desc(xs + (uint32_t)((part * 2 + h) * G::xsub_bytes + jj * 64 + ks * 32));
+                  umma_bf16(d, ad, bd, idesc, (uint32_t)(ks | part));
+                }
+              }
+            }
+            umma_commit(&accfull[t]);
+          }
+          if (!ok) break;
+          umma_commit(&aempty[a]);
+        }
+        if (!ok) break;
+        umma_commit(&empty[s]);
+      }
+      // every MMA issued has finished before the TMEM is freed
+      umma_commit(mma_done);
+      mbar_wait_timed(mma_done, 0, p.status);
+    }
+  } else if (warp >= kUmCtrlWarps && warp < kUmCtrlWarps + G::EPI) {
+    // ---------------- epilogue
+    const int e = warp - kUmCtrlWarps;
+    const int q = warp & 3;                 // TMEM lane quarter of this warp
+    const int m = (e >> 2) % MACC;          // accumulator (rows 128 m ..)
+    const int cg = e / (4 * MACC);          // column group
+    const int v = m * 128 + q * 32 + lane;  // virtual row of this thread
+    float acc[CW];
+#pragma unroll
+    for (int i = 0; i < CW; ++i) acc[i] = 0.0f;
+    bool ok = true;
+    for (int cl = 0; cl < nch && ok; ++cl) {
+      const int s = cl % S, w = cl / S;
+      if (!um_wait_warp(&full[s], (uint32_t)(w & 1), abort, p.status)) { ok = false; break; }
+      const uint32_t raw = ring + (uint32_t)(s * G::stage_bytes + G::x_bytes);
+      for (int j = 0; j < kUmChunkBlocks; ++j) {
+        const int g = 4 * cl + j, t = g & (kUmAccBufs - 1), vv = g / kUmAccBufs;
+        if (!um_wait_warp(&accfull[t], (uint32_t)(vv & 1), abort, p.status)) { ok = false; break; }
+        tc05_fence_after();
+        const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((t * MACC + m) * N + cg * CW);
+        const float dsc = __uint_as_float(lds_u32(raw + (uint32_t)(v * G::raw_pitch + j * G::bb)));
+        uint32_t r0[16];
+        tmem_ld16(ta, r0);
+        if constexpr (CW == 32) {
+          uint32_t r1[16];
+          tmem_ld16(ta + 16, r1);
+          tmem_wait_ld(r0);
+          tmem_wait_ld(r1);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) acc[16 + i] = fmaf(dsc, __uint_as_float(r1[i]), acc[16 + i]);
+        } else {
+          tmem_wait_ld(r0);
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[i] = fmaf(dsc, __uint_as_float(r0[i]), acc[i]);
+        tc05_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&accempty[t]);
+      }
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(&empty[s]);
+    }
+    // store: row of this thread and its CW inputs
+    const bool up = DUAL && v >= HR;
+    const size_t row = rb + (size_t)(DUAL ? v % HR : v);
+    if (p.S > 1 || !DUAL) {
+      if (ok && row < p.rows) {
+#pragma unroll
+        for (int i = 0; i < CW; ++i) {
+          const int b = cg * CW + i;
+          if (b >= p.B) break;
+          if (p.S > 1) {
+            p.part[(((size_t)slice * (DUAL ? 2 : 1) + (up ? 1 : 0)) * p.B + b) * p.rows + row] = acc[i];
+          } else {
+            float yv = acc[i];
+            if (p.bias) yv += p.bias[row];
+            if (p.residual) yv = p.residual[(size_t)b * p.y_stride + row] + yv;
+            p.y[(size_t)b * p.y_stride + row] = yv;
+          }
+        }
+      }
+    } else {
+      // dual, one slice: the up rows hand their sums to the gate rows
+      // through shared memory (the A buffers: every MMA has completed)
+      float* xch = reinterpret_cast<float*>(gbase);  // [N][HR]
+      if (up) {
+#pragma unroll
+        for (int i = 0; i < CW; ++i) xch[(size_t)(cg * CW + i) * HR + (v - HR)] = acc[i];
+      }
+      named_barrier_sync(1, 32 * G::EPI);
+      if (!up && ok && row < p.rows) {
+#pragma unroll
+        for (int i = 0; i < CW; ++i) {
+          const int b = cg * CW + i;
+          if (b >= p.B) break;
+          p.y[(size_t)b * p.y_stride + row] = silu(acc[i]) * xch[(size_t)b * HR + v];
+        }
+      }
+    }
+    tc05_fence_before();
+  } else {
+    // ---------------- converters: raw codes -> bf16 A tiles
+    const int k = warp < kUmCtrlWarps ? warp - 2 : 2 + (warp - kUmCtrlWarps - G::EPI);
+    for (int cl = 0; cl < nch; ++cl) {
+      const int s = cl % S, w = cl / S;
+      if (!um_wait_warp(&full[s], (uint32_t)(w & 1), abort, p.status)) break;
+      const uint32_t raw = ring + (uint32_t)(s * G::stage_bytes + G::x_bytes);
+      bool ok = true;
+      for (int h = 0; h < 2; ++h) {
+        const int hh = 2 * cl + h, a = hh & 1, u = hh >> 1;
+        if (u >= 1 && !um_wait_warp(&aempty[a], (uint32_t)((u - 1) & 1), abort, p.status)) {
+          ok = false;
+          break;
+        }
+        const uint32_t ab = abuf0 + (uint32_t)(a * G::a_bytes);
+        for (int it = k; it < G::ITEMS; it += kUmConvWarps) {
+          const int rg = it >> 1, jj = it & 1;
+          const int v = rg * 8 + (lane & 7), c4 = lane >> 3;  // row; 16-byte chunk of the block
+          const uint32_t src = raw + (uint32_t)(v * G::raw_pitch + (2 * h + jj) * G::bb + 4);
+          uint32_t o0, o1, o2, o3;
+          if (DT == MINQ_Q4_0) {
+            const uint32_t cw = lds_u32(src + 4 * c4);
+            const uint32_t cw4 = cw >> 4;
+            o0 = q4_pair_bf16(cw, cw4, 0);
+            o1 = q4_pair_bf16(cw, cw4, 1);
+            o2 = q4_pair_bf16(cw, cw4, 2);
+            o3 = q4_pair_bf16(cw, cw4, 3);
+          } else {
+            const uint32_t w0 = lds_u32(src + 8 * c4), w1 = lds_u32(src + 8 * c4 + 4);
+            o0 = q8_pair_bf16(w0, 0);
+            o1 = q8_pair_bf16(w0, 2);
+            o2 = q8_pair_bf16(w1, 0);
+            o3 = q8_pair_bf16(w1, 2);
+          }
+          const int ch = jj * 4 + c4;
+          sts_v4(ab + (uint32_t)((v >> 3) * 1024 + (v & 7) * 128 + (((ch ^ (v & 7)) & 7) << 4)), o0,
+                 o1, o2, o3);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&afull[a]);
+      }
+      if (!ok) break;
+    }
+  }
+
+  pdl_launch_dependents();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc05_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(G::TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// Sum of the S slices' partials in slice order, then the epilogue.
+template <bool DUAL>
+__global__ void __launch_bounds__(256) um_reduce_kernel(UmParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
+  constexpr int H2 = DUAL ? 2 : 1;
+  const size_t n = (size_t)p.B * p.rows;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t b = i / p.rows, row = i - b * p.rows;
+    float v[H2];
+#pragma unroll
+    for (int hh = 0; hh < H2; ++hh) {
+      v[hh] = 0.0f;
+      for (int sl = 0; sl < p.S; ++sl) v[hh] += p.part[(((size_t)sl * H2 + hh) * p.B + b) * p.rows + row];
+    }
+    float y;
+    if (DUAL) {
+      y = silu(v[0]) * v[H2 - 1];
+    } else {
+      y = v[0];
+      if (p.bias) y += p.bias[row];
+      if (p.residual) y = p.residual[b * p.y_stride + row] + y;
+    }
+    p.y[b * p.y_stride + row] = y;
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 um_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// Raw weight rows: the row-major block stream as bytes [rows][row_bytes],
+// boxes of one chunk (4 blocks) x box_rows rows, no swizzle.
+minq_status um_weight_map(const void* w, size_t rows, int nb, int bb, int box_rows, CUtensorMap* out) {
+  auto fn = um_encode_fn();
+  if (!fn) return fail(MINQ_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const uint64_t row_bytes = (uint64_t)nb * bb;
+  cuuint64_t dims[2] = {row_bytes, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)(kUmChunkBlocks * bb), (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(w), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(MINQ_ERR_CUDA, "cuTensorMapEncodeTiled (weights) failed (" + std::to_string((int)r) + ")");
+  return MINQ_OK;
+}
+
+// Inputs x_hi / x_lo: bf16 [B][cols], boxes of 64 columns x N inputs with
+// the 128-byte swizzle (rows past B read as zero).
+minq_status um_input_map(const __nv_bfloat16* x, int B, int cols, int N, CUtensorMap* out) {
+  auto fn = um_encode_fn();
+  if (!fn) return fail(MINQ_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)B};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)N};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<__nv_bfloat16*>(x), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(MINQ_ERR_CUDA, "cuTensorMapEncodeTiled (inputs) failed (" + std::to_string((int)r) + ")");
+  return MINQ_OK;
+}
+
+template <int DT, int N, bool DUAL>
+minq_status um_launch(const void* w0, const void* w1, const __nv_bfloat16* xh,
+                      const __nv_bfloat16* xl, int cols, UmParams p, unsigned tiles, cudaStream_t s) {
+  using G = UmGeom<DT, N>;
+  constexpr int HR = DUAL ? G::ROWS / 2 : G::ROWS;
+  CUtensorMap m0, m1, mh, ml;
+  const int nb = cols / kBlock;
+  MINQ_TRY(um_weight_map(w0, p.rows, nb, G::bb, HR, &m0));
+  if (DUAL) {
+    MINQ_TRY(um_weight_map(w1, p.rows, nb, G::bb, HR, &m1));
+  } else {
+    m1 = m0;
+  }
+  MINQ_TRY(um_input_map(xh, p.B, cols, N, &mh));
+  MINQ_TRY(um_input_map(xl, p.B, cols, N, &ml));
+  p.stages = std::min(G::max_stages(), std::max(2, p.slice_chunks));
+  const size_t smem = G::smem(p.stages);
+  auto k = qmm_umma_kernel<DT, N, DUAL>;
+  MINQ_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(k), smem));
+  MINQ_CUDA_TRY(launch_k(k, dim3(tiles, (unsigned)p.S), dim3(G::THREADS), smem, s, m0, m1, mh, ml, p));
+  if (p.S > 1) {
+    const size_t n = (size_t)p.B * p.rows;
+    const unsigned gr = (unsigned)std::min<size_t>((n + 255) / 256, 148 * 8);
+    MINQ_CUDA_TRY(launch_k(um_reduce_kernel<DUAL>, dim3(gr), dim3(256), 0, s, p));
+  }
+  return MINQ_OK;
+}
+
+template <int DT, bool DUAL>
+minq_status um_dispatch_n(const void* w0, const void* w1, const __nv_bfloat16* xh,
+                          const __nv_bfloat16* xl, int cols, const UmParams& p, unsigned tiles,
+                          cudaStream_t s) {
+  if (p.B <= 16) return um_launch<DT, 16, DUAL>(w0, w1, xh, xl, cols, p, tiles, s);
+  if (p.B <= 32) return um_launch<DT, 32, DUAL>(w0, w1, xh, xl, cols, p, tiles, s);
+  return um_launch<DT, 64, DUAL>(w0, w1, xh, xl, cols, p, tiles, s);
+}
+
+}  // namespace
+
+bool qmatmul_umma_takes(int dtype, int cols, int B, size_t xp_floats) {
+  return (dtype == MINQ_Q4_0 || dtype == MINQ_Q8_0) && B >= 1 && B <= 64 && cols > 0 &&
+         cols % (kUmChunkBlocks * kBlock) == 0 && xp_floats >= (size_t)B * cols;
+}
+
+minq_status launch_qmatmul_umma(int dtype, const void* w0, const void* w1, size_t rows, int cols,
+                                int B, const float* x, size_t x_stride, const float* norm_w,
+                                float eps, float* xp, size_t xp_floats, const float* bias,
+                                const float* residual, float* y, size_t y_stride, float* part,
+                                size_t part_floats, cudaStream_t s) {
+  if (!qmatmul_umma_takes(dtype, cols, B, xp_floats) || rows == 0)
+    return fail(MINQ_ERR_ARG, "tcgen05 batched matvec: dtype, shape or scratch");
+  if ((uintptr_t)w0 % 16 || (w1 && (uintptr_t)w1 % 16) || (uintptr_t)xp % 16 ||
+      (uintptr_t)x % 16 || x_stride % 4 || (norm_w && (uintptr_t)norm_w % 16))
+    return fail(MINQ_ERR_ARG, "tcgen05 batched matvec operands must be 16-byte aligned");
+  if (rows > (size_t)INT32_MAX) return fail(MINQ_ERR_SHAPE, "tcgen05 batched matvec: too many rows");
+  __nv_bfloat16* xh = reinterpret_cast<__nv_bfloat16*>(xp);
+  __nv_bfloat16* xl = xh + (size_t)B * cols;
+  MINQ_CUDA_TRY(launch_k(um_xprep_kernel,
+                         dim3((unsigned)B, (unsigned)((cols + kUmPrepCols - 1) / kUmPrepCols)),
+                         dim3(256), 0, s, x, x_stride, cols, norm_w, eps, xh, xl));
+  UmParams p{};
+  p.rows = rows;
+  p.B = B;
+  p.bias = bias;
+  p.residual = residual;
+  p.y = y;
+  p.y_stride = y_stride;
+  p.part = part;
+  p.status = device_status_word();
+  const bool dual = w1 != nullptr;
+  const int rows_cta = dtype == MINQ_Q8_0 ? 128 : 256;
+  const int hr = dual ? rows_cta / 2 : rows_cta;
+  const size_t tiles = (rows + hr - 1) / hr;
+  p.nchunks = cols / (kUmChunkBlocks * kBlock);
+  // K slices: at most one wave of CTAs (one per SM), each slice at least
+  // two chunks, the partials within the workspace
+  const size_t sms = (size_t)sm_count();
+  int S = (int)std::max<size_t>(1, sms / tiles);
+  S = std::min(S, std::max(1, p.nchunks / 2));
+  const int halves = dual ? 2 : 1;
+  while (S > 1 && (!part || (size_t)S * halves * B * rows > part_floats)) --S;
+  p.slice_chunks = (p.nchunks + S - 1) / S;
+  p.S = (p.nchunks + p.slice_chunks - 1) / p.slice_chunks;
+  if (dtype == MINQ_Q4_0)
+    return dual ? um_dispatch_n<MINQ_Q4_0, true>(w0, w1, xh, xl, cols, p, (unsigned)tiles, s)
+                : um_dispatch_n<MINQ_Q4_0, false>(w0, w1, xh, xl, cols, p, (unsigned)tiles, s);
+  return dual ? um_dispatch_n<MINQ_Q8_0, true>(w0, w1, xh, xl, cols, p, (unsigned)tiles, s)
+              : um_dispatch_n<MINQ_Q8_0, false>(w0, w1, xh, xl, cols, p, (unsigned)tiles, s);
+}
+
+}  // namespace minq

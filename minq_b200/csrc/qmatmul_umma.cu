@@ -6,13 +6,17 @@
 // bias / residual / SwiGLU are applied after the sum.
 //
 // Operands. A = weight codes of 128 rows as exact bf16 (Q4_0: nibble - 8,
-// Q8_0: the i8 code), B = the inputs split into x_hi = bf16(x) and x_lo =
-// bf16(x - x_hi): both parts accumulate into the same TMEM tile, so a
+// Q8_0: the i8 code), held in TMEM (lane = row, two bf16 per column);
+// B = the inputs split into x_hi = bf16(x) and x_lo = bf16(x - x_hi) in
+// shared memory: both parts accumulate into the same TMEM tile, so a
 // block's sum_k code_k x_k carries the input to 2^-18 of |x| (16
 // significand bits of the split, then f32 accumulation). The block scale d
 // multiplies each 32-column block's sum once, in block order, into the
 // row's running f32 sum (acc += d * sum, quantize.rs:252-280), so every
-// block gets its own accumulator in TMEM and an epilogue pass.
+// block gets its own accumulator in TMEM and an epilogue pass. Q4_0 codes
+// are unpacked in the column order 0, 4, 1, 5, 2, 6, 3, 7 of each 8-column
+// group (two lop3 / one bf16 subtraction per pair) and the inputs are
+// written in the same order; the sum over k does not depend on it.
 //
 // Data flow in one CTA (ROWS weight rows x one K slice, chunks of 4 blocks
 // = 128 columns):
@@ -20,15 +24,18 @@
 //                    row-major block stream, no swizzle) and the four
 //                    64-column x_hi / x_lo tiles (128-byte swizzle) into a
 //                    ring of stages; warp 0 also owns the TMEM allocation
-//   converter warps  raw codes -> bf16 A tiles in the K-major 128-byte
-//                    swizzled layout tcgen05 reads (one 64-column half
-//                    chunk per A buffer, two A buffers)
-//   warp 1, lane 0   tcgen05.mma: per block, (ROWS/128) accumulators of
-//                    128 x N f32, four MMAs each (two k steps x hi/lo),
-//                    then tcgen05.commit to the block's mbarrier
-//   epilogue warps   tcgen05.ld of their 32 lanes x 32 columns, acc +=
-//                    d * sum, release the accumulator; at the end bias /
-//                    residual / SwiGLU and the store (or the slice partial)
+//   warp 1, lane 0   tcgen05.mma (A from TMEM, B from shared memory): per
+//                    block, (ROWS/128) accumulators of 128 x N f32, four
+//                    MMAs each (two k steps x hi/lo), then tcgen05.commit
+//   row workers      one thread per weight row and half chunk: unpack that
+//                    row's codes of its half (2 blocks) into TMEM with
+//                    tcgen05.st; and, for its half of the N columns,
+//                    tcgen05.ld of each block's sums, acc += d * sum, release
+//                    the accumulator; at the end bias / residual / SwiGLU
+//                    and the store (or the slice partial)
+// A worker's loop over chunks c: sums of blocks 0-1 of c, unpack chunk c+1,
+// sums of blocks 2-3 of c, so the MMAs of c+1 run while c is summed and two
+// accumulator sets suffice.
 // Every mbarrier wait is time-bounded (1 s); a timeout sets the device
 // status word and an abort flag that ends every role's loop, after which
 // the producer waits for its copies in flight, the MMA thread for its
@@ -51,11 +58,9 @@ namespace minq {
 namespace {
 
 constexpr int kUmChunkBlocks = 4;  // blocks per staged chunk (128 columns)
-constexpr int kUmCtrlWarps = 4;    // warp 0 producer / TMEM, warp 1 MMA, warps 2-3 converters
-constexpr int kUmExtraConv = 4;    // more converter warps after the epilogue warps
-constexpr int kUmConvWarps = 2 + kUmExtraConv;
+constexpr int kUmCtrlWarps = 4;    // warp 0 producer / TMEM, warp 1 MMA (warps 2-3 idle)
 constexpr int kUmMaxStages = 6;
-constexpr int kUmAccBufs = 2;      // TMEM accumulator sets (block g uses set g mod 2)
+constexpr int kUmIssuers = 2;      // MMA-issuing warps (1, 2): blocks 0-1 and 2-3 of each chunk
 constexpr size_t kUmSmemLimit = 227 * 1024;
 
 constexpr int pow2_at_least(int v) {
@@ -64,26 +69,32 @@ constexpr int pow2_at_least(int v) {
   return p;
 }
 
-template <int DT, int N>
+// NP: inputs padded to 16 / 32 / 64. One MMA (M = 128 weight rows, K = 16)
+// takes x_hi and x_lo of all NP inputs as its N = 2 NP columns: measured on
+// B200, a kind::f16 MMA costs ~51 cycles for any N <= 64 (64 at N = 128), so
+// stacking the two parts halves the MMA time of a chunk.
+template <int DT, int NP>
 struct UmGeom {
-  static constexpr int ROWS = DT == MINQ_Q8_0 ? 128 : 256;     // weight rows per CTA
+  static constexpr int ROWS = 128;                            // weight rows per CTA
+  static constexpr int NN = 2 * NP;                           // MMA N: x_hi rows, then x_lo rows
   static constexpr int bb = DT == MINQ_Q8_0 ? kQ8Bytes : kQ4Bytes;
   static constexpr int raw_pitch = kUmChunkBlocks * bb;       // bytes of one row of a raw chunk
   static constexpr int raw_bytes = ROWS * raw_pitch;
-  static constexpr int xsub_bytes = N * 128;                  // 64 bf16 columns x N inputs
-  static constexpr int x_bytes = 4 * xsub_bytes;              // {hi, lo} x {columns 0-63, 64-127}
+  static constexpr int xsub_bytes = NN * 128;                 // one 64-column half: hi rows, lo rows
+  static constexpr int x_bytes = 2 * xsub_bytes;
   static constexpr int stage_bytes = (x_bytes + raw_bytes + 1023) & ~1023;
-  static constexpr int a_bytes = ROWS * 128;                  // one A buffer: ROWS x 64 bf16
-  static constexpr int MACC = ROWS / 128;                     // accumulators per block
-  static constexpr int CW = N < 32 ? N : 32;                  // columns per epilogue warp
-  static constexpr int CG = N / CW;                           // column groups
-  static constexpr int EPI = 4 * MACC * CG;                   // epilogue warps
-  static constexpr int WARPS = kUmCtrlWarps + EPI + kUmExtraConv;
+  static constexpr int WG = NP == 64 ? 4 : 2;                 // epilogue warps per TMEM lane quarter
+  static constexpr int CW = NP / WG;                          // inputs summed per epilogue thread
+  static constexpr int UNP = 4;                               // unpacker warps (one per lane quarter)
+  static constexpr int EPI = 4 * WG;                          // epilogue warps
+  static constexpr int WARPS = kUmCtrlWarps + UNP + EPI;
   static constexpr int THREADS = 32 * WARPS;
-  static constexpr int TMEM_COLS = pow2_at_least(kUmAccBufs * MACC * N);
-  static constexpr int ITEMS = ROWS / 4;                      // converter items per half chunk
-  // dynamic shared memory for S stages: alignment slack, A buffers, ring, barriers
-  static constexpr size_t smem(int S) { return 1024 + 2 * (size_t)a_bytes + (size_t)S * stage_bytes + 256; }
+  static constexpr int NBUF = NN <= 64 ? 4 : 3;               // TMEM accumulator sets (block g: set g mod NBUF)
+  static constexpr int ACC_COLS = NBUF * NN;                  // TMEM columns of the accumulators
+  static constexpr int A_COL0 = ACC_COLS;                     // A tiles: 2 chunks x 4 blocks x 16 columns
+  static constexpr int TMEM_COLS = pow2_at_least(A_COL0 + 128);
+  // dynamic shared memory for S stages: alignment slack, ring, barriers
+  static constexpr size_t smem(int S) { return 1024 + (size_t)S * stage_bytes + 256; }
   static constexpr int max_stages() {
     int s = kUmMaxStages;
     while (s > 2 && smem(s) > kUmSmemLimit) --s;
@@ -133,13 +144,14 @@ __device__ __forceinline__ constexpr uint32_t um_idesc() {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_bf16(uint32_t dtmem, uint64_t adesc, uint64_t bdesc,
-                                          uint32_t idesc, uint32_t accumulate) {
+// D (TMEM) (+)= A (TMEM, 128 lanes x 16 bf16) x B (shared memory descriptor).
+__device__ __forceinline__ void umma_bf16_ts(uint32_t dtmem, uint32_t atmem, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(dtmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(dtmem),
+      "r"(atmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -151,8 +163,14 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                : "memory");
 }
 
-// 32 lanes x 16 columns of f32 from TMEM (lane quarter of this warp).
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+// 32 lanes x 8 / 16 columns of f32 from TMEM (lane quarter of this warp).
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
       "%12, %13, %14, %15}, [%16];"
@@ -164,27 +182,55 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 
 // Wait for this thread's TMEM loads; the registers pass through the asm so
 // no use of them can be scheduled before the wait.
-__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
-  asm volatile("tcgen05.wait::ld.sync.aligned;"
-               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
-                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
-                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
-               :
-               : "memory");
+template <int K>
+__device__ __forceinline__ void tmem_wait_ld(uint32_t* r) {
+  static_assert(K == 8 || K == 16 || K == 32, "");
+  if constexpr (K == 8) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                   "+r"(r[6]), "+r"(r[7])
+                 :
+                 : "memory");
+  } else if constexpr (K == 16) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                   "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                   "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
+  } else {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                   "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                   "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]),
+                   "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                   "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                   "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
+  }
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+// 32 lanes x 32 columns into TMEM (lane quarter of this warp); completion
+// is awaited with tcgen05.wait::st.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+      "%29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
 }
+
 
 __device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
   uint32_t v;
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
   return v;
-}
-__device__ __forceinline__ void sts_v4(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
-  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w)
-               : "memory");
 }
 
 __device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) {
@@ -198,13 +244,16 @@ __device__ __forceinline__ __nv_bfloat162 bits_bf2(uint32_t u) {
   return v;
 }
 
-// Codes 2e, 2e + 1 of a Q4_0 code word w (byte e: low nibble = the even
-// column) as exact bf16 (code - 8): 0x4300 | n is bf16(128 + n), minus
-// bf16(136) = 0x4308. w4 = w >> 4 supplies the high nibbles.
-__device__ __forceinline__ uint32_t q4_pair_bf16(uint32_t w, uint32_t w4, int e) {
-  uint32_t v = __byte_perm(w, w4, (uint32_t)e | ((uint32_t)(4 + e) << 8));
-  v = (v & 0x000F000Fu) | 0x43004300u;
-  return bf2_bits(__hsub2(bits_bf2(v), bits_bf2(0x43084308u)));
+// The 8 codes of a Q4_0 code word w (nibble i = column i of its 8-column
+// group) as exact bf16 (code - 8), in the order 0, 4, 1, 5, 2, 6, 3, 7:
+// (w >> 4j) & 0x000F000F | 0x43004300 holds bf16(128 + nibble j) and
+// bf16(128 + nibble j + 4); subtracting bf16(136) = 0x4308 leaves code - 8.
+__device__ __forceinline__ void q4_word_bf16(uint32_t w, uint32_t* o) {
+  const __nv_bfloat162 off = bits_bf2(0x43084308u);
+  o[0] = bf2_bits(__hsub2(bits_bf2((w & 0x000F000Fu) | 0x43004300u), off));
+  o[1] = bf2_bits(__hsub2(bits_bf2(((w >> 4) & 0x000F000Fu) | 0x43004300u), off));
+  o[2] = bf2_bits(__hsub2(bits_bf2(((w >> 8) & 0x000F000Fu) | 0x43004300u), off));
+  o[3] = bf2_bits(__hsub2(bits_bf2(((w >> 12) & 0x000F000Fu) | 0x43004300u), off));
 }
 
 // Codes (bytes) e, e + 1 of a Q8_0 code word as exact bf16.
@@ -232,6 +281,17 @@ __device__ __forceinline__ bool um_wait(uint64_t* bar, uint32_t parity, volatile
   }
 }
 
+// One lane of a converged warp (elect.sync).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // The same for a whole warp: every lane waits, and the warp goes on only
 // if all of them saw the phase (an abort seen by one lane stops all).
 __device__ __forceinline__ bool um_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort,
@@ -242,17 +302,19 @@ __device__ __forceinline__ bool um_wait_warp(uint64_t* bar, uint32_t parity, vol
 
 // ---------------------------------------------------------------------------
 
-// x[b] -> x_hi / x_lo (bf16, natural column order), optionally RMSNorm'd
-// first with the reference's f32 operations (x * inv * w). CTA (b, j)
-// writes columns [1024 j, 1024 j + 1024) of input b, four per thread.
+// x[b] -> x_hi / x_lo (bf16), optionally RMSNorm'd first with the
+// reference's f32 operations (x * inv * w). With `perm`, position p of each
+// 8-column group holds column (0, 4, 1, 5, 2, 6, 3, 7)[p] (the order the Q4_0
+// codes are unpacked in); else columns stay in place. CTA (b, j) writes
+// columns [1024 j, 1024 j + 1024) of input b, eight per thread.
 constexpr int kUmPrepCols = 1024;
-__global__ void __launch_bounds__(256) um_xprep_kernel(const float* __restrict__ x, size_t x_stride,
+__global__ void __launch_bounds__(128) um_xprep_kernel(const float* __restrict__ x, size_t x_stride,
                                                       int n, const float* __restrict__ w, float eps,
-                                                      __nv_bfloat16* __restrict__ xh,
+                                                      int perm, __nv_bfloat16* __restrict__ xh,
                                                       __nv_bfloat16* __restrict__ xl) {
   pdl_wait();
   pdl_launch_dependents();
-  __shared__ float red[9];
+  __shared__ float red[5];
   const float* row = x + (size_t)blockIdx.x * x_stride;
   float inv = 1.0f;
   if (w) {
@@ -272,62 +334,74 @@ __global__ void __launch_bounds__(256) um_xprep_kernel(const float* __restrict__
     if (threadIdx.x == 0) {
       float v = 0.0f;
       for (int k = 0; k < (int)(blockDim.x >> 5); ++k) v += red[k];
-      red[8] = 1.0f / sqrtf(v / (float)n + eps);
+      red[4] = 1.0f / sqrtf(v / (float)n + eps);
     }
     __syncthreads();
-    inv = red[8];
+    inv = red[4];
   }
-  const int c = blockIdx.y * kUmPrepCols + 4 * threadIdx.x;
+  const int c = blockIdx.y * kUmPrepCols + 8 * threadIdx.x;
   if (c >= n) return;
-  float4 v = *reinterpret_cast<const float4*>(row + c);
+  float v[8];
+  *reinterpret_cast<float4*>(v) = *reinterpret_cast<const float4*>(row + c);
+  *reinterpret_cast<float4*>(v + 4) = *reinterpret_cast<const float4*>(row + c + 4);
   if (w) {
-    const float4 g = *reinterpret_cast<const float4*>(w + c);
-    v.x = v.x * inv * g.x;
-    v.y = v.y * inv * g.y;
-    v.z = v.z * inv * g.z;
-    v.w = v.w * inv * g.w;
+    float g[8];
+    *reinterpret_cast<float4*>(g) = *reinterpret_cast<const float4*>(w + c);
+    *reinterpret_cast<float4*>(g + 4) = *reinterpret_cast<const float4*>(w + c + 4);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = v[i] * inv * g[i];
   }
-  const __nv_bfloat162 h01 = __floats2bfloat162_rn(v.x, v.y);
-  const __nv_bfloat162 h23 = __floats2bfloat162_rn(v.z, v.w);
-  const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
-  const __nv_bfloat162 l01 = __floats2bfloat162_rn(v.x - f01.x, v.y - f01.y);
-  const __nv_bfloat162 l23 = __floats2bfloat162_rn(v.z - f23.x, v.w - f23.y);
-  const size_t o = (size_t)blockIdx.x * n + c;
-  uint2 hh, ll;
-  hh.x = bf2_bits(h01);
-  hh.y = bf2_bits(h23);
-  ll.x = bf2_bits(l01);
-  ll.y = bf2_bits(l23);
-  *reinterpret_cast<uint2*>(xh + o) = hh;
-  *reinterpret_cast<uint2*>(xl + o) = ll;
+  float o[8];
+  if (perm) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      o[2 * i] = v[i];
+      o[2 * i + 1] = v[i + 4];
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = v[i];
+  }
+  uint4 hh, ll;
+  uint32_t* hp = &hh.x;
+  uint32_t* lp = &ll.x;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+    const float2 f = __bfloat1622float2(h);
+    hp[i] = bf2_bits(h);
+    lp[i] = bf2_bits(__floats2bfloat162_rn(o[2 * i] - f.x, o[2 * i + 1] - f.y));
+  }
+  const size_t off = (size_t)blockIdx.x * n + c;
+  *reinterpret_cast<uint4*>(xh + off) = hh;
+  *reinterpret_cast<uint4*>(xl + off) = ll;
 }
 
-template <int DT, int N, bool DUAL>
-__global__ void __launch_bounds__(UmGeom<DT, N>::THREADS, 1)
+template <int DT, int NP, bool DUAL>
+__global__ void __launch_bounds__(UmGeom<DT, NP>::THREADS, 1)
     qmm_umma_kernel(const __grid_constant__ CUtensorMap mw0, const __grid_constant__ CUtensorMap mw1,
                     const __grid_constant__ CUtensorMap mxh, const __grid_constant__ CUtensorMap mxl,
                     UmParams p) {
-  using G = UmGeom<DT, N>;
-  constexpr int ROWS = G::ROWS, MACC = G::MACC, CW = G::CW;
+  using G = UmGeom<DT, NP>;
+  constexpr int ROWS = G::ROWS, NN = G::NN, CW = G::CW;
   constexpr int HR = DUAL ? ROWS / 2 : ROWS;  // rows of each matrix in this CTA
   extern __shared__ unsigned char um_sm[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int S = p.stages;
 
-  // shared memory: [align][A0][A1][stage 0..S-1: x tiles | raw][barriers]
+  // shared memory: [align][stage 0..S-1: x tiles | raw][barriers]
   const uint32_t base = (smem_u32(um_sm) + 1023u) & ~1023u;
   unsigned char* gbase = um_sm + (base - smem_u32(um_sm));
-  const uint32_t abuf0 = base;
-  const uint32_t ring = base + 2 * G::a_bytes;
-  unsigned char* ctl = gbase + 2 * G::a_bytes + (size_t)S * G::stage_bytes;
+  const uint32_t ring = base;
+  unsigned char* ctl = gbase + (size_t)S * G::stage_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(ctl);
   uint64_t* empty = full + kUmMaxStages;
   uint64_t* afull = empty + kUmMaxStages;
   uint64_t* aempty = afull + 2;
   uint64_t* accfull = aempty + 2;
-  uint64_t* accempty = accfull + kUmAccBufs;
-  uint64_t* mma_done = accempty + kUmAccBufs;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* accempty = accfull + 4;
+  uint64_t* mma_done = accempty + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 2);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int slice = blockIdx.y;
@@ -339,17 +413,18 @@ __global__ void __launch_bounds__(UmGeom<DT, N>::THREADS, 1)
     if (lane == 0) {
       for (int i = 0; i < S; ++i) {
         mbar_init(&full[i], 1);
-        mbar_init(&empty[i], 1 + G::EPI);
+        mbar_init(&empty[i], kUmIssuers + G::UNP + G::EPI);
       }
       for (int i = 0; i < 2; ++i) {
-        mbar_init(&afull[i], kUmConvWarps);
-        mbar_init(&aempty[i], 1);
+        mbar_init(&afull[i], G::UNP);
+        mbar_init(&aempty[i], kUmIssuers);
       }
-      for (int i = 0; i < kUmAccBufs; ++i) {
+      for (int i = 0; i < G::NBUF; ++i) {
         mbar_init(&accfull[i], 1);
         mbar_init(&accempty[i], G::EPI);
       }
-      mbar_init(mma_done, 1);
+      mbar_init(&mma_done[0], 1);
+      mbar_init(&mma_done[1], 1);
       *abort = 0;
       mbar_fence_init();
       asm volatile("prefetch.tensormap [%0];" ::"l"(&mw0) : "memory");
@@ -371,133 +446,206 @@ __global__ void __launch_bounds__(UmGeom<DT, N>::THREADS, 1)
   pdl_wait();
 
   if (warp == 0) {
-    // ---------------- producer
-    if (lane == 0) {
-      const uint64_t pol = policy_evict_first();
-      int issued = 0;
-      for (int cl = 0; cl < nch; ++cl) {
-        const int s = cl % S, w = cl / S;
-        if (w >= 1 && !um_wait(&empty[s], (uint32_t)((w - 1) & 1), abort, p.status)) break;
-        unsigned char* st = gbase + 2 * G::a_bytes + (size_t)s * G::stage_bytes;
+    // ---------------- producer: the warp runs the loop converged, one
+    // elected lane issues the copies. Stage: for each 64-column half, x_hi
+    // of the NP inputs then x_lo (the B operand, 2 NP rows), then the raw
+    // weight rows.
+    const uint64_t pol = policy_evict_first();
+    int issued = 0;
+    for (int cl = 0; cl < nch; ++cl) {
+      const int s = cl % S, w = cl / S;
+      if (w >= 1 && !um_wait_warp(&empty[s], (uint32_t)((w - 1) & 1), abort, p.status)) break;
+      if (elect_one()) {
+        unsigned char* st = gbase + (size_t)s * G::stage_bytes;
         mbar_arrive_expect_tx(&full[s], (uint32_t)(G::x_bytes + G::raw_bytes));
         const int kc = kc0 + cl;
 #pragma unroll
-        for (int part = 0; part < 2; ++part)
+        for (int sh = 0; sh < 2; ++sh)
 #pragma unroll
-          for (int sh = 0; sh < 2; ++sh)
-            tma_load_2d_nohint(st + (part * 2 + sh) * G::xsub_bytes, part ? &mxl : &mxh,
+          for (int part = 0; part < 2; ++part)
+            tma_load_2d_nohint(st + sh * G::xsub_bytes + part * NP * 128, part ? &mxl : &mxh,
                                kc * 128 + sh * 64, 0, &full[s]);
         unsigned char* raw = st + G::x_bytes;
         tma_load_2d(raw, &mw0, kc * G::raw_pitch, (int)rb, &full[s], pol);
         if (DUAL) tma_load_2d(raw + HR * G::raw_pitch, &mw1, kc * G::raw_pitch, (int)rb, &full[s], pol);
-        issued = cl + 1;
       }
-      // copies still in flight land before the CTA may exit
-      for (int cl = max(0, issued - S); cl < issued; ++cl)
-        mbar_wait_timed(&full[cl % S], (uint32_t)((cl / S) & 1), p.status);
+      __syncwarp();
+      issued = cl + 1;
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issue (one thread)
+    // copies still in flight land before the CTA may exit
+    for (int cl = max(0, issued - S); cl < issued; ++cl)
+      mbar_wait_timed(&full[cl % S], (uint32_t)((cl / S) & 1), p.status);
+  } else if (warp == 1 || warp == 2) {
+    // ---------------- MMA issue: lane 0 of warp 1 issues blocks 0-1 of
+    // every chunk, lane 0 of warp 2 blocks 2-3 (A tile cl mod 2; block g
+    // accumulates in set g mod NBUF with two MMAs, k steps, of N = 2 NP).
+    // A kind::f16 MMA of N <= 64 takes ~51 cycles in the tensor core, about
+    // the latency of a handful of dependent instructions of one thread, so
+    // two threads issue, and each keeps its per-block work to a barrier
+    // test, two adds, the MMAs and the commit: descriptors are formed once
+    // and the stage and its phase advance incrementally.
+    const int hi = warp - 1;  // which pair of blocks
     if (lane == 0) {
-      constexpr uint32_t idesc = um_idesc<N>();
-      for (int cl = 0; cl < nch; ++cl) {
-        const int s = cl % S, w = cl / S;
-        if (!um_wait(&full[s], (uint32_t)(w & 1), abort, p.status)) break;
-        const uint32_t xs = ring + (uint32_t)(s * G::stage_bytes);
-        bool ok = true;
-        for (int h = 0; h < 2 && ok; ++h) {
-          const int hh = 2 * cl + h, a = hh & 1, u = hh >> 1;
-          if (!um_wait(&afull[a], (uint32_t)(u & 1), abort, p.status)) { ok = false; break; }
-          tc05_fence_after();
-          const uint32_t ab = abuf0 + (uint32_t)(a * G::a_bytes);
-          for (int jj = 0; jj < 2; ++jj) {
-            const int g = 4 * cl + 2 * h + jj, t = g & (kUmAccBufs - 1), vv = g / kUmAccBufs;
-            if (vv >= 1 && !um_wait(&accempty[t], (uint32_t)((vv - 1) & 1), abort, p.status)) {
-              ok = false;
-              break;
-            }
-            tc05_fence_after();
+      constexpr uint32_t idesc = um_idesc<NN>();
+      const uint64_t bdesc0 = sw128_desc(ring) + (uint64_t)((uint32_t)(hi * G::xsub_bytes) >> 4);
+      const uint32_t a_tm = tmem + (uint32_t)(G::A_COL0 + hi * 32);
+      int s = 0;                  // stage of chunk cl
+      uint32_t sphase = 0;        // parity of its full barrier
+      int g = 2 * hi;             // block index of the next MMA pair
+      bool ok = true;
+      for (int cl = 0; cl < nch && ok; ++cl) {
+        const int a = cl & 1;
+        if (!um_wait(&full[s], sphase, abort, p.status)) break;
+        if (!um_wait(&afull[a], (uint32_t)((cl >> 1) & 1), abort, p.status)) break;
+        const uint64_t bs = bdesc0 + (uint64_t)((uint32_t)(s * G::stage_bytes) >> 4);
+        const uint32_t as = a_tm + (uint32_t)(a * 64);
 #pragma unroll
-            for (int m = 0; m < MACC; ++m) {
-              const uint32_t d = tmem + (uint32_t)((t * MACC + m) * N);
-#pragma unroll
-              for (int ks = 0; ks < 2; ++ks) {
-                const uint64_t ad = sw128_desc(ab + (uint32_t)(m * 16384 + jj * 64 + ks * 32));
-#pragma unroll
-                for (int part = 0; part < 2; ++part) {
-                  const uint64_t bd =
-                      sw128_desc(xs + (uint32_t)((part * 2 + h) * G::xsub_bytes + jj * 64 + ks * 32));
-                  umma_bf16(d, ad, bd, idesc, (uint32_t)(ks | part));
-                }
-              }
-            }
-            umma_commit(&accfull[t]);
+        for (int jj = 0; jj < 2; ++jj) {
+          // set t was last used by block g - NBUF (either issuer): wait
+          // until that block's sums are read
+          const int t = g % G::NBUF, vv = g / G::NBUF;
+          if (vv >= 1 && !um_wait(&accempty[t], (uint32_t)((vv - 1) & 1), abort, p.status)) {
+            ok = false;
+            break;
           }
-          if (!ok) break;
-          umma_commit(&aempty[a]);
+          tc05_fence_after();
+          const uint32_t d = tmem + (uint32_t)(t * NN);
+          umma_bf16_ts(d, as + (uint32_t)(jj * 16), bs + (uint64_t)((jj * 64) >> 4), idesc, 0u);
+          umma_bf16_ts(d, as + (uint32_t)(jj * 16 + 8), bs + (uint64_t)((jj * 64 + 32) >> 4), idesc, 1u);
+          umma_commit(&accfull[t]);
+          g += jj == 0 ? 1 : 3;  // next block of this issuer (skip the other pair)
         }
         if (!ok) break;
+        umma_commit(&aempty[a]);
         umma_commit(&empty[s]);
+        if (++s == S) {
+          s = 0;
+          sphase ^= 1u;
+        }
       }
       // every MMA issued has finished before the TMEM is freed
-      umma_commit(mma_done);
-      mbar_wait_timed(mma_done, 0, p.status);
+      umma_commit(&mma_done[hi]);
+      mbar_wait_timed(&mma_done[hi], 0, p.status);
     }
-  } else if (warp >= kUmCtrlWarps && warp < kUmCtrlWarps + G::EPI) {
-    // ---------------- epilogue
-    const int e = warp - kUmCtrlWarps;
-    const int q = warp & 3;                 // TMEM lane quarter of this warp
-    const int m = (e >> 2) % MACC;          // accumulator (rows 128 m ..)
-    const int cg = e / (4 * MACC);          // column group
-    const int v = m * 128 + q * 32 + lane;  // virtual row of this thread
-    float acc[CW];
+  } else if (warp >= kUmCtrlWarps && warp < kUmCtrlWarps + G::UNP) {
+    // ---------------- unpackers: thread = weight row (TMEM lane); each
+    // chunk's 4 blocks of codes -> bf16 into A tile cl mod 2, two blocks per
+    // TMEM store
+    const int v = (warp & 3) * 32 + lane;
+    const uint32_t lq = (uint32_t)((warp & 3) * 32) << 16;
+    for (int cl = 0; cl < nch; ++cl) {
+      const int s = cl % S, w = cl / S, a = cl & 1;
+      if (!um_wait_warp(&full[s], (uint32_t)(w & 1), abort, p.status)) break;
+      if (cl >= 2 && !um_wait_warp(&aempty[a], (uint32_t)(((cl >> 1) - 1) & 1), abort, p.status)) break;
+      const uint32_t src = ring + (uint32_t)(s * G::stage_bytes + G::x_bytes + v * G::raw_pitch + 4);
 #pragma unroll
-    for (int i = 0; i < CW; ++i) acc[i] = 0.0f;
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t o[32];
+        if (DT == MINQ_Q4_0) {
+          uint32_t wd[8];
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) wd[4 * j + i] = lds_u32(src + (uint32_t)((2 * hh + j) * G::bb + 4 * i));
+#pragma unroll
+          for (int i = 0; i < 8; ++i) q4_word_bf16(wd[i], o + 4 * i);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const uint32_t wd = lds_u32(src + (uint32_t)((2 * hh + j) * G::bb + 4 * i));
+              o[16 * j + 2 * i] = q8_pair_bf16(wd, 0);
+              o[16 * j + 2 * i + 1] = q8_pair_bf16(wd, 2);
+            }
+        }
+        // the store reads its registers when issued; one wait covers both
+        tmem_st32(tmem + lq + (uint32_t)(G::A_COL0 + a * 64 + hh * 32), o);
+      }
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc05_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&afull[a]);
+        mbar_arrive(&empty[s]);
+      }
+    }
+  } else if (warp >= kUmCtrlWarps + G::UNP) {
+    // ---------------- epilogue: thread = weight row (TMEM lane), inputs
+    // [u CW, u CW + CW): acc += d * (block sums of x_hi, x_lo)
+    const int wi = warp - kUmCtrlWarps - G::UNP;
+    const int q = warp & 3;
+    const int u = wi >> 2;
+    const int v = q * 32 + lane;
+    const uint32_t lq = (uint32_t)(q * 32) << 16;
+    constexpr int JB = 1;                    // blocks per epilogue step (2 measured no faster)
+    float2 acc[CW];
+#pragma unroll
+    for (int i = 0; i < CW; ++i) acc[i] = make_float2(0.0f, 0.0f);
     bool ok = true;
     for (int cl = 0; cl < nch && ok; ++cl) {
       const int s = cl % S, w = cl / S;
       if (!um_wait_warp(&full[s], (uint32_t)(w & 1), abort, p.status)) { ok = false; break; }
-      const uint32_t raw = ring + (uint32_t)(s * G::stage_bytes + G::x_bytes);
-      for (int j = 0; j < kUmChunkBlocks; ++j) {
-        const int g = 4 * cl + j, t = g & (kUmAccBufs - 1), vv = g / kUmAccBufs;
-        if (!um_wait_warp(&accfull[t], (uint32_t)(vv & 1), abort, p.status)) { ok = false; break; }
-        tc05_fence_after();
-        const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((t * MACC + m) * N + cg * CW);
-        const float dsc = __uint_as_float(lds_u32(raw + (uint32_t)(v * G::raw_pitch + j * G::bb)));
-        uint32_t r0[16];
-        tmem_ld16(ta, r0);
-        if constexpr (CW == 32) {
-          uint32_t r1[16];
-          tmem_ld16(ta + 16, r1);
-          tmem_wait_ld(r0);
-          tmem_wait_ld(r1);
+      const uint32_t raw = ring + (uint32_t)(s * G::stage_bytes + G::x_bytes + v * G::raw_pitch);
+      float dsc[kUmChunkBlocks];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) acc[16 + i] = fmaf(dsc, __uint_as_float(r1[i]), acc[16 + i]);
-        } else {
-          tmem_wait_ld(r0);
+      for (int j = 0; j < kUmChunkBlocks; ++j) dsc[j] = __uint_as_float(lds_u32(raw + (uint32_t)(j * G::bb)));
+      // JB blocks per step: one wait each, all their TMEM loads, one
+      // wait::ld, the releases, then the FMAs (fewer serial steps per block)
+#pragma unroll
+      for (int j0 = 0; j0 < kUmChunkBlocks; j0 += JB) {
+        uint32_t r[JB][2 * CW];
+#pragma unroll
+        for (int jb = 0; jb < JB; ++jb) {
+          const int g = 4 * cl + j0 + jb, t = g % G::NBUF, vv = g / G::NBUF;
+          if (!um_wait_warp(&accfull[t], (uint32_t)(vv & 1), abort, p.status)) { ok = false; break; }
+          tc05_fence_after();
+          const uint32_t ta = tmem + lq + (uint32_t)(t * NN + u * CW);
+          if constexpr (CW == 8) {
+            tmem_ld8(ta, r[jb]);
+            tmem_ld8(ta + NP, r[jb] + 8);
+          } else {
+            tmem_ld16(ta, r[jb]);
+            tmem_ld16(ta + NP, r[jb] + 16);
+          }
         }
+        if (!ok) break;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) acc[i] = fmaf(dsc, __uint_as_float(r0[i]), acc[i]);
+        for (int jb = 0; jb < JB; ++jb) tmem_wait_ld<2 * CW>(r[jb]);
         tc05_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&accempty[t]);
+        if (lane == 0) {
+#pragma unroll
+          for (int jb = 0; jb < JB; ++jb) mbar_arrive(&accempty[(4 * cl + j0 + jb) % G::NBUF]);
+        }
+#pragma unroll
+        for (int jb = 0; jb < JB; ++jb) {
+          const float2 d2 = make_float2(dsc[j0 + jb], dsc[j0 + jb]);
+#pragma unroll
+          for (int i = 0; i < CW; ++i)
+            acc[i] = __ffma2_rn(d2, make_float2(__uint_as_float(r[jb][i]), __uint_as_float(r[jb][CW + i])), acc[i]);
+        }
       }
       __syncwarp();
       if (ok && lane == 0) mbar_arrive(&empty[s]);
     }
+
     // store: row of this thread and its CW inputs
+    float accs[CW];
+#pragma unroll
+    for (int i = 0; i < CW; ++i) accs[i] = acc[i].x + acc[i].y;
     const bool up = DUAL && v >= HR;
     const size_t row = rb + (size_t)(DUAL ? v % HR : v);
     if (p.S > 1 || !DUAL) {
       if (ok && row < p.rows) {
 #pragma unroll
         for (int i = 0; i < CW; ++i) {
-          const int b = cg * CW + i;
+          const int b = u * CW + i;
           if (b >= p.B) break;
           if (p.S > 1) {
-            p.part[(((size_t)slice * (DUAL ? 2 : 1) + (up ? 1 : 0)) * p.B + b) * p.rows + row] = acc[i];
+            p.part[(((size_t)slice * (DUAL ? 2 : 1) + (up ? 1 : 0)) * p.B + b) * p.rows + row] = accs[i];
           } else {
-            float yv = acc[i];
+            float yv = accs[i];
             if (p.bias) yv += p.bias[row];
             if (p.residual) yv = p.residual[(size_t)b * p.y_stride + row] + yv;
             p.y[(size_t)b * p.y_stride + row] = yv;
@@ -506,67 +654,25 @@ __global__ void __launch_bounds__(UmGeom<DT, N>::THREADS, 1)
       }
     } else {
       // dual, one slice: the up rows hand their sums to the gate rows
-      // through shared memory (the A buffers: every MMA has completed)
-      float* xch = reinterpret_cast<float*>(gbase);  // [N][HR]
+      // through shared memory (the ring, once the epilogue warps are done;
+      // every copy and MMA has completed by then)
+      float* xch = reinterpret_cast<float*>(gbase);  // [NP][HR]
+      named_barrier_sync(1, 32 * G::EPI);
       if (up) {
 #pragma unroll
-        for (int i = 0; i < CW; ++i) xch[(size_t)(cg * CW + i) * HR + (v - HR)] = acc[i];
+        for (int i = 0; i < CW; ++i) xch[(size_t)(u * CW + i) * HR + (v - HR)] = accs[i];
       }
       named_barrier_sync(1, 32 * G::EPI);
       if (!up && ok && row < p.rows) {
 #pragma unroll
         for (int i = 0; i < CW; ++i) {
-          const int b = cg * CW + i;
+          const int b = u * CW + i;
           if (b >= p.B) break;
-          p.y[(size_t)b * p.y_stride + row] = silu(acc[i]) * xch[(size_t)b * HR + v];
+          p.y[(size_t)b * p.y_stride + row] = silu(accs[i]) * xch[(size_t)b * HR + v];
         }
       }
     }
     tc05_fence_before();
-  } else {
-    // ---------------- converters: raw codes -> bf16 A tiles
-    const int k = warp < kUmCtrlWarps ? warp - 2 : 2 + (warp - kUmCtrlWarps - G::EPI);
-    for (int cl = 0; cl < nch; ++cl) {
-      const int s = cl % S, w = cl / S;
-      if (!um_wait_warp(&full[s], (uint32_t)(w & 1), abort, p.status)) break;
-      const uint32_t raw = ring + (uint32_t)(s * G::stage_bytes + G::x_bytes);
-      bool ok = true;
-      for (int h = 0; h < 2; ++h) {
-        const int hh = 2 * cl + h, a = hh & 1, u = hh >> 1;
-        if (u >= 1 && !um_wait_warp(&aempty[a], (uint32_t)((u - 1) & 1), abort, p.status)) {
-          ok = false;
-          break;
-        }
-        const uint32_t ab = abuf0 + (uint32_t)(a * G::a_bytes);
-        for (int it = k; it < G::ITEMS; it += kUmConvWarps) {
-          const int rg = it >> 1, jj = it & 1;
-          const int v = rg * 8 + (lane & 7), c4 = lane >> 3;  // row; 16-byte chunk of the block
-          const uint32_t src = raw + (uint32_t)(v * G::raw_pitch + (2 * h + jj) * G::bb + 4);
-          uint32_t o0, o1, o2, o3;
-          if (DT == MINQ_Q4_0) {
-            const uint32_t cw = lds_u32(src + 4 * c4);
-            const uint32_t cw4 = cw >> 4;
-            o0 = q4_pair_bf16(cw, cw4, 0);
-            o1 = q4_pair_bf16(cw, cw4, 1);
-            o2 = q4_pair_bf16(cw, cw4, 2);
-            o3 = q4_pair_bf16(cw, cw4, 3);
-          } else {
-            const uint32_t w0 = lds_u32(src + 8 * c4), w1 = lds_u32(src + 8 * c4 + 4);
-            o0 = q8_pair_bf16(w0, 0);
-            o1 = q8_pair_bf16(w0, 2);
-            o2 = q8_pair_bf16(w1, 0);
-            o3 = q8_pair_bf16(w1, 2);
-          }
-          const int ch = jj * 4 + c4;
-          sts_v4(ab + (uint32_t)((v >> 3) * 1024 + (v & 7) * 128 + (((ch ^ (v & 7)) & 7) << 4)), o0,
-                 o1, o2, o3);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&afull[a]);
-      }
-      if (!ok) break;
-    }
   }
 
   pdl_launch_dependents();
@@ -656,10 +762,10 @@ minq_status um_input_map(const __nv_bfloat16* x, int B, int cols, int N, CUtenso
   return MINQ_OK;
 }
 
-template <int DT, int N, bool DUAL>
+template <int DT, int NP, bool DUAL>
 minq_status um_launch(const void* w0, const void* w1, const __nv_bfloat16* xh,
                       const __nv_bfloat16* xl, int cols, UmParams p, unsigned tiles, cudaStream_t s) {
-  using G = UmGeom<DT, N>;
+  using G = UmGeom<DT, NP>;
   constexpr int HR = DUAL ? G::ROWS / 2 : G::ROWS;
   CUtensorMap m0, m1, mh, ml;
   const int nb = cols / kBlock;
@@ -669,11 +775,13 @@ minq_status um_launch(const void* w0, const void* w1, const __nv_bfloat16* xh,
   } else {
     m1 = m0;
   }
-  MINQ_TRY(um_input_map(xh, p.B, cols, N, &mh));
-  MINQ_TRY(um_input_map(xl, p.B, cols, N, &ml));
+  MINQ_TRY(um_input_map(xh, p.B, cols, NP, &mh));
+  MINQ_TRY(um_input_map(xl, p.B, cols, NP, &ml));
   p.stages = std::min(G::max_stages(), std::max(2, p.slice_chunks));
-  const size_t smem = G::smem(p.stages);
-  auto k = qmm_umma_kernel<DT, N, DUAL>;
+  // at least 120 KB so one CTA holds an SM: its TMEM allocation never waits
+  // for another CTA's
+  const size_t smem = std::max<size_t>(G::smem(p.stages), 120 * 1024);
+  auto k = qmm_umma_kernel<DT, NP, DUAL>;
   MINQ_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(k), smem));
   MINQ_CUDA_TRY(launch_k(k, dim3(tiles, (unsigned)p.S), dim3(G::THREADS), smem, s, m0, m1, mh, ml, p));
   if (p.S > 1) {
@@ -715,7 +823,8 @@ minq_status launch_qmatmul_umma(int dtype, const void* w0, const void* w1, size_
   __nv_bfloat16* xl = xh + (size_t)B * cols;
   MINQ_CUDA_TRY(launch_k(um_xprep_kernel,
                          dim3((unsigned)B, (unsigned)((cols + kUmPrepCols - 1) / kUmPrepCols)),
-                         dim3(256), 0, s, x, x_stride, cols, norm_w, eps, xh, xl));
+                         dim3(128), 0, s, x, x_stride, cols, norm_w, eps,
+                         dtype == MINQ_Q4_0 ? 1 : 0, xh, xl));
   UmParams p{};
   p.rows = rows;
   p.B = B;
@@ -726,7 +835,7 @@ minq_status launch_qmatmul_umma(int dtype, const void* w0, const void* w1, size_
   p.part = part;
   p.status = device_status_word();
   const bool dual = w1 != nullptr;
-  const int rows_cta = dtype == MINQ_Q8_0 ? 128 : 256;
+  const int rows_cta = 128;
   const int hr = dual ? rows_cta / 2 : rows_cta;
   const size_t tiles = (rows + hr - 1) / hr;
   p.nchunks = cols / (kUmChunkBlocks * kBlock);

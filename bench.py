@@ -49,6 +49,10 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 NCU_TRAFFIC_RATIO = {"qmatvec": 1.002, "decode_mk": 1.003}
 sys.path.insert(0, ROOT)
 
+# Greedy tokens the GPU decodes from the bench's cache state for the parity
+# record (the oracle decodes from a copy of the same state).
+PARITY_TOKENS = 64
+
 WORKLOADS = {
     # name: (arch, prompt tokens)
     "qwen3-4b-q4_0": ("qwen3-4b", 2048),
@@ -88,6 +92,9 @@ def parse():
     ap.add_argument("--prompt", type=int, default=None, help="prefill length override")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sub-records", action="store_true",
+                    help="default workload only: skip the batched (data-sharded) and "
+                         "tensor-parallel sub-records")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--layers", type=int, default=None,
                     help="keep only the first N layers: a smaller case of the same kernels "
@@ -248,6 +255,8 @@ def run_reference(args, world, rank):
     from oracle import oracle as orc
     from minq_b200 import synth
     from dataclasses import replace
+    # torchrun sets OMP_NUM_THREADS=1: the arm uses every host core
+    orc.set_threads(os.cpu_count() or 1)
     arch, prompt_len = WORKLOADS[args.workload]
     prompt_len = args.prompt or prompt_len
     cfg0, qk_norm, tied = synth.ARCH[arch]
@@ -277,7 +286,9 @@ def run_reference(args, world, rank):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000 * el / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{args.workload} decode bs=1 at KV length {prompt_len}",
+        "config": {"workload": f"{args.workload} decode bs=1 after a {prompt_len}-token prefill",
+                   "kv_length": f"{prompt_len}..{prompt_len + args.warmup + args.steps}",
+                   "host": "whole host CPU: OpenMP threads = os.cpu_count()",
                    "cache_flush": "weights 3.8 GB > L2"},
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
                          "sample": f"{args.steps} decode tokens after {args.warmup} warm-up, "
@@ -311,6 +322,8 @@ def run_reference_workload(args, rank):
     from minq_b200 import synth
     from dataclasses import replace
     K, W = max(1, min(args.steps, 3)), max(0, min(args.warmup, 1))
+    # torchrun sets OMP_NUM_THREADS=1: the arm uses every host core
+    orc.set_threads(os.cpu_count() or 1)
     cores = orc.max_threads()
     if args.workload in (TP_WORKLOAD, BATCH_WORKLOAD):
         tp = args.workload == TP_WORKLOAD
@@ -406,7 +419,7 @@ def run_minq(args, world, rank, local):
     if args.layers:
         cfg0 = replace(cfg0, n_layers=args.layers)
     K, W = args.steps, args.warmup
-    max_seq = prompt_len + W + 2 * K + 3 * min(K, 16) + 32
+    max_seq = prompt_len + W + 2 * K + 3 * min(K, 16) + PARITY_TOKENS + 40
     cfg = replace(cfg0, max_seq_len=max_seq)
     model = build_model(mq, synth, cfg, qk_norm, tied, args.seed + rank)
     cache = model.new_cache()
@@ -477,6 +490,26 @@ def run_minq(args, world, rank, local):
     ms_e2e_max = max_over_ranks(world, ms_e2e)
     e2e_value = world * K / (ms_e2e_max / 1000.0)
 
+    # ---- parity state (rank 0, N=1): the cache after the timed and e2e
+    # steps, then PARITY_TOKENS greedy tokens decoded from it on the GPU
+    # (decode megakernel through minq_forward); the oracle later decodes from
+    # a copy of the same state and the two token streams are compared ----
+    par_state = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        n_pos = cache.len
+        kvd = cfg.n_kv_heads * cfg.head_dim
+        kall = np.empty((cfg.n_layers, n_pos, kvd), np.float32)
+        vall = np.empty((cfg.n_layers, n_pos, kvd), np.float32)
+        for li in range(cfg.n_layers):
+            kall[li], vall[li] = cache.read(li, 0, n_pos)
+        start = int(h_tok[0])
+        gpu_toks = []
+        tok = start
+        for _ in range(PARITY_TOKENS):
+            tok = model.forward_argmax([tok], cache)
+            gpu_toks.append(int(tok))
+        par_state = (n_pos, kall, vall, start, gpu_toks)
+
     # ---- per-kernel timing pass (same loop launched eagerly, events around
     # each launch of one kernel family) ----
     model.set_graphs(False)
@@ -535,38 +568,52 @@ def run_minq(args, world, rank, local):
                             if dom in NCU_TRAFFIC_RATIO else None),
                 "per_launch_bytes": d["bytes"] / d["launches"], "avg_launch_us": d["avg_us"]}
 
-    # ---- CPU baseline (rank 0, N=1): oracle continues the same sequence ----
+    # ---- CPU baseline (rank 0, N=1): the oracle continues the same sequence
+    # from the same cache state; its tokens are the parity record ----
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    parity = None
+    if par_state is not None:
         try:
             from oracle import oracle as orc
-            n_pos = cache.len
+            orc.set_threads(os.cpu_count() or 1)
+            n_pos, kall, vall, start, gpu_toks = par_state
             om = cpu_model(orc, synth, replace(cfg, max_seq_len=n_pos + 256), qk_norm, tied,
                            args.seed + rank)
             oc = om.new_cache()
-            kvd = cfg.n_kv_heads * cfg.head_dim
-            kall = np.empty((cfg.n_layers, n_pos, kvd), np.float32)
-            vall = np.empty((cfg.n_layers, n_pos, kvd), np.float32)
-            for li in range(cfg.n_layers):
-                kall[li], vall[li] = cache.read(li, 0, n_pos)
             oc.fill(kall, vall)
             del kall, vall
-            n, el = time_cpu_decode(orc, om, oc, int(h_tok[0]), 3, args.cpu_seconds)
+            par_state = None
+            ref_toks = []
+            tok = start
+            t0 = time.perf_counter()
+            while True:
+                tok = orc.argmax(om.forward([tok], oc))
+                ref_toks.append(int(tok))
+                el = time.perf_counter() - t0
+                if len(ref_toks) >= PARITY_TOKENS or (len(ref_toks) >= 32 and el >= args.cpu_seconds):
+                    break
+            n = len(ref_toks)
             cpu = {"value": n / el, "unit": "tok/s", "cores": orc.max_threads(), "kind": "port",
                    "sample": f"{n} greedy decode tokens of the same model from the same "
                              f"{n_pos}-position cache state, {el:.1f} s"}
+            first = next((i for i, (a, b) in enumerate(zip(gpu_toks, ref_toks)) if a != b), None)
+            parity = {"tokens": n, "match": first is None, "first_mismatch": first,
+                      "from": f"the GPU's cache after prefill + timed steps ({n_pos} positions)",
+                      "gpu": "decode megakernel (minq_forward)", "oracle": "forward_token + argmax"}
             del om, oc
         except Exception as e:  # the baseline must not sink the GPU number
             cpu = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
                    "sample": f"failed: {type(e).__name__}: {e}"}
+            parity = {"tokens": 0, "match": None, "first_mismatch": None,
+                      "error": f"{type(e).__name__}: {e}"}
 
     if rank == 0:
         line = {
             "metric": "decode tok/s", "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": K, "warmup": W, "ms_per_step": ms_max / K, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"{args.workload} decode bs=1 after a {prompt_len}-token "
-                                   f"prefill (KV length {prompt_len}..{prompt_len + W + K})",
+            "config": {"workload": f"{args.workload} decode bs=1 after a {prompt_len}-token prefill",
+                       "kv_length": f"{prompt_len}..{prompt_len + W + K}",
                        "model": arch, "layers": cfg.n_layers, "quant": cfg.dtype, "global_batch": world,
                        "parallelism": f"replicas x{world}",
                        "cache_flush": "inputs > L2: 3.8 GB of weights streamed per step"
@@ -581,21 +628,40 @@ def run_minq(args, world, rank, local):
             "roofline": roof,
             "kernels": fams,
             "cpu_baseline": cpu,
+            "parity": parity,
             "clocks": clk,
         }
-        print(json.dumps(line), flush=True)
     del cache, model
+    torch.cuda.empty_cache()
+    # ---- sub-records of the partitioned workloads at the same N: the
+    # LLaMA-3-8B batch of 64 sequences data-sharded over the ranks, and the
+    # long-context Qwen3-4B Q8_0 decode tensor-parallel over them (1 GPU: the
+    # decode megakernel), each with its own clock and roofline ----
+    if not args.no_sub_records and args.workload == "qwen3-4b-q4_0" and not args.layers:
+        bline = run_batch(args, world, rank, local, steps=16, warmup=4, emit=False)
+        tline = run_tp(args, world, rank, local, steps=16, warmup=4, emit=False)
+        tpar = tp_parity(world, rank, local) if world > 1 else None
+        if rank == 0:
+            line["batched"] = bline
+            if tline is not None:
+                tline["parity"] = tpar
+            line["tp"] = tline
+    if rank == 0:
+        print(json.dumps(line), flush=True)
 
 
-def run_tp(args, world, rank, local):
+def run_tp(args, world, rank, local, steps=None, warmup=None, emit=True):
     """One greedy sequence of the long-context workload, tensor-parallel over
-    the `world` ranks (single GPU: the decode megakernel)."""
+    the `world` ranks (single GPU: the decode megakernel). Returns rank 0's
+    JSON line (printed when `emit`)."""
     import torch
     import minq_b200 as mq
     from minq_b200 import synth
     from dataclasses import replace
     torch.cuda.set_device(local)
-    ctx, K, W = 32768, args.steps, args.warmup
+    ctx = 32768
+    K = steps if steps is not None else args.steps
+    W = warmup if warmup is not None else args.warmup
     cfg0, qk_norm, tied = synth.ARCH["qwen3-4b"]
     cfg = replace(cfg0, dtype="q8_0", max_seq_len=ctx + W + 2 * K + 16)
     model = build_model(mq, synth, cfg, qk_norm, tied, args.seed)  # every rank: the same weights
@@ -663,8 +729,12 @@ def run_tp(args, world, rank, local):
     per_gpu = (model.weight_bytes - lm) / world + lm + \
         2 * 4 * cfg.n_kv_heads * cfg.head_dim * (ctx + W + K / 2) * cfg.n_layers / world
     gbs = per_gpu / (ms_max / K * 1e-3) / 1e9
+    del cache, model
+    torch.cuda.empty_cache()
+    ar = allreduce_cost(world, cfg) if world > 1 else None
+    line = None
     if rank == 0:
-        print(json.dumps({
+        line = {
             "metric": "decode tok/s", "value": K / (ms_max / 1000.0), "unit": "tok/s",
             "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_max / K,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
@@ -679,23 +749,107 @@ def run_tp(args, world, rank, local):
             "roofline": {"bound": "hbm", "kernel": "decode step (per GPU)", "achieved": gbs,
                          "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                          "traffic": None, "per_launch_bytes": per_gpu},
+            "allreduce": ar,
             "cpu_baseline": None,
             "clocks": clk,
-        }), flush=True)
+        }
+        if emit:
+            print(json.dumps(line), flush=True)
+    return line
+
+
+def allreduce_cost(world, cfg):
+    """Device time of the step's collective, measured beside it: 2 all-reduces
+    of hidden_size f32 per layer (after o_proj and down_proj) as NCCL
+    all-reduces of the same size over the same GPUs (torch's communicator),
+    1000 back to back between CUDA events, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    x = torch.ones(cfg.hidden_size, dtype=torch.float32, device="cuda")
+    for _ in range(50):
+        dist.all_reduce(x)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 1000
+    e0.record()
+    for _ in range(n):
+        dist.all_reduce(x)
+    e1.record()
+    torch.cuda.synchronize()
+    us = max_over_ranks(world, 1000.0 * e0.elapsed_time(e1) / n)
+    per_tok = 2 * cfg.n_layers
+    return {"per_allreduce_us": us, "per_token": per_tok, "us_per_token": us * per_tok,
+            "bytes": 4 * cfg.hidden_size,
+            "how": "NCCL all-reduce of hidden_size f32 on the same GPUs, 1000 back to back"}
+
+
+# A model small enough for the oracle whose heads and intermediate rows split
+# over 2, 4 or 8 ranks (tensor-parallel parity inside the scaling run).
+TP_PARITY_CFG = dict(hidden_size=512, intermediate_size=1024, n_layers=2, n_heads=16,
+                     n_kv_heads=8, head_dim=64, vocab_size=300, max_seq_len=64, rope_theta=1e6,
+                     rms_norm_eps=1e-6, has_qkv_bias=True, dtype="q8_0")
+TP_PARITY_PROMPT = [5, 17, 230, 41, 99, 7]
+
+
+def tp_parity(world, rank, local):
+    """Tensor-parallel decode over the ranks of a 2-layer Q8_0 model with
+    q|k|v bias against the oracle (rank 0): last-prompt logits max-abs < 1e-3
+    and 9 greedy tokens identical (model.rs:932-940 tolerance)."""
+    import torch
+    import torch.distributed as dist
+    import minq_b200 as mq
+    from minq_b200 import synth
+    from minq_b200.minq_format import ModelConfig, quantize_tensor_rule
+    from oracle import oracle as orc
+    cfg = ModelConfig(**TP_PARITY_CFG)
+    recs = []
+    for n, t, sh, d in synth.random_model_records(cfg, 31, qk_norm=True, with_bias=True):
+        if n == "lm_head.weight":
+            continue
+        recs.append((n, 1, sh, orc.quantize(1, d)) if quantize_tensor_rule(n, sh) else (n, t, sh, d))
+    model = mq.Model.from_tensors(cfg, recs)
+    uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+    if rank == 0:
+        uid.copy_(torch.frombuffer(bytearray(mq.tp_unique_id()), dtype=torch.uint8))
+    dist.broadcast(uid, 0)
+    model.tp_init(rank, world, bytes(uid.cpu().numpy().tobytes()))
+    cache = model.new_cache()
+    tok, logits = model.forward_argmax(TP_PARITY_PROMPT, cache, logits=True)
+    toks = [tok]
+    for _ in range(8):
+        toks.append(model.forward_argmax([toks[-1]], cache))
+    torch.cuda.synchronize()
     del cache, model
+    res = None
+    if rank == 0:
+        om = orc.Model.from_tensors(TP_PARITY_CFG, {n: (t, sh, d) for n, t, sh, d in recs})
+        ref = om.forward(TP_PARITY_PROMPT, om.new_cache())
+        ref_toks, _ = orc.greedy_generate(om, TP_PARITY_PROMPT, 9)
+        err = float(np.abs(np.asarray(logits) - ref).max())
+        first = next((i for i, (a, b) in enumerate(zip(toks, ref_toks)) if a != b), None)
+        res = {"ranks": world, "logits_max_abs": err, "tokens": len(toks),
+               "tokens_match": toks == list(ref_toks), "first_mismatch": first,
+               "ok": bool(err < 1e-3 and toks == list(ref_toks)),
+               "model": "2 layers, hidden 512, 16/8 heads, hd 64, Q8_0 + q|k|v bias"}
+    dist.barrier()
+    return res
 
 
-def run_batch(args, world, rank, local):
+def run_batch(args, world, rank, local, steps=None, warmup=None, emit=True):
     """64 independent greedy sequences of the LLaMA-3-8B shape in Q4_0, 64 /
     world per rank (no collective): the prompts go through batched steps
     (one token of every sequence per step), then batched decode steps with
-    each step's argmax fed back on the device."""
+    each step's argmax fed back on the device. Returns rank 0's JSON line
+    (printed when `emit`)."""
     import torch
     import minq_b200 as mq
     from minq_b200 import synth
     from dataclasses import replace
     torch.cuda.set_device(local)
-    total, K, W = 64, args.steps, args.warmup
+    total = 64
+    K = steps if steps is not None else args.steps
+    W = warmup if warmup is not None else args.warmup
     prompt = args.prompt or 512
     if total % world:
         raise SystemExit(f"{BATCH_WORKLOAD}: 64 sequences do not split over {world} ranks")
@@ -705,6 +859,7 @@ def run_batch(args, world, rank, local):
         cfg0 = replace(cfg0, n_layers=args.layers)
     cfg = replace(cfg0, max_seq_len=prompt + W + 2 * K + 16)
     model = build_model(mq, synth, cfg, qk_norm, tied, args.seed)
+    weight_bytes = model.weight_bytes
     cache = model.new_cache(batch=B)
     rng = np.random.default_rng(args.seed + 100 + rank)
     prompts = rng.integers(0, cfg.vocab_size, (B, prompt))
@@ -762,8 +917,20 @@ def run_batch(args, world, rank, local):
     flops = 2.0 * params * B
     tfs = flops / (ms_max / K * 1e-3) / 1e12
     peak = peaks.get("bf16_tflops") or 1590.0
+    hbm_peak = peaks.get("hbm_gbs") or 6650.0
+    kv_len = prompt + W + (K - 1) / 2.0
+    step_bytes = float(weight_bytes) + B * 2 * 4 * cfg.n_kv_heads * hd * kv_len * cfg.n_layers
+    gbs = step_bytes / (ms_max / K * 1e-3) / 1e9
+    roof = {"bound": "hbm", "kernel": "batched step (per GPU)", "achieved": gbs,
+            "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak, "traffic": None,
+            "per_step_bytes": step_bytes,
+            "note": "weights once per step + every sequence's K/V history; the tensor-core "
+                    "view of the same step is roofline_tensor"}
+    del cache, model
+    torch.cuda.empty_cache()
+    line = None
     if rank == 0:
-        print(json.dumps({
+        line = {
             "metric": "decode tok/s (batched)", "value": total * K / (ms_max / 1000.0),
             "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "strong",
@@ -779,13 +946,15 @@ def run_batch(args, world, rank, local):
             "prefill": {"tokens": total * prompt, "tok_s": total * prompt / prefill_s,
                         "mode": "batched steps, one prompt token of every sequence per step"},
             "gpu_launches": int(launches_per_step * K),
-            "roofline": {"bound": "tensor" if B >= 16 else "hbm", "kernel": "batched step (per GPU)",
-                         "achieved": tfs, "peak": peak, "unit": "TFLOP/s", "frac": tfs / peak,
-                         "traffic": None, "per_launch_flops": flops},
+            "roofline": roof,
+            "roofline_tensor": {"achieved": tfs, "peak": peak, "unit": "TFLOP/s",
+                                "frac": tfs / peak, "per_step_flops": flops},
             "cpu_baseline": None,
             "clocks": clk,
-        }), flush=True)
-    del cache, model
+        }
+        if emit:
+            print(json.dumps(line), flush=True)
+    return line
 
 
 def _ppl_flops(cfg, n_pos, n_scored, context):

@@ -6,9 +6,37 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <vector>
+
 #include "../../include/minq_cuda.h"
 
 namespace minq {
+
+// tp_allreduce.cu: one-shot all-reduce of the residual stream over the
+// tensor-parallel ranks through NVLink peer memory (receive buffers mapped
+// by CUDA IPC; see the file's header comment).
+struct TpAr {
+  bool on = false;
+  int world = 1, rank = 0, sites = 0, H = 0, ncta = 0;
+  char* base = nullptr;                 // this rank's buffer (receive slots, then flags)
+  float* recv = nullptr;                // [sites][world][H]
+  int* flag = nullptr;                  // [sites][world][ncta]
+  float** peer_recv = nullptr;          // device array [world]: every rank's receive slots
+  int** peer_flag = nullptr;            // device array [world]: every rank's flags
+  unsigned long long* step = nullptr;   // device token counter (the epoch)
+  std::vector<void*> opened;            // IPC mappings of other processes' buffers
+};
+// Whether the peer path is wanted (MINQ_TP_NCCL=1 keeps the NCCL all-reduce).
+bool tp_ar_wanted();
+// Collective over the ranks of `nccl_comm`: allocate and map the buffers;
+// ar->on stays false (the NCCL path) when any rank cannot map its peers.
+minq_status tp_ar_setup(TpAr* ar, int rank, int world, int H, int sites, void* nccl_comm,
+                        cudaStream_t s);
+void tp_ar_release(TpAr* ar);
+// x = sum over the ranks of x, all-reduce number `site` of the token.
+minq_status launch_tp_allreduce(const TpAr& ar, float* x, int site, cudaStream_t s);
+// The token's all-reduces are done: advance the epoch.
+minq_status launch_tp_ar_advance(const TpAr& ar, cudaStream_t s);
 
 // quant.cu
 minq_status launch_quantize(int dtype, const float* x, size_t n, void* out, cudaStream_t s);

@@ -78,6 +78,7 @@ struct minq_model {
   // intermediate rows; the full counts on a single GPU
   int tp_rank = 0, tp_world = 1;
   void* tp_comm = nullptr;  // ncclComm_t
+  minq::TpAr tpar;          // peer-memory all-reduce (NCCL when off)
   int nh_l = 0, nkv_l = 0;
   uint64_t I_l = 0;
   cudaStream_t stream = nullptr;
@@ -536,8 +537,10 @@ minq_status linear(minq_model* m, const DevLinear& l, const float* x, const floa
 
 }  // namespace
 
-// x = sum over the tensor-parallel ranks of x (in place, on the model stream).
-static minq_status tp_allreduce_x(minq_model* m) {
+// x = sum over the tensor-parallel ranks of x (in place, on the model
+// stream); `site` numbers the all-reduce within the token (2 per layer).
+static minq_status tp_allreduce_x(minq_model* m, int site) {
+  if (m->tpar.on) return launch_tp_allreduce(m->tpar, m->x, site, m->stream);
   const NcclApi& nc = nccl_api();
   const ncclResult_t r = nc.AllReduce(m->x, m->x, m->cfg.hidden_size, ncclFloat, ncclSum,
                                       static_cast<ncclComm_t>(m->tp_comm), m->stream);
@@ -587,7 +590,7 @@ minq_status forward_token(minq_model* m, minq_cache* c, const uint32_t* d_tok, s
                               head_stride, pos_stride, m->att, c->ws, c->ws_bytes, s, dpos,
                               (int)c->max_seq));
     MINQ_TRY(linear(m, L.o, m->att, nullptr, nullptr, res, m->x));  // x += o
-    if (tp) MINQ_TRY(tp_allreduce_x(m));
+    if (tp) MINQ_TRY(tp_allreduce_x(m, (int)(2 * li)));
     // MLP sub-layer: h = silu(gate(rmsnorm(x))) * up(rmsnorm(x)); x += down(h)
     if (L.gate.tag != MINQ_F32 && L.gate.tag == L.up.tag) {
       MINQ_TRY(launch_qmatvec(L.gate.tag, L.gate.ptr, L.up.ptr, I, H, m->x, L.ffn_norm, eps,
@@ -599,8 +602,9 @@ minq_status forward_token(minq_model* m, minq_cache* c, const uint32_t* d_tok, s
       MINQ_TRY(launch_swiglu(m->gbuf, m->ubuf, m->hbuf, I, s));
     }
     MINQ_TRY(linear(m, L.down, m->hbuf, nullptr, nullptr, res, m->x));  // x += down
-    if (tp) MINQ_TRY(tp_allreduce_x(m));
+    if (tp) MINQ_TRY(tp_allreduce_x(m, (int)(2 * li + 1)));
   }
+  if (tp && m->tpar.on) MINQ_TRY(launch_tp_ar_advance(m->tpar, s));
   if (want_logits) {
     const uint64_t V = cfg.vocab_size;
     if (m->lm_head.tag == MINQ_F32) {
@@ -1032,6 +1036,7 @@ void minq_model_free(minq_model* m) {
   if (!m) return;
   cudaSetDevice(m->device);
   if (m->stream) cudaStreamSynchronize(m->stream);
+  minq::tp_ar_release(&m->tpar);
   if (m->tp_comm) nccl_api().CommDestroy(static_cast<ncclComm_t>(m->tp_comm));
   for (void* p : m->allocs) cudaFree(p);
   if (m->stream) cudaStreamDestroy(m->stream);
@@ -1163,6 +1168,9 @@ minq_status minq_tp_init(minq_model* m, int rank, int world, const void* unique_
     }
   }
   MINQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  if (tp_ar_wanted())
+    MINQ_TRY(tp_ar_setup(&m->tpar, rank, world, (int)c.hidden_size, (int)(2 * c.n_layers), comm,
+                         m->stream));
   m->tp_comm = comm;
   m->tp_rank = rank;
   m->tp_world = world;

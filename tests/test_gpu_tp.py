@@ -1,8 +1,9 @@
 """Tensor-parallel decode (minq_tp_init: q|k|v rows and o_proj columns split
 by head, gate/up rows and down_proj columns split by intermediate row, one
-NCCL all-reduce after o_proj and after down_proj) on 2 GPUs, one process per
-GPU, against the CPU oracle: logits max-abs < 1e-3, greedy tokens identical.
-Needs two GPUs; skipped on one."""
+all-reduce after o_proj and after down_proj) on 2 GPUs, one process per GPU,
+against the CPU oracle: logits max-abs < 1e-3, greedy tokens identical. Both
+all-reduce paths: the one-shot peer-memory kernel (default) and NCCL
+(MINQ_TP_NCCL=1). Needs two GPUs; skipped on one."""
 import multiprocessing as mp
 
 import numpy as np
@@ -29,8 +30,10 @@ def _records(orc):
     return cfg, out
 
 
-def _worker(rank, world, uid, q):
+def _worker(rank, world, uid, q, nccl):
     try:
+        import os
+        os.environ["MINQ_TP_NCCL"] = "1" if nccl else "0"
         import torch
         torch.cuda.set_device(rank)
         import minq_b200 as mq
@@ -48,7 +51,8 @@ def _worker(rank, world, uid, q):
         q.put((rank, None, None, repr(e)))
 
 
-def test_tensor_parallel_two_gpus_matches_oracle(orc):
+@pytest.mark.parametrize("nccl", [False, True], ids=["peer_allreduce", "nccl_allreduce"])
+def test_tensor_parallel_two_gpus_matches_oracle(orc, nccl):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -56,7 +60,7 @@ def test_tensor_parallel_two_gpus_matches_oracle(orc):
     uid = mq.tp_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, uid, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, uid, q, nccl)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}

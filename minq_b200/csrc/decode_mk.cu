@@ -498,16 +498,112 @@ __device__ bool mk_grid_sync(const MkParams& p, unsigned long long target, int* 
   return *reinterpret_cast<volatile int*>(flag) != 0;
 }
 
+// The residual stream's (value, epoch) pairs (MkParams::xr_*): one 8-byte
+// store per row, so a reader never sees a value without its epoch.
+__device__ __forceinline__ void mk_st_pair(uint2* dst, float v, unsigned ep) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(dst), "r"(__float_as_uint(v)),
+               "r"(ep)
+               : "memory");
+}
+__device__ __forceinline__ uint4 mk_ld_pairs2(const uint2* src) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(src)
+               : "memory");
+  return v;
+}
+
+// Give up a wait: the device status word and the abort flag.
+__device__ __forceinline__ bool mk_wait_expired(const MkParams& p, uint64_t t0) {
+  if (*reinterpret_cast<volatile int*>(p.abort_flag)) return true;
+  if (global_timer_ns() - t0 > kWaitLimitNs) {
+    atomicOr(p.status, kDeviceTimeout);
+    atomicExch(p.abort_flag, 1);
+    return true;
+  }
+  return false;
+}
+
+// x[i .. i + 7] of an exchange site (src = slot 0 at element i, slots H
+// apart): every pair of the nsum slots is waited for until it carries epoch
+// ep (bounded), then the values are summed over the slots in rank order.
+template <int NW>
+__device__ __forceinline__ void mk_ld8_site(const MkParams& p, const uint2* src, unsigned ep,
+                                            float4& a, float4& b) {
+#pragma unroll 1
+  for (int q = 0; q < NW; ++q) {
+    const uint2* e = src + (size_t)q * p.H;
+    uint4 w0 = mk_ld_pairs2(e), w1 = mk_ld_pairs2(e + 2), w2 = mk_ld_pairs2(e + 4),
+          w3 = mk_ld_pairs2(e + 6);
+    if (((w0.y ^ ep) | (w0.w ^ ep) | (w1.y ^ ep) | (w1.w ^ ep) | (w2.y ^ ep) | (w2.w ^ ep) |
+         (w3.y ^ ep) | (w3.w ^ ep)) != 0u) {
+      const uint64_t t0 = global_timer_ns();
+      for (uint32_t n = 1;; ++n) {
+        w0 = mk_ld_pairs2(e);
+        w1 = mk_ld_pairs2(e + 2);
+        w2 = mk_ld_pairs2(e + 4);
+        w3 = mk_ld_pairs2(e + 6);
+        if (((w0.y ^ ep) | (w0.w ^ ep) | (w1.y ^ ep) | (w1.w ^ ep) | (w2.y ^ ep) | (w2.w ^ ep) |
+             (w3.y ^ ep) | (w3.w ^ ep)) == 0u)
+          break;
+        if ((n & 15) == 0 && mk_wait_expired(p, t0)) break;
+        __nanosleep(64);  // fewer polls of L2 while the rows arrive
+      }
+    }
+    const float4 ca = make_float4(__uint_as_float(w0.x), __uint_as_float(w0.z),
+                                  __uint_as_float(w1.x), __uint_as_float(w1.z));
+    const float4 cb = make_float4(__uint_as_float(w2.x), __uint_as_float(w2.z),
+                                  __uint_as_float(w3.x), __uint_as_float(w3.z));
+    if (q == 0) {
+      a = ca;
+      b = cb;
+    } else {
+      a.x += ca.x; a.y += ca.y; a.z += ca.z; a.w += ca.w;
+      b.x += cb.x; b.y += cb.y; b.z += cb.z; b.w += cb.w;
+    }
+  }
+}
+
+// x[i] of an exchange site (src = slot 0 at element i), as mk_ld8_site.
+template <int NW>
+__device__ __forceinline__ float mk_ld1_site(const MkParams& p, const uint2* src, unsigned ep) {
+  float a = 0.0f;
+#pragma unroll 1
+  for (int q = 0; q < NW; ++q) {
+    const uint2* e = src + (size_t)q * p.H;
+    uint2 w;
+    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(w.x), "=r"(w.y) : "l"(e) : "memory");
+    if (w.y != ep) {
+      const uint64_t t0 = global_timer_ns();
+      for (uint32_t n = 1;; ++n) {
+        asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(w.x), "=r"(w.y) : "l"(e) : "memory");
+        if (w.y == ep) break;
+        if ((n & 15) == 0 && mk_wait_expired(p, t0)) break;
+      }
+    }
+    a = q == 0 ? __uint_as_float(w.x) : a + __uint_as_float(w.x);
+  }
+  return a;
+}
+
 // Stage the lm_head input in shared memory: xs = rmsnorm(src) * gain
-// (tensor.rs:219-227), n floats, n % 8 == 0.
-__device__ void mk_stage_x(const MkParams& p, float* xs, const float* src, int n,
-                           const float* gain, float* misc) {
+// (tensor.rs:219-227), n floats, n % 8 == 0; src is the last exchange site.
+template <int NW>
+__device__ void mk_stage_x(const MkParams& p, float* xs, const float* x, const uint2* site,
+                           unsigned ep, int n, const float* gain, float* misc) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int ng = n >> 3;
   float4* xs4 = reinterpret_cast<float4*>(xs);
   float ss = 0.0f;
   for (int gi = tid; gi < ng; gi += kMkConsumers) {
-    const float4 a = ldcg4(src + 8 * gi), b = ldcg4(src + 8 * gi + 4);
+    float4 a, b;
+    if constexpr (NW == 1) {
+      a = ldcg4(x + 8 * gi);
+      b = ldcg4(x + 8 * gi + 4);
+    } else {
+      mk_ld8_site<NW>(p, site + 8 * gi, ep, a, b);
+    }
     xs4[2 * gi] = a;
     xs4[2 * gi + 1] = b;
     ss = fmaf(a.x, a.x, ss);
@@ -539,7 +635,9 @@ __device__ void mk_stage_x(const MkParams& p, float* xs, const float* src, int n
 }
 
 // Stage a projection input as fixed-point planes: v = src (n floats, n % 32
-// == 0), times gain when gain is set, then per 32-column block b:
+// == 0), or, with `site`, the residual stream of an exchange site (the sum
+// of its nsum slots once they carry epoch ep), times gain when gain is set,
+// then per 32-column block b:
 // e = exponent of max|v| (2^(e-1) <= max < 2^e), m = rint(v * 2^(kMkFx - e))
 // (|m| <= 2^kMkFx), split into kMkNP signed base-256 digits
 // (m = sum_q 256^q d_q, d_q in [-128, 127]). xp gets kMkRecW words per block
@@ -550,9 +648,10 @@ __device__ void mk_stage_x(const MkParams& p, float* xs, const float* src, int n
 // in misc[w]: RMSNorm (tensor.rs:219-227) is linear in the input, so its
 // scale 1 / rms multiplies each row's sum in the projection's epilogue and
 // the planes need not wait for the reduction.
-template <int DT>
+template <int DT, int NW>
 __device__ void mk_stage_planes(const MkParams& p, uint32_t* xp, float* xsb, const float* src,
-                                int n, const float* gain, float* misc) {
+                                const uint2* site, unsigned ep, int n, const float* gain,
+                                float* misc) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int ng = n >> 3;
   const float4 zero = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -562,8 +661,15 @@ __device__ void mk_stage_planes(const MkParams& p, uint32_t* xp, float* xsb, con
 #pragma unroll
   for (int r = 0; r < MR; ++r) {
     const int gi = tid + r * kMkConsumers;
-    va[r] = gi < ng ? ldcg4(src + 8 * gi) : zero;
-    vb[r] = gi < ng ? ldcg4(src + 8 * gi + 4) : zero;
+    if (gi >= ng) {
+      va[r] = zero;
+      vb[r] = zero;
+    } else if (NW > 1 && site) {
+      mk_ld8_site<NW>(p, site + 8 * gi, ep, va[r], vb[r]);
+    } else {
+      va[r] = ldcg4(src + 8 * gi);
+      vb[r] = ldcg4(src + 8 * gi + 4);
+    }
   }
   if (gain) {
     float ss = 0.0f;
@@ -1134,10 +1240,10 @@ __device__ void mk_lm_head(const MkParams& p, const float* xs, unsigned long lon
   }
 }
 
-template <int DT>
+template <int DT, int NW>
 __device__ void mk_consumers(const MkParams& p, unsigned char* sm, MkFeed& f, const MkCta* cta,
-                             int L,
-                             uint32_t tok, unsigned long long bbase, unsigned hbase) {
+                             int L, uint32_t tok, unsigned long long bbase, unsigned hbase,
+                             unsigned ep) {
   float* misc = reinterpret_cast<float*>(sm + kMkMiscOff);         // [0..32]: reductions
   int* misc_i = reinterpret_cast<int*>(sm + kMkMiscOff + 160);     // flags
   unsigned long long* best_s = reinterpret_cast<unsigned long long*>(sm + kMkMiscOff + 256);
@@ -1157,10 +1263,22 @@ __device__ void mk_consumers(const MkParams& p, unsigned char* sm, MkFeed& f, co
     for (int i = threadIdx.x; i < 2 * half; i += kMkConsumers)
       rope_cs[i] = i < half ? p.rope_cos[(size_t)L * half + i] : p.rope_sin[(size_t)L * half + i - half];
   }
+  // One GPU (NW == 1): x in p.x, a grid barrier after every phase. Tensor
+  // parallel (NW ranks): x in the exchange sites (see MkParams), whose
+  // epochs order o_proj / down_proj and their readers instead of a barrier
+  // (a barrier across GPUs costs system-scope fences and remote atomics).
+  const uint2* xsite = nullptr;  // tensor parallel: the residual stream's site (null: embedding)
+  auto site_of = [&](int st) { return p.xr_local + (size_t)st * NW * p.H; };
+  auto x_store = [&](int st, int row, float v) {
+    const size_t off = ((size_t)st * NW + p.tp_rank) * p.H + row;
+#pragma unroll
+    for (int q = 0; q < NW; ++q) mk_st_pair(p.xr_dst[q] + off, v, ep);
+  };
+  const bool add_res = NW == 1 || p.tp_rank == 0;
   for (int li = 0; li < p.n_layers && ok; ++li) {
     const MkLayerPtrs& lp = f.lps[li];
     // P1: q|k|v
-    mk_stage_planes<DT>(p, xp, xsb, xsrc, p.H, lp.attn_norm, misc);
+    mk_stage_planes<DT, NW>(p, xp, xsb, xsrc, xsite, ep, p.H, lp.attn_norm, misc);
     const float* bias = lp.bias_qkv;
     mk_consume_mat<DT, false>(
         p, p.qkv, xp, xsb, f, cta, L, red, it, misc, p.H,
@@ -1171,30 +1289,56 @@ __device__ void mk_consumers(const MkParams& p, unsigned char* sm, MkFeed& f, co
     if (p.hd == 128) mk_consume_attn<DT, 4>(p, li, L, hbase, xs, f, cta, rope_cs, misc_i, it);
     else mk_consume_attn<DT, 2>(p, li, L, hbase, xs, f, cta, rope_cs, misc_i, it);
     if (!(ok = barrier())) break;
-    // P3: x = x + W_o att
-    mk_stage_planes<DT>(p, xp, xsb, p.att, p.qd, nullptr, misc);
-    const float* res = xsrc;
+    // P3: x = x + W_o att (tensor parallel: this rank's partial sum, the
+    // residual from rank 0 only, into site 2 li of every rank)
+    mk_stage_planes<DT, 1>(p, xp, xsb, p.att, nullptr, ep, p.qd, nullptr, misc);
+    const uint2* rsite = xsite;
+    const float* rsrc = xsrc;
     mk_consume_mat<DT, false>(
-        p, p.o, xp, xsb, f, cta, L, red, it, nullptr, 0, [&](int row) { return ldcg(res + row); },
-        [&](int row, float v, float, float r) { p.x[row] = r + v; });
-    xsrc = p.x;
-    if (!(ok = barrier())) break;
+        p, p.o, xp, xsb, f, cta, L, red, it, nullptr, 0,
+        [&](int row) {
+          if constexpr (NW == 1) return ldcg(rsrc + row);
+          else {
+            if (!add_res) return 0.0f;
+            return rsite ? mk_ld1_site<NW>(p, rsite + row, ep) : ldcg(rsrc + row);
+          }
+        },
+        [&](int row, float v, float, float r) {
+          if constexpr (NW == 1) p.x[row] = r + v;
+          else x_store(2 * li, row, r + v);
+        });
+    const uint2* xo = NW == 1 ? nullptr : site_of(2 * li);
+    if constexpr (NW == 1) {
+      xsrc = p.x;
+      if (!(ok = barrier())) break;
+    }
     // P4: h = silu(gate) * up
-    mk_stage_planes<DT>(p, xp, xsb, p.x, p.H, lp.ffn_norm, misc);
+    mk_stage_planes<DT, NW>(p, xp, xsb, p.x, xo, ep, p.H, lp.ffn_norm, misc);
     mk_consume_mat<DT, true>(
         p, p.gu, xp, xsb, f, cta, L, red, it, misc, p.H, [&](int) { return 0.0f; },
         [&](int row, float g, float u, float) { p.h[row] = silu(g) * u; });
     if (!(ok = barrier())) break;
-    // P5: x = x + W_down h
-    mk_stage_planes<DT>(p, xp, xsb, p.h, p.I, nullptr, misc);
+    // P5: x = x + W_down h (tensor parallel: into site 2 li + 1)
+    mk_stage_planes<DT, 1>(p, xp, xsb, p.h, nullptr, ep, p.I, nullptr, misc);
     mk_consume_mat<DT, false>(
         p, p.down, xp, xsb, f, cta, L, red, it, nullptr, 0,
-        [&](int row) { return ldcg(p.x + row); },
-        [&](int row, float v, float, float r) { p.x[row] = r + v; });
-    if (!(ok = barrier())) break;
+        [&](int row) {
+          if constexpr (NW == 1) return ldcg(p.x + row);
+          else return add_res ? mk_ld1_site<NW>(p, xo + row, ep) : 0.0f;
+        },
+        [&](int row, float v, float, float r) {
+          if constexpr (NW == 1) p.x[row] = r + v;
+          else x_store(2 * li + 1, row, r + v);
+        });
+    if constexpr (NW == 1) {
+      if (!(ok = barrier())) break;
+    } else {
+      xsite = site_of(2 * li + 1);
+      ok = !*reinterpret_cast<volatile int*>(p.abort_flag);
+    }
   }
   if (ok && p.want_logits) {
-    mk_stage_x(p, xs, p.x, p.H, p.final_norm, misc);
+    mk_stage_x<NW>(p, xs, p.x, xsite, ep, p.H, p.final_norm, misc);
     mk_lm_head(p, xs, best_s);
     ok = barrier();
     if (ok && blockIdx.x == 0) {
@@ -1212,6 +1356,7 @@ __device__ void mk_consumers(const MkParams& p, unsigned char* sm, MkFeed& f, co
       }
     }
   }
+  if (NW > 1 && ok && blockIdx.x == 0 && threadIdx.x == 0) *p.xr_epoch = ep;
   if (ok && blockIdx.x == 0 && threadIdx.x == 0) {
     *p.d_pos = L + 1;
     *p.bar_base = bbase + (unsigned long long)nbar * G;
@@ -1219,13 +1364,14 @@ __device__ void mk_consumers(const MkParams& p, unsigned char* sm, MkFeed& f, co
   }
 }
 
-template <int DT>
+template <int DT, int NW>
 __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_constant__ MkParams p) {
   extern __shared__ __align__(128) unsigned char sm[];
   const int L = *reinterpret_cast<volatile const int*>(p.d_pos);
   const uint32_t tok = *reinterpret_cast<volatile const uint32_t*>(p.d_tok);
   const unsigned long long bbase = *reinterpret_cast<volatile const unsigned long long*>(p.bar_base);
   const unsigned hbase = *reinterpret_cast<volatile const unsigned*>(p.head_base);
+  const unsigned ep = NW > 1 ? *reinterpret_cast<volatile const unsigned*>(p.xr_epoch) + 1u : 0u;
   MkCta* cta = reinterpret_cast<MkCta*>(sm + kMkCtaOff);
   if (threadIdx.x == 0) mk_cta_plan<DT>(p, L, cta);
   __syncthreads();
@@ -1260,7 +1406,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     mk_producer<DT>(p, f, cta, L);
     return;
   }
-  mk_consumers<DT>(p, sm, f, cta, L, tok, bbase, hbase);
+  mk_consumers<DT, NW>(p, sm, f, cta, L, tok, bbase, hbase, ep);
 }
 
 // ---------------------------------------------------------------- host
@@ -1296,9 +1442,9 @@ size_t mk_smem_bytes(size_t scratch_bytes, int n_layers) {
   return total <= 227 * 1024 ? total : 0;
 }
 
-template <int DT>
+template <int DT, int NW>
 static minq_status mk_launch_inst(const MkParams& p, int grid, size_t smem, cudaStream_t s) {
-  auto k = decode_mk_kernel<DT>;
+  auto k = decode_mk_kernel<DT, NW>;
   MINQ_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(k), smem));
   int per_sm = 0;
   MINQ_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kMkThreads, smem));
@@ -1323,8 +1469,14 @@ static minq_status mk_launch_inst(const MkParams& p, int grid, size_t smem, cuda
 
 minq_status launch_decode_mk(const MkParams& p, int dtype, int grid, size_t smem,
                              cudaStream_t s) {
-  if (dtype == MINQ_Q8_0) return mk_launch_inst<MINQ_Q8_0>(p, grid, smem, s);
-  return mk_launch_inst<MINQ_Q4_0>(p, grid, smem, s);
+  const bool q8 = dtype == MINQ_Q8_0;
+  switch (p.tp_world) {
+    case 1: return q8 ? mk_launch_inst<MINQ_Q8_0, 1>(p, grid, smem, s) : mk_launch_inst<MINQ_Q4_0, 1>(p, grid, smem, s);
+    case 2: return q8 ? mk_launch_inst<MINQ_Q8_0, 2>(p, grid, smem, s) : mk_launch_inst<MINQ_Q4_0, 2>(p, grid, smem, s);
+    case 4: return q8 ? mk_launch_inst<MINQ_Q8_0, 4>(p, grid, smem, s) : mk_launch_inst<MINQ_Q4_0, 4>(p, grid, smem, s);
+    case 8: return q8 ? mk_launch_inst<MINQ_Q8_0, 8>(p, grid, smem, s) : mk_launch_inst<MINQ_Q4_0, 8>(p, grid, smem, s);
+    default: return fail(MINQ_ERR_ARG, "decode megakernel: 1, 2, 4 or 8 tensor-parallel ranks");
+  }
 }
 
 }  // namespace minq

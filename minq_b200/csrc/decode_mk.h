@@ -65,6 +65,17 @@ struct MkParams {
   int* abort_flag;             // set when any CTA gives up; every CTA stops
   int want_logits;
   int scratch_bytes;           // x / attention scratch in shared memory
+  // The residual stream after the o_proj and down_proj of every layer
+  // (exchange sites 2 li and 2 li + 1): [tp_world][H] pairs (value bits,
+  // epoch) per site, each row written by one 8-byte store into every rank's
+  // slots (tensor parallel: this rank's partial sum, rank 0 adding the
+  // residual; one GPU: the row itself). Readers wait until the pairs they
+  // need carry this launch's epoch and sum the slots in rank order, so no
+  // grid barrier follows o_proj or down_proj.
+  int tp_world, tp_rank;
+  uint2* const* xr_dst;        // [tp_world]: every rank's pair slots
+  const uint2* xr_local;       // this rank's slots [2 n_layers][tp_world][H]
+  unsigned* xr_epoch;          // launches so far; this launch's epoch is + 1
 };
 
 // The projection plan, or rows == 0 when the consumer's row sums (2 x halves

@@ -24,6 +24,7 @@ struct TpAr {
   float** peer_recv = nullptr;          // device array [world]: every rank's receive slots
   int** peer_flag = nullptr;            // device array [world]: every rank's flags
   unsigned long long* step = nullptr;   // device token counter (the epoch)
+  unsigned long long* ctr = nullptr;    // the decode megakernel's exchange epoch (low word)
   std::vector<void*> opened;            // IPC mappings of other processes' buffers
 };
 // Whether the peer path is wanted (MINQ_TP_NCCL=1 keeps the NCCL all-reduce).

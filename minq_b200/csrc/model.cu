@@ -116,6 +116,9 @@ struct minq_model {
     unsigned long long* argmax_part = nullptr;
     unsigned long long* bar = nullptr;  // [0] counter, [1] base
     int* abort_flag = nullptr;
+    uint2* xr = nullptr;       // residual stream exchange sites [2 n_layers][H] (one GPU)
+    uint2** xr_dst = nullptr;  // device array {xr}
+    unsigned* xr_epoch = nullptr;
   } mk;
 };
 
@@ -283,8 +286,10 @@ minq_status setup_megakernel(minq_model* m) {
   const char* env = std::getenv("MINQ_MEGAKERNEL");
   if (env && env[0] == '0') return MINQ_OK;
   const minq_config& c = m->cfg;
-  const uint64_t H = c.hidden_size, I = c.intermediate_size, hd = c.head_dim;
-  const uint64_t nh = c.n_heads, nkv = c.n_kv_heads, qd = nh * hd, kvd = nkv * hd;
+  // this rank's heads and intermediate rows (all of them on one GPU)
+  const uint64_t H = c.hidden_size, I = m->I_l, hd = c.head_dim;
+  const uint64_t nh = (uint64_t)m->nh_l, nkv = (uint64_t)m->nkv_l, qd = nh * hd, kvd = nkv * hd;
+  if (m->tp_world > 1 && !m->tpar.on) return MINQ_OK;  // the megakernel needs the peer slots
   if (c.n_layers == 0 || nkv == 0 || nh % nkv != 0) return MINQ_OK;
   const uint64_t G = nh / nkv;
   if ((hd != 64 && hd != 128) || G > 8) return MINQ_OK;
@@ -340,6 +345,15 @@ minq_status setup_megakernel(minq_model* m) {
   k.abort_flag = reinterpret_cast<int*>(k.head_ctr + nkv);             // 1
   k.head_base = reinterpret_cast<unsigned*>(k.abort_flag + 1);         // 1 (in the slack)
   MINQ_CUDA_TRY(cudaMemset(p, 0, nkv * 4 + 4 + 2 * 8 + (size_t)grid * 8 + 64));
+  // the residual stream's exchange sites (value, epoch pairs) and epoch
+  const size_t xr_bytes = 2 * nl * H * sizeof(uint2);
+  MINQ_TRY(dmalloc(m, &p, xr_bytes + 256));
+  MINQ_CUDA_TRY(cudaMemset(p, 0, xr_bytes + 256));
+  k.xr = static_cast<uint2*>(p);
+  k.xr_epoch = reinterpret_cast<unsigned*>(static_cast<char*>(p) + xr_bytes);
+  MINQ_TRY(dmalloc(m, &p, sizeof(uint2*)));
+  k.xr_dst = static_cast<uint2**>(p);
+  MINQ_CUDA_TRY(cudaMemcpy(k.xr_dst, &k.xr, sizeof(uint2*), cudaMemcpyHostToDevice));
   k.ok = true;
   return MINQ_OK;
 }
@@ -506,11 +520,11 @@ minq_status model_finish(minq_model* m) {
   MINQ_TRY(dmalloc(m, &p, m->d_tokens_cap * 4));
   m->d_tokens = static_cast<uint32_t*>(p);
   if (!device_status_word()) return fail(MINQ_ERR_CUDA, "cannot allocate the device status word");
-  if (m->shape_error.empty()) MINQ_TRY(setup_megakernel(m));
-  MINQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
   m->nh_l = (int)c.n_heads;
   m->nkv_l = (int)c.n_kv_heads;
   m->I_l = c.intermediate_size;
+  if (m->shape_error.empty()) MINQ_TRY(setup_megakernel(m));
+  MINQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
   m->finished = true;
   return MINQ_OK;
 }
@@ -834,9 +848,9 @@ static minq_status run_megakernel(minq_model* m, minq_cache* c, bool logits) {
   p.gu = k.gu;
   p.down = k.down;
   p.H = (int)cfg.hidden_size;
-  p.I = (int)cfg.intermediate_size;
-  p.nh = (int)cfg.n_heads;
-  p.nkv = (int)cfg.n_kv_heads;
+  p.I = (int)m->I_l;
+  p.nh = m->nh_l;
+  p.nkv = m->nkv_l;
   p.hd = (int)cfg.head_dim;
   p.G = p.nh / p.nkv;
   p.qd = p.nh * p.hd;
@@ -871,6 +885,17 @@ static minq_status run_megakernel(minq_model* m, minq_cache* c, bool logits) {
   p.abort_flag = k.abort_flag;
   p.want_logits = logits ? 1 : 0;
   p.scratch_bytes = k.scratch;
+  p.tp_world = m->tp_world;
+  p.tp_rank = m->tp_rank;
+  if (m->tp_world > 1) {  // every rank's exchange slots, mapped at minq_tp_init
+    p.xr_dst = reinterpret_cast<uint2* const*>(m->tpar.peer_recv);
+    p.xr_local = reinterpret_cast<const uint2*>(m->tpar.recv);
+    p.xr_epoch = reinterpret_cast<unsigned*>(m->tpar.ctr);
+  } else {
+    p.xr_dst = k.xr_dst;
+    p.xr_local = k.xr;
+    p.xr_epoch = k.xr_epoch;
+  }
   return launch_decode_mk(p, k.dtype, k.grid, k.smem, m->stream);
 }
 
@@ -881,6 +906,9 @@ static minq_status reset_megakernel(minq_model* m) {
   const size_t nkv = m->cfg.n_kv_heads;
   MINQ_CUDA_TRY(cudaMemsetAsync(k.bar, 0, nkv * 4 + 4 + 2 * 8 + (size_t)k.grid * 8 + 64,
                                 m->stream));
+  if (m->tp_world == 1 && k.xr)  // pairs of an aborted launch must not match the next epoch
+    MINQ_CUDA_TRY(cudaMemsetAsync(k.xr, 0, 2 * m->cfg.n_layers * m->cfg.hidden_size * sizeof(uint2) + 256,
+                                  m->stream));
   return MINQ_OK;
 }
 
@@ -1177,8 +1205,11 @@ minq_status minq_tp_init(minq_model* m, int rank, int world, const void* unique_
   m->nh_l = (int)nhl;
   m->nkv_l = (int)nkvl;
   m->I_l = Il;
-  m->mk.ok = false;  // the decode megakernel runs on one GPU; graph-captured
-                     // steps record the all-reduces with the kernels
+  // the decode megakernel runs the rank's slices when the peer all-reduce
+  // slots are mapped and the shapes fit it; otherwise the per-op step runs
+  // (graph-captured with its all-reduces)
+  m->mk.ok = false;
+  if (m->tpar.on) MINQ_TRY(setup_megakernel(m));
   return MINQ_OK;
 }
 

@@ -125,9 +125,13 @@ minq_status tp_ar_setup(TpAr* ar, int rank, int world, int H, int sites, void* n
   if (world < 2 || H % 4 != 0) return MINQ_OK;  // the NCCL path serves these
   const NcclApi& nc = nccl_api();
   const int ncta = (H + kArCols - 1) / kArCols;
-  const size_t recv_bytes = (size_t)sites * world * H * 4;
+  // 8 bytes per element: the per-op kernel's f32 slots use the first half,
+  // the decode megakernel's (value, epoch) pairs all of it
+  const size_t recv_bytes = (size_t)sites * world * H * 8;
   const size_t flag_bytes = (size_t)sites * world * ncta * 4;
-  const size_t bytes = ((recv_bytes + 255) & ~(size_t)255) + flag_bytes;
+  const size_t recv_pad = (recv_bytes + 255) & ~(size_t)255;
+  const size_t ctr_off = (recv_pad + flag_bytes + 255) & ~(size_t)255;
+  const size_t bytes = ctr_off + 256;  // + the decode megakernel's exchange epoch
   int dev = 0;
   MINQ_CUDA_TRY(cudaGetDevice(&dev));
   char* buf = nullptr;
@@ -136,7 +140,8 @@ minq_status tp_ar_setup(TpAr* ar, int rank, int world, int H, int sites, void* n
   MINQ_CUDA_TRY(cudaDeviceSynchronize());
   ar->base = buf;
   ar->recv = reinterpret_cast<float*>(buf);
-  ar->flag = reinterpret_cast<int*>(buf + ((recv_bytes + 255) & ~(size_t)255));
+  ar->flag = reinterpret_cast<int*>(buf + recv_pad);
+  ar->ctr = reinterpret_cast<unsigned long long*>(buf + ctr_off);
   // exchange (IPC handle, pid, pointer, device) with every rank: each rank
   // fills its own row, a byte-sum all-reduce gathers them
   ArPeerInfo mine{};
@@ -191,7 +196,7 @@ minq_status tp_ar_setup(TpAr* ar, int rank, int world, int H, int sites, void* n
     }
     if (pb) {
       precv[q] = reinterpret_cast<float*>(pb);
-      pflag[q] = reinterpret_cast<int*>(pb + ((recv_bytes + 255) & ~(size_t)255));
+      pflag[q] = reinterpret_cast<int*>(pb + recv_pad);
     }
   }
   // every rank takes the peer path or none does

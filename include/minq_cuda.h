@@ -269,6 +269,8 @@ minq_status minq_cache_read(const minq_cache* c, size_t layer, size_t start, siz
 minq_status minq_cache_write_device(minq_cache* c, size_t layer, size_t start, size_t n,
                                     const float* d_k, const float* d_v);
 minq_status minq_cache_set_len(minq_cache* c, size_t len);
+/* Frees the cache. A model freed first releases the device memory of its
+ * caches still open; their handles then stay valid only for this call. */
 void minq_cache_free(minq_cache* c);
 
 /* Model::forward (model.rs:254-270): run `tokens` (host) through the model,
@@ -396,6 +398,15 @@ minq_status minq_generate_sampled(minq_model* m, minq_sampler* s, const uint32_t
 
 /* The model's CUDA stream (cudaStream_t as void*). */
 void* minq_model_stream(minq_model* m);
+
+/* Failure injection for tests (no reference counterpart): make a bounded
+ * device-side wait of the next decode-megakernel step run out by moving its
+ * target out of reach on the host. what = 0: the per-head attention merge
+ * counters; 1: the grid barrier. That step then returns MINQ_ERR_TIMEOUT
+ * after the wait limit (1 s) with the megakernel's barrier state reset, and
+ * later steps run normally (the cache of the failed step should be reset).
+ * MINQ_ERR_ARG when the model does not use the decode megakernel. */
+minq_status minq_debug_inject_timeout(minq_model* m, int what);
 
 #ifdef __cplusplus
 }

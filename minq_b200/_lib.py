@@ -122,6 +122,7 @@ SIGNATURES = {
     "minq_sampler_sample": (I, [P, P, S, P]),
     "minq_sampler_rng_u32": (I, [P, S, P]),
     "minq_generate_sampled": (I, [P, P, P, S, S, P, S, TOKEN_CB, P, P, C.POINTER(GenStats)]),
+    "minq_debug_inject_timeout": (I, [P, I]),
 }
 
 _lib = None

@@ -25,6 +25,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <set>
 #include <string>
 #include <vector>
 
@@ -86,6 +87,7 @@ struct minq_model {
   bool use_graphs = true;
   std::map<std::string, DevTensor> pending;
   std::vector<void*> allocs;
+  std::set<minq_cache*> caches;  // live caches: freed with the model if still open
   // assembled
   const float* embed = nullptr;
   std::vector<DevLayer> layers;
@@ -162,6 +164,24 @@ struct minq_cache {
   float* plog = nullptr;
   double* pnll = nullptr;
 };
+
+// The cache's device memory and graphs (its model's device current, stream idle).
+static void cache_release_device(minq_cache* c) {
+  for (cudaGraphExec_t g : c->step)
+    if (g) cudaGraphExecDestroy(g);
+  c->step[0] = c->step[1] = nullptr;
+  cudaFree(c->k);
+  cudaFree(c->v);
+  cudaFree(c->ws);
+  cudaFree(c->d_pos);
+  for (void* b : {(void*)c->bx, (void*)c->bqkv, (void*)c->bq, (void*)c->batt, (void*)c->bh,
+                  (void*)c->blog, (void*)c->bxn, (void*)c->bpart, (void*)c->btok,
+                  (void*)c->barg, (void*)c->px, (void*)c->pqkv, (void*)c->pq, (void*)c->patt,
+                  (void*)c->ph, (void*)c->pxn, (void*)c->ppart, c->pws, (void*)c->plog,
+                  (void*)c->pnll})
+    cudaFree(b);
+}
+
 
 namespace minq {
 
@@ -556,8 +576,10 @@ minq_status linear(minq_model* m, const DevLinear& l, const float* x, const floa
 static minq_status tp_allreduce_x(minq_model* m, int site) {
   if (m->tpar.on) return launch_tp_allreduce(m->tpar, m->x, site, m->stream);
   const NcclApi& nc = nccl_api();
-  const ncclResult_t r = nc.AllReduce(m->x, m->x, m->cfg.hidden_size, ncclFloat, ncclSum,
-                                      static_cast<ncclComm_t>(m->tp_comm), m->stream);
+  ncclResult_t r = nc.AllReduce(m->x, m->x, m->cfg.hidden_size, ncclFloat, ncclSum,
+                                static_cast<ncclComm_t>(m->tp_comm), m->stream);
+  r = nccl_settle(static_cast<ncclComm_t>(m->tp_comm), r,
+                  std::chrono::steady_clock::now() + std::chrono::seconds(30));
   if (r != ncclSuccess) return fail(MINQ_ERR_NCCL, std::string("ncclAllReduce: ") + nc.GetErrorString(r));
   return MINQ_OK;
 }
@@ -1060,10 +1082,36 @@ minq_status minq_model_set_graphs(minq_model* m, int enabled) {
 
 void* minq_model_stream(minq_model* m) { return m ? (void*)m->stream : nullptr; }
 
+minq_status minq_debug_inject_timeout(minq_model* m, int what) {
+  if (!m) return fail(MINQ_ERR_ARG, "null model");
+  auto& k = m->mk;
+  if (!k.ok) return fail(MINQ_ERR_ARG, "the decode megakernel is not in use for this model");
+  if (what != 0 && what != 1) return fail(MINQ_ERR_ARG, "what: 0 (head counters) or 1 (grid barrier)");
+  MINQ_CUDA_TRY(cudaSetDevice(m->device));
+  MINQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  if (what == 0) {  // the next launch's per-head merge targets lie 2^30 splits ahead
+    unsigned v = 0;
+    MINQ_CUDA_TRY(cudaMemcpy(&v, k.head_base, 4, cudaMemcpyDeviceToHost));
+    v += 1u << 30;
+    MINQ_CUDA_TRY(cudaMemcpy(k.head_base, &v, 4, cudaMemcpyHostToDevice));
+  } else {          // the next launch's grid-barrier targets lie 2^40 arrivals ahead
+    unsigned long long v = 0;
+    MINQ_CUDA_TRY(cudaMemcpy(&v, k.bar + 1, 8, cudaMemcpyDeviceToHost));
+    v += 1ull << 40;
+    MINQ_CUDA_TRY(cudaMemcpy(k.bar + 1, &v, 8, cudaMemcpyHostToDevice));
+  }
+  return MINQ_OK;
+}
+
 void minq_model_free(minq_model* m) {
   if (!m) return;
   cudaSetDevice(m->device);
   if (m->stream) cudaStreamSynchronize(m->stream);
+  for (minq_cache* c : m->caches) {  // caches still open: release them, keep the handles
+    cache_release_device(c);
+    c->m = nullptr;
+  }
+  m->caches.clear();
   minq::tp_ar_release(&m->tpar);
   if (m->tp_comm) nccl_api().CommDestroy(static_cast<ncclComm_t>(m->tp_comm));
   for (void* p : m->allocs) cudaFree(p);
@@ -1174,8 +1222,31 @@ minq_status minq_tp_init(minq_model* m, int rank, int world, const void* unique_
   ncclUniqueId id;
   std::memcpy(&id, unique_id, sizeof(id));
   ncclComm_t comm = nullptr;
-  const ncclResult_t r = nc.CommInitRank(&comm, world, id, rank);
-  if (r != ncclSuccess) return fail(MINQ_ERR_NCCL, std::string("ncclCommInitRank: ") + nc.GetErrorString(r));
+  // the ranks meet under a host deadline (MINQ_TP_INIT_TIMEOUT_S, default
+  // 120 s): a non-blocking communicator is polled and aborted when a rank
+  // never joins, so the call returns MINQ_ERR_NCCL instead of blocking
+  const char* tenv = std::getenv("MINQ_TP_INIT_TIMEOUT_S");
+  const double tmo = tenv && std::atof(tenv) > 0 ? std::atof(tenv) : 120.0;
+  const auto deadline = std::chrono::steady_clock::now() +
+                        std::chrono::milliseconds((long long)(tmo * 1000.0));
+  ncclResult_t r;
+  if (nc.nonblocking) {
+    ncclConfig_t ncfg = NCCL_CONFIG_INITIALIZER;
+    ncfg.blocking = 0;
+    r = nc.CommInitRankConfig(&comm, world, id, rank, &ncfg);
+    if (r == ncclInProgress || r == ncclSuccess) {
+      r = nccl_settle(comm, ncclInProgress, deadline);
+      if (r == ncclInProgress)
+        return fail(MINQ_ERR_NCCL, "ncclCommInitRank: the ranks did not all join within " +
+                                       std::to_string(tmo) + " s (communicator aborted)");
+    }
+  } else {
+    r = nc.CommInitRank(&comm, world, id, rank);
+  }
+  if (r != ncclSuccess) {
+    if (comm && nc.CommAbort) nc.CommAbort(comm);
+    return fail(MINQ_ERR_NCCL, std::string("ncclCommInitRank: ") + nc.GetErrorString(r));
+  }
   // this rank's heads and intermediate rows (q/k/v rows by head, gate/up
   // rows, o_proj / down_proj columns)
   const uint64_t nhl = nh / world, nkvl = nkv / world, Il = I / world, qd = nh * hd, kvd = nkv * hd;
@@ -1241,6 +1312,7 @@ minq_status minq_cache_new(minq_model* m, size_t batch, size_t max_seq, minq_cac
     delete c;
     return cuda_fail(e, "cudaMalloc(kv cache)");
   }
+  m->caches.insert(c);
   *out = c;
   return MINQ_OK;
 }
@@ -1315,22 +1387,17 @@ minq_status minq_cache_read(const minq_cache* c, size_t layer, size_t start, siz
   return cache_copy(c, layer, start, n, k, v, false);
 }
 
+// A cache outlived by its model (freed first, e.g. by a garbage collector
+// finalising both in any order) had its device memory released with the
+// model; only the handle remains.
 void minq_cache_free(minq_cache* c) {
   if (!c) return;
-  cudaSetDevice(c->m->device);
-  cudaStreamSynchronize(c->m->stream);
-  for (cudaGraphExec_t g : c->step)
-    if (g) cudaGraphExecDestroy(g);
-  cudaFree(c->k);
-  cudaFree(c->v);
-  cudaFree(c->ws);
-  cudaFree(c->d_pos);
-  for (void* b : {(void*)c->bx, (void*)c->bqkv, (void*)c->bq, (void*)c->batt, (void*)c->bh,
-                  (void*)c->blog, (void*)c->bxn, (void*)c->bpart, (void*)c->btok,
-                  (void*)c->barg, (void*)c->px, (void*)c->pqkv, (void*)c->pq, (void*)c->patt,
-                  (void*)c->ph, (void*)c->pxn, (void*)c->ppart, c->pws, (void*)c->plog,
-                  (void*)c->pnll})
-    cudaFree(b);
+  if (c->m) {
+    cudaSetDevice(c->m->device);
+    cudaStreamSynchronize(c->m->stream);
+    cache_release_device(c);
+    c->m->caches.erase(c);
+  }
   delete c;
 }
 

@@ -6,7 +6,9 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
 #include <mutex>
+#include <thread>
 
 namespace minq {
 
@@ -17,7 +19,12 @@ struct NcclApi {
                             cudaStream_t) = nullptr;
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
+  // non-blocking communicators (initialisation under a host deadline)
+  ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
   bool ok = false;
+  bool nonblocking = false;
 };
 
 // The process's NCCL (already loaded, else libnccl.so.2 from the library
@@ -37,8 +44,32 @@ inline const NcclApi& nccl_api() {
         reinterpret_cast<decltype(api.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
     api.ok = api.GetUniqueId && api.CommInitRank && api.AllReduce && api.CommDestroy &&
              api.GetErrorString;
+    api.CommInitRankConfig =
+        reinterpret_cast<decltype(api.CommInitRankConfig)>(dlsym(h, "ncclCommInitRankConfig"));
+    api.CommGetAsyncError =
+        reinterpret_cast<decltype(api.CommGetAsyncError)>(dlsym(h, "ncclCommGetAsyncError"));
+    api.CommAbort = reinterpret_cast<decltype(api.CommAbort)>(dlsym(h, "ncclCommAbort"));
+    api.nonblocking = api.CommInitRankConfig && api.CommGetAsyncError && api.CommAbort;
   });
   return api;
+}
+
+// Wait until an operation on a non-blocking communicator (returned
+// ncclInProgress) has finished its host-side part, up to `deadline`;
+// ncclInProgress on a blocking one never occurs. On expiry the communicator
+// is aborted and ncclInProgress returned.
+inline ncclResult_t nccl_settle(ncclComm_t comm, ncclResult_t r,
+                                std::chrono::steady_clock::time_point deadline) {
+  const NcclApi& nc = nccl_api();
+  while (r == ncclInProgress) {
+    if (std::chrono::steady_clock::now() > deadline) {
+      nc.CommAbort(comm);
+      return ncclInProgress;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(200));
+    if (nc.CommGetAsyncError(comm, &r) != ncclSuccess) return ncclInternalError;
+  }
+  return r;
 }
 
 }  // namespace minq

@@ -155,8 +155,10 @@ minq_status tp_ar_setup(TpAr* ar, int rank, int world, int H, int sites, void* n
   unsigned char* d_info = nullptr;
   MINQ_CUDA_TRY(cudaMalloc(&d_info, sizeof(ArPeerInfo) * world));
   MINQ_CUDA_TRY(cudaMemcpy(d_info, all.data(), sizeof(ArPeerInfo) * world, cudaMemcpyHostToDevice));
+  const auto deadline = std::chrono::steady_clock::now() + std::chrono::seconds(60);
   ncclResult_t r = nc.AllReduce(d_info, d_info, sizeof(ArPeerInfo) * world, ncclUint8, ncclSum,
                                 static_cast<ncclComm_t>(nccl_comm), s);
+  r = nccl_settle(static_cast<ncclComm_t>(nccl_comm), r, deadline);
   cudaError_t e = cudaStreamSynchronize(s);
   if (r == ncclSuccess && e == cudaSuccess)
     e = cudaMemcpy(all.data(), d_info, sizeof(ArPeerInfo) * world, cudaMemcpyDeviceToHost);
@@ -204,6 +206,7 @@ minq_status tp_ar_setup(TpAr* ar, int rank, int world, int H, int sites, void* n
   MINQ_CUDA_TRY(cudaMalloc(&d_ok, sizeof(int)));
   MINQ_CUDA_TRY(cudaMemcpy(d_ok, &ok, sizeof(int), cudaMemcpyHostToDevice));
   r = nc.AllReduce(d_ok, d_ok, 1, ncclInt32, ncclMin, static_cast<ncclComm_t>(nccl_comm), s);
+  r = nccl_settle(static_cast<ncclComm_t>(nccl_comm), r, deadline);
   e = cudaStreamSynchronize(s);
   if (r == ncclSuccess && e == cudaSuccess) e = cudaMemcpy(&ok, d_ok, sizeof(int), cudaMemcpyDeviceToHost);
   cudaFree(d_ok);

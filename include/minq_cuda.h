@@ -4,9 +4,9 @@
  *
  * The reference (kn1g78/minq) is a Rust crate with no FFI; every entry point
  * below replaces one Rust function on the hot path and is what a thin Rust
- * FFI crate (`minq-cuda-sys`) would bind. The Rust-side `extern "C"` block
- * and the hook points in `Linear::matvec` / `Model::forward` are written out
- * in INTEGRATION.md.
+ * FFI crate (`minq-cuda-sys`) would bind: an `extern "C"` block declaring
+ * these functions, called from `Linear::matvec` and `Model::forward` when
+ * the crate is built with the CUDA backend.
  *
  * Conventions
  *  - Every function returns a minq_status; on error, minq_last_error()
@@ -209,11 +209,19 @@ minq_status minq_attend(const float* q, const float* k, const float* v, size_t l
  * with that device current; make that first call before any stream capture.
  * Calls that may overlap on the GPU (other streams, other host threads)
  * share the one scratch and race: order them on one stream or with events.
- * Nothing in the scratch needs to start at zero. Bounded-wait timeouts
- * inside this call are not recorded for minq_device_status. */
+ * Nothing in the scratch needs to start at zero. A bounded device-side
+ * wait that times out inside this call is recorded in a second file-scope
+ * word, which minq_attend_static_status (and minq_device_status) report as
+ * MINQ_ERR_TIMEOUT and clear. head_dim > 256 or n_heads > 4096: MINQ_ERR_SHAPE
+ * as in minq_attend. */
 minq_status minq_attend_static(const float* q, const float* k, const float* v, size_t len,
                                size_t n_heads, size_t n_kv, size_t head_dim, float* out,
                                void* stream);
+
+/* Synchronises the current device, then reads and clears the timeout word of
+ * minq_attend_static: MINQ_OK, or MINQ_ERR_TIMEOUT when a call since the last
+ * read left `out` incomplete. Allocates nothing. */
+minq_status minq_attend_static_status(void);
 
 /* ---------------------------------------------------------------------- */
 /* Model (model.rs:88-98, assemble :522-574, load_minq :711-715)           */

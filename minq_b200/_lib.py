@@ -89,6 +89,7 @@ SIGNATURES = {
                              S, P]),
     "minq_attend": (I, [P, P, P, S, S, S, S, P, P, S, P]),
     "minq_attend_static": (I, [P, P, P, S, S, S, S, P, P]),
+    "minq_attend_static_status": (I, []),
     "minq_model_load": (I, [C.c_char_p, C.POINTER(P)]),
     "minq_model_new": (I, [C.POINTER(Config), C.POINTER(P)]),
     "minq_model_add_tensor": (I, [P, C.c_char_p, I, S, U64P, P, S, I]),

@@ -650,7 +650,7 @@ minq_status launch_attention(const float* q, const float* k, const float* v, siz
                              int nh, int nkv, int hd, int len, size_t seq_stride,
                              size_t head_stride, size_t pos_stride, float* out, void* ws,
                              size_t ws_bytes, cudaStream_t s, const int* d_pos, int cap_len,
-                             bool record_status, int len_step) {
+                             bool record_status, int len_step, int* status_word) {
   if (!d_pos && len <= 0) return fail(MINQ_ERR_SHAPE, "attention over an empty history");
   if (len_step < 0 || (len_step && d_pos))
     return fail(MINQ_ERR_ARG, "per-entry history lengths take host positions");
@@ -672,7 +672,7 @@ minq_status launch_attention(const float* q, const float* k, const float* v, siz
   p.nkv = nkv;
   p.len = len;
   p.len_step = len_step;
-  p.status = record_status ? device_status_word() : nullptr;
+  p.status = !record_status ? nullptr : (status_word ? status_word : device_status_word());
   p.d_pos = d_pos;
   // The TMA path needs each KV head's positions contiguous (head-major
   // cache) and 16-byte aligned tiles.

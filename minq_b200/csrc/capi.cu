@@ -176,7 +176,9 @@ uint64_t minq_kernel_launches(void) { return g_launches.load(std::memory_order_r
 minq_status minq_device_status(void) {
   MINQ_TRY(require_device());
   MINQ_CUDA_TRY(cudaDeviceSynchronize());
-  return take_device_status();
+  const minq_status a = take_device_status();
+  const minq_status b = take_static_attn_status();
+  return a != MINQ_OK ? a : b;
 }
 
 minq_status minq_kernel_timer_start(const char* family) {

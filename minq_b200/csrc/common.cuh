@@ -34,6 +34,9 @@ minq_status ensure_dynamic_smem(const void* kernel, size_t bytes);
 // (allocated once per device), and its synchronous read-and-clear.
 int* device_status_word();
 minq_status take_device_status();
+// Read-and-clear of minq_attend_static's file-scope status word on the
+// current device (no allocation; the caller has synchronised).
+minq_status take_static_attn_status();
 
 #define MINQ_CUDA_TRY(expr)                                    \
   do {                                                         \

@@ -118,9 +118,12 @@ minq_status launch_attention(const float* q, const float* k, const float* v, siz
                              int nh, int nkv, int hd, int len, size_t seq_stride,
                              size_t head_stride, size_t pos_stride, float* out, void* ws,
                              size_t ws_bytes, cudaStream_t s, const int* d_pos = nullptr,
-                             int cap_len = 0, bool record_status = true, int len_step = 0);
+                             int cap_len = 0, bool record_status = true, int len_step = 0,
+                             int* status_word = nullptr);
 // record_status = false: bounded-wait timeouts are not recorded (and the
-// lazily allocated device status word is never touched). len_step > 0
+// lazily allocated device status word is never touched); status_word, when
+// set, replaces that allocated word as the place timeouts are recorded
+// (minq_attend_static's file-scope word). len_step > 0
 // (host positions only): entry b attends over len + b * len_step positions,
 // e.g. the tokens of a prompt chunk over one cache (seq_stride 0).
 minq_status launch_rope_append(const float* q_in, const float* k_in, const float* v_in,

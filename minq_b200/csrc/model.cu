@@ -195,6 +195,29 @@ minq_status dmalloc(minq_model* m, void** p, size_t bytes) {
   return MINQ_OK;
 }
 
+// Grows the staged-token buffer m->d_tokens to hold n ids. The old buffer is
+// freed (after the model's stream has drained any copy or kernel that still
+// reads it) and leaves m->allocs, so repeated calls on growing inputs keep
+// one buffer, not every earlier one.
+minq_status reserve_tokens(minq_model* m, size_t n) {
+  if (n <= m->d_tokens_cap) return MINQ_OK;
+  const size_t cap = std::max(n, 2 * m->d_tokens_cap);
+  MINQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  void* old = m->d_tokens;
+  if (old) {
+    auto it = std::find(m->allocs.begin(), m->allocs.end(), old);
+    if (it != m->allocs.end()) m->allocs.erase(it);
+    MINQ_CUDA_TRY(cudaFree(old));
+  }
+  m->d_tokens = nullptr;
+  m->d_tokens_cap = 0;
+  void* p;
+  MINQ_TRY(dmalloc(m, &p, cap * 4));
+  m->d_tokens = static_cast<uint32_t*>(p);
+  m->d_tokens_cap = cap;
+  return MINQ_OK;
+}
+
 // RopeTables::new (model.rs:171-186): freq = 1 / theta^(2i/hd), angle =
 // pos * freq, (sin, cos) = angle.sin_cos(), all in f32 through glibc. The
 // calls go through volatile pointers so the host compiler neither folds nor
@@ -1416,12 +1439,7 @@ static minq_status forward_impl(minq_model* m, minq_cache* c, const uint32_t* h_
   MINQ_CUDA_TRY(cudaSetDevice(m->device));
   const uint32_t* toks = d_tokens;
   if (h_tokens) {
-    if (n > m->d_tokens_cap) {
-      void* p;
-      MINQ_TRY(dmalloc(m, &p, n * 4));
-      m->d_tokens = static_cast<uint32_t*>(p);
-      m->d_tokens_cap = n;
-    }
+    MINQ_TRY(reserve_tokens(m, n));
     MINQ_CUDA_TRY(cudaMemcpyAsync(m->d_tokens, h_tokens, n * 4, cudaMemcpyHostToDevice,
                                   m->stream));
     toks = m->d_tokens;
@@ -1664,12 +1682,7 @@ minq_status minq_generate_sampled(minq_model* m, minq_sampler* smp, const uint32
 
 // Token ids to the device (m->d_tokens), after the common checks.
 static minq_status upload_tokens(minq_model* m, const uint32_t* h, size_t n) {
-  if (n > m->d_tokens_cap) {
-    void* p;
-    MINQ_TRY(dmalloc(m, &p, n * 4));
-    m->d_tokens = static_cast<uint32_t*>(p);
-    m->d_tokens_cap = n;
-  }
+  MINQ_TRY(reserve_tokens(m, n));
   MINQ_CUDA_TRY(cudaMemcpyAsync(m->d_tokens, h, n * 4, cudaMemcpyHostToDevice, m->stream));
   return MINQ_OK;
 }

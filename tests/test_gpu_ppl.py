@@ -107,3 +107,17 @@ def test_eval_ppl_errors(mq, orc):
     # the library still serves after the errors
     r = mq.eval_ppl(model, good, 16)
     assert r.scored_positions == om.eval_ppl(good, 16)["scored_positions"]
+
+
+def test_eval_ppl_growing_inputs_reuse_one_token_buffer(mq, orc):
+    """Inputs past the staged-token buffer's first capacity (4096 ids) grow it
+    in place: the old buffer is released, later shorter and longer inputs
+    still score like the oracle."""
+    cfg, model, om = _pair(mq, orc, CASES[1])
+    rng = np.random.default_rng(11)
+    for n in (5000, 3000, 9000, 9001):
+        toks = rng.integers(0, cfg.vocab_size, n)
+        r = mq.eval_ppl(model, toks, 16)
+        ref = om.eval_ppl(toks, 16)
+        assert r.total_tokens == n and r.scored_positions == ref["scored_positions"]
+        assert abs(r.mean_nll - ref["mean_nll"]) <= 2e-3, n

@@ -96,3 +96,34 @@ def test_attend_static_rejects_oversize_before_any_launch(mq):
     assert st == _lib.ERR_ARG
     msg = lib.minq_last_error().decode()
     assert "static scratch" in msg and "minq_attend" in msg
+
+
+def test_attend_static_rejects_unsupported_heads_as_shape(mq):
+    """head_dim > 256 and n_heads > 4096 are shape errors with minq_attend's
+    wording even when their scratch would fit (runs without a GPU)."""
+    from minq_b200 import _lib
+    lib = _lib.lib()
+    dummy = P(256)
+    st = lib.minq_attend_static(dummy, dummy, dummy, 4, 2, 1, 512, dummy, None)
+    assert st == _lib.ERR_SHAPE
+    assert "unsupported head_dim 512" in lib.minq_last_error().decode()
+    st = lib.minq_attend_static(dummy, dummy, dummy, 4, 8192, 8192, 8, dummy, None)
+    assert st == _lib.ERR_SHAPE
+    assert "n_heads" in lib.minq_last_error().decode()
+
+
+@pytest.mark.gpu
+def test_gpu_attend_static_status_word_reads_clear(mq):
+    """After completed calls the entry point's own timeout word reads clear,
+    through its getter and through minq_device_status."""
+    import torch
+    from minq_b200 import _lib
+    lib = _lib.lib()
+    q, k, v = _inputs(5, 900, 8, 2, 64)
+    qd, kd, vd = (torch.from_numpy(a).cuda() for a in (q, k, v))
+    out = torch.empty(8 * 64, dtype=torch.float32, device="cuda")
+    for _ in range(3):
+        _lib.check(lib.minq_attend_static(_ptr(qd), _ptr(kd), _ptr(vd), 900, 8, 2, 64,
+                                          _ptr(out), None))
+    assert lib.minq_attend_static_status() == _lib.OK
+    assert lib.minq_device_status() == _lib.OK

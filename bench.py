@@ -732,6 +732,20 @@ def run_tp(args, world, rank, local, steps=None, warmup=None, emit=True):
     del cache, model
     torch.cuda.empty_cache()
     ar = allreduce_cost(world, cfg) if world > 1 else None
+    if launches_per_step == 1:
+        path = ("decode megakernel, one launch per token" if world == 1 else
+                "decode megakernel, one launch per token per rank; o_proj and down_proj rows "
+                "exchanged inside the launch as (value, epoch) pairs stored into every rank's "
+                "peer-mapped slots")
+    else:
+        path = (f"per-op kernels replayed as a CUDA graph, {launches_per_step} launches per "
+                f"token" + ("" if world == 1 else
+                            ", all-reduces by the one-shot peer-memory kernel (NCCL when "
+                            "MINQ_TP_NCCL=1 or peers cannot be mapped)"))
+    if ar is not None and launches_per_step == 1:
+        ar["note"] = ("the timed step does not call NCCL: its exchange runs inside the "
+                      "megakernel; this is what the same 2 x n_layers all-reduces would cost "
+                      "as separate NCCL calls")
     line = None
     if rank == 0:
         line = {
@@ -749,6 +763,7 @@ def run_tp(args, world, rank, local, steps=None, warmup=None, emit=True):
             "roofline": {"bound": "hbm", "kernel": "decode step (per GPU)", "achieved": gbs,
                          "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                          "traffic": None, "per_launch_bytes": per_gpu},
+            "path": path,
             "allreduce": ar,
             "cpu_baseline": None,
             "clocks": clk,

@@ -646,8 +646,63 @@ def run_minq(args, world, rank, local):
             if tline is not None:
                 tline["parity"] = tpar
             line["tp"] = tline
+            if world == 1:
+                line["load"] = load_record(args, cfg)
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def load_record(args, cfg):
+    """minq_model_load (format.rs:149-277 + model.rs:711-715) of the bench's
+    own model written to a .minq file: the file mapped and indexed in place,
+    each tensor uploaded through pinned double buffers on a copy stream. Timed
+    wall clock around the call, once after evicting the file's pages from the
+    page cache (posix_fadvise DONTNEED: read from the file system) and once
+    with them cached. Returns the record, or its error."""
+    import tempfile
+    import torch
+    import minq_b200 as mq
+    from minq_b200 import synth
+    from minq_b200.minq_format import write_minq_header, write_minq_record
+    arch, _ = WORKLOADS[args.workload]
+    _, qk_norm, tied = synth.ARCH[arch]
+    path = os.path.join(tempfile.gettempdir(), f"minq_bench_{os.getpid()}.minq")
+    try:
+        with open(path, "wb") as f:
+            write_minq_header(f, cfg)
+            for name, tag, shape, data in synth.synth_records(cfg, args.seed, qk_norm, tied):
+                write_minq_record(f, name, tag, shape, data.detach().cpu().numpy())
+                del data
+            f.flush()
+            os.fsync(f.fileno())
+        size = os.path.getsize(path)
+        out = {"file_bytes": size, "model": f"{arch} {cfg.dtype}, {cfg.n_layers} layers"}
+        for kind in ("uncached", "page_cached"):
+            if kind == "uncached":
+                fd = os.open(path, os.O_RDONLY)
+                try:
+                    os.posix_fadvise(fd, 0, 0, os.POSIX_FADV_DONTNEED)
+                finally:
+                    os.close(fd)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            m = mq.Model.load_minq(path)
+            torch.cuda.synchronize()
+            el = time.perf_counter() - t0
+            out[kind] = {"s": el, "gb_s": size / el / 1e9}
+            del m
+            torch.cuda.empty_cache()
+        out["how"] = ("mmap + index in place, per tensor one cudaMalloc, host threads copy "
+                      "64 MiB chunks into two pinned buffers, one cudaMemcpyAsync per chunk on "
+                      "a copy stream; the tied lm_head aliases the f32 embedding (uploaded once)")
+        return out
+    except Exception as e:  # the load record must not sink the decode number
+        return {"error": f"{type(e).__name__}: {e}"}
+    finally:
+        try:
+            os.unlink(path)
+        except OSError:
+            pass
 
 
 def run_tp(args, world, rank, local, steps=None, warmup=None, emit=True):

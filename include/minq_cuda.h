@@ -227,7 +227,10 @@ minq_status minq_attend_static_status(void);
 /* Model (model.rs:88-98, assemble :522-574, load_minq :711-715)           */
 
 /* load_minq: parse a .minq file (format.rs:149-277) and upload it to the
- * current device. */
+ * current device. The file is mapped read-only and indexed in place (the
+ * reader's length, shape and tag checks; MINQ_ERR_FORMAT / MINQ_ERR_IO as
+ * read_minq), then each tensor goes from the mapping through two pinned
+ * staging buffers to the device on a copy stream. */
 minq_status minq_model_load(const char* path, minq_model** out);
 
 /* Builder mirroring assemble(config, get): create, add named tensors (host

@@ -12,12 +12,18 @@
 #include <map>
 #include <memory>
 
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
 namespace minq {
 
 namespace {
 
+// Bounds-checked reads from the mapped file.
 struct Cursor {
-  FILE* f;
+  const uint8_t* base;
   uint64_t pos = 0, len = 0;
   std::string path;
   minq_status take(uint64_t n, const char* what, std::string* err) {
@@ -31,13 +37,20 @@ struct Cursor {
              std::to_string(pos) + ", file is " + std::to_string(len) + " bytes";
       return MINQ_ERR_FORMAT;
     }
-    pos = end;
     return MINQ_OK;
   }
-  bool read(void* dst, size_t n) { return n == 0 || std::fread(dst, 1, n, f) == n; }
+  // copies n bytes that take() admitted and moves past them
+  void read(void* dst, uint64_t n) {
+    if (n) std::memcpy(dst, base + pos, n);
+    pos += n;
+  }
 };
 
 }  // namespace
+
+MinqMapping::~MinqMapping() {
+  if (base) munmap(const_cast<uint8_t*>(base), len);
+}
 
 // Flat JSON object of ModelConfig (model.rs:29-45) as serde_json writes it.
 minq_status parse_config_json(const std::string& s, minq_config* c, std::string* err) {
@@ -112,56 +125,67 @@ minq_status parse_config_json(const std::string& s, minq_config* c, std::string*
   return MINQ_OK;
 }
 
-minq_status read_minq_file(const std::string& path, minq_config* cfg,
-                           std::vector<MinqRecord>* records, std::string* err) {
-  Cursor r;
-  r.path = path;
-  r.f = std::fopen(path.c_str(), "rb");
-  if (!r.f) {
+minq_status index_minq_file(const std::string& path, minq_config* cfg,
+                            std::vector<MinqRecord>* records, MinqMapping* map,
+                            std::string* err) {
+  const int fd = open(path.c_str(), O_RDONLY | O_CLOEXEC);
+  if (fd < 0) {
     *err = "io error: cannot open " + path;
     return MINQ_ERR_IO;
   }
-  std::unique_ptr<FILE, int (*)(FILE*)> guard(r.f, std::fclose);
-  std::fseek(r.f, 0, SEEK_END);
-  r.len = (uint64_t)std::ftell(r.f);
-  std::fseek(r.f, 0, SEEK_SET);
-  auto short_read = [&] {
-    *err = "io error: failed to fill whole buffer";
+  struct stat sb;
+  if (fstat(fd, &sb) != 0) {
+    close(fd);
+    *err = "io error: cannot stat " + path;
     return MINQ_ERR_IO;
-  };
+  }
+  const uint64_t flen = (uint64_t)sb.st_size;
+  if (flen > 0) {
+    void* a = mmap(nullptr, flen, PROT_READ, MAP_PRIVATE, fd, 0);
+    if (a == MAP_FAILED) {
+      close(fd);
+      *err = "io error: cannot map " + path;
+      return MINQ_ERR_IO;
+    }
+    madvise(a, flen, MADV_SEQUENTIAL);
+    map->base = static_cast<const uint8_t*>(a);
+    map->len = flen;
+  }
+  close(fd);  // the mapping keeps the file
+  Cursor r;
+  r.base = map->base;
+  r.len = flen;
+  r.path = path;
   minq_status st;
   if ((st = r.take(8, "magic", err))) return st;
   char magic[8];
-  if (!r.read(magic, 8)) return short_read();
+  r.read(magic, 8);
   if (std::memcmp(magic, "MINQ0001", 8) != 0 && std::memcmp(magic, "MINFER01", 8) != 0) {
     *err = path + ": not a .minq/.minfer file (bad magic)";
     return MINQ_ERR_FORMAT;
   }
   if ((st = r.take(4, "config length", err))) return st;
   uint32_t cfg_len;
-  if (!r.read(&cfg_len, 4)) return short_read();
+  r.read(&cfg_len, 4);
   if ((st = r.take(cfg_len, "config json", err))) return st;
   std::string js(cfg_len, '\0');
-  if (!r.read(&js[0], cfg_len)) return short_read();
+  r.read(&js[0], cfg_len);
   if ((st = parse_config_json(js, cfg, err))) return st;
-  while (true) {
-    uint8_t first;
-    if (std::fread(&first, 1, 1, r.f) != 1) break;  // clean EOF (format.rs:173-177)
+  while (r.pos < r.len) {  // clean EOF between records (format.rs:173-177)
     if ((st = r.take(4, "tensor name length", err))) return st;
-    uint8_t rest[3];
-    if (!r.read(rest, 3)) return short_read();
-    uint64_t name_len = first | ((uint64_t)rest[0] << 8) | ((uint64_t)rest[1] << 16) |
-                        ((uint64_t)rest[2] << 24);
+    uint32_t name_len;
+    r.read(&name_len, 4);
     if ((st = r.take(name_len, "tensor name", err))) return st;
     MinqRecord rec;
     rec.name.assign(name_len, '\0');
-    if (!r.read(&rec.name[0], name_len)) return short_read();
+    r.read(&rec.name[0], name_len);
     if ((st = r.take(2, "tensor tag/ndim", err))) return st;
     uint8_t tag, ndim;
-    if (!r.read(&tag, 1) || !r.read(&ndim, 1)) return short_read();
+    r.read(&tag, 1);
+    r.read(&ndim, 1);
     if ((st = r.take(8ull * ndim, "tensor shape", err))) return st;
     rec.shape.resize(ndim);
-    if (!r.read(rec.shape.data(), 8ull * ndim)) return short_read();
+    r.read(rec.shape.data(), 8ull * ndim);
     uint64_t numel = 1;
     for (uint64_t d : rec.shape) {
       if (d != 0 && numel > UINT64_MAX / d) {
@@ -172,7 +196,7 @@ minq_status read_minq_file(const std::string& path, minq_config* cfg,
     }
     if ((st = r.take(8, "tensor data length", err))) return st;
     uint64_t data_len;
-    if (!r.read(&data_len, 8)) return short_read();
+    r.read(&data_len, 8);
     uint64_t expected = 0;
     if (tag == MINQ_F32) {
       if (numel > UINT64_MAX / 4) {
@@ -208,8 +232,9 @@ minq_status read_minq_file(const std::string& path, minq_config* cfg,
     }
     if ((st = r.take(data_len, "tensor data", err))) return st;
     rec.tag = tag;
-    rec.data.resize(data_len);
-    if (!r.read(rec.data.data(), data_len)) return short_read();
+    rec.offset = r.pos;
+    rec.nbytes = data_len;
+    r.pos += data_len;
     records->push_back(std::move(rec));
   }
   return MINQ_OK;

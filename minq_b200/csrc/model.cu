@@ -27,6 +27,7 @@
 #include <map>
 #include <set>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "common.cuh"
@@ -1008,12 +1009,11 @@ minq_status minq_model_new(const minq_config* cfg, minq_model** out) {
   return MINQ_OK;
 }
 
-minq_status minq_model_add_tensor(minq_model* m, const char* name, minq_dtype tag, size_t ndim,
-                                  const uint64_t* shape, const void* data, size_t nbytes,
-                                  int data_on_device) {
-  if (!m || !name || (ndim && !shape) || (nbytes && !data))
-    return fail(MINQ_ERR_ARG, "null argument");
-  if (m->finished) return fail(MINQ_ERR_MODEL, "model already finished");
+// The record checks of minq_model_add_tensor (format.rs:212-249): a known
+// storage tag, 2-D block-aligned quantized shapes, data length equal to the
+// shape-derived byte count.
+static minq_status check_record(const char* name, minq_dtype tag, size_t ndim,
+                                const uint64_t* shape, size_t nbytes) {
   if (tag != MINQ_F32 && tag != MINQ_Q8_0 && tag != MINQ_Q4_0)
     return fail(MINQ_ERR_FORMAT, std::string("tensor `") + name + "`: unknown storage tag " +
                                      std::to_string((int)tag));
@@ -1034,6 +1034,24 @@ minq_status minq_model_add_tensor(minq_model* m, const char* name, minq_dtype ta
     return fail(MINQ_ERR_FORMAT, std::string("tensor `") + name + "`: data length " +
                                      std::to_string(nbytes) + " != shape-derived " +
                                      std::to_string(expected));
+  return MINQ_OK;
+}
+
+// Records the device tensor under its name; the last record of a name wins,
+// like the reference's HashMap (its earlier buffer stays in m->allocs).
+static void put_tensor(minq_model* m, const char* name, DevTensor t) {
+  auto it = m->pending.find(name);
+  if (it != m->pending.end()) it->second = t;
+  else m->pending.emplace(name, t);
+}
+
+minq_status minq_model_add_tensor(minq_model* m, const char* name, minq_dtype tag, size_t ndim,
+                                  const uint64_t* shape, const void* data, size_t nbytes,
+                                  int data_on_device) {
+  if (!m || !name || (ndim && !shape) || (nbytes && !data))
+    return fail(MINQ_ERR_ARG, "null argument");
+  if (m->finished) return fail(MINQ_ERR_MODEL, "model already finished");
+  MINQ_TRY(check_record(name, tag, ndim, shape, nbytes));
   DevTensor t;
   t.tag = tag;
   t.shape.assign(shape, shape + ndim);
@@ -1044,10 +1062,98 @@ minq_status minq_model_add_tensor(minq_model* m, const char* name, minq_dtype ta
   t.ptr = p;
   MINQ_CUDA_TRY(cudaMemcpy(p, data, nbytes,
                            data_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
-  auto it = m->pending.find(name);
-  if (it != m->pending.end()) it->second = t;  // last record wins, like the HashMap
-  else m->pending.emplace(name, t);
+  put_tensor(m, name, t);
   return MINQ_OK;
+}
+
+// Host-to-device upload of mapped file bytes through two pinned staging
+// buffers on a copy stream: while one buffer's cudaMemcpyAsync runs, host
+// threads fill the other from the mapping (the first touch of a mapped page
+// reads it from the file). One cudaMemcpyAsync per chunk.
+namespace {
+struct PinnedUpload {
+  cudaStream_t s = nullptr;
+  unsigned char* buf[2] = {nullptr, nullptr};
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+  bool busy[2] = {false, false};
+  size_t chunk = 0;
+  int next = 0;
+  unsigned threads = 1;
+
+  minq_status init() {
+    chunk = size_t(64) << 20;
+    if (const char* e = std::getenv("MINQ_LOAD_CHUNK_BYTES"))
+      chunk = std::max<size_t>(4096, std::strtoull(e, nullptr, 10));
+    threads = std::max(1u, std::min(8u, std::thread::hardware_concurrency()));
+    MINQ_CUDA_TRY(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    for (int i = 0; i < 2; ++i) {
+      MINQ_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&buf[i]), chunk, cudaHostAllocDefault));
+      MINQ_CUDA_TRY(cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming));
+    }
+    return MINQ_OK;
+  }
+  ~PinnedUpload() {
+    if (s) cudaStreamSynchronize(s);
+    for (int i = 0; i < 2; ++i) {
+      if (ev[i]) cudaEventDestroy(ev[i]);
+      if (buf[i]) cudaFreeHost(buf[i]);
+    }
+    if (s) cudaStreamDestroy(s);
+  }
+  void fill(unsigned char* dst, const unsigned char* src, size_t n) {
+    const unsigned t = n >= (size_t(8) << 20) ? threads : 1u;
+    if (t == 1) {
+      std::memcpy(dst, src, n);
+      return;
+    }
+    std::vector<std::thread> pool;
+    const size_t part = (n + t - 1) / t;
+    for (unsigned i = 0; i < t; ++i) {
+      const size_t a = i * part, b = std::min(n, a + part);
+      if (a < b) pool.emplace_back([=] { std::memcpy(dst + a, src + a, b - a); });
+    }
+    for (auto& th : pool) th.join();
+  }
+  minq_status copy(void* dev, const unsigned char* src, size_t n) {
+    for (size_t off = 0; off < n; off += chunk) {
+      const size_t len = std::min(chunk, n - off);
+      const int b = next;
+      next ^= 1;
+      if (busy[b]) MINQ_CUDA_TRY(cudaEventSynchronize(ev[b]));
+      fill(buf[b], src + off, len);
+      MINQ_CUDA_TRY(cudaMemcpyAsync(static_cast<unsigned char*>(dev) + off, buf[b], len,
+                                    cudaMemcpyHostToDevice, s));
+      MINQ_CUDA_TRY(cudaEventRecord(ev[b], s));
+      busy[b] = true;
+    }
+    return MINQ_OK;
+  }
+  minq_status finish() {
+    MINQ_CUDA_TRY(cudaStreamSynchronize(s));
+    return MINQ_OK;
+  }
+};
+}  // namespace
+
+static minq_status upload_records(minq_model* m, const MinqMapping& map,
+                                  const std::vector<MinqRecord>& recs) {
+  MINQ_CUDA_TRY(cudaSetDevice(m->device));
+  PinnedUpload up;
+  MINQ_TRY(up.init());
+  for (const MinqRecord& r : recs) {
+    MINQ_TRY(check_record(r.name.c_str(), (minq_dtype)r.tag, r.shape.size(), r.shape.data(),
+                          r.nbytes));
+    DevTensor t;
+    t.tag = (minq_dtype)r.tag;
+    t.shape = r.shape;
+    t.nbytes = r.nbytes;
+    void* p;
+    MINQ_TRY(dmalloc(m, &p, r.nbytes));
+    t.ptr = p;
+    MINQ_TRY(up.copy(p, map.base + r.offset, r.nbytes));
+    put_tensor(m, r.name.c_str(), t);
+  }
+  return up.finish();
 }
 
 minq_status minq_model_finish(minq_model* m) {
@@ -1061,21 +1167,14 @@ minq_status minq_model_load(const char* path, minq_model** out) {
   if (!path || !out) return fail(MINQ_ERR_ARG, "null argument");
   minq_config cfg{};
   std::vector<MinqRecord> recs;
+  MinqMapping map;
   std::string err;
-  minq_status st = read_minq_file(path, &cfg, &recs, &err);
+  minq_status st = index_minq_file(path, &cfg, &recs, &map, &err);
   if (st != MINQ_OK) return fail(st, err);
   minq_model* m = nullptr;
   MINQ_TRY(minq_model_new(&cfg, &m));
-  for (MinqRecord& r : recs) {
-    st = minq_model_add_tensor(m, r.name.c_str(), (minq_dtype)r.tag, r.shape.size(),
-                               r.shape.data(), r.data.data(), r.data.size(), 0);
-    std::vector<uint8_t>().swap(r.data);
-    if (st != MINQ_OK) {
-      minq_model_free(m);
-      return st;
-    }
-  }
-  st = minq_model_finish(m);
+  st = upload_records(m, map, recs);
+  if (st == MINQ_OK) st = minq_model_finish(m);
   if (st != MINQ_OK) {
     std::string msg = minq_last_error();
     minq_model_free(m);

@@ -114,3 +114,39 @@ def test_quantize_selection_rule():  # main.rs:343-346
     assert not quantize_tensor_rule("model.layers.0.input_layernorm.weight", [64])
     assert not quantize_tensor_rule("model.layers.0.self_attn.q_proj.bias", [64])
     assert not quantize_tensor_rule("x.weight", [8, 33])
+
+
+def _lib_load(path):
+    import ctypes as C
+    from minq_b200 import _lib
+    L = _lib.lib()
+    h = C.c_void_p()
+    st = L.minq_model_load(str(path).encode(), C.byref(h))
+    if st == _lib.OK:
+        L.minq_model_free(h)
+    return st, L.minq_last_error().decode()
+
+
+@pytest.mark.parametrize("tag", sorted(CRAFTED))
+def test_library_loader_rejects_malformed_records(tmp_path, mq, tag):  # format.rs:386-434
+    """The product loader (mapped file, indexed in place) refuses the same
+    records before it touches a device."""
+    from minq_b200 import _lib
+    st, msg = _lib_load(crafted(tmp_path, tag, CRAFTED[tag]))
+    assert st == _lib.ERR_FORMAT, msg
+
+
+def test_library_loader_reads_a_valid_file_up_to_the_device(tmp_path, mq, orc):
+    """A valid file is indexed and handed to the uploader: on a machine
+    without a GPU the load stops there with a device error (no CPU path)."""
+    from minq_b200 import _lib
+    import torch
+    p = tmp_path / "m.minq"
+    write_minq(p, make_config(), sample_records(orc))
+    st, msg = _lib_load(p)
+    if torch.cuda.is_available():
+        assert st in (_lib.OK, _lib.ERR_SHAPE, _lib.ERR_MODEL), msg
+    else:
+        assert st == _lib.ERR_CUDA and "no CUDA device" in msg, msg
+    st, msg = _lib_load(tmp_path / "missing.minq")
+    assert st == _lib.ERR_IO and "cannot open" in msg

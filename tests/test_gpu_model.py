@@ -154,7 +154,13 @@ def test_missing_tensor_is_a_model_error(mq):
         mq.Model.from_tensors(cfg, recs)
 
 
-def test_load_minq_file(mq, orc, tmp_path):  # model.rs:711 via format.rs
+@pytest.mark.parametrize("chunk", [None, 4096, 12304])
+def test_load_minq_file(mq, orc, tmp_path, monkeypatch, chunk):  # model.rs:711 via format.rs
+    """The mapped-file loader (pinned double buffers, one copy per chunk) with
+    its default chunk and with chunks far smaller than the tensors, so every
+    tensor crosses several buffers and both buffers recycle."""
+    if chunk:
+        monkeypatch.setenv("MINQ_LOAD_CHUNK_BYTES", str(chunk))
     cfg = tiny_config(2, dtype="q4_0", hidden=128, inter=256)
     recs = quantize_records(synth.random_model_records(cfg, 11), 2, orc)
     p = tmp_path / "tiny.minq"
@@ -163,6 +169,8 @@ def test_load_minq_file(mq, orc, tmp_path):  # model.rs:711 via format.rs
     om = orc.Model.load_minq(str(p))
     toks = [9, 8, 7, 6]
     close(om.forward(toks, om.new_cache()), gm.forward(toks, gm.new_cache()))
+    built = mq.Model.from_tensors(cfg, recs)
+    assert np.array_equal(gm.forward(toks, gm.new_cache()), built.forward(toks, built.new_cache()))
 
 
 def test_engine_generate_matches_oracle_greedy(mq, orc):  # engine.rs:98

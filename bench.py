@@ -60,7 +60,8 @@ WORKLOADS = {
 }
 # Long-context tensor-parallel decode: the Qwen3-4B shape in Q8_0 with the KV
 # cache pre-filled (N(0, 1)) at 32768 positions, greedy decode split over the
-# ranks (heads and intermediate rows; NCCL all-reduce after o_proj / down_proj).
+# ranks (heads and intermediate rows; the o_proj / down_proj partial sums
+# exchanged through peer memory inside the decode megakernel).
 TP_WORKLOAD = "qwen3-4b-q8_0-tp32k"
 # Batched decode: 64 independent greedy sequences of the LLaMA-3-8B shape in
 # Q4_0 (512-token prompts), data-sharded over the ranks with no collective.

@@ -18,27 +18,33 @@
 // group (two lop3 / one bf16 subtraction per pair) and the inputs are
 // written in the same order; the sum over k does not depend on it.
 //
-// Data flow in one CTA (ROWS weight rows x one K slice, chunks of 4 blocks
-// = 128 columns):
-//   warp 0, lane 0   TMA: the chunk's raw weight rows (a 2-D box of the
-//                    row-major block stream, no swizzle) and the four
-//                    64-column x_hi / x_lo tiles (128-byte swizzle) into a
-//                    ring of stages; warp 0 also owns the TMEM allocation
-//   warp 1, lane 0   tcgen05.mma (A from TMEM, B from shared memory): per
-//                    block, (ROWS/128) accumulators of 128 x N f32, four
-//                    MMAs each (two k steps x hi/lo), then tcgen05.commit
-//   row workers      one thread per weight row and half chunk: unpack that
-//                    row's codes of its half (2 blocks) into TMEM with
-//                    tcgen05.st; and, for its half of the N columns,
-//                    tcgen05.ld of each block's sums, acc += d * sum, release
-//                    the accumulator; at the end bias / residual / SwiGLU
-//                    and the store (or the slice partial)
-// A worker's loop over chunks c: sums of blocks 0-1 of c, unpack chunk c+1,
-// sums of blocks 2-3 of c, so the MMAs of c+1 run while c is summed and two
-// accumulator sets suffice.
+// Data flow in one CTA (128 weight rows -- 64 + 64 for gate and up -- by
+// one K slice, in chunks of 4 blocks = 128 columns through a ring of S
+// shared-memory stages):
+//   warp 0           TMA, one elected lane: per chunk the raw weight rows (a
+//                    2-D box of the row-major block stream, no swizzle,
+//                    evict-first) and the four 64-column x_hi / x_lo tiles
+//                    (128-byte swizzle; x_hi rows then x_lo rows, the
+//                    B operand of N = 2 NP); warp 0 also owns the TMEM
+//                    allocation
+//   warps 1, 2       tcgen05.mma issue, one lane each: warp 1 blocks 0-1 of
+//                    every chunk, warp 2 blocks 2-3. A comes from TMEM (the
+//                    chunk's A tile), B from the stage; block g accumulates
+//                    in TMEM set g mod NBUF with two k-step MMAs, then
+//                    tcgen05.commit to that set's barrier
+//   4 unpacker warps thread = weight row (TMEM lane): the chunk's codes ->
+//                    exact bf16 with lop3 / one bf16 subtraction per pair,
+//                    tcgen05.st into A tile (chunk mod 2)
+//   4 WG epilogue    thread = weight row and CW inputs: tcgen05.ld of each
+//   warps            block's hi and lo sums, release of the set, then
+//                    (acc_hi, acc_lo) += d * (sum_hi, sum_lo) as one paired
+//                    FMA, in block order; at the end acc_hi + acc_lo, bias /
+//                    residual / SwiGLU and the store (or the slice partial)
+// With fewer row tiles than SMs the K range splits into S slices whose
+// partials um_reduce_kernel sums in slice order.
 // Every mbarrier wait is time-bounded (1 s); a timeout sets the device
 // status word and an abort flag that ends every role's loop, after which
-// the producer waits for its copies in flight, the MMA thread for its
+// the producer waits for its copies in flight, the MMA threads for their
 // MMAs, and warp 0 frees the TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -58,7 +64,7 @@ namespace minq {
 namespace {
 
 constexpr int kUmChunkBlocks = 4;  // blocks per staged chunk (128 columns)
-constexpr int kUmCtrlWarps = 4;    // warp 0 producer / TMEM, warp 1 MMA (warps 2-3 idle)
+constexpr int kUmCtrlWarps = 4;    // warp 0 producer / TMEM, warps 1-2 MMA issue (warp 3 idle)
 constexpr int kUmMaxStages = 6;
 constexpr int kUmIssuers = 2;      // MMA-issuing warps (1, 2): blocks 0-1 and 2-3 of each chunk
 constexpr size_t kUmSmemLimit = 227 * 1024;

@@ -621,7 +621,7 @@ def run_minq(args, world, rank, local):
                        if arch == "qwen3-4b" else "inputs > L2",
                        "weight_bytes": model.weight_bytes},
             "prefill": {"tokens": prompt_len, "tok_s": prompt_len / prefill_s,
-                        "mode": "chunks of 64 tokens (batched projections on the tensor cores, causal split-KV attention), then the last token as a decode step"},
+                        "mode": "chunks of 64 tokens (batched projections and causal flash attention on the tensor cores: tcgen05 kind::f16 / kind::tf32), then the last token as a decode step" if os.environ.get("MINQ_FLASH_PREFILL", "1") != "0" else "chunks of 64 tokens (batched projections on the tensor cores, split-KV attention per token), then the last token as a decode step"},
             "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4,
                     "d2h_bytes_per_step": 4 * V + 4},
             "gpu_launches": int(launches),

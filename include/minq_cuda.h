@@ -198,6 +198,27 @@ minq_status minq_attend(const float* q, const float* k, const float* v, size_t l
                         size_t n_heads, size_t n_kv, size_t head_dim, float* out,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* Causal attention of a prompt chunk, the reference's prompt loop
+ * (model.rs:259-268 -> forward_token's attend, model.rs:223-248, one call per
+ * token) done for n_tokens tokens at once: token t (position p0 + t) attends
+ * over positions 0..=p0+t of a head-major layer cache whose positions
+ * 0..p0+n_tokens-1 already hold every key and value, the chunk's own
+ * included (kv head h at k_cache + h*head_stride, [position][head_dim]).
+ *   q    [n_tokens, n_heads, head_dim]   RoPE'd queries
+ *   out  [n_tokens, n_heads, head_dim]
+ * Runs on the tensor cores (tcgen05 kind::tf32 with hi/lo split operands,
+ * f32 accumulation: about the f32 arithmetic of the reference's dot
+ * products). head_dim 64 or 128 (else MINQ_ERR_SHAPE); q, k, v, out
+ * 16-byte aligned and head_stride a multiple of 4 (else MINQ_ERR_ARG).
+ * `workspace` (device) holds minq_attn_prefill_workspace_bytes(n_tokens,
+ * n_heads, n_kv, head_dim) bytes (0: none needed). */
+size_t minq_attn_prefill_workspace_bytes(size_t n_tokens, size_t n_heads, size_t n_kv,
+                                         size_t head_dim);
+minq_status minq_attend_prefill(const float* q, const float* k_cache, const float* v_cache,
+                                size_t head_stride, size_t p0, size_t n_tokens, size_t n_heads,
+                                size_t n_kv, size_t head_dim, float* out, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
 /* minq_attend without a workspace argument: the split-KV scratch is a
  * 32 MiB array inside the library, so the call allocates no device memory.
  * No reference counterpart: added for callers that cannot allocate or own

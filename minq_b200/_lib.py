@@ -89,6 +89,8 @@ SIGNATURES = {
                              S, P]),
     "minq_attend": (I, [P, P, P, S, S, S, S, P, P, S, P]),
     "minq_attend_static": (I, [P, P, P, S, S, S, S, P, P]),
+    "minq_attn_prefill_workspace_bytes": (S, [S, S, S, S]),
+    "minq_attend_prefill": (I, [P, P, P, S, S, S, S, S, S, P, P, S, P]),
     "minq_attend_static_status": (I, []),
     "minq_model_load": (I, [C.c_char_p, C.POINTER(P)]),
     "minq_model_new": (I, [C.POINTER(Config), C.POINTER(P)]),

@@ -372,4 +372,28 @@ minq_status minq_attend(const float* q, const float* k, const float* v, size_t l
                           head_dim, kvd, out, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
+size_t minq_attn_prefill_workspace_bytes(size_t n_tokens, size_t n_heads, size_t n_kv,
+                                         size_t head_dim) {
+  if (n_tokens == 0 || n_tokens > (1u << 20) || n_heads > 4096 || head_dim > 256) return 0;
+  return prefill_attention_workspace((int)n_tokens, (int)n_heads, (int)n_kv, (int)head_dim);
+}
+
+minq_status minq_attend_prefill(const float* q, const float* k_cache, const float* v_cache,
+                                size_t head_stride, size_t p0, size_t n_tokens, size_t n_heads,
+                                size_t n_kv, size_t head_dim, float* out, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  if (!q || !k_cache || !v_cache || !out) return fail(MINQ_ERR_ARG, "null pointer");
+  if (n_kv == 0 || n_heads % n_kv != 0)
+    return fail(MINQ_ERR_MODEL, "n_heads must be a multiple of n_kv_heads");
+  if (n_tokens == 0 || n_tokens > (1u << 20) || p0 > (1u << 30) || n_heads > 4096)
+    return fail(MINQ_ERR_SHAPE, "prefill attention: token count or position out of range");
+  if (!prefill_attention_supported((int)n_heads, (int)n_kv, (int)head_dim))
+    return fail(MINQ_ERR_SHAPE, "unsupported head_dim " + std::to_string(head_dim) +
+                                    " for prefill attention (supported: 64, 128)");
+  MINQ_TRY(require_device());
+  return launch_prefill_attention(q, k_cache, v_cache, head_stride, (int)p0, (int)n_tokens,
+                                  (int)n_heads, (int)n_kv, (int)head_dim, out, workspace,
+                                  workspace_bytes, (cudaStream_t)stream);
+}
+
 }  // extern "C"

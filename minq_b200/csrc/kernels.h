@@ -126,6 +126,17 @@ minq_status launch_attention(const float* q, const float* k, const float* v, siz
 // (minq_attend_static's file-scope word). len_step > 0
 // (host positions only): entry b attends over len + b * len_step positions,
 // e.g. the tokens of a prompt chunk over one cache (seq_stride 0).
+// attn_prefill_tc.cu: causal attention of T prompt tokens at positions
+// p0 .. p0 + T - 1 over a head-major layer cache (kv head h at
+// k + h * head_stride, [position][hd]) that already holds their keys, on
+// the tensor cores (tcgen05 kind::tf32, hi / lo split operands). q, out:
+// [T][nh][hd]. workspace: prefill_attention_workspace(T, nh, nkv, hd) bytes.
+bool prefill_attention_supported(int nh, int nkv, int hd);
+size_t prefill_attention_workspace(int T, int nh, int nkv, int hd);
+minq_status launch_prefill_attention(const float* q, const float* kc, const float* vc,
+                                     size_t head_stride, int p0, int T, int nh, int nkv, int hd,
+                                     float* out, void* ws, size_t ws_bytes, cudaStream_t s,
+                                     int* status_word = nullptr);
 minq_status launch_rope_append(const float* q_in, const float* k_in, const float* v_in,
                                size_t q_in_bstride, size_t kv_in_bstride, const float* q_norm,
                                const float* k_norm, float eps, const float* cos_t,

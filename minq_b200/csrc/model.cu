@@ -810,6 +810,8 @@ static minq_status prefill_ready(minq_model* m, minq_cache* c, bool* ok, bool us
   for (size_t t = 1; t <= B; ++t)
     ws = std::max(ws, attn_workspace_need(t, (int)cfg.n_heads, (int)cfg.n_kv_heads,
                                           (int)cfg.head_dim, (int)c->max_seq, true));
+  ws = std::max(ws, prefill_attention_workspace((int)B, (int)cfg.n_heads, (int)cfg.n_kv_heads,
+                                                (int)cfg.head_dim));
   c->pws_bytes = ws + 256;
   MINQ_TRY(alloc(&c->pws, c->pws_bytes));
   return MINQ_OK;
@@ -826,6 +828,14 @@ static minq_status forward_chunk(minq_model* m, minq_cache* c, const uint32_t* d
   const int p0 = (int)c->len;
   cudaStream_t s = m->stream;
   const size_t layer_elems = (size_t)nkv * c->max_seq * hd, head_stride = c->max_seq * hd;
+  // causal chunk attention: the tensor-core kernel for head_dim 64 / 128
+  // (MINQ_FLASH_PREFILL=0: the split-KV decode kernel, one entry per token)
+  static const bool flash_env = [] {
+    const char* e = std::getenv("MINQ_FLASH_PREFILL");
+    return !(e && e[0] == '0');
+  }();
+  const bool flash = flash_env && prefill_attention_supported(nh, nkv, hd) &&
+                     (uintptr_t)c->k % 16 == 0 && (uintptr_t)c->v % 16 == 0;
   MINQ_TRY(launch_embed_batch(m->embed, d_toks, V, H, T, c->px, s));
   for (uint64_t li = 0; li < cfg.n_layers; ++li) {
     const DevLayer& L = m->layers[li];
@@ -839,8 +849,12 @@ static minq_status forward_chunk(minq_model* m, minq_cache* c, const uint32_t* d
     MINQ_TRY(launch_rope_append(c->pqkv, c->pqkv + qd, c->pqkv + qd + kvd, qkv_rows, qkv_rows,
                                 L.q_norm, L.k_norm, eps, m->rope_cos, m->rope_sin, (size_t)T, nh,
                                 nkv, hd, p0, c->pq, kc, vc, 0, head_stride, hd, s, nullptr, 1));
-    MINQ_TRY(launch_attention(c->pq, kc, vc, (size_t)T, nh, nkv, hd, p0 + 1, 0, head_stride, hd,
-                              c->patt, c->pws, c->pws_bytes, s, nullptr, 0, true, 1));
+    if (flash)  // every token of the chunk at once on the tensor cores
+      MINQ_TRY(launch_prefill_attention(c->pq, kc, vc, head_stride, p0, T, nh, nkv, hd, c->patt,
+                                        c->pws, c->pws_bytes, s));
+    else
+      MINQ_TRY(launch_attention(c->pq, kc, vc, (size_t)T, nh, nkv, hd, p0 + 1, 0, head_stride,
+                                hd, c->patt, c->pws, c->pws_bytes, s, nullptr, 0, true, 1));
     MINQ_TRY(launch_qmatmul(L.o.tag, L.o.ptr, nullptr, H, (int)qd, T, c->patt, qd, nullptr, eps,
                             c->pxn, c->pxn_floats, nullptr, c->px, c->px, H, c->ppart,
                             c->ppart_floats, s));  // x += o

@@ -66,3 +66,16 @@ def test_no_cpu_fallback_without_gpu(mq):
     st = _lib.lib().minq_model_new(C.byref(cfg), C.byref(h))
     assert st == _lib.ERR_CUDA
     assert b"no CUDA device" in _lib.lib().minq_last_error()
+
+
+def test_prefill_attention_argument_checks(mq):
+    """minq_attend_prefill rejects unsupported shapes before touching a device."""
+    from minq_b200 import _lib
+    L = _lib.lib()
+    d = C.c_void_p(256)  # never dereferenced: every check below comes first
+    assert L.minq_attend_prefill(None, d, d, 128, 0, 4, 8, 2, 128, d, None, 0, None) == _lib.ERR_ARG
+    assert L.minq_attend_prefill(d, d, d, 128, 0, 4, 7, 2, 128, d, None, 0, None) == _lib.ERR_MODEL
+    assert L.minq_attend_prefill(d, d, d, 96, 0, 4, 8, 2, 96, d, None, 0, None) == _lib.ERR_SHAPE
+    assert b"head_dim 96" in L.minq_last_error()
+    assert L.minq_attend_prefill(d, d, d, 128, 0, 0, 8, 2, 128, d, None, 0, None) == _lib.ERR_SHAPE
+    assert L.minq_attn_prefill_workspace_bytes(0, 8, 2, 128) == 0

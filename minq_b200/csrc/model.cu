@@ -360,6 +360,8 @@ minq_status setup_megakernel(minq_model* m) {
   // history splits per kv head: up to one CTA each, as many as the merge
   // buffer in shared memory allows
   k.nsplit = std::max(1, grid / (int)nkv);
+  if (const char* e = std::getenv("MINQ_MK_SPLITS"))  // at most this many splits per kv head
+    if (std::atoi(e) > 0) k.nsplit = std::min(k.nsplit, std::atoi(e));
   for (;;) {
     k.scratch = (int)mk_scratch_bytes((int)H, (int)I, (int)qd, (int)G, (int)hd, k.nsplit);
     k.smem = mk_smem_bytes(k.scratch, (int)c.n_layers);

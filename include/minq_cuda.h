@@ -328,6 +328,19 @@ minq_status minq_forward(minq_model* m, minq_cache* c, const uint32_t* tokens, s
 minq_status minq_forward_batch(minq_model* m, minq_cache* c, const uint32_t* tokens, size_t n,
                                float* logits_out, uint32_t* argmax_out);
 
+/* Prompts of the `batch` sequences of a batched cache (the reference's
+ * Model::forward prompt loop, model.rs:254-270, run per sequence): sequence b
+ * takes tokens[b*n .. b*n + n - 1] (host) at the cache's common positions
+ * len .. len + n - 1. All but the last token of each sequence go through the
+ * chunked prefill (64 tokens of one sequence per pass: projections and causal
+ * attention on the tensor cores), the last tokens as one batched step whose
+ * logits (`logits_out`, host, batch x vocab floats, or NULL) and argmax
+ * (`argmax_out`, host, batch ids, or NULL) are returned. The cache and the
+ * outputs match n calls of minq_forward_batch with column i of `tokens`.
+ * Errors as minq_forward_batch. */
+minq_status minq_prefill_batch(minq_model* m, minq_cache* c, const uint32_t* tokens, size_t n,
+                               float* logits_out, uint32_t* argmax_out);
+
 /* Greedy continuation of a batched cache on the device: n_steps batched
  * steps, each feeding every sequence its previous argmax (no host
  * synchronisation); `d_tokens_out` (device, n_steps x batch ids, or NULL). */

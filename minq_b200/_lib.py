@@ -111,6 +111,7 @@ SIGNATURES = {
     "minq_forward_device": (I, [P, P, P, S, P, P]),
     "minq_decode_steps": (I, [P, P, S, P]),
     "minq_forward_batch": (I, [P, P, P, S, P, P]),
+    "minq_prefill_batch": (I, [P, P, P, S, P, P]),
     "minq_tp_unique_id": (I, [P]),
     "minq_cache_write_device": (I, [P, S, S, S, P, P]),
     "minq_tp_init": (I, [P, C.c_int, C.c_int, P]),

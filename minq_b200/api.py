@@ -352,6 +352,23 @@ class Model:
                                        am.ctypes.data_as(C.c_void_p)))
         return am, out
 
+    def prefill_batch(self, prompts, cache: "KVCache", logits: bool = True):
+        """The prompts of a batch cache: prompts[b] (equal lengths n, one row
+        per sequence) through Model::forward (model.rs:254-270) per sequence,
+        all but the last tokens in chunks of 64 on the tensor cores, the last
+        tokens as one batched step. Returns (argmax [batch], logits [batch,
+        vocab] or None) of that step."""
+        toks = np.ascontiguousarray(np.asarray(prompts, dtype=np.uint32))
+        if toks.ndim != 2:
+            raise ValueError("prompts: one row of token ids per sequence")
+        B, n = toks.shape
+        am = np.zeros(B, dtype=np.uint32)
+        out = np.empty((B, self.config.vocab_size), dtype=np.float32) if logits else None
+        check(lib().minq_prefill_batch(self._h, cache._h, toks.ctypes.data_as(C.c_void_p), n,
+                                       out.ctypes.data_as(C.c_void_p) if logits else None,
+                                       am.ctypes.data_as(C.c_void_p)))
+        return am, out
+
     def forward_batch_steps(self, cache: "KVCache", n: int, d_tokens_out: int | None = None):
         """Greedy continuation of a batch cache on the device: n batched steps,
         every sequence fed its previous argmax; no host synchronisation."""

@@ -68,10 +68,16 @@ namespace minq {
 
 constexpr int kMkCW = 16;                      // warps
 constexpr int kMkConsumers = 32 * kMkCW;       // threads (all of them load and compute)
-constexpr int kMkProducers = 4;                // copy warps; warp k issues tiles k, k + 4, ...
+#ifndef MINQ_MK_PRODUCERS
+#define MINQ_MK_PRODUCERS 4
+#endif
+#ifndef MINQ_MK_SLOTS
+#define MINQ_MK_SLOTS 8
+#endif
+constexpr int kMkProducers = MINQ_MK_PRODUCERS;  // copy warps; warp k issues tiles k, k + P, ...
 constexpr int kMkThreads = kMkConsumers + 32 * kMkProducers;
 constexpr int kMkSlot = 16384;                 // bytes per ring slot
-constexpr int kMkS = 8;                        // ring slots (a multiple of kMkProducers)
+constexpr int kMkS = MINQ_MK_SLOTS;            // ring slots (a multiple of kMkProducers)
 static_assert(kMkS % kMkProducers == 0, "each producer warp owns its own slots");
 // Projection inputs are staged as exact fixed-point planes: per 32-column
 // block, m = rint(x * 2^(kMkFx - e)) with 2^(e-1) <= max|x| < 2^e, written
@@ -1210,17 +1216,33 @@ __device__ void mk_consume_attn(const MkParams& p, int li, int L, unsigned hbase
     sm_o[i] = __ldcg(e + d);
   }
   mk_sync();
-  for (int j = tid; j < n_o; j += kMkConsumers) {
-    float M = -INFINITY;
-    for (int s_ = 0; s_ < ns; ++s_) M = fmaxf(M, sm_m[s_ * n_o + j]);
-    float Ls = 0.0f, O = 0.0f;
-    for (int s_ = 0; s_ < ns; ++s_) {
-      const float mw = sm_m[s_ * n_o + j];
-      const float fs = mw == -INFINITY ? 0.0f : expf(mw - M);
-      Ls = fmaf(sm_l[s_ * n_o + j], fs, Ls);
-      O = fmaf(sm_o[s_ * n_o + j], fs, O);
+  // 16 lanes per output: lane t of a half-warp takes the splits t, t + 16,
+  // ..., then max and sums over the half-warp (a uniform trip count keeps
+  // every lane of a warp in the shuffles)
+  {
+    const int sub = tid & 15;
+    const int jpass = (n_o + kMkConsumers / 16 - 1) / (kMkConsumers / 16);
+    for (int q = 0; q < jpass; ++q) {
+      const int j = q * (kMkConsumers / 16) + (tid >> 4);
+      const bool act = j < n_o;
+      float M = -INFINITY;
+      for (int s_ = sub; act && s_ < ns; s_ += 16) M = fmaxf(M, sm_m[s_ * n_o + j]);
+#pragma unroll
+      for (int o_ = 8; o_ > 0; o_ >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o_));
+      float Ls = 0.0f, O = 0.0f;
+      for (int s_ = sub; act && s_ < ns; s_ += 16) {
+        const float mw = sm_m[s_ * n_o + j];
+        const float fs = mw == -INFINITY ? 0.0f : expf(mw - M);
+        Ls = fmaf(sm_l[s_ * n_o + j], fs, Ls);
+        O = fmaf(sm_o[s_ * n_o + j], fs, O);
+      }
+#pragma unroll
+      for (int o_ = 8; o_ > 0; o_ >>= 1) {
+        Ls += __shfl_xor_sync(0xffffffffu, Ls, o_);
+        O += __shfl_xor_sync(0xffffffffu, O, o_);
+      }
+      if (act && sub == 0) p.att[(size_t)kh * no + o0 + j] = O * (1.0f / Ls);
     }
-    p.att[(size_t)kh * no + o0 + j] = O * (1.0f / Ls);
   }
 }
 

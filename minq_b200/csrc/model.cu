@@ -780,12 +780,13 @@ constexpr int kPrefillChunk = kQmmMaxB;
 // Whether the model takes chunked prefill (the batched step's shape rules,
 // one GPU), and its activations on first use. MINQ_CHUNKED_PREFILL=0 turns
 // chunked prompts off (use_env); the full-sequence sweep ignores it.
-static minq_status prefill_ready(minq_model* m, minq_cache* c, bool* ok, bool use_env = true) {
+static minq_status prefill_ready(minq_model* m, minq_cache* c, bool* ok, bool use_env = true,
+                                  bool any_batch = false) {
   *ok = false;
   const minq_config& cfg = m->cfg;
   const char* env = std::getenv("MINQ_CHUNKED_PREFILL");
   if (use_env && env && env[0] == '0') return MINQ_OK;
-  if (m->tp_world > 1 || c->batch != 1) return MINQ_OK;
+  if (m->tp_world > 1 || (c->batch != 1 && !any_batch)) return MINQ_OK;
   if (cfg.hidden_size % 32 || cfg.intermediate_size % 32 || (cfg.n_heads * cfg.head_dim) % 32)
     return MINQ_OK;
   for (const DevLayer& L : m->layers)
@@ -820,7 +821,8 @@ static minq_status prefill_ready(minq_model* m, minq_cache* c, bool* ok, bool us
 }
 
 // T <= kPrefillChunk tokens (device ids) at positions c->len .. c->len + T - 1.
-static minq_status forward_chunk(minq_model* m, minq_cache* c, const uint32_t* d_toks, int T) {
+static minq_status forward_chunk(minq_model* m, minq_cache* c, const uint32_t* d_toks, int T,
+                                 size_t seq = 0) {
   const minq_config& cfg = m->cfg;
   const int H = (int)cfg.hidden_size, hd = (int)cfg.head_dim, nh = (int)cfg.n_heads,
             nkv = (int)cfg.n_kv_heads;
@@ -829,7 +831,9 @@ static minq_status forward_chunk(minq_model* m, minq_cache* c, const uint32_t* d
   const float eps = cfg.rms_norm_eps;
   const int p0 = (int)c->len;
   cudaStream_t s = m->stream;
-  const size_t layer_elems = (size_t)nkv * c->max_seq * hd, head_stride = c->max_seq * hd;
+  // sequence `seq` of the cache ([layer][batch][kv head][max_seq][hd])
+  const size_t seq_elems = (size_t)nkv * c->max_seq * hd, layer_elems = c->batch * seq_elems,
+               head_stride = c->max_seq * hd;
   // causal chunk attention: the tensor-core kernel for head_dim 64 / 128
   // (MINQ_FLASH_PREFILL=0: the split-KV decode kernel, one entry per token)
   static const bool flash_env = [] {
@@ -844,8 +848,8 @@ static minq_status forward_chunk(minq_model* m, minq_cache* c, const uint32_t* d
     MINQ_TRY(launch_qmatmul(L.qkv.tag, L.qkv.ptr, nullptr, qkv_rows, H, T, c->px, H, L.attn_norm,
                             eps, c->pxn, c->pxn_floats, L.bias_qkv, nullptr, c->pqkv, qkv_rows,
                             c->ppart, c->ppart_floats, s));
-    float* kc = c->k + li * layer_elems;
-    float* vc = c->v + li * layer_elems;
+    float* kc = c->k + li * layer_elems + seq * seq_elems;
+    float* vc = c->v + li * layer_elems + seq * seq_elems;
     // token i: rotated at position p0 + i and appended there (one sequence:
     // sequence stride 0), then attends over p0 + i + 1 positions
     MINQ_TRY(launch_rope_append(c->pqkv, c->pqkv + qd, c->pqkv + qd + kvd, qkv_rows, qkv_rows,
@@ -1808,6 +1812,69 @@ static minq_status check_rows(const minq_model* m, const uint32_t* t, size_t n) 
       return fail(MINQ_ERR_SHAPE, "row index " + std::to_string(t[i]) + " out of bounds for " +
                                       std::to_string(m->cfg.vocab_size) + " rows");
   return MINQ_OK;
+}
+
+minq_status minq_prefill_batch(minq_model* m, minq_cache* c, const uint32_t* tokens, size_t n,
+                               float* logits_out, uint32_t* argmax_out) {
+  if (!m || !c) return fail(MINQ_ERR_ARG, "null argument");
+  if (c->m != m) return fail(MINQ_ERR_ARG, "cache belongs to another model");
+  if (n == 0 || !tokens) return fail(MINQ_ERR_MODEL, "empty token sequence");
+  if (!m->shape_error.empty()) return fail(MINQ_ERR_SHAPE, m->shape_error);
+  MINQ_CUDA_TRY(cudaSetDevice(m->device));
+  const size_t B = c->batch;
+  if (c->len + n > m->cfg.max_seq_len)  // model.rs:260-265
+    return fail(MINQ_ERR_MODEL,
+                "sequence exceeds max_seq_len (" + std::to_string(m->cfg.max_seq_len) + ")");
+  if (c->len + n > c->max_seq)
+    return fail(MINQ_ERR_MODEL,
+                "sequence exceeds the cache capacity (" + std::to_string(c->max_seq) + ")");
+  MINQ_TRY(check_rows(m, tokens, B * n));
+  MINQ_TRY(batch_ready(m, c));
+  bool chunked = false;
+  MINQ_TRY(prefill_ready(m, c, &chunked, true, true));
+  const size_t p0 = c->len;
+  std::vector<uint32_t> col(B);
+  if (chunked && n > 1) {
+    // every sequence's prompt but its last token, in chunks of 64 tokens at
+    // the common positions p0 .. p0 + n - 2 of that sequence's cache
+    MINQ_TRY(upload_tokens(m, tokens, B * n));
+    for (size_t b = 0; b < B; ++b) {
+      c->len = p0;
+      for (size_t i = 0; i + 1 < n; i += kPrefillChunk) {
+        const int T = (int)std::min<size_t>(kPrefillChunk, n - 1 - i);
+        minq_status st = forward_chunk(m, c, m->d_tokens + b * n + i, T, b);
+        if (st != MINQ_OK) {
+          c->len = p0;
+          return st;
+        }
+      }
+    }
+    c->len = p0 + n - 1;
+    c->d_pos_valid = false;
+  } else {
+    for (size_t i = 0; i + 1 < n; ++i) {  // one batched step per prompt position
+      for (size_t b = 0; b < B; ++b) col[b] = tokens[b * n + i];
+      MINQ_CUDA_TRY(cudaMemcpyAsync(c->btok, col.data(), B * 4, cudaMemcpyHostToDevice, m->stream));
+      MINQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
+      MINQ_TRY(forward_batch_step(m, c, false));
+      c->len += 1;
+      c->d_pos_valid = false;
+    }
+  }
+  // the last prompt token of every sequence as one batched step (logits)
+  for (size_t b = 0; b < B; ++b) col[b] = tokens[b * n + n - 1];
+  MINQ_CUDA_TRY(cudaMemcpyAsync(c->btok, col.data(), B * 4, cudaMemcpyHostToDevice, m->stream));
+  const bool want = logits_out || argmax_out;
+  MINQ_TRY(forward_batch_step(m, c, want));
+  c->len += 1;
+  c->d_pos_valid = false;
+  if (logits_out)
+    MINQ_CUDA_TRY(cudaMemcpyAsync(logits_out, c->blog, B * m->cfg.vocab_size * 4,
+                                  cudaMemcpyDeviceToHost, m->stream));
+  if (argmax_out)
+    MINQ_CUDA_TRY(cudaMemcpyAsync(argmax_out, c->barg, B * 4, cudaMemcpyDeviceToHost, m->stream));
+  MINQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  return take_device_status();
 }
 
 // A batch-1 scratch cache of max_seq positions with the chunk buffers (and,

@@ -165,7 +165,8 @@ def test_gpu_attend_golden(mq, golden, torch):
 
 @pytest.mark.parametrize("nh,nkv,hd,L", [(4, 4, 16, 1), (4, 2, 16, 2), (14, 2, 64, 31),
                                          (14, 2, 64, 700), (32, 8, 128, 1), (32, 8, 128, 33),
-                                         (32, 8, 128, 2049), (32, 8, 128, 8192), (4, 1, 8, 70),
+                                         (32, 8, 128, 2049), (32, 8, 128, 8192), (32, 8, 128, 32768),
+                                         (4, 1, 8, 70),
                                          (16, 1, 32, 300), (64, 4, 256, 129)])
 def test_gpu_attend_matches_oracle(mq, orc, torch, nh, nkv, hd, L):
     rng = np.random.default_rng(nh * L + hd)
@@ -178,7 +179,8 @@ def test_gpu_attend_matches_oracle(mq, orc, torch, nh, nkv, hd, L):
 
 
 @pytest.mark.parametrize("B,L,qk_norm", [(1, 512, False), (8, 512, True), (1, 2048, True),
-                                         (64, 512, False), (8, 8192, False)])
+                                         (64, 512, False), (8, 8192, False), (64, 2048, True),
+                                         (1, 32768, False)])
 def test_gpu_attn_decode_step_matches_oracle(mq, orc, torch, B, L, qk_norm):
     """Decode-attention op (GQA 32/8, hd 128): RoPE(theta 1e6) on q and the new k at
     pos = L, optional q/k RMSNorm, append, attend over L+1 positions — against the

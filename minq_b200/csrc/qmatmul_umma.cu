@@ -51,6 +51,7 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -120,6 +121,8 @@ struct UmParams {
   float* y;               // [B][y_stride]
   size_t y_stride;
   float* part;            // S > 1: [S][halves][B][rows]
+  int tile0;              // first row tile of the launch (blockIdx.x + tile0)
+  size_t row0, nrows;     // rows the reduce kernel finishes (S > 1)
   int* status;
 };
 
@@ -413,7 +416,7 @@ __global__ void __launch_bounds__(UmGeom<DT, NP>::THREADS, 1)
   const int slice = blockIdx.y;
   const int kc0 = slice * p.slice_chunks;
   const int nch = min(p.nchunks, kc0 + p.slice_chunks) - kc0;
-  const size_t rb = (size_t)blockIdx.x * HR;  // first row of each matrix
+  const size_t rb = (size_t)(blockIdx.x + p.tile0) * HR;  // first row of each matrix
 
   if (warp == 0) {
     if (lane == 0) {
@@ -698,10 +701,10 @@ __global__ void __launch_bounds__(256) um_reduce_kernel(UmParams p) {
   pdl_wait();
   pdl_launch_dependents();
   constexpr int H2 = DUAL ? 2 : 1;
-  const size_t n = (size_t)p.B * p.rows;
+  const size_t n = (size_t)p.B * p.nrows;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x) {
-    const size_t b = i / p.rows, row = i - b * p.rows;
+    const size_t b = i / p.nrows, row = p.row0 + (i - b * p.nrows);
     float v[H2];
 #pragma unroll
     for (int hh = 0; hh < H2; ++hh) {
@@ -791,7 +794,7 @@ minq_status um_launch(const void* w0, const void* w1, const __nv_bfloat16* xh,
   MINQ_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(k), smem));
   MINQ_CUDA_TRY(launch_k(k, dim3(tiles, (unsigned)p.S), dim3(G::THREADS), smem, s, m0, m1, mh, ml, p));
   if (p.S > 1) {
-    const size_t n = (size_t)p.B * p.rows;
+    const size_t n = (size_t)p.B * p.nrows;
     const unsigned gr = (unsigned)std::min<size_t>((n + 255) / 256, 148 * 8);
     MINQ_CUDA_TRY(launch_k(um_reduce_kernel<DUAL>, dim3(gr), dim3(256), 0, s, p));
   }
@@ -845,20 +848,68 @@ minq_status launch_qmatmul_umma(int dtype, const void* w0, const void* w1, size_
   const int hr = dual ? rows_cta / 2 : rows_cta;
   const size_t tiles = (rows + hr - 1) / hr;
   p.nchunks = cols / (kUmChunkBlocks * kBlock);
-  // K slices: at most one wave of CTAs (one per SM), each slice at least
-  // two chunks, the partials within the workspace
+  p.tile0 = 0;
+  p.row0 = 0;
+  p.nrows = rows;
+  // K slices. Cost model in units of one full-K CTA's time: waves of CTAs
+  // (one per SM) / slices, plus ~2 % per slice for the partials' reduce.
+  // Single launch: S slices of every row tile. When the row tiles overrun
+  // whole waves by a few (Qwen3-4B gate/up: 152 tiles on 148 SMs), the
+  // overrun tiles go to a second launch split over the SMs instead of
+  // taking a whole extra wave each.
   const size_t sms = (size_t)sm_count();
-  int S = (int)std::max<size_t>(1, sms / tiles);
-  S = std::min(S, std::max(1, p.nchunks / 2));
   const int halves = dual ? 2 : 1;
-  while (S > 1 && (!part || (size_t)S * halves * B * rows > part_floats)) --S;
-  p.slice_chunks = (p.nchunks + S - 1) / S;
-  p.S = (p.nchunks + p.slice_chunks - 1) / p.slice_chunks;
-  if (dtype == MINQ_Q4_0)
-    return dual ? um_dispatch_n<MINQ_Q4_0, true>(w0, w1, xh, xl, cols, p, (unsigned)tiles, s)
-                : um_dispatch_n<MINQ_Q4_0, false>(w0, w1, xh, xl, cols, p, (unsigned)tiles, s);
-  return dual ? um_dispatch_n<MINQ_Q8_0, true>(w0, w1, xh, xl, cols, p, (unsigned)tiles, s)
-              : um_dispatch_n<MINQ_Q8_0, false>(w0, w1, xh, xl, cols, p, (unsigned)tiles, s);
+  const int smax = std::max(1, p.nchunks / 2);  // each slice at least two chunks
+  auto fits = [&](int S) {
+    return S == 1 || (part && (size_t)S * halves * B * rows <= part_floats);
+  };
+  constexpr double kRed = 0.02;
+  double best = 1e30;
+  int S = 1;
+  for (int c = 1; c <= smax && fits(c); ++c) {
+    const double cost = (double)((tiles * c + sms - 1) / sms) / c + (c > 1 ? kRed * c : 0.0);
+    if (cost < best - 1e-9) {
+      best = cost;
+      S = c;
+    }
+  }
+  static const bool plan_env = [] {  // MINQ_UM_PLAN=0: one wave-filling rule only
+    const char* e = std::getenv("MINQ_UM_PLAN");
+    return !(e && e[0] == '0');
+  }();
+  if (!plan_env) {
+    S = (int)std::min<size_t>(std::max<size_t>(1, sms / tiles), (size_t)smax);
+    while (S > 1 && !fits(S)) --S;
+  }
+  size_t head = tiles;
+  int St = 1;
+  if (plan_env && tiles > sms && tiles % sms != 0) {
+    const size_t h = tiles / sms * sms, tail = tiles - h;
+    int c = std::min(smax, (int)(sms / tail));
+    while (c > 1 && !fits(c)) --c;
+    const double cost = (double)(h / sms) + 1.0 / c + kRed * c * (double)tail / (double)tiles;
+    if (c > 1 && cost < best - 1e-9) {
+      head = h;
+      St = c;
+    }
+  }
+  auto go = [&](UmParams q, size_t t0, size_t nt, int slices) -> minq_status {
+    q.tile0 = (int)t0;
+    q.slice_chunks = (q.nchunks + slices - 1) / slices;
+    q.S = (q.nchunks + q.slice_chunks - 1) / q.slice_chunks;
+    q.row0 = t0 * hr;
+    q.nrows = std::min(rows, (t0 + nt) * hr) - q.row0;
+    if (dtype == MINQ_Q4_0)
+      return dual ? um_dispatch_n<MINQ_Q4_0, true>(w0, w1, xh, xl, cols, q, (unsigned)nt, s)
+                  : um_dispatch_n<MINQ_Q4_0, false>(w0, w1, xh, xl, cols, q, (unsigned)nt, s);
+    return dual ? um_dispatch_n<MINQ_Q8_0, true>(w0, w1, xh, xl, cols, q, (unsigned)nt, s)
+                : um_dispatch_n<MINQ_Q8_0, false>(w0, w1, xh, xl, cols, q, (unsigned)nt, s);
+  };
+  if (head < tiles) {
+    MINQ_TRY(go(p, 0, head, 1));
+    return go(p, head, tiles - head, St);
+  }
+  return go(p, 0, tiles, S);
 }
 
 }  // namespace minq

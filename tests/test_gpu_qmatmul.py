@@ -61,6 +61,10 @@ CASES = [
     (1, 4864, 896, 32),
     (1, 2560, 4096, 64),
     (1, 129, 384, 3),
+    # row tiles past one wave of SMs: 152 tiles = 148 + 4 (the 4 split over
+    # the SMs in a second launch), and 224 tiles (every tile in K slices)
+    (2, 19456, 512, 16),
+    (2, 28672, 1024, 64),
 ]
 
 

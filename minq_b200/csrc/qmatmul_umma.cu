@@ -24,24 +24,25 @@
 //   warp 0           TMA, one elected lane: per chunk the raw weight rows (a
 //                    2-D box of the row-major block stream, no swizzle,
 //                    evict-first) and the four 64-column x_hi / x_lo tiles
-//                    (128-byte swizzle; x_hi rows then x_lo rows, the
-//                    B operand of N = 2 NP); warp 0 also owns the TMEM
-//                    allocation
+//                    (128-byte swizzle; x_hi rows then x_lo rows, each
+//                    half a B operand of N = NP); warp 0 also owns the
+//                    TMEM allocation
 //   warps 1, 2       tcgen05.mma issue, one lane each: warp 1 blocks 0-1 of
 //                    every chunk, warp 2 blocks 2-3. A comes from TMEM (the
 //                    chunk's A tile), B from the stage; block g accumulates
-//                    in TMEM set g mod NBUF with two k-step MMAs, then
+//                    in TMEM set g mod NBUF with four MMAs (two k steps,
+//                    x_hi and x_lo into the same columns), then
 //                    tcgen05.commit to that set's barrier
 //   4 unpacker warps thread = weight row (TMEM lane): the chunk's codes ->
 //                    exact bf16 with lop3 / one bf16 subtraction per pair,
 //                    tcgen05.st into A tile (chunk mod 2)
 //   4 WG epilogue    thread = weight row and CW inputs: tcgen05.ld of each
-//   warps            block's hi and lo sums, release of the set, then
-//                    (acc_hi, acc_lo) += d * (sum_hi, sum_lo) as one paired
-//                    FMA, in block order; at the end acc_hi + acc_lo, bias /
-//                    residual / SwiGLU and the store (or the slice partial)
-// With fewer row tiles than SMs the K range splits into S slices whose
-// partials um_reduce_kernel sums in slice order.
+//   warps            block's sums, release of the set, then acc += d * sum
+//                    in block order; at the end bias / residual / SwiGLU
+//                    and the store (or the slice partial)
+// The K range splits into S slices (a wave cost model picks S; row tiles
+// that overrun whole waves go to a second launch) whose partials
+// um_reduce_kernel sums in slice order.
 // Every mbarrier wait is time-bounded (1 s); a timeout sets the device
 // status word and an abort flag that ends every role's loop, after which
 // the producer waits for its copies in flight, the MMA threads for their
@@ -76,10 +77,12 @@ constexpr int pow2_at_least(int v) {
   return p;
 }
 
-// NP: inputs padded to 16 / 32 / 64. One MMA (M = 128 weight rows, K = 16)
-// takes x_hi and x_lo of all NP inputs as its N = 2 NP columns: measured on
-// B200, a kind::f16 MMA costs ~51 cycles for any N <= 64 (64 at N = 128), so
-// stacking the two parts halves the MMA time of a chunk.
+// NP: inputs padded to 16 / 32 / 64. The stage holds x_hi and x_lo of the NP
+// inputs as 2 NP rows; each part is the B operand (N = NP) of its own MMA
+// into the same accumulator columns. (Stacking both as one MMA of N = 2 NP
+// costs less tensor time -- a kind::f16 MMA takes ~51 cycles for any N <= 64,
+// 64 at N = 128 -- but doubles the columns of an accumulator set and so
+// halves the sets in flight; the tensor pipe is not what bounds the kernel.)
 template <int DT, int NP>
 struct UmGeom {
   static constexpr int ROWS = 128;                            // weight rows per CTA
@@ -96,12 +99,18 @@ struct UmGeom {
   static constexpr int EPI = 4 * WG;                          // epilogue warps
   static constexpr int WARPS = kUmCtrlWarps + UNP + EPI;
   static constexpr int THREADS = 32 * WARPS;
-  static constexpr int NBUF = NN <= 64 ? 4 : 3;               // TMEM accumulator sets (block g: set g mod NBUF)
-  static constexpr int ACC_COLS = NBUF * NN;                  // TMEM columns of the accumulators
+  // x_hi and x_lo accumulate into the same TMEM columns (two MMAs of N = NP
+  // per k step): an accumulator set is NP columns, so up to 8 sets rotate
+  // between the MMA issuers and the epilogue (measured against one MMA of
+  // N = 2 NP into 2 NP columns with 3-4 sets: LLaMA-3-8B x 64 batched step
+  // 10.05 -> 8.38 ms, Qwen3-4B 2048-token prefill 10030 -> 11560 tok/s)
+  static constexpr int NACC = NP;                             // TMEM columns of one accumulator set
+  static constexpr int NBUF = (384 / NACC) < 8 ? 384 / NACC : 8;  // sets (block g: set g mod NBUF)
+  static constexpr int ACC_COLS = NBUF * NACC;                // TMEM columns of the accumulators
   static constexpr int A_COL0 = ACC_COLS;                     // A tiles: 2 chunks x 4 blocks x 16 columns
   static constexpr int TMEM_COLS = pow2_at_least(A_COL0 + 128);
   // dynamic shared memory for S stages: alignment slack, ring, barriers
-  static constexpr size_t smem(int S) { return 1024 + (size_t)S * stage_bytes + 256; }
+  static constexpr size_t smem(int S) { return 1024 + (size_t)S * stage_bytes + 512; }
   static constexpr int max_stages() {
     int s = kUmMaxStages;
     while (s > 2 && smem(s) > kUmSmemLimit) --s;
@@ -408,8 +417,8 @@ __global__ void __launch_bounds__(UmGeom<DT, NP>::THREADS, 1)
   uint64_t* afull = empty + kUmMaxStages;
   uint64_t* aempty = afull + 2;
   uint64_t* accfull = aempty + 2;
-  uint64_t* accempty = accfull + 4;
-  uint64_t* mma_done = accempty + 4;
+  uint64_t* accempty = accfull + 8;
+  uint64_t* mma_done = accempty + 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 2);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -487,7 +496,8 @@ __global__ void __launch_bounds__(UmGeom<DT, NP>::THREADS, 1)
   } else if (warp == 1 || warp == 2) {
     // ---------------- MMA issue: lane 0 of warp 1 issues blocks 0-1 of
     // every chunk, lane 0 of warp 2 blocks 2-3 (A tile cl mod 2; block g
-    // accumulates in set g mod NBUF with two MMAs, k steps, of N = 2 NP).
+    // accumulates in set g mod NBUF with four MMAs of N = NP: two k steps,
+    // x_hi and x_lo).
     // A kind::f16 MMA of N <= 64 takes ~51 cycles in the tensor core, about
     // the latency of a handful of dependent instructions of one thread, so
     // two threads issue, and each keeps its per-block work to a barrier
@@ -495,7 +505,7 @@ __global__ void __launch_bounds__(UmGeom<DT, NP>::THREADS, 1)
     // and the stage and its phase advance incrementally.
     const int hi = warp - 1;  // which pair of blocks
     if (lane == 0) {
-      constexpr uint32_t idesc = um_idesc<NN>();
+      constexpr uint32_t idesc = um_idesc<NP>();
       const uint64_t bdesc0 = sw128_desc(ring) + (uint64_t)((uint32_t)(hi * G::xsub_bytes) >> 4);
       const uint32_t a_tm = tmem + (uint32_t)(G::A_COL0 + hi * 32);
       int s = 0;                  // stage of chunk cl
@@ -518,9 +528,14 @@ __global__ void __launch_bounds__(UmGeom<DT, NP>::THREADS, 1)
             break;
           }
           tc05_fence_after();
-          const uint32_t d = tmem + (uint32_t)(t * NN);
+          const uint32_t d = tmem + (uint32_t)(t * G::NACC);
+          // x_lo rows start NP rows (NP * 128 bytes) after x_hi's
+          constexpr uint32_t lo = (uint32_t)(NP * 128) >> 4;
           umma_bf16_ts(d, as + (uint32_t)(jj * 16), bs + (uint64_t)((jj * 64) >> 4), idesc, 0u);
+          umma_bf16_ts(d, as + (uint32_t)(jj * 16), bs + (uint64_t)(((jj * 64) >> 4) + lo), idesc, 1u);
           umma_bf16_ts(d, as + (uint32_t)(jj * 16 + 8), bs + (uint64_t)((jj * 64 + 32) >> 4), idesc, 1u);
+          umma_bf16_ts(d, as + (uint32_t)(jj * 16 + 8), bs + (uint64_t)(((jj * 64 + 32) >> 4) + lo),
+                       idesc, 1u);
           umma_commit(&accfull[t]);
           g += jj == 0 ? 1 : 3;  // next block of this issuer (skip the other pair)
         }
@@ -588,9 +603,9 @@ __global__ void __launch_bounds__(UmGeom<DT, NP>::THREADS, 1)
     const int v = q * 32 + lane;
     const uint32_t lq = (uint32_t)(q * 32) << 16;
     constexpr int JB = 1;                    // blocks per epilogue step (2 measured no faster)
-    float2 acc[CW];
+    float acc[CW];
 #pragma unroll
-    for (int i = 0; i < CW; ++i) acc[i] = make_float2(0.0f, 0.0f);
+    for (int i = 0; i < CW; ++i) acc[i] = 0.0f;
     bool ok = true;
     for (int cl = 0; cl < nch && ok; ++cl) {
       const int s = cl % S, w = cl / S;
@@ -603,24 +618,19 @@ __global__ void __launch_bounds__(UmGeom<DT, NP>::THREADS, 1)
       // wait::ld, the releases, then the FMAs (fewer serial steps per block)
 #pragma unroll
       for (int j0 = 0; j0 < kUmChunkBlocks; j0 += JB) {
-        uint32_t r[JB][2 * CW];
+        uint32_t r[JB][CW];
 #pragma unroll
         for (int jb = 0; jb < JB; ++jb) {
           const int g = 4 * cl + j0 + jb, t = g % G::NBUF, vv = g / G::NBUF;
           if (!um_wait_warp(&accfull[t], (uint32_t)(vv & 1), abort, p.status)) { ok = false; break; }
           tc05_fence_after();
-          const uint32_t ta = tmem + lq + (uint32_t)(t * NN + u * CW);
-          if constexpr (CW == 8) {
-            tmem_ld8(ta, r[jb]);
-            tmem_ld8(ta + NP, r[jb] + 8);
-          } else {
-            tmem_ld16(ta, r[jb]);
-            tmem_ld16(ta + NP, r[jb] + 16);
-          }
+          const uint32_t ta = tmem + lq + (uint32_t)(t * G::NACC + u * CW);
+          if constexpr (CW == 8) tmem_ld8(ta, r[jb]);  // one sum per input (x_hi + x_lo)
+          else tmem_ld16(ta, r[jb]);
         }
         if (!ok) break;
 #pragma unroll
-        for (int jb = 0; jb < JB; ++jb) tmem_wait_ld<2 * CW>(r[jb]);
+        for (int jb = 0; jb < JB; ++jb) tmem_wait_ld<CW>(r[jb]);
         tc05_fence_before();
         __syncwarp();
         if (lane == 0) {
@@ -629,10 +639,8 @@ __global__ void __launch_bounds__(UmGeom<DT, NP>::THREADS, 1)
         }
 #pragma unroll
         for (int jb = 0; jb < JB; ++jb) {
-          const float2 d2 = make_float2(dsc[j0 + jb], dsc[j0 + jb]);
 #pragma unroll
-          for (int i = 0; i < CW; ++i)
-            acc[i] = __ffma2_rn(d2, make_float2(__uint_as_float(r[jb][i]), __uint_as_float(r[jb][CW + i])), acc[i]);
+          for (int i = 0; i < CW; ++i) acc[i] = fmaf(dsc[j0 + jb], __uint_as_float(r[jb][i]), acc[i]);
         }
       }
       __syncwarp();
@@ -642,7 +650,7 @@ __global__ void __launch_bounds__(UmGeom<DT, NP>::THREADS, 1)
     // store: row of this thread and its CW inputs
     float accs[CW];
 #pragma unroll
-    for (int i = 0; i < CW; ++i) accs[i] = acc[i].x + acc[i].y;
+    for (int i = 0; i < CW; ++i) accs[i] = acc[i];
     const bool up = DUAL && v >= HR;
     const size_t row = rb + (size_t)(DUAL ? v % HR : v);
     if (p.S > 1 || !DUAL) {

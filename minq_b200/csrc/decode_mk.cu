@@ -54,7 +54,6 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
-#include <cstdlib>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -68,16 +67,10 @@ namespace minq {
 
 constexpr int kMkCW = 16;                      // warps
 constexpr int kMkConsumers = 32 * kMkCW;       // threads (all of them load and compute)
-#ifndef MINQ_MK_PRODUCERS
-#define MINQ_MK_PRODUCERS 4
-#endif
-#ifndef MINQ_MK_SLOTS
-#define MINQ_MK_SLOTS 8
-#endif
-constexpr int kMkProducers = MINQ_MK_PRODUCERS;  // copy warps; warp k issues tiles k, k + P, ...
+constexpr int kMkProducers = 4;                // copy warps; warp k issues tiles k, k + 4, ...
 constexpr int kMkThreads = kMkConsumers + 32 * kMkProducers;
 constexpr int kMkSlot = 16384;                 // bytes per ring slot
-constexpr int kMkS = MINQ_MK_SLOTS;            // ring slots (a multiple of kMkProducers)
+constexpr int kMkS = 8;                        // ring slots (a multiple of kMkProducers)
 static_assert(kMkS % kMkProducers == 0, "each producer warp owns its own slots");
 // Projection inputs are staged as exact fixed-point planes: per 32-column
 // block, m = rint(x * 2^(kMkFx - e)) with 2^(e-1) <= max|x| < 2^e, written
@@ -779,14 +772,9 @@ __device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const uint32_t
   constexpr int BB = DT == MINQ_Q8_0 ? kQ8Bytes : kQ4Bytes;
   constexpr int TB = MkTile<DT>::blocks;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nb = m.cols / kBlock;
-  const bool seg = m.rps > 0;  // several rows per step, row sums per half-warp
-  const int WG = seg ? m.wg : (nb + 31) >> 5, T = kMkCW / WG, RPS = seg ? m.rps : 1;
-  const int SL = seg ? nb >> 4 : WG;  // row-sum slots of a row
-  const int grp = warp / WG, wc = warp - grp * WG, li = 32 * wc + lane;
-  const int col = seg ? li % nb : li, rsub = seg ? li / nb : 0;
-  const int slot = seg ? ((li & ~15) % nb) >> 4 : wc;  // this half-warp's / warp's slot
-  const bool in_grp = grp < T, has_col = in_grp && (seg ? rsub < RPS : col < nb);
+  const int nb = m.cols / kBlock, WG = (nb + 31) >> 5, T = kMkCW / WG;
+  const int grp = warp / WG, wc = warp - grp * WG, col = 32 * wc + lane;
+  const bool in_grp = grp < T, has_col = in_grp && col < nb;
   int rb, cnt;
   mk_share(m.rows, &rb, &cnt);
   const int halves = DUAL ? 2 : 1;
@@ -806,7 +794,7 @@ __device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const uint32_t
     if (has_col) sb = xsb[col];
   }
   const float pre = tid < cnt ? pre_ld(rb + tid) : 0.0f;  // cnt <= 512
-  const int plane = halves * cnt * SL;  // floats per tile parity
+  const int plane = halves * cnt * WG;  // floats per tile parity
   for (int i = tid; i < 2 * plane; i += kMkConsumers) red[i] = 0.0f;
   mk_sync();
   const int total = cnt * nb;  // < 2^16 for every eligible shape
@@ -816,35 +804,8 @@ __device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const uint32_t
     const int half = DUAL ? (tt & 1) : 0, k = DUAL ? tt >> 1 : tt;
     const int g0 = k * TB, g1 = min(g0 + TB, total);
     const int r_lo = g0 / nb, r_hi = (g1 - 1) / nb;
-    float* rr = red + (k & 1) * plane + half * cnt * SL + slot;
+    float* rr = red + (k & 1) * plane + half * cnt * WG + wc;
     const uint32_t base = smem_u32(tile) - (uint32_t)(g0 * BB);  // block g at base + g * BB
-    if (seg) {  // rows R + RPS k + rsub, k = 0..3
-      for (int R = r_lo; R <= r_hi; R += 4 * RPS) {
-        float v[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int row = R + RPS * k + rsub, g = row * nb + col;
-          v[k] = has_col && row <= r_hi && g >= g0 && g < g1
-                     ? mk_block_dot<DT>(base + (uint32_t)(g * BB), xw) * sb
-                     : 0.0f;
-        }
-        // transposed sum inside each half-warp (its lanes share one row of
-        // each step): lanes with bit 3 keep rows 2, 3, then lanes with bit 2
-        // the odd row; lanes 0, 4, 8, 12 of the half end with rows k = 0..3
-        const bool u8 = lane & 8, u4 = lane & 4;
-        float a0 = u8 ? v[2] : v[0], a1 = u8 ? v[3] : v[1];
-        a0 += __shfl_xor_sync(0xffffffffu, u8 ? v[0] : v[2], 8);
-        a1 += __shfl_xor_sync(0xffffffffu, u8 ? v[1] : v[3], 8);
-        float s = u4 ? a1 : a0;
-        s += __shfl_xor_sync(0xffffffffu, u4 ? a0 : a1, 4);
-        s += __shfl_xor_sync(0xffffffffu, s, 2);
-        s += __shfl_xor_sync(0xffffffffu, s, 1);
-        const int k = ((lane >> 2) & 2) | ((lane >> 2) & 1);
-        const int row = R + RPS * k + rsub;
-        if ((lane & 3) == 0 && has_col && row <= r_hi) rr[(size_t)row * SL] = s;
-      }
-      return;
-    }
     for (int R = r_lo; R <= r_hi; R += 4) {  // four rows at a time for ILP
       float v[4];
 #pragma unroll
@@ -867,7 +828,7 @@ __device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const uint32_t
       s += __shfl_xor_sync(0xffffffffu, s, 2);
       s += __shfl_xor_sync(0xffffffffu, s, 1);
       const int k = ((lane >> 4) << 1) | ((lane >> 3) & 1);
-      if ((lane & 7) == 0 && R + k <= r_hi) rr[(size_t)(R + k) * SL] = s;
+      if ((lane & 7) == 0 && R + k <= r_hi) rr[(size_t)(R + k) * WG] = s;
     }
   };
   // Group g computes the tiles g, g + T, ...: its warps wait only for those
@@ -887,9 +848,9 @@ __device__ void mk_consume_mat(const MkParams& p, const MkMat& m, const uint32_t
     const int t = tid;
     float v0 = 0.0f, v1 = 0.0f;
     for (int q = 0; q < 2; ++q)
-      for (int w = 0; w < SL; ++w) {
-        v0 += red[q * plane + (size_t)t * SL + w];
-        if (DUAL) v1 += red[q * plane + ((size_t)cnt + t) * SL + w];
+      for (int w = 0; w < WG; ++w) {
+        v0 += red[q * plane + (size_t)t * WG + w];
+        if (DUAL) v1 += red[q * plane + ((size_t)cnt + t) * WG + w];
       }
     if (norm_ss) {  // the RMSNorm scale of the staged input (mk_stage_planes)
       float ss = 0.0f;
@@ -1216,33 +1177,17 @@ __device__ void mk_consume_attn(const MkParams& p, int li, int L, unsigned hbase
     sm_o[i] = __ldcg(e + d);
   }
   mk_sync();
-  // 16 lanes per output: lane t of a half-warp takes the splits t, t + 16,
-  // ..., then max and sums over the half-warp (a uniform trip count keeps
-  // every lane of a warp in the shuffles)
-  {
-    const int sub = tid & 15;
-    const int jpass = (n_o + kMkConsumers / 16 - 1) / (kMkConsumers / 16);
-    for (int q = 0; q < jpass; ++q) {
-      const int j = q * (kMkConsumers / 16) + (tid >> 4);
-      const bool act = j < n_o;
-      float M = -INFINITY;
-      for (int s_ = sub; act && s_ < ns; s_ += 16) M = fmaxf(M, sm_m[s_ * n_o + j]);
-#pragma unroll
-      for (int o_ = 8; o_ > 0; o_ >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o_));
-      float Ls = 0.0f, O = 0.0f;
-      for (int s_ = sub; act && s_ < ns; s_ += 16) {
-        const float mw = sm_m[s_ * n_o + j];
-        const float fs = mw == -INFINITY ? 0.0f : expf(mw - M);
-        Ls = fmaf(sm_l[s_ * n_o + j], fs, Ls);
-        O = fmaf(sm_o[s_ * n_o + j], fs, O);
-      }
-#pragma unroll
-      for (int o_ = 8; o_ > 0; o_ >>= 1) {
-        Ls += __shfl_xor_sync(0xffffffffu, Ls, o_);
-        O += __shfl_xor_sync(0xffffffffu, O, o_);
-      }
-      if (act && sub == 0) p.att[(size_t)kh * no + o0 + j] = O * (1.0f / Ls);
+  for (int j = tid; j < n_o; j += kMkConsumers) {
+    float M = -INFINITY;
+    for (int s_ = 0; s_ < ns; ++s_) M = fmaxf(M, sm_m[s_ * n_o + j]);
+    float Ls = 0.0f, O = 0.0f;
+    for (int s_ = 0; s_ < ns; ++s_) {
+      const float mw = sm_m[s_ * n_o + j];
+      const float fs = mw == -INFINITY ? 0.0f : expf(mw - M);
+      Ls = fmaf(sm_l[s_ * n_o + j], fs, Ls);
+      O = fmaf(sm_o[s_ * n_o + j], fs, O);
     }
+    p.att[(size_t)kh * no + o0 + j] = O * (1.0f / Ls);
   }
 }
 
@@ -1476,26 +1421,6 @@ MkMat mk_plan_mat(int dtype, bool dual, uint64_t rows, uint64_t cols, int grid) 
     return m;
   m.rows = (int)rows;
   m.cols = (int)cols;
-  // Lanes computing at once: (16 / wg groups) x (rows per step) x nb. With
-  // one row per step a group of ceil(nb / 32) warps leaves lanes idle when
-  // nb is not a multiple of 32 (nb = 80: 400 of 512); when half-warps can
-  // own whole row pieces (nb % 16 == 0), a group whose lanes hold several
-  // rows' blocks may use more of them (nb = 80: 5 warps x 2 rows, 480).
-  const uint64_t lanes0 = ((uint64_t)kMkCW / wg) * nb;
-  const char* env = std::getenv("MINQ_MK_MULTIROW");  // 0: one row per step everywhere
-  if (nb % 16 == 0 && !(env && env[0] == '0')) {
-    uint64_t best = lanes0;
-    for (uint64_t w = 1; w <= (uint64_t)kMkCW; ++w) {
-      const uint64_t rps = 32 * w / nb;
-      if (rps < 1 || rps > 8) continue;
-      const uint64_t lanes = ((uint64_t)kMkCW / w) * rps * nb;
-      if (lanes > best && 2 * (dual ? 2 : 1) * rmax * (nb / 16) <= 2048) {
-        best = lanes;
-        m.wg = (int)w;
-        m.rps = (int)rps;
-      }
-    }
-  }
   return m;
 }
 

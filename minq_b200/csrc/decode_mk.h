@@ -15,11 +15,6 @@ namespace minq {
 struct MkMat {
   int rows;
   int cols;
-  // consumer mapping: rps == 0: a group of ceil(cols / 1024) warps, one
-  // column block per lane, one row per step; rps > 0 (cols / 32 a multiple
-  // of 16): groups of wg warps whose lanes cover rps rows of a step (lane i:
-  // block i mod nb of row i / nb), row sums per half-warp
-  int wg, rps;
 };
 
 // Per-layer weights and vectors (device array).

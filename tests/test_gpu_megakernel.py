@@ -61,9 +61,8 @@ CASES = [
     ("q4_gqa4_hd128_qknorm", "q4_0", 512, 768, 8, 2, 128, 257, True, False, 12),
     ("q4_mha_hd64", "q4_0", 128, 256, 2, 2, 64, 129, False, False, 7),
     ("q8_gqa8_hd128", "q8_0", 256, 384, 8, 1, 128, 200, True, True, 9),
-    # 48 column blocks: groups of 3 warps cover two rows per step (a warp
-    # straddles the rows), the half-warp row sums of the multi-row mapping
-    ("q4_h1536_two_rows_per_step", "q4_0", 1536, 1280, 12, 4, 128, 300, True, False, 9),
+    # 48 column blocks per row (two warps, 16 idle lanes), 40 for down_proj
+    ("q4_h1536_i1280", "q4_0", 1536, 1280, 12, 4, 128, 300, True, False, 9),
 ]
 
 

@@ -66,6 +66,9 @@ TP_WORKLOAD = "qwen3-4b-q8_0-tp32k"
 # Batched decode: 64 independent greedy sequences of the LLaMA-3-8B shape in
 # Q4_0 (512-token prompts), data-sharded over the ranks with no collective.
 BATCH_WORKLOAD = "llama3-8b-q4_0-b64"
+# Greedy steps of the whole batch whose sequence-0 tokens are checked against
+# the oracle (one GPU, CPU baseline on).
+BATCH_PARITY_TOKENS = 16
 # Isolated GQA decode attention (32 query / 8 kv heads, head_dim 128): RoPE +
 # append + attend over L+1 positions for B sequences, swept over
 # L in {512, 2048, 8192, 32768} x B in {1, 8, 64}.
@@ -920,8 +923,10 @@ def run_batch(args, world, rank, local, steps=None, warmup=None, emit=True):
     """64 independent greedy sequences of the LLaMA-3-8B shape in Q4_0, 64 /
     world per rank (no collective): the prompts go through minq_prefill_batch
     (chunks of one sequence's tokens), then batched decode steps with
-    each step's argmax fed back on the device. Returns rank 0's JSON line
-    (printed when `emit`)."""
+    each step's argmax fed back on the device. On one GPU (with the CPU
+    baseline on) the line carries a parity record: sequence 0's greedy
+    continuation inside the batch against the oracle decoding from a copy of
+    sequence 0's cache. Returns rank 0's JSON line (printed when `emit`)."""
     import torch
     import minq_b200 as mq
     from minq_b200 import synth
@@ -937,7 +942,8 @@ def run_batch(args, world, rank, local, steps=None, warmup=None, emit=True):
     cfg0, qk_norm, tied = synth.ARCH["llama3-8b"]
     if args.layers:
         cfg0 = replace(cfg0, n_layers=args.layers)
-    cfg = replace(cfg0, max_seq_len=prompt + W + 2 * K + 16)
+    cfg = replace(cfg0, max_seq_len=prompt + W + 2 * K + 16 + BATCH_PARITY_TOKENS)
+    parity = world == 1 and not args.no_cpu_baseline
     model = build_model(mq, synth, cfg, qk_norm, tied, args.seed)
     weight_bytes = model.weight_bytes
     cache = model.new_cache(batch=B)
@@ -981,9 +987,28 @@ def run_batch(args, world, rank, local, steps=None, warmup=None, emit=True):
     # device continuation replays the same kernels)
     from minq_b200 import _lib
     n0 = _lib.lib().minq_kernel_launches()
-    model.forward_batch(toks, cache, logits=False)
+    am, _ = model.forward_batch(toks, cache, logits=False)
     torch.cuda.synchronize()
     launches_per_step = _lib.lib().minq_kernel_launches() - n0
+    toks = [int(t) for t in am]
+    # parity state: sequence 0's cache (minq_cache_read reads sequence 0 of a
+    # batch), then BATCH_PARITY_TOKENS greedy steps of the whole batch, of
+    # which sequence 0's tokens are kept
+    par_state = None
+    if parity:
+        n_pos = cache.len
+        kvd = cfg.n_kv_heads * cfg.head_dim
+        kall = np.empty((cfg.n_layers, n_pos, kvd), np.float32)
+        vall = np.empty((cfg.n_layers, n_pos, kvd), np.float32)
+        for li in range(cfg.n_layers):
+            kall[li], vall[li] = cache.read(li, 0, n_pos)
+        start = toks[0]
+        gpu_toks = []
+        for _ in range(BATCH_PARITY_TOKENS):
+            am, _ = model.forward_batch(toks, cache, logits=False)
+            toks = [int(t) for t in am]
+            gpu_toks.append(toks[0])
+        par_state = (n_pos, kall, vall, start, gpu_toks)
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -1009,6 +1034,33 @@ def run_batch(args, world, rank, local, steps=None, warmup=None, emit=True):
                     "view of the same step is roofline_tensor"}
     del cache, model
     torch.cuda.empty_cache()
+    par = None
+    if par_state is not None:
+        try:
+            from oracle import oracle as orc
+            orc.set_threads(os.cpu_count() or 1)
+            n_pos, kall, vall, start, gpu_toks = par_state
+            par_state = None
+            om = cpu_model(orc, synth, replace(cfg, max_seq_len=n_pos + BATCH_PARITY_TOKENS + 8),
+                           qk_norm, tied, args.seed)
+            oc = om.new_cache()
+            oc.fill(kall, vall)
+            del kall, vall
+            ref_toks = []
+            tok = start
+            for _ in range(len(gpu_toks)):
+                tok = int(orc.argmax(om.forward([tok], oc)))
+                ref_toks.append(tok)
+            first = next((i for i, (a, b) in enumerate(zip(gpu_toks, ref_toks)) if a != b), None)
+            par = {"tokens": len(ref_toks), "match": first is None, "first_mismatch": first,
+                   "from": f"sequence 0 of the batch of {B}: its cache after prefill + timed "
+                           f"steps ({n_pos} positions)",
+                   "gpu": "batched step (minq_forward_batch, tcgen05 projections)",
+                   "oracle": "forward_token + argmax, one sequence"}
+            del om, oc
+        except Exception as e:  # the check must not sink the GPU number
+            par = {"tokens": 0, "match": None, "first_mismatch": None,
+                   "error": f"{type(e).__name__}: {e}"}
     line = None
     if rank == 0:
         line = {
@@ -1033,6 +1085,7 @@ def run_batch(args, world, rank, local, steps=None, warmup=None, emit=True):
             "roofline_tensor": {"achieved": tfs, "peak": peak, "unit": "TFLOP/s",
                                 "frac": tfs / peak, "per_step_flops": flops},
             "cpu_baseline": None,
+            "parity": par,
             "clocks": clk,
         }
         if emit:

@@ -390,24 +390,40 @@ struct Config {  // model.rs:29-45
   std::string dtype = "f32";
 };
 
+// Heads of attend() in parallel (off by default: the reference loops over
+// them on one thread). Each head's arithmetic is the same either way, so the
+// output is bit-identical; checks over long histories turn it on to finish
+// sooner, the timed CPU baseline leaves it off.
+bool g_attn_parallel = false;
+
 // model.rs:223-248 — serial over heads; scores, softmax, weighted V sum.
 void attend(const float* q, const float* k, const float* v, size_t len, const Config& c,
             float* out) {
   size_t hd = c.head_dim, kv_dim = c.n_kv * hd, group = c.n_heads / c.n_kv;
   float scale = 1.0f / std::sqrt(static_cast<float>(hd));
-  std::vector<float> scores(len);
   std::fill(out, out + c.n_heads * hd, 0.0f);
-  for (size_t h = 0; h < c.n_heads; ++h) {
+  auto head = [&](size_t h, float* scores) {
     const float* qh = q + h * hd;
     size_t off = (h / group) * hd;
     for (size_t t = 0; t < len; ++t) scores[t] = dot(qh, k + t * kv_dim + off, hd) * scale;
-    softmax(scores.data(), len);
+    softmax(scores, len);
     float* oh = out + h * hd;
     for (size_t t = 0; t < len; ++t) {
       const float* vt = v + t * kv_dim + off;
       float w = scores[t];
       for (size_t i = 0; i < hd; ++i) oh[i] += w * vt[i];
     }
+  };
+  if (!g_attn_parallel) {
+    std::vector<float> scores(len);
+    for (size_t h = 0; h < c.n_heads; ++h) head(h, scores.data());
+    return;
+  }
+#pragma omp parallel num_threads(nthreads())
+  {
+    std::vector<float> scores(len);
+#pragma omp for schedule(dynamic, 1)
+    for (long h = 0; h < static_cast<long>(c.n_heads); ++h) head((size_t)h, scores.data());
   }
 }
 
@@ -818,6 +834,7 @@ extern "C" {
 const char* orc_last_error() { return g_err.c_str(); }
 void orc_set_simd(int on) { g_simd = on != 0; }
 void orc_set_threads(int n) { g_threads = n; }
+void orc_set_attn_parallel(int on) { g_attn_parallel = on != 0; }
 int orc_max_threads() { return omp_get_max_threads(); }
 
 int orc_quantize(int dtype, const float* x, size_t n, uint8_t* out) {

@@ -56,6 +56,7 @@ def lib():
             "orc_last_error": (C.c_char_p, []),
             "orc_set_simd": (None, [I]),
             "orc_set_threads": (None, [I]),
+            "orc_set_attn_parallel": (None, [I]),
             "orc_max_threads": (I, []),
             "orc_quantize": (I, [I, P, S, P]),
             "orc_dequantize": (I, [I, P, S, P, S]),
@@ -126,6 +127,13 @@ def set_simd(on: bool) -> None:
 
 def set_threads(n: int) -> None:
     lib().orc_set_threads(int(n))
+
+
+def set_attn_parallel(on: bool) -> None:
+    """Run attend()'s heads on the OpenMP threads (bit-identical output; the
+    reference, model.rs:223-248, and so the timed baseline, loop over them on
+    one thread)."""
+    lib().orc_set_attn_parallel(1 if on else 0)
 
 
 def max_threads() -> int:

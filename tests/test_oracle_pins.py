@@ -276,3 +276,20 @@ def test_argmax_total_cmp_and_ties(orc):  # sampler.rs:10
     neg_nan = np.array([0xFFC00000], dtype=np.uint32).view(np.float32)[0]
     assert orc.argmax(np.array([neg_nan, -np.inf], F)) == 1        # -NaN sorts lowest
     assert orc.argmax(np.array([], F)) == 0
+
+
+def test_attend_parallel_heads_bit_identical(orc):
+    """The opt-in parallel-heads attend (used by the long-history checks) gives
+    the same bits as the reference's serial loop over heads (model.rs:223-248)."""
+    rng = np.random.default_rng(3)
+    nh, nkv, hd, L = 32, 8, 128, 777
+    q = rng.standard_normal(nh * hd).astype(np.float32)
+    k = rng.standard_normal((L, nkv * hd)).astype(np.float32)
+    v = rng.standard_normal((L, nkv * hd)).astype(np.float32)
+    serial = orc.attend(q, k, v, L, nh, nkv, hd)
+    orc.set_attn_parallel(True)
+    try:
+        par = orc.attend(q, k, v, L, nh, nkv, hd)
+    finally:
+        orc.set_attn_parallel(False)
+    assert np.array_equal(serial.view(np.uint32), par.view(np.uint32))

@@ -79,7 +79,8 @@ int argmax_parts_capacity();
 // column slices' partials. From kQmmTcMinB quantized inputs on, the product
 // runs on the tensor cores (qmatmul_tc.cu; measured on the LLaMA-3-8B
 // shape: 3.3x faster than the CUDA-core kernel already at 8 inputs, 2.9x at
-// 4), so the CUDA-core kernel serves one input and f32 weights.
+// 4), so the CUDA-core kernel serves one input and f32 weights below
+// kF32GemmMinB inputs (from there on, f32_gemm.cu).
 constexpr int kQmmMaxB = 64;
 constexpr int kQmmTcMinB = 2;
 minq_status launch_qmatmul(int dtype, const void* w0, const void* w1, size_t rows, int cols,
@@ -87,6 +88,14 @@ minq_status launch_qmatmul(int dtype, const void* w0, const void* w1, size_t row
                            float* xn_scratch, size_t xn_floats, const float* bias,
                            const float* residual, float* y, size_t y_stride, float* part,
                            size_t part_floats, cudaStream_t s);
+// f32_gemm.cu: Y[b] = W X[b] for dense f32 weights and kF32GemmMinB..64
+// inputs (the tied lm_head over a perplexity chunk's positions or a batch),
+// register-tiled on the CUDA cores; launch_qmatmul routes f32 weights
+// without bias / residual there.
+constexpr int kF32GemmMinB = 32;
+bool f32_gemm_takes(int B, int cols, const void* w, const float* x, size_t x_stride);
+minq_status launch_f32_gemm(const float* w, size_t rows, int cols, const float* x, size_t x_stride,
+                            int B, float* y, size_t y_stride, cudaStream_t s);
 // qmatmul_tc.cu: whether the tensor-core form takes the shape, and the launch.
 bool qmatmul_tc_takes(int dtype, int cols, int B, size_t xp_floats);
 minq_status launch_qmatmul_tc(int dtype, const void* w0, const void* w1, size_t rows, int cols,

@@ -351,6 +351,9 @@ minq_status launch_qmatmul(int dtype, const void* w0, const void* w1, size_t row
     x = xn_scratch;
     x_stride = (size_t)cols;
   }
+  if (dtype == MINQ_F32 && !bias && !residual && f32_gemm_takes(B, cols, w0, x, x_stride))
+    return launch_f32_gemm(static_cast<const float*>(w0), rows, cols, x, x_stride, B, y, y_stride,
+                           s);
   QmmParams p{};
   p.w0 = w0;
   p.w1 = w1;

@@ -46,6 +46,9 @@ CASES = [
     # tied f32 lm_head at 12 inputs: static + dynamic shared memory of the
     # CUDA-core kernel just above the 48 KB default (the opt-in must count both)
     ("q4_hd128_tied_b12", "q4_0", 512, 768, 8, 2, 128, 200, True, False, True, 12),
+    # tied f32 lm_head at 40 inputs: the register-tiled f32 GEMM (from 32
+    # inputs on; 257 rows leave a one-row last tile)
+    ("q8_qwen_bias_tied_b40_gemm", "q8_0", 256, 384, 4, 2, 64, 257, True, True, True, 40),
 ]
 
 

@@ -1891,7 +1891,8 @@ static minq_status sweep_cache(minq_model* m, size_t max_seq, bool scoring, minq
   if (st == MINQ_OK && scoring) {
     const size_t V = m->cfg.vocab_size;
     cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&c->plog), kPrefillChunk * V * 4);
-    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&c->pnll), kPrefillChunk * 8);
+    // one f64 nll per scored position of a window (read once per window)
+    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&c->pnll), max_seq * 8);
     if (e != cudaSuccess) st = cuda_fail(e, "cudaMalloc(perplexity buffers)");
   }
   if (st != MINQ_OK) {
@@ -1956,7 +1957,8 @@ minq_status minq_eval_ppl(minq_model* m, const uint32_t* tokens, size_t n, size_
   const size_t H = m->cfg.hidden_size, V = m->cfg.vocab_size;
   const size_t n_windows = (n + context - 1) / context;
   cudaStream_t s = m->stream;
-  double nll_sum = 0.0, part[kPrefillChunk];
+  double nll_sum = 0.0;
+  std::vector<double> part(context);
   size_t count = 0;
   minq_status st = MINQ_OK;
   for (size_t w0 = 0, wi = 0; st == MINQ_OK && w0 < n; w0 += context, ++wi) {
@@ -1966,7 +1968,10 @@ minq_status minq_eval_ppl(minq_model* m, const uint32_t* tokens, size_t n, size_
     if ((st = check_rows(m, tokens + w0, len)) != MINQ_OK) break;
     c->len = 0;
     c->d_pos_valid = false;
-    // positions 0 .. len - 2: the last one predicts nothing (ppl.rs:75-82)
+    // positions 0 .. len - 2: the last one predicts nothing (ppl.rs:75-82);
+    // the chunks' nll values stay on the device until the window ends, so
+    // the host enqueues the next chunk while the GPU runs this one
+    size_t wn = 0;
     for (size_t i = 0; st == MINQ_OK && i + 1 < len; i += kPrefillChunk) {
       const int T = (int)std::min<size_t>(kPrefillChunk, len - 1 - i);
       if ((st = forward_chunk(m, c, m->d_tokens + w0 + i, T)) != MINQ_OK) break;
@@ -1978,16 +1983,19 @@ minq_status minq_eval_ppl(minq_model* m, const uint32_t* tokens, size_t n, size_
                           H, m->final_norm, m->cfg.rms_norm_eps, c->pxn, c->pxn_floats, nullptr,
                           nullptr, c->plog, V, c->ppart, c->ppart_floats, s);
       if (st == MINQ_OK)
-        st = launch_nll_rows(c->plog, V, R, m->d_tokens + w0 + i + r0 + 1, c->pnll, s);
+        st = launch_nll_rows(c->plog, V, R, m->d_tokens + w0 + i + r0 + 1, c->pnll + wn, s);
       if (st != MINQ_OK) break;
-      cudaError_t e = cudaMemcpyAsync(part, c->pnll, (size_t)R * 8, cudaMemcpyDeviceToHost, s);
+      wn += (size_t)R;
+    }
+    if (st == MINQ_OK && wn) {
+      cudaError_t e = cudaMemcpyAsync(part.data(), c->pnll, wn * 8, cudaMemcpyDeviceToHost, s);
       if (e == cudaSuccess) e = cudaStreamSynchronize(s);
       if (e != cudaSuccess) {
-        st = cuda_fail(e, "perplexity chunk");
+        st = cuda_fail(e, "perplexity window");
         break;
       }
-      for (int r = 0; r < R; ++r) nll_sum += part[r];  // position order, as ppl.rs:81
-      count += (size_t)R;
+      for (size_t r = 0; r < wn; ++r) nll_sum += part[r];  // position order, as ppl.rs:81
+      count += wn;
     }
     if (st == MINQ_OK && on_window)
       on_window(wi + 1, n_windows, count ? std::exp(nll_sum / (double)count) : NAN, user);

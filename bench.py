@@ -103,6 +103,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=None,
                     help="keep only the first N layers: a smaller case of the same kernels "
                          "for profiler captures (its number is not the workload's)")
+    ap.add_argument("--attn-points", default=None,
+                    help="attention sweep: only these BxL points (e.g. 64x512,8x8192), for "
+                         "profiler captures of one point (the line's value needs 8x8192)")
     return ap.parse_args()
 
 
@@ -1321,48 +1324,50 @@ def run_attn(args, world, rank, local):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     s = torch.cuda.current_stream()
     sweep = []
-    for B in (1, 8, 64):
-        for L in (512, 2048, 8192, 32768):
-            ms_ = L + 1
-            g = torch.Generator(device="cuda").manual_seed(B * 100003 + L)
-            kc = torch.randn((B, nkv, ms_, hd), device="cuda", generator=g)
-            vc = torch.randn((B, nkv, ms_, hd), device="cuda", generator=g)
-            q = torch.randn((B, nh, hd), device="cuda", generator=g)
-            kn = torch.randn((B, nkv, hd), device="cuda", generator=g)
-            vn = torch.randn((B, nkv, hd), device="cuda", generator=g)
-            pos = torch.arange(ms_, dtype=torch.float32, device="cuda")[:, None]
-            inv = 1.0 / (1e6 ** (torch.arange(0, hd, 2, device="cuda", dtype=torch.float32) / hd))
-            cs, sn = torch.cos(pos * inv).contiguous(), torch.sin(pos * inv).contiguous()
-            out = torch.empty((B, nh, hd), device="cuda")
-            wsb = L_.minq_attn_workspace_bytes(B, nh, L + 1)
-            ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device="cuda")
-            big = 8.0 * B * nkv * hd * (L + 1) > 4 * (126 << 20)
+    points = [(B, L) for B in (1, 8, 64) for L in (512, 2048, 8192, 32768)]
+    if args.attn_points:
+        points = [tuple(int(v) for v in pt.split("x")) for pt in args.attn_points.split(",")]
+    for B, L in points:
+        ms_ = L + 1
+        g = torch.Generator(device="cuda").manual_seed(B * 100003 + L)
+        kc = torch.randn((B, nkv, ms_, hd), device="cuda", generator=g)
+        vc = torch.randn((B, nkv, ms_, hd), device="cuda", generator=g)
+        q = torch.randn((B, nh, hd), device="cuda", generator=g)
+        kn = torch.randn((B, nkv, hd), device="cuda", generator=g)
+        vn = torch.randn((B, nkv, hd), device="cuda", generator=g)
+        pos = torch.arange(ms_, dtype=torch.float32, device="cuda")[:, None]
+        inv = 1.0 / (1e6 ** (torch.arange(0, hd, 2, device="cuda", dtype=torch.float32) / hd))
+        cs, sn = torch.cos(pos * inv).contiguous(), torch.sin(pos * inv).contiguous()
+        out = torch.empty((B, nh, hd), device="cuda")
+        wsb = L_.minq_attn_workspace_bytes(B, nh, L + 1)
+        ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device="cuda")
+        big = 8.0 * B * nkv * hd * (L + 1) > 4 * (126 << 20)
 
-            def call():
-                _lib.check(L_.minq_attn_decode(
-                    P(q), P(kn), P(vn), None, None, eps, P(cs), P(sn), B, nh, nkv, hd, L, P(kc),
-                    P(vc), nkv * ms_ * hd, ms_ * hd, hd, P(out), P(ws), wsb,
-                    C.c_void_p(s.cuda_stream)))
-            for _ in range(max(3, args.warmup)):
-                call()
+        def call():
+            _lib.check(L_.minq_attn_decode(
+                P(q), P(kn), P(vn), None, None, eps, P(cs), P(sn), B, nh, nkv, hd, L, P(kc),
+                P(vc), nkv * ms_ * hd, ms_ * hd, hd, P(out), P(ws), wsb,
+                C.c_void_p(s.cuda_stream)))
+        for _ in range(max(3, args.warmup)):
+            call()
+        torch.cuda.synchronize()
+        tot, n = 0.0, max(8, args.steps // 4)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for _ in range(n):
+            if not big:
+                flush.zero_()
+            e0.record(s)
+            call()
+            e1.record(s)
             torch.cuda.synchronize()
-            tot, n = 0.0, max(8, args.steps // 4)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            for _ in range(n):
-                if not big:
-                    flush.zero_()
-                e0.record(s)
-                call()
-                e1.record(s)
-                torch.cuda.synchronize()
-                tot += e0.elapsed_time(e1)
-            us = 1000.0 * tot / n
-            byts = 8.0 * B * nkv * hd * (L + 1) + 4.0 * B * (2 * nh + 4 * nkv) * hd
-            sweep.append({"B": B, "L": L, "us": round(us, 2), "GB_s": round(byts / us / 1e3, 1),
-                          "frac": round(byts / us / 1e3 / peak, 3)})
-            del kc, vc, q, kn, vn, out, ws
-            torch.cuda.empty_cache()
-    head = next(x for x in sweep if x["B"] == 8 and x["L"] == 8192)
+            tot += e0.elapsed_time(e1)
+        us = 1000.0 * tot / n
+        byts = 8.0 * B * nkv * hd * (L + 1) + 4.0 * B * (2 * nh + 4 * nkv) * hd
+        sweep.append({"B": B, "L": L, "us": round(us, 2), "GB_s": round(byts / us / 1e3, 1),
+                      "frac": round(byts / us / 1e3 / peak, 3)})
+        del kc, vc, q, kn, vn, out, ws
+        torch.cuda.empty_cache()
+    head = next((x for x in sweep if x["B"] == 8 and x["L"] == 8192), sweep[0])
     if rank == 0:
         print(json.dumps({
             "metric": "decode attention GB/s", "value": head["GB_s"], "unit": "GB/s",

@@ -21,6 +21,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "ktimer.h"
@@ -245,19 +246,158 @@ struct TmaAttnCfg {
   static constexpr int TILE_FLOATS = TP * HD;
 };
 
+// Per-lane layout of the TMA-fed kernels' consumer warps (see below).
+template <int HD>
+struct TmaLanes {
+  static constexpr int EPL = 8;                       // q / K elements per lane in QK
+  static constexpr int LPP = HD / EPL;                // lanes per position
+  static constexpr int PPS = 32 / LPP;                // positions per sub-step
+  static constexpr int NSUB = TmaAttnCfg<HD>::TP / PPS;
+  static constexpr int DPL = HD >= 32 ? HD / 32 : 1;  // PV dims per lane
+  static constexpr int PV_LANES = HD / DPL;
+};
+
+// This lane's slice of the (pre-scaled) queries of heads g0 .. g0+ng-1 of
+// sequence b's kv head kvh.
+template <int HD, int GMAX>
+__device__ __forceinline__ void tma_load_q(const AttnParams& p, int b, int kvh, int G, int g0,
+                                           int ng, int j, float (&qr)[GMAX][TmaLanes<HD>::EPL]) {
+  using LN = TmaLanes<HD>;
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g) {
+    const float* qh = p.q + ((size_t)b * p.nh + kvh * G + g0 + (g < ng ? g : 0)) * HD;
+#pragma unroll
+    for (int e = 0; e < LN::EPL; ++e) {
+      const int idx = (e < 4) ? 4 * j + e : HD / 2 + 4 * j + e - 4;
+      qr[g][e] = g < ng ? qh[idx] * p.scale : 0.0f;
+    }
+  }
+}
+
+// One tile of npos positions (K rows kt_s, V rows vt_s in shared memory):
+// QK^T for every head of the group, the online-softmax update of this
+// warp's running max / sum, and p V into the warp's outputs.
+template <int HD, int GMAX>
+__device__ __forceinline__ void tma_attn_tile(const float (&qr)[GMAX][TmaLanes<HD>::EPL],
+                                              const float* kt_s, const float* vt_s, int npos,
+                                              float* sc, float (&m_w)[GMAX], float (&l_w)[GMAX],
+                                              float (&o)[GMAX][TmaLanes<HD>::DPL]) {
+  using LN = TmaLanes<HD>;
+  constexpr int TP = TmaAttnCfg<HD>::TP, EPL = LN::EPL, LPP = LN::LPP, PPS = LN::PPS,
+                NSUB = LN::NSUB, DPL = LN::DPL, PV_LANES = LN::PV_LANES;
+  const int lane = threadIdx.x & 31, j = lane % LPP, pslot = lane / LPP;
+#pragma unroll 2
+  for (int ss = 0; ss < NSUB; ++ss) {
+    const int tl = ss * PPS + pslot;
+    const float* kt = kt_s + tl * HD;
+    const float4 a = *reinterpret_cast<const float4*>(kt + 4 * j);
+    const float4 c = *reinterpret_cast<const float4*>(kt + HD / 2 + 4 * j);
+    const float kv[EPL] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+#pragma unroll
+    for (int g = 0; g < GMAX; ++g) {
+      float sv = 0.0f;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) sv = fmaf(qr[g][e], kv[e], sv);
+#pragma unroll
+      for (int off = LPP / 2; off > 0; off >>= 1) sv += __shfl_xor_sync(0xffffffffu, sv, off);
+      if (j == 0) sc[g * 32 + tl] = tl < npos ? sv : -INFINITY;
+    }
+  }
+  __syncwarp();
+  float pr[GMAX];
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g) {
+    const float sv = lane < TP ? sc[g * 32 + lane] : -INFINITY;
+    const float mt = warp_max(sv);
+    const float mn = fmaxf(m_w[g], mt);
+    const float corr = m_w[g] == -INFINITY ? 0.0f : expf(m_w[g] - mn);
+    pr[g] = sv == -INFINITY ? 0.0f : expf(sv - mn);
+    l_w[g] = l_w[g] * corr + pr[g];
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) o[g][d] *= corr;
+    m_w[g] = mn;
+  }
+#pragma unroll 4
+  for (int tl = 0; tl < npos; ++tl) {
+    const float* vt = vt_s + tl * HD;
+    float vv[DPL];
+    if (lane < PV_LANES) {
+      if constexpr (DPL == 4) {
+        const float4 a = *reinterpret_cast<const float4*>(vt + 4 * lane);
+        vv[0] = a.x; vv[1] = a.y; vv[2] = a.z; vv[3] = a.w;
+      } else if constexpr (DPL == 2) {
+        const float2 a = *reinterpret_cast<const float2*>(vt + 2 * lane);
+        vv[0] = a.x; vv[1] = a.y;
+      } else {
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) vv[d] = vt[DPL * lane + d];
+      }
+    } else {
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) vv[d] = 0.0f;
+    }
+#pragma unroll
+    for (int g = 0; g < GMAX; ++g) {
+      const float pt = __shfl_sync(0xffffffffu, pr[g], tl);
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) o[g][d] = fmaf(pt, vv[d], o[g][d]);
+    }
+  }
+  __syncwarp();
+}
+
+// A warp's running (max, sum, out) per head into shared memory for the
+// CTA's merge (s_m / s_l: [warp][GMAX], s_o: [warp][GMAX][HD]).
+template <int HD, int GMAX>
+__device__ __forceinline__ void tma_store_warp_state(int warp, const float (&m_w)[GMAX],
+                                                     const float (&l_w)[GMAX],
+                                                     const float (&o)[GMAX][TmaLanes<HD>::DPL],
+                                                     float* s_m, float* s_l, float* s_o) {
+  using LN = TmaLanes<HD>;
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g) {
+    const float lsum = warp_sum(l_w[g]);
+    if (lane == 0) {
+      s_m[warp * GMAX + g] = m_w[g];
+      s_l[warp * GMAX + g] = lsum;
+    }
+    if (lane < LN::PV_LANES) {
+#pragma unroll
+      for (int d = 0; d < LN::DPL; ++d) s_o[(warp * GMAX + g) * HD + LN::DPL * lane + d] = o[g][d];
+    }
+  }
+}
+
+// Merge of the 4 consumer warps' states for output element idx = g * HD + d:
+// the unnormalised sum O, its max M and sum L.
+template <int HD, int GMAX>
+__device__ __forceinline__ void tma_merge_warps(int idx, const float* s_m, const float* s_l,
+                                                const float* s_o, float* O_, float* M_, float* L_) {
+  const int g = idx / HD, d = idx % HD;
+  float M = -INFINITY;
+  for (int w = 0; w < 4; ++w) M = fmaxf(M, s_m[w * GMAX + g]);
+  float L = 0.0f, O = 0.0f;
+  for (int w = 0; w < 4; ++w) {
+    const float mw = s_m[w * GMAX + g];
+    if (mw == -INFINITY) continue;
+    const float f = expf(mw - M);
+    L = fmaf(s_l[w * GMAX + g], f, L);
+    O = fmaf(s_o[(w * GMAX + g) * HD + d], f, O);
+  }
+  *O_ = O;
+  *M_ = M;
+  *L_ = L;
+}
+
 template <int HD, int GMAX>
 __global__ void __launch_bounds__(160) attn_tma_kernel(AttnParams p) {
   using CFG = TmaAttnCfg<HD>;
   constexpr int TP = CFG::TP, S = CFG::S, TF = CFG::TILE_FLOATS;
   constexpr int NWC = 4;                       // consumer warps
   static_assert(S % NWC == 0, "every ring slot must belong to one consumer warp");
-  constexpr int EPL = 8;
-  constexpr int LPP = HD / EPL;
-  constexpr int PPS = 32 / LPP;
-  constexpr int NSUB = TP / PPS;
-  constexpr int DPL = HD >= 32 ? HD / 32 : 1;
-  constexpr int PV_LANES = HD / DPL;
-  static_assert(HD >= 16 && HD <= 256 && TP % PPS == 0, "head_dim");
+  constexpr int EPL = TmaLanes<HD>::EPL, LPP = TmaLanes<HD>::LPP, DPL = TmaLanes<HD>::DPL;
+  static_assert(HD >= 16 && HD <= 256 && TP % TmaLanes<HD>::PPS == 0, "head_dim");
 
   extern __shared__ __align__(128) unsigned char smem_raw[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);
@@ -317,18 +457,8 @@ __global__ void __launch_bounds__(160) attn_tma_kernel(AttnParams p) {
     for (int i = max(0, ntiles - S); ok && i < ntiles; ++i)
       ok = mbar_wait(&empty[i % S], (uint32_t)(i / S) & 1u, p.status);
   } else {
-    const int j = lane % LPP;
-    const int pslot = lane / LPP;
     float qr[GMAX][EPL];
-#pragma unroll
-    for (int g = 0; g < GMAX; ++g) {
-      const float* qh = p.q + ((size_t)b * p.nh + kvh * G + g0 + (g < ng ? g : 0)) * HD;
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) {
-        const int idx = (e < 4) ? 4 * j + e : HD / 2 + 4 * j + e - 4;
-        qr[g][e] = g < ng ? qh[idx] * p.scale : 0.0f;
-      }
-    }
+    tma_load_q<HD, GMAX>(p, b, kvh, G, g0, ng, lane % LPP, qr);
     float m_w[GMAX], l_w[GMAX], o[GMAX][DPL];
 #pragma unroll
     for (int g = 0; g < GMAX; ++g) {
@@ -342,94 +472,17 @@ __global__ void __launch_bounds__(160) attn_tma_kernel(AttnParams p) {
       const int s = i % S;
       if (!mbar_wait(&full[s], (uint32_t)(i / S) & 1u, p.status)) break;
       const float* kt_s = tiles + (size_t)s * 2 * TF;
-      const float* vt_s = kt_s + TF;
       const int npos = min(TP, t_end - (t_begin + i * TP));
-#pragma unroll 2
-      for (int ss = 0; ss < NSUB; ++ss) {
-        const int tl = ss * PPS + pslot;
-        const float* kt = kt_s + tl * HD;
-        const float4 a = *reinterpret_cast<const float4*>(kt + 4 * j);
-        const float4 c = *reinterpret_cast<const float4*>(kt + HD / 2 + 4 * j);
-        const float kv[EPL] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
-#pragma unroll
-        for (int g = 0; g < GMAX; ++g) {
-          float sv = 0.0f;
-#pragma unroll
-          for (int e = 0; e < EPL; ++e) sv = fmaf(qr[g][e], kv[e], sv);
-#pragma unroll
-          for (int off = LPP / 2; off > 0; off >>= 1) sv += __shfl_xor_sync(0xffffffffu, sv, off);
-          if (j == 0) sc[g * 32 + tl] = tl < npos ? sv : -INFINITY;
-        }
-      }
-      __syncwarp();
-      float pr[GMAX];
-#pragma unroll
-      for (int g = 0; g < GMAX; ++g) {
-        const float sv = lane < TP ? sc[g * 32 + lane] : -INFINITY;
-        const float mt = warp_max(sv);
-        const float mn = fmaxf(m_w[g], mt);
-        const float corr = m_w[g] == -INFINITY ? 0.0f : expf(m_w[g] - mn);
-        pr[g] = sv == -INFINITY ? 0.0f : expf(sv - mn);
-        l_w[g] = l_w[g] * corr + pr[g];
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) o[g][d] *= corr;
-        m_w[g] = mn;
-      }
-#pragma unroll 4
-      for (int tl = 0; tl < npos; ++tl) {
-        const float* vt = vt_s + tl * HD;
-        float vv[DPL];
-        if (lane < PV_LANES) {
-          if constexpr (DPL == 4) {
-            const float4 a = *reinterpret_cast<const float4*>(vt + 4 * lane);
-            vv[0] = a.x; vv[1] = a.y; vv[2] = a.z; vv[3] = a.w;
-          } else if constexpr (DPL == 2) {
-            const float2 a = *reinterpret_cast<const float2*>(vt + 2 * lane);
-            vv[0] = a.x; vv[1] = a.y;
-          } else {
-#pragma unroll
-            for (int d = 0; d < DPL; ++d) vv[d] = vt[DPL * lane + d];
-          }
-        } else {
-#pragma unroll
-          for (int d = 0; d < DPL; ++d) vv[d] = 0.0f;
-        }
-#pragma unroll
-        for (int g = 0; g < GMAX; ++g) {
-          const float pt = __shfl_sync(0xffffffffu, pr[g], tl);
-#pragma unroll
-          for (int d = 0; d < DPL; ++d) o[g][d] = fmaf(pt, vv[d], o[g][d]);
-        }
-      }
-      __syncwarp();
+      tma_attn_tile<HD, GMAX>(qr, kt_s, kt_s + TF, npos, sc, m_w, l_w, o);
       if (lane == 0) mbar_arrive(&empty[s]);
     }
-#pragma unroll
-    for (int g = 0; g < GMAX; ++g) {
-      const float lsum = warp_sum(l_w[g]);
-      if (lane == 0) {
-        s_m[warp * GMAX + g] = m_w[g];
-        s_l[warp * GMAX + g] = lsum;
-      }
-      if (lane < PV_LANES) {
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) s_o[(warp * GMAX + g) * HD + DPL * lane + d] = o[g][d];
-      }
-    }
+    tma_store_warp_state<HD, GMAX>(warp, m_w, l_w, o, s_m, s_l, s_o);
   }
   __syncthreads();
   for (int idx = threadIdx.x; idx < ng * HD; idx += blockDim.x) {
     const int g = idx / HD, d = idx % HD;
-    float M = -INFINITY;
-    for (int w = 0; w < NWC; ++w) M = fmaxf(M, s_m[w * GMAX + g]);
-    float L = 0.0f, O = 0.0f;
-    for (int w = 0; w < NWC; ++w) {
-      const float mw = s_m[w * GMAX + g];
-      if (mw == -INFINITY) continue;
-      const float f = expf(mw - M);
-      L = fmaf(s_l[w * GMAX + g], f, L);
-      O = fmaf(s_o[(w * GMAX + g) * HD + d], f, O);
-    }
+    float O, M, L;
+    tma_merge_warps<HD, GMAX>(idx, s_m, s_l, s_o, &O, &M, &L);
     const size_t row = (size_t)b * p.nh + kvh * G + g0 + g;
     if (nsplit == 1) {
       p.out[row * HD + d] = O / L;
@@ -448,6 +501,167 @@ static size_t tma_attn_smem() {
   using CFG = TmaAttnCfg<HD>;
   return 128 + sizeof(float) * ((size_t)CFG::S * 2 * CFG::TILE_FLOATS + 4 * GMAX * 32 +
                                 2 * 4 * GMAX + 4 * GMAX * HD);
+}
+
+// ---------------------------------------------------------------------------
+// Balanced ("stream-K") form of the TMA-fed kernel for histories of one
+// host-known length. The work is the list of T = units x NT tiles, unit u =
+// (sequence, kv head, query group) with NT tiles of TP positions each, in
+// that order; CTA c of the G CTAs (a fixed number per SM) takes tiles
+// [c T / G, (c + 1) T / G), so every SM streams the same number of bytes and
+// the grid ends in one wave, whatever the batch and length. A CTA's range
+// may cross units: at each unit boundary its warps merge their states and
+// write the unit's partial into slot c - c_first(u) of the unit's rows
+// (c_first(u): the CTA holding the unit's first tile); the combine kernel
+// merges a unit's slots c_first(u) .. c_last(u). The ring protocol and the
+// tile arithmetic are those of attn_tma_kernel (consumer warp w takes the
+// range's tiles w, w + 4, ...).
+struct SkPlan {
+  long long T;  // tiles in all
+  int NT;       // tiles per unit
+  int G;        // CTAs
+};
+
+// The CTA whose range holds tile t: the largest c with floor(c T / G) <= t.
+__device__ __host__ __forceinline__ int sk_cta_of(long long t, const SkPlan& k) {
+  return (int)(((t + 1) * k.G - 1) / k.T);
+}
+
+template <int HD, int GMAX>
+__global__ void __launch_bounds__(160) attn_sk_kernel(AttnParams p, SkPlan k) {
+  using CFG = TmaAttnCfg<HD>;
+  constexpr int TP = CFG::TP, S = CFG::S, TF = CFG::TILE_FLOATS;
+  constexpr int NWC = 4;
+  static_assert(S % NWC == 0, "every ring slot must belong to one consumer warp");
+  constexpr int EPL = TmaLanes<HD>::EPL, LPP = TmaLanes<HD>::LPP, DPL = TmaLanes<HD>::DPL;
+
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);
+  uint64_t* empty = full + S;
+  float* tiles = reinterpret_cast<float*>(smem_raw + 128);  // [S][2][TF]
+  float* s_sc = tiles + (size_t)S * 2 * TF;                  // [NWC][GMAX][32]
+  float* s_m = s_sc + NWC * GMAX * 32;                       // [NWC][GMAX]
+  float* s_l = s_m + NWC * GMAX;                             // [NWC][GMAX]
+  float* s_o = s_l + NWC * GMAX;                             // [NWC][GMAX][HD]
+
+  pdl_wait();  // K/V (this position) and q come from the previous kernel
+  pdl_launch_dependents();
+  const long long r0 = (long long)blockIdx.x * k.T / k.G;
+  const long long r1 = (long long)(blockIdx.x + 1) * k.T / k.G;
+  if (r1 <= r0) return;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int G = p.nh / p.nkv, qgroups = (G + 7) / 8, len = p.len;
+  // unit u -> (sequence, kv head, first query head of the group)
+  auto unit = [&](long long u, int* b, int* kvh, int* g0) {
+    *g0 = (int)(u % qgroups) * 8;
+    *kvh = (int)((u / qgroups) % p.nkv);
+    *b = (int)(u / ((long long)qgroups * p.nkv));
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  const int n = (int)(r1 - r0);  // tiles of this CTA
+  if (warp == NWC) {  // producer: the range's tiles in order, across units
+    bool ok = true;
+    for (int i = 0; i < n && ok; ++i) {
+      const int s = i % S;
+      ok = mbar_wait(&empty[s], ((uint32_t)(i / S) & 1u) ^ 1u, p.status);
+      if (!ok) break;
+      const long long t = r0 + i;
+      int b, kvh, g0;
+      unit(t / k.NT, &b, &kvh, &g0);
+      const int pos0 = (int)(t % k.NT) * TP;
+      const uint32_t bytes = (uint32_t)(min(TP, len - pos0) * HD * 4);
+      if (lane == 0) {
+        const size_t off = (size_t)b * p.seq_stride + (size_t)kvh * p.head_stride + (size_t)pos0 * HD;
+        mbar_arrive_expect_tx(&full[s], 2 * bytes);
+        bulk_g2s(tiles + (size_t)s * 2 * TF, p.k + off, bytes, &full[s]);
+        bulk_g2s(tiles + (size_t)s * 2 * TF + TF, p.v + off, bytes, &full[s]);
+      }
+      __syncwarp();
+    }
+    for (int i = max(0, n - S); ok && i < n; ++i)
+      ok = mbar_wait(&empty[i % S], (uint32_t)(i / S) & 1u, p.status);
+    return;
+  }
+  // consumers: one segment (the range's part of one unit) at a time
+  bool ok = true;
+  float* sc = s_sc + warp * GMAX * 32;
+  for (long long u = r0 / k.NT; u * k.NT < r1; ++u) {
+    const long long a = max(r0, u * k.NT), e = min(r1, (u + 1) * k.NT);
+    int b, kvh, g0;
+    unit(u, &b, &kvh, &g0);
+    const int ng = min(GMAX, G - g0);
+    float qr[GMAX][EPL];
+    tma_load_q<HD, GMAX>(p, b, kvh, G, g0, ng, lane % LPP, qr);
+    float m_w[GMAX], l_w[GMAX], o[GMAX][DPL];
+#pragma unroll
+    for (int g = 0; g < GMAX; ++g) {
+      m_w[g] = -INFINITY;
+      l_w[g] = 0.0f;
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) o[g][d] = 0.0f;
+    }
+    // this warp's tiles of the segment: range indices i = t - r0 with i = warp mod 4
+    const int ia = (int)(a - r0), ie = (int)(e - r0);
+    for (int i = ia + ((warp - ia % NWC) + NWC) % NWC; ok && i < ie; i += NWC) {
+      const int s = i % S;
+      if (!(ok = mbar_wait(&full[s], (uint32_t)(i / S) & 1u, p.status))) break;
+      const float* kt_s = tiles + (size_t)s * 2 * TF;
+      const int pos0 = (int)((r0 + i) % k.NT) * TP;
+      tma_attn_tile<HD, GMAX>(qr, kt_s, kt_s + TF, min(TP, len - pos0), sc, m_w, l_w, o);
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    tma_store_warp_state<HD, GMAX>(warp, m_w, l_w, o, s_m, s_l, s_o);
+    named_barrier_sync(1, 32 * NWC);
+    const int slot = (int)blockIdx.x - sk_cta_of(u * k.NT, k);
+    for (int idx = threadIdx.x; idx < ng * HD; idx += 32 * NWC) {
+      const int g = idx / HD, d = idx % HD;
+      float O, M, L;
+      tma_merge_warps<HD, GMAX>(idx, s_m, s_l, s_o, &O, &M, &L);
+      const size_t row = (size_t)b * p.nh + kvh * G + g0 + g;
+      p.ws_o[(row * p.ws_stride + slot) * HD + d] = O;
+      if (d == 0) {
+        p.ws_ml[(row * p.ws_stride + slot) * 2 + 0] = M;
+        p.ws_ml[(row * p.ws_stride + slot) * 2 + 1] = L;
+      }
+    }
+    named_barrier_sync(1, 32 * NWC);  // the warp states are rewritten by the next segment
+  }
+}
+
+// Merge of every (sequence, query head)'s stream-K slots: the CTAs that
+// covered its unit, c_first .. c_last.
+__global__ void attn_sk_combine_kernel(const float* ws_o, const float* ws_ml, SkPlan k, int nh,
+                                       int nkv, int stride, int hd, float* out) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const size_t row = blockIdx.x;  // b * nh + h
+  const int G = nh / nkv, qgroups = (G + 7) / 8;
+  const int b = (int)(row / nh), h = (int)(row % nh);
+  const long long u = ((long long)b * nkv + h / G) * qgroups + (h % G) / 8;
+  const int nslot = sk_cta_of(u * k.NT + k.NT - 1, k) - sk_cta_of(u * k.NT, k) + 1;
+  const float* ml = ws_ml + row * stride * 2;
+  float M = -INFINITY;
+  for (int s = 0; s < nslot; ++s) M = fmaxf(M, ml[2 * s]);
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float L = 0.0f, O = 0.0f;
+    for (int s = 0; s < nslot; ++s) {
+      const float m = ml[2 * s];
+      if (m == -INFINITY) continue;
+      const float f = expf(m - M);
+      L = fmaf(ml[2 * s + 1], f, L);
+      O = fmaf(ws_o[(row * stride + s) * hd + d], f, O);
+    }
+    out[row * hd + d] = O / L;
+  }
 }
 
 // Merge the splits of every (sequence, query head).
@@ -642,6 +856,57 @@ static minq_status launch_tma_hd(const AttnParams& p, int gmax, dim3 grid, cudaS
   }
 }
 
+template <int HD, int GMAX>
+static minq_status launch_sk_inst(const AttnParams& p, const SkPlan& k, cudaStream_t s) {
+  const size_t smem = tma_attn_smem<HD, GMAX>();
+  auto kern = attn_sk_kernel<HD, GMAX>;
+  MINQ_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem));
+  MINQ_CUDA_TRY(launch_k(kern, dim3((unsigned)k.G), dim3(160), smem, s, p, k));
+  return MINQ_OK;
+}
+
+template <int HD>
+static minq_status launch_sk_hd(const AttnParams& p, const SkPlan& k, int gmax, cudaStream_t s) {
+  switch (gmax) {
+    case 1: return launch_sk_inst<HD, 1>(p, k, s);
+    case 2: return launch_sk_inst<HD, 2>(p, k, s);
+    case 4: return launch_sk_inst<HD, 4>(p, k, s);
+    default: return launch_sk_inst<HD, 8>(p, k, s);
+  }
+}
+
+// The stream-K plan (attn_sk_kernel) for `batch` entries of `len` positions:
+// three CTAs per SM (MINQ_ATTN_SK_CTAS: 1..3 per SM, 0 keeps the
+// split-per-unit plan), taken when there are at least 16 units and 24
+// tiles per CTA. Measured on B200 (GQA 32/8, head_dim 128), against the
+// split-per-unit plan: B 64 / L 8192 4.42 -> 5.91 TB/s, B 64 / L 2048 3.97
+// -> 5.15, B 8 / L 32768 4.67 -> 5.69, B 8 / L 8192 4.01 -> 4.51, B 64 /
+// L 512 3.00 -> 3.50; slower below those sizes (one sequence: 2-35 %, its
+// split plan already fills the SMs evenly; B 8 / L <= 2048: 4-20 %), and
+// two CTAs per SM slower everywhere. False when the plan is not taken or
+// the partial slots do not fit `ws_bytes`.
+constexpr int kSkMinUnits = 16;
+constexpr int kSkMinTilesPerCta = 24;
+static bool attn_sk_plan(size_t batch, int nh, int nkv, int hd, int len, size_t ws_bytes,
+                         SkPlan* k, int* stride) {
+  static const int per_sm = [] {
+    const char* e = std::getenv("MINQ_ATTN_SK_CTAS");
+    return e ? std::max(0, std::min(3, std::atoi(e))) : 3;
+  }();
+  if (per_sm == 0 || len <= 0) return false;
+  const int tp = std::min(32, 2048 / hd);
+  const long long units = (long long)batch * nkv * ((nh / nkv + 7) / 8);
+  k->NT = (len + tp - 1) / tp;
+  k->T = units * k->NT;
+  k->G = per_sm * sm_count();
+  if (units < kSkMinUnits || k->T < (long long)kSkMinTilesPerCta * k->G) return false;
+  int mx = 0;
+  for (long long u = 0; u < units; ++u)
+    mx = std::max(mx, sk_cta_of(u * k->NT + k->NT - 1, *k) - sk_cta_of(u * k->NT, *k) + 1);
+  *stride = mx;
+  return batch * nh * (size_t)mx * (hd + 2) * sizeof(float) <= ws_bytes;
+}
+
 // Decode attention over `len` positions (host-known), or, when `d_pos` is
 // set, over *d_pos + 1 positions read on the device, with the grid sized
 // for `cap_len` positions (a graph-captured step replays for any length up
@@ -679,6 +944,31 @@ minq_status launch_attention(const float* q, const float* k, const float* v, siz
   const bool tma = hd >= 16 && hd <= 256 && (hd & (hd - 1)) == 0 && pos_stride == (size_t)hd &&
                    (uintptr_t)k % 16 == 0 && (uintptr_t)v % 16 == 0 &&
                    seq_stride % 4 == 0 && head_stride % 4 == 0;
+  // host-known histories of one length: the balanced stream-K plan
+  SkPlan sk{};
+  int sk_stride = 0;
+  if (tma && !d_pos && len_step == 0 && ws &&
+      attn_sk_plan(batch, nh, nkv, hd, len, ws_bytes, &sk, &sk_stride)) {
+    p.scale = 1.0f / sqrtf((float)hd);
+    p.out = out;
+    p.ws_stride = sk_stride;
+    p.ws_o = static_cast<float*>(ws);
+    p.ws_ml = p.ws_o + batch * nh * (size_t)sk_stride * hd;
+    ScopedKTimer timer(KF_ATTENTION, s, 8.0 * batch * nkv * hd * (double)len + 8.0 * batch * nh * hd);
+    switch (hd) {
+      case 16: MINQ_TRY(launch_sk_hd<16>(p, sk, gmax, s)); break;
+      case 32: MINQ_TRY(launch_sk_hd<32>(p, sk, gmax, s)); break;
+      case 64: MINQ_TRY(launch_sk_hd<64>(p, sk, gmax, s)); break;
+      case 128: MINQ_TRY(launch_sk_hd<128>(p, sk, gmax, s)); break;
+      default: MINQ_TRY(launch_sk_hd<256>(p, sk, gmax, s)); break;
+    }
+    MINQ_LAUNCH_CHECK("attn_sk_kernel");
+    MINQ_CUDA_TRY(launch_k(attn_sk_combine_kernel, dim3((unsigned)(batch * nh)),
+                           dim3(std::min(hd, 128)), 0, s, (const float*)p.ws_o,
+                           (const float*)p.ws_ml, sk, nh, nkv, sk_stride, hd, out));
+    MINQ_LAUNCH_CHECK("attn_sk_combine_kernel");
+    return MINQ_OK;
+  }
   attn_split_plan(tma, batch, nh, nkv, hd, size_len, &p.chunk, &p.q_round);
   p.nsplit = (size_len + p.chunk - 1) / p.chunk;  // grid (split slots)
   p.ws_stride = p.nsplit;

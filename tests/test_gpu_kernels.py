@@ -184,9 +184,28 @@ def test_gpu_attend_matches_oracle(mq, orc, torch, nh, nkv, hd, L):
 def test_gpu_attn_decode_step_matches_oracle(mq, orc, torch, B, L, qk_norm):
     """Decode-attention op (GQA 32/8, hd 128): RoPE(theta 1e6) on q and the new k at
     pos = L, optional q/k RMSNorm, append, attend over L+1 positions — against the
-    oracle's per_head_norm + RopeTables + attend for every sequence."""
+    oracle's per_head_norm + RopeTables + attend for every sequence. From B = 8 /
+    L = 8192 and B = 64 / L = 512 on, the balanced (stream-K) plan runs."""
+    _attn_decode_check(orc, torch, B, L, qk_norm, 32, 8, 128, range(B))
+
+
+@pytest.mark.parametrize("nh,nkv,hd,B,L", [(14, 2, 64, 64, 6000), (32, 2, 128, 16, 3000),
+                                           (8, 8, 256, 16, 4000)])
+def test_gpu_attn_balanced_plan_head_layouts(mq, orc, torch, nh, nkv, hd, B, L):
+    """The balanced (stream-K) plan on other head layouts: head_dim 64 (32-position
+    tiles), 16 query heads per kv head (two query groups of 8), head_dim 256 with
+    one query head per kv head; ragged last tiles. Sequences at both ends and one
+    in the middle are checked against the oracle."""
+    orc.set_attn_parallel(True)
+    try:
+        _attn_decode_check(orc, torch, B, L, False, nh, nkv, hd, (0, B // 2 + 1, B - 1))
+    finally:
+        orc.set_attn_parallel(False)
+
+
+def _attn_decode_check(orc, torch, B, L, qk_norm, nh, nkv, hd, check):
     from minq_b200 import _lib
-    nh, nkv, hd, eps = 32, 8, 128, 1e-6
+    eps = 1e-6
     rng = np.random.default_rng(B * 1000 + L)
     max_seq = L + 1
     cs, sn = orc.rope_tables(hd, max_seq, 1e6)
@@ -210,7 +229,7 @@ def test_gpu_attn_decode_step_matches_oracle(mq, orc, torch, B, L, qk_norm):
     torch.cuda.synchronize()
     got = out.cpu().numpy()
     kc_after = d["kc"].cpu().numpy()
-    for b in range(B):
+    for b in check:
         qb, kb = q[b].reshape(-1).copy(), kn[b].reshape(-1).copy()
         if qk_norm:
             qb = orc.per_head_norm(qb, qg, eps, hd)

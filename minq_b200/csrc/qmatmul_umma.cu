@@ -401,7 +401,7 @@ __global__ void __launch_bounds__(UmGeom<DT, NP>::THREADS, 1)
                     const __grid_constant__ CUtensorMap mxh, const __grid_constant__ CUtensorMap mxl,
                     UmParams p) {
   using G = UmGeom<DT, NP>;
-  constexpr int ROWS = G::ROWS, NN = G::NN, CW = G::CW;
+  constexpr int ROWS = G::ROWS, CW = G::CW;
   constexpr int HR = DUAL ? ROWS / 2 : ROWS;  // rows of each matrix in this CTA
   extern __shared__ unsigned char um_sm[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;

@@ -17,8 +17,10 @@
 //     and V. Producer k owns the tiles k, k + 4, ... and so its own slots. The
 //     producers run ahead across phase and layer boundaries, so HBM keeps
 //     streaming while the consumers wait at a grid barrier. (One CTA per SM
-//     issuing TMA copies was measured at half of the HBM bandwidth; cp.async
-//     from several warps sustains it.)
+//     issuing TMA copies of the weights was measured at half of the HBM
+//     bandwidth; cp.async from several warps sustains it. For the K/V
+//     history the opposite holds at long lengths: from kMkBulkMinLen
+//     positions on, each attention tile is two 1-D bulk copies.)
 //   * 16 consumer warps execute the phases of each layer:
 //       P1 q|k|v = W_qkv rmsnorm(x) + bias                 (rows split over CTAs)
 //       P2 attention: CTA = (kv head, split of the history); q/k RMSNorm +
@@ -71,6 +73,13 @@ constexpr int kMkProducers = 4;                // copy warps; warp k issues tile
 constexpr int kMkThreads = kMkConsumers + 32 * kMkProducers;
 constexpr int kMkSlot = 16384;                 // bytes per ring slot
 constexpr int kMkS = 8;                        // ring slots (a multiple of kMkProducers)
+// From this history length on, attention tiles come in by two 1-D bulk
+// copies (K, V) instead of 1024 16-byte cp.async pieces: measured on the
+// Qwen3-4B shape in Q8_0, 4.55 -> 3.74 ms per token at 32768 positions and
+// 2.41 -> 2.37 ms at 4096 (with the pieces, the step time followed the
+// number of producer warps, not the ring depth), but 1.916 -> 1.935 ms in
+// Q4_0 at 2048, where the pieces stay.
+constexpr int kMkBulkMinLen = 3072;
 static_assert(kMkS % kMkProducers == 0, "each producer warp owns its own slots");
 // Projection inputs are staged as exact fixed-point planes: per 32-column
 // block, m = rint(x * 2^(kMkFx - e)) with 2^(e-1) <= max|x| < 2^e, written
@@ -353,7 +362,8 @@ __device__ __forceinline__ void mk_feed_skip(MkFeed& f) {
 // lanes, then have the slot's full barrier track the copies
 // (cp.async.mbarrier.arrive). Projection tiles: a contiguous run of the
 // CTA's blocks (gate and up alternating in the gate/up phase). Attention
-// tiles: the pieces of K (swizzled) and of V. False on abort.
+// tiles: the pieces of K (swizzled) and of V, or from kMkBulkMinLen on two
+// bulk copies. False on abort.
 template <int DT>
 __device__ bool mk_issue(const MkParams& p, MkFeed& f, const MkCta* cta, int L) {
   constexpr int BB = DT == MINQ_Q8_0 ? kQ8Bytes : kQ4Bytes;
@@ -370,6 +380,22 @@ __device__ bool mk_issue(const MkParams& p, MkFeed& f, const MkCta* cta, int L) 
     const int p0 = (cta->t0 + f.idx) * tp, np = min(tp, L - p0);
     const size_t off = (size_t)f.li * p.cache_layer_stride + (size_t)cta->kh * p.max_seq * hd +
                        (size_t)p0 * hd;
+    if (L >= kMkBulkMinLen) {
+      // K and V rows of the tile are contiguous runs of the head-major
+      // cache: one 1-D bulk copy each (the TMA engine), completing on the
+      // slot's full barrier as transaction bytes; the other lanes arrive
+      // without a copy, so the barrier still counts the warp's 32 lanes
+      const uint32_t bytes = (uint32_t)(np * hd * 4);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&f.full[slot], 2 * bytes);
+        bulk_g2s(dst, p.kc + off, bytes, &f.full[slot]);
+        bulk_g2s(dst + tp * hd * 4, p.vc + off, bytes, &f.full[slot]);
+      } else {
+        mbar_arrive(&f.full[slot]);
+      }
+      mk_feed_skip(f);
+      return true;
+    }
     // K row r's 16-byte chunk c lands at chunk c ^ (r mod 16) of the row (16
     // <= the chunks per row), so the consumer's lane r reads chunk c of its
     // row where every lane reads chunk c of q without a bank conflict
@@ -404,16 +430,31 @@ __device__ bool mk_issue(const MkParams& p, MkFeed& f, const MkCta* cta, int L) 
 template <int DT>
 __device__ void mk_producer(const MkParams& p, MkFeed& f, const MkCta* cta, int L) {
   const int k = ((int)threadIdx.x - kMkConsumers) >> 5;
+  int last[kMkS / kMkProducers];  // the last tile issued into each own slot
+#pragma unroll
+  for (int j = 0; j < kMkS / kMkProducers; ++j) last[j] = -1;
   if (!*reinterpret_cast<volatile int*>(p.abort_flag)) {
     while (mk_feed_settle(p, f, cta)) {
       if (f.issued % kMkProducers == k) {
+        const int it = f.issued;
         if (!mk_issue<DT>(p, f, cta, L)) break;
+        last[(it % kMkS) / kMkProducers] = it;
       } else {
         mk_feed_skip(f);
       }
     }
   }
-  asm volatile("cp.async.wait_all;" ::: "memory");  // nothing in flight at exit
+  // nothing in flight at exit (the consumers skip their waits after an
+  // abort): this warp's cp.async pieces, then the bulk copies, whose
+  // completion is the full phase of the slot's last tile (time-bounded)
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  if ((threadIdx.x & 31) == 0) {
+#pragma unroll
+    for (int j = 0; j < kMkS / kMkProducers; ++j)
+      if (last[j] >= 0)
+        mbar_wait_timed(&f.full[last[j] % kMkS], (uint32_t)(last[j] / kMkS) & 1u, p.status);
+  }
+  __syncwarp();
 }
 
 // Consumer wait for the tile `it`; never leaves the caller's barrier
@@ -918,7 +959,8 @@ __device__ void mk_head_prep(const MkParams& p, const float* src, const float* g
 // the score of position l mod 16 for head l / 16. The running max m and sum
 // l are replicated in every lane, o[g] holds the lane's dims of head g; only
 // heads g < gw are live. Ks: K rows in the producer's swizzled chunk order
-// (swz) or plain (the new position); V: plain rows. np >= 1 positions.
+// (swz: the cp.async tiles) or plain (bulk-copied tiles, the new position);
+// V: plain rows. np >= 1 positions.
 template <int DPL>
 __device__ __forceinline__ void mk_attn_tile(const float (&q)[2][DPL], int gw, uint32_t Ks,
                                              bool swz, uint32_t V, int np, float scale,
@@ -1016,8 +1058,8 @@ __device__ __forceinline__ void mk_attn_tile(const float (&q)[2][DPL], int gw, u
 }
 
 // Attention phase of one CTA: kv head kh, history tiles [t0, t1) of TP
-// positions (swizzled K rows, then V rows, in the slot) and, in the head's
-// last split, the new position. The query heads form HG = ceil(G / 2) pairs;
+// positions (K rows, swizzled below kMkBulkMinLen, then V rows, in the
+// slot) and, in the head's last split, the new position. The query heads form HG = ceil(G / 2) pairs;
 // warp w serves pair w mod HG on the tiles t0 + w / HG, t0 + w / HG + 16 / HG,
 // ..., the new position going to the warps next in that order; the warp
 // states then merge
@@ -1084,8 +1126,8 @@ __device__ void mk_consume_attn(const MkParams& p, int li, int L, unsigned hbase
     const uint32_t cnt_rel = warp % HG == 0 ? (uint32_t)(kMkCW - HG + 1) : 1u;
     for (int i = slot; i < ntile; i += WPG) {
       const uint32_t kt = smem_u32(mk_next_tile(p, f, it + i));
-      mk_attn_tile<DPL>(q, gw, kt, true, kt + (uint32_t)(TP * HD * 4), min(TP, L - (t0 + i) * TP),
-                        p.scale, m, l, o);
+      mk_attn_tile<DPL>(q, gw, kt, L < kMkBulkMinLen, kt + (uint32_t)(TP * HD * 4),
+                        min(TP, L - (t0 + i) * TP), p.scale, m, l, o);
       mk_release(f, it + i, cnt_rel);
     }
   }
